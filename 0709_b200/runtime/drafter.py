@@ -1,0 +1,303 @@
+"""Drafter runtime: frontier decode over the native paged route pool.
+
+The drafter keeps one committed prefix (page list) and a view per live route
+(shared prefix pages + a short list of private tail pages).  A frontier step:
+1. forks pool views for routes created since the last step,
+2. plans one appended token per route (in-place lease or tail-page COW),
+3. runs one batched forward (COW page copies first, then the model, whose
+   attention reads the shared prefix once for every row),
+4. returns logits and host-reserved node ids (no device round trip for ids).
+
+Commit promotes the selected stage-1 route's pages into the prefix without
+copying KV and rebases the retained stage-2 routes; fallback drops every route
+and extends the prefix with one causal EXTEND forward.
+
+Parity: reference src/atlas_0709/flashinfer_paged/sglang_runtime.py:1120-1346
+(SGLangFlashInferFrontierModelBackend), :800-959 (prepare_frontier), :1171-1251
+(known-token EXTEND), :1256-1297 (commit_stage1_and_promote).
+"""
+
+from __future__ import annotations
+
+import time
+from typing import Any, Sequence
+
+import torch
+
+from ..ops import _native
+from ..ops.attn_desc import AttnDesc
+from ..types import DraftPrefixState, FrontierDecodeOutput, PrefixKVView, RouteState
+from .engine import LlamaEngine
+from .store import KVTreeStore
+
+
+class PrefixPageMirror:
+    """Device copy of a pool's prefix page list, updated incrementally."""
+
+    def __init__(self, capacity: int, device: torch.device) -> None:
+        self.dev = torch.zeros(int(capacity), dtype=torch.int32, device=device)
+        self.host: list[int] = []
+        self.h2d_copies = 0
+
+    def sync(self, pages: torch.Tensor) -> None:
+        new = pages.tolist()
+        if len(new) > self.dev.numel():
+            grown = torch.zeros(max(len(new), 2 * self.dev.numel()), dtype=torch.int32, device=self.dev.device)
+            grown[: self.dev.numel()].copy_(self.dev)
+            self.dev = grown
+        start = 0
+        n = min(len(new), len(self.host))
+        while start < n and new[start] == self.host[start]:
+            start += 1
+        if start < len(new):
+            self.dev[start: len(new)].copy_(pages[start:].to(self.dev.device, non_blocking=True))
+            self.h2d_copies += 1
+        self.host = new
+
+    def view(self) -> torch.Tensor:
+        return self.dev[: max(1, len(self.host))]
+
+
+class DrafterRuntime:
+    def __init__(
+        self,
+        engine: LlamaEngine,
+        *,
+        page_pool: Any | None = None,
+        prefill_chunk_size: int = 8192,
+        max_tail_pages: int = 8,
+    ) -> None:
+        self.engine = engine
+        self.host = _native.host()
+        self.page_pool = page_pool if page_pool is not None else self.host.PagePool(engine.num_pages, engine.page_size)
+        self.route_pool = self.host.RoutePool(self.page_pool)
+        self.page_size = engine.page_size
+        self.prefill_chunk_size = int(prefill_chunk_size)
+        self.max_tail_pages = int(max_tail_pages)
+        self.device = engine.device
+        self.mirror = PrefixPageMirror(1024, self.device)
+        self.route_store: KVTreeStore | None = None
+        self.prefix_token_ids: tuple[int, ...] = ()
+        self.prefix_next_token_logits: torch.Tensor | None = None
+        self.counters = {
+            "decode_steps": 0,
+            "decode_rows": 0,
+            "attention_metadata_page_indices": 0,
+            "hot_path_host_transfer_batches": 0,
+            "hot_path_host_transfer_elements": 0,
+            "extend_calls": 0,
+            "extend_tokens": 0,
+        }
+
+    # ---------------------------------------------------------------- store
+    def bind_store(self, store: KVTreeStore) -> None:
+        self.route_store = store
+        store.add_route_release_hook(self._fork_children)
+
+    def _fork_children(self, previous: Sequence[RouteState], nxt: Sequence[RouteState]) -> None:
+        for child in nxt:
+            if child.parent_route_id is not None and not self.route_pool.has_route(child.route_id):
+                self.route_pool.fork(int(child.route_id), int(child.parent_route_id))
+
+    # -------------------------------------------------------------- prefix
+    def _sync_prefix(self) -> None:
+        self.mirror.sync(self.route_pool.prefix_pages())
+
+    def reset(self) -> None:
+        self.route_pool.clear()
+        self.prefix_token_ids = ()
+        self.prefix_next_token_logits = None
+        self.mirror.host = []
+
+    @torch.inference_mode()
+    def prefill(self, prompt_token_ids: Sequence[int]) -> DraftPrefixState:
+        toks = tuple(int(t) for t in prompt_token_ids)
+        if not toks:
+            raise ValueError("drafter prefill requires a non-empty prompt")
+        self.reset()
+        slots, copies = self.route_pool.append_prefix(len(toks))
+        self.engine.copy_pages(copies)
+        self._sync_prefix()
+        logits = self.engine.prefill_sequence(
+            torch.tensor(toks, dtype=torch.int32).to(self.device),
+            start_pos=0,
+            slots=slots.to(self.device),
+            pages=self.mirror.view(),
+            chunk_size=self.prefill_chunk_size,
+        )
+        self.prefix_token_ids = toks
+        self.prefix_next_token_logits = logits.unsqueeze(0)
+        if self.route_store is not None:
+            self.route_store.committed_token_ids = list(toks)
+        return self.prefix_state()
+
+    def prefix_state(self) -> DraftPrefixState:
+        assert self.prefix_next_token_logits is not None
+        return DraftPrefixState(
+            token_ids=torch.tensor(self.prefix_token_ids, dtype=torch.long),
+            prefix_kv_view=PrefixKVView(committed_length=len(self.prefix_token_ids)),
+            next_token_logits=self.prefix_next_token_logits,
+            committed_length=len(self.prefix_token_ids),
+        )
+
+    # -------------------------------------------------------------- decode
+    def _ensure_views(self, routes: Sequence[RouteState]) -> None:
+        rp = self.route_pool
+        for r in routes:
+            rid = int(r.route_id)
+            if rp.has_route(rid):
+                continue
+            parent = r.parent_route_id
+            if parent is not None and rp.has_route(int(parent)):
+                rp.fork(rid, int(parent))
+            else:
+                rp.fork_from_prefix(rid)
+            if rp.route_len(rid) != r.kv_view.length:
+                raise RuntimeError(
+                    f"route {rid} physical length {rp.route_len(rid)} != logical length {r.kv_view.length}"
+                )
+
+    def row_descriptor(self, rids: Sequence[int]) -> tuple[AttnDesc, torch.Tensor]:
+        tails, lens = self.route_pool.row_tables(list(rids), self.max_tail_pages)
+        dev = self.device
+        lens_d = lens.to(dev, non_blocking=True)
+        desc = AttnDesc(
+            prefix_pages=self.mirror.view(),
+            n_shared_pages=int(self.route_pool.prefix_full_pages),
+            shared_len=int(self.route_pool.prefix_len),
+            mask_base=int(self.route_pool.prefix_len),
+            row_full=lens_d,
+            row_len=lens_d,
+            row_mask=torch.full((len(rids), 1), -1, dtype=torch.int64, device=dev),
+            tail_pages=tails.to(dev, non_blocking=True),
+        )
+        return desc, lens
+
+    @torch.inference_mode()
+    def decode_frontier_one_token(
+        self, active_routes: Sequence[RouteState], attention_backend: Any = None
+    ) -> FrontierDecodeOutput:
+        if self.route_store is None:
+            raise RuntimeError("bind_store() must be called before decoding")
+        t0 = time.perf_counter()
+        self._ensure_views(active_routes)
+        rids = [int(r.route_id) for r in active_routes]
+        slots, copies = self.route_pool.prepare_append(rids)
+        self.engine.copy_pages(copies)
+        desc, lens = self.row_descriptor(rids)
+        dev = self.device
+        tokens = torch.tensor([int(r.pending_token_id) for r in active_routes], dtype=torch.int32)
+        positions = lens - 1
+        logits = self.engine.forward(
+            tokens.to(dev, non_blocking=True), positions.to(dev, non_blocking=True), slots.to(dev, non_blocking=True), desc
+        )
+        node_ids = tuple(self.route_store.reserve_node_ids(len(active_routes)))
+        c = self.counters
+        c["decode_steps"] += 1
+        c["decode_rows"] += len(rids)
+        c["attention_metadata_page_indices"] += int(self.route_pool.prefix_full_pages) + int(desc.tail_pages.numel())
+        return FrontierDecodeOutput(
+            route_ids=torch.tensor(rids, dtype=torch.long),
+            next_token_logits=logits,
+            new_node_ids=node_ids,
+            new_node_ids_cpu=node_ids,
+            model_ms=(time.perf_counter() - t0) * 1000.0,
+            metadata={
+                "backend": "b200_native_paged_decode",
+                "paged_kv": True,
+                "route_tail_page_cow": True,
+                "shared_prefix_attention": True,
+                "cow_pages_copied_step": int(copies.shape[0]),
+                "cow_pages_copied_total": int(self.route_pool.cow_pages_copied),
+                "cow_tokens_copied_total": int(self.route_pool.cow_tokens_copied),
+                "attention_backend": str(attention_backend),
+            },
+        )
+
+    # -------------------------------------------------------------- commit
+    @torch.inference_mode()
+    def commit_stage1_and_promote(
+        self, *, committed_route: RouteState, retained_routes: Sequence[RouteState]
+    ) -> tuple[list[RouteState], dict[str, int]]:
+        store = self.route_store
+        assert store is not None
+        nodes = store.node_path_for_route(committed_route)
+        if not nodes:
+            raise ValueError("cannot commit a stage-1 route with no materialized nodes")
+        self._ensure_views([committed_route, *retained_routes])
+        keep = [int(r.route_id) for r in retained_routes]
+        released_routes, freed = self.route_pool.retain([*keep, int(committed_route.route_id)])
+        freed += self.route_pool.commit(int(committed_route.route_id))
+        tokens = store.commit_route(committed_route)
+        self.prefix_token_ids = (*self.prefix_token_ids, *tokens)
+        if self.route_pool.prefix_len != len(self.prefix_token_ids):
+            raise RuntimeError("drafter physical prefix diverged from the logical prefix")
+        promoted = store.promote_routes_after_commit(
+            committed_route, retained_routes, PrefixKVView(committed_length=len(self.prefix_token_ids))
+        )
+        self._sync_prefix()
+        live = {n for r in promoted for n in r.kv_view.node_ids}
+        for nid in [n for n in store.nodes if n not in live]:
+            del store.nodes[nid]
+        return promoted, {
+            "committed_kv_tokens": len(nodes),
+            "retained_routes": len(promoted),
+            "released_route_rows": int(released_routes) + 1,
+            "released_kv_pages": int(freed),
+        }
+
+    def drop_speculative(self) -> dict[str, int]:
+        released, freed = self.route_pool.retain([])
+        if self.route_store is not None:
+            self.route_store.reset_speculative()
+        return {"released_route_rows": int(released), "released_kv_pages": int(freed)}
+
+    @torch.inference_mode()
+    def append_known_tokens_as_prefix(self, token_ids: Sequence[int]) -> torch.Tensor:
+        """Extend the committed prefix by known tokens with one causal EXTEND forward."""
+        suffix = tuple(int(t) for t in token_ids)
+        if not suffix:
+            raise ValueError("known prefix extension cannot be empty")
+        if self.route_pool.num_routes:
+            raise RuntimeError("drop speculative routes before extending the prefix")
+        start = int(self.route_pool.prefix_len)
+        slots, copies = self.route_pool.append_prefix(len(suffix))
+        self.engine.copy_pages(copies)
+        self._sync_prefix()
+        logits = self.engine.prefill_sequence(
+            torch.tensor(suffix, dtype=torch.int32).to(self.device),
+            start_pos=start,
+            slots=slots.to(self.device),
+            pages=self.mirror.view(),
+            chunk_size=self.prefill_chunk_size,
+        )
+        self.prefix_token_ids = (*self.prefix_token_ids, *suffix)
+        self.prefix_next_token_logits = logits.unsqueeze(0)
+        self.counters["extend_calls"] += 1
+        self.counters["extend_tokens"] += len(suffix)
+        return logits
+
+    # ---------------------------------------------------------- validation
+    def validate_route_physical_state(self, route: RouteState) -> None:
+        rid = int(route.route_id)
+        if not self.route_pool.has_route(rid):
+            raise RuntimeError(f"Drafter route {rid} has no physical view")
+        if self.route_pool.route_len(rid) != route.kv_view.length:
+            raise RuntimeError(
+                f"Drafter route {rid} physical length does not match logical KV: "
+                f"physical={self.route_pool.route_len(rid)}, logical={route.kv_view.length}"
+            )
+        self.route_pool.validate()
+
+    def page_reference_counts(self) -> dict[int, int]:
+        return dict(sorted(self.route_pool.recomputed_refcounts().items()))
+
+    def hot_path_counters(self) -> dict[str, int]:
+        return {
+            **self.counters,
+            "cow_pages_copied": int(self.route_pool.cow_pages_copied),
+            "cow_tokens_copied": int(self.route_pool.cow_tokens_copied),
+            "in_place_appends": int(self.route_pool.in_place_appends),
+            "prefix_page_h2d_copies": int(self.mirror.h2d_copies),
+            "pool_used_pages": int(self.page_pool.used_pages),
+        }

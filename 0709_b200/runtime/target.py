@@ -1,0 +1,652 @@
+"""Target verifier: one deduplicated, ancestor-masked tree forward per round.
+
+A persistent session holds the committed prefix in a page list of the native
+pool.  ``verify_payloads`` builds the prefix trie of the k stage-1 paths (the
+native ``build_tree``), writes the unique nodes' KV to scratch positions
+``P..P+N-1`` of the same page list in one forward whose attention reads the
+prefix once for all nodes and masks the node region by ancestry, scores every
+path from the node logits with optional front-loaded weights, selects a route
+(best of k, seeded route-level sampling, or the first route), and then either
+compacts the selected nodes' KV in place into positions ``P..P+d-1`` (one
+multi-layer move kernel) or, on low confidence, runs greedy AR decoding whose
+argmax chain stays on the device.
+
+Parity: reference src/atlas_0709/target_runtime.py:33-935 (validation,
+selection, sampling audit, intervention metadata, truncation, fallback
+reasons and order, commit semantics, runtime metadata).
+"""
+
+from __future__ import annotations
+
+import hashlib
+import json
+import math
+import time
+from typing import Sequence
+
+import torch
+
+from ..ops import _native
+from ..ops.attn_desc import AttnDesc, single_sequence_desc
+from ..types import PrefixState, TargetRouteScore, TargetVerifyResult, VerifyRoutePayload
+from .drafter import PrefixPageMirror
+from .engine import LlamaEngine
+
+ROUTE_SAMPLE_DOMAIN = "atlas0709-target-route-sample-v1"
+
+
+def validate_score_weights(weights: Sequence[float] | None) -> tuple[float, ...] | None:
+    if weights is None:
+        return None
+    vals = tuple(float(v) for v in weights)
+    if not vals:
+        return None
+    if any(v < 0.0 for v in vals):
+        raise ValueError("score weights must be non-negative")
+    total = sum(vals)
+    if total <= 0.0:
+        raise ValueError("at least one score weight must be positive")
+    return tuple(v / total for v in vals)
+
+
+def token_path_hash(token_ids: Sequence[int]) -> str:
+    payload = json.dumps([int(t) for t in token_ids], separators=(",", ":")).encode("utf-8")
+    return hashlib.sha256(payload).hexdigest()
+
+
+class TargetVerifier:
+    def __init__(
+        self,
+        engine: LlamaEngine,
+        *,
+        k: int = 3,
+        d: int = 4,
+        page_pool=None,
+        score_weights: Sequence[float] | None = None,
+        fallback_threshold: float | None = None,
+        first_token_threshold: float | None = None,
+        fallback_ar_tokens: int = 4,
+        profile_fallback_ar: bool = False,
+        route_selection_policy: str = "target_best",
+        route_sampling_temperature: float = 1.0,
+        model_name: str = "random-init",
+        prefill_chunk_size: int = 8192,
+    ) -> None:
+        self.engine = engine
+        self.k = int(k)
+        self.d = int(d)
+        if self.k <= 0 or self.d <= 0:
+            raise ValueError("k and d must be positive")
+        self.host = _native.host()
+        self.page_pool = page_pool if page_pool is not None else self.host.PagePool(engine.num_pages, engine.page_size)
+        self.seq = self.host.RoutePool(self.page_pool)
+        self.device = engine.device
+        self.page_size = engine.page_size
+        self.mirror = PrefixPageMirror(1024, self.device)
+        self.score_weights = validate_score_weights(score_weights)
+        self.fallback_threshold = None if fallback_threshold is None else float(fallback_threshold)
+        self.first_token_threshold = None if first_token_threshold is None else float(first_token_threshold)
+        self.fallback_ar_tokens = int(fallback_ar_tokens)
+        if self.fallback_ar_tokens <= 0:
+            raise ValueError("fallback_ar_tokens must be positive")
+        self.profile_fallback_ar = bool(profile_fallback_ar)
+        policy = str(route_selection_policy).strip().lower()
+        if policy not in {"target_best", "target_sample", "first_route"}:
+            raise ValueError("route_selection_policy must be one of: target_best, target_sample, first_route")
+        self.route_selection_policy = policy
+        temp = float(route_sampling_temperature)
+        if not math.isfinite(temp) or temp <= 0.0:
+            raise ValueError("route_sampling_temperature must be finite and positive")
+        self.route_sampling_temperature = temp
+        if policy == "first_route" and (self.fallback_threshold is not None or self.first_token_threshold is not None):
+            raise ValueError(
+                "first_route is a strict diagnostic policy and requires fallback thresholds to be disabled"
+            )
+        self.model_name = model_name
+        self.prefill_chunk_size = int(prefill_chunk_size)
+        self.prefix_token_ids: tuple[int, ...] = ()
+        self._prefix_logits: torch.Tensor | None = None
+        self._committed_verify_rounds = 0
+        self._last_fallback_ar_profile: dict[str, object] | None = None
+
+    # -------------------------------------------------------------- prefill
+    def _sync(self) -> None:
+        self.mirror.sync(self.seq.prefix_pages())
+
+    @torch.inference_mode()
+    def prefill(self, prompt_token_ids: Sequence[int]) -> PrefixState:
+        toks = tuple(int(t) for t in prompt_token_ids)
+        if not toks:
+            raise ValueError("target prefill requires a non-empty prompt")
+        self.seq.clear()
+        self.mirror.host = []
+        slots, _ = self.seq.append_prefix(len(toks))
+        self._sync()
+        logits = self.engine.prefill_sequence(
+            torch.tensor(toks, dtype=torch.int32).to(self.device),
+            start_pos=0,
+            slots=slots.to(self.device),
+            pages=self.mirror.view(),
+            chunk_size=self.prefill_chunk_size,
+        )
+        self.prefix_token_ids = toks
+        self._prefix_logits = logits
+        self._committed_verify_rounds = 0
+        self._last_fallback_ar_profile = None
+        return PrefixState(
+            token_ids=toks, next_token_logits=logits, committed_length=len(toks), metadata=self.runtime_metadata()
+        )
+
+    # --------------------------------------------------------------- verify
+    @torch.inference_mode()
+    def verify_payloads(
+        self,
+        *,
+        prefix_token_ids: Sequence[int],
+        routes: Sequence[VerifyRoutePayload],
+        fallback_max_tokens: int | None = None,
+        selected_path_max_tokens: int | None = None,
+        eos_token_id: int | None = None,
+        route_sampling_seed: int | None = None,
+        route_sampling_round: int | None = None,
+    ) -> TargetVerifyResult:
+        prefix = tuple(int(t) for t in prefix_token_ids)
+        if self._prefix_logits is None:
+            self.prefill(prefix)
+        elif prefix != self.prefix_token_ids:
+            raise RuntimeError(
+                "target committed prefix mismatch; incremental verify cannot silently rebuild KV: "
+                f"request_len={len(prefix)}, target_len={len(self.prefix_token_ids)}"
+            )
+        paths, depth = self._validate_routes(routes)
+        tree = self.run_tree(paths)
+        scores = self._score_routes(routes, paths, tree["path_logprobs"])
+        best = max(scores, key=self._best_key)
+        selected, sampling_meta = self._select_route_with_metadata(
+            scores, route_sampling_seed=route_sampling_seed, route_sampling_round=route_sampling_round
+        )
+        reason = self._fallback_reason(selected)
+        p_before = len(self.prefix_token_ids)
+        common = {
+            **self.runtime_metadata(),
+            "route_count": len(routes),
+            "path_depth": int(depth),
+            "node_count": int(tree["node_count"]),
+            "unmerged_path_node_count": int(len(routes) * depth),
+            "kv_len": int(p_before + tree["node_count"]),
+            "prefix_len_before": int(p_before),
+            "selection_policy": self._selection_policy_name(),
+            "selection_score_name": (
+                "weighted_target_logprob" if self.score_weights is not None else "target_logprob"
+            ),
+            "fallback_threshold": self.fallback_threshold,
+            "first_token_threshold": self.first_token_threshold,
+            "fallback_ar_tokens": int(self.fallback_ar_tokens),
+            **sampling_meta,
+            **self._route_intervention_metadata(scores, selected),
+        }
+        best_fields = {
+            "best_route_id": int(best.route_id),
+            "best_selection_score": float(best.effective_selection_score),
+            "best_first_token_logprob": (
+                None if best.first_token_logprob is None else float(best.first_token_logprob)
+            ),
+        }
+        if reason is not None:
+            limit = self.fallback_ar_tokens if fallback_max_tokens is None else min(
+                int(fallback_max_tokens), self.fallback_ar_tokens
+            )
+            generated = self._generate_fallback_ar(max_tokens=limit, eos_token_id=eos_token_id)
+            return TargetVerifyResult(
+                selected_route_id=None,
+                scores=scores,
+                decision="fallback_ar",
+                fallback_token_ids=tuple(generated),
+                fallback_reason=reason,
+                metadata={
+                    **common,
+                    "prefix_len_after": int(len(self.prefix_token_ids)),
+                    "target_kv_commit": "fallback_ar_in_place",
+                    "target_reprefill_after_verify": False,
+                    "fallback_triggered": True,
+                    "fallback_reason": reason,
+                    "fallback_token_count": int(len(generated)),
+                    **best_fields,
+                    "fallback_ar_profile": self._last_fallback_ar_profile,
+                },
+            )
+        idx = next(i for i, r in enumerate(routes) if int(r.route_id) == int(selected.route_id))
+        node_path = tree["node_paths"][idx]
+        committed_path, committed_nodes = self._truncate_selected_path(
+            token_ids=paths[idx], node_ids=node_path, max_tokens=selected_path_max_tokens, eos_token_id=eos_token_id
+        )
+        self._commit_selected_path(committed_path, committed_nodes, tree["logits"])
+        return TargetVerifyResult(
+            selected_route_id=selected.route_id,
+            scores=scores,
+            metadata={
+                **common,
+                "prefix_len_after": int(len(self.prefix_token_ids)),
+                "target_kv_commit": "selected_tree_path_in_place",
+                "target_reprefill_after_verify": False,
+                "fallback_triggered": False,
+                **best_fields,
+                "selected_route_id": int(selected.route_id),
+                "selected_selection_score": float(selected.effective_selection_score),
+                "selected_path_committed_tokens": int(len(committed_path)),
+                "selected_path_was_truncated": bool(len(committed_path) != len(paths[idx])),
+            },
+        )
+
+    def _validate_routes(self, routes: Sequence[VerifyRoutePayload]) -> tuple[list[tuple[int, ...]], int]:
+        if not routes:
+            raise ValueError("verify requires at least one route")
+        if len(routes) != self.k:
+            raise ValueError(f"verify route count does not match configured k: routes={len(routes)}, k={self.k}")
+        ids = [int(r.route_id) for r in routes]
+        if len(set(ids)) != len(ids):
+            raise ValueError("verify route ids must be unique")
+        paths = [tuple(int(t) for t in r.token_ids) for r in routes]
+        for r, p in zip(routes, paths):
+            if r.draft_token_logprobs and len(r.draft_token_logprobs) != len(p):
+                raise ValueError(
+                    "draft_token_logprobs must be empty or match route depth: "
+                    f"route_id={int(r.route_id)}, values={len(r.draft_token_logprobs)}, depth={len(p)}"
+                )
+        lengths = {len(p) for p in paths}
+        if len(lengths) != 1:
+            raise ValueError(f"all verify routes must have the same depth, got {sorted(lengths)}")
+        depth = next(iter(lengths))
+        if depth <= 0:
+            raise ValueError("verify routes must contain at least one token")
+        if depth != self.d:
+            raise ValueError(f"verify route depth does not match configured d: depth={depth}, d={self.d}")
+        return paths, depth
+
+    # ------------------------------------------------------- tree forward
+    @torch.inference_mode()
+    def run_tree(self, paths: Sequence[Sequence[int]]) -> dict[str, object]:
+        """One masked forward over the deduplicated trie; returns logits and path log-probs."""
+        tokens, parents, depths, node_paths, masks = self.host.build_tree(
+            torch.tensor([list(p) for p in paths], dtype=torch.int64)
+        )
+        n = int(tokens.numel())
+        p = len(self.prefix_token_ids)
+        scratch = self.seq.reserve_scratch(p + n)
+        self._sync()
+        dev = self.device
+        lens = torch.full((n,), p + n, dtype=torch.int32)
+        desc = single_sequence_desc(
+            self.mirror.view(),
+            lens.to(dev, non_blocking=True),
+            shared_len=p,
+            mask_base=p,
+            masks=masks.to(dev, non_blocking=True),
+            full=torch.full((n,), p, dtype=torch.int32).to(dev, non_blocking=True),
+        )
+        positions = (depths + p).to(torch.int32)
+        logits = self.engine.forward(
+            tokens.to(torch.int32).to(dev, non_blocking=True),
+            positions.to(dev, non_blocking=True),
+            scratch.to(dev, non_blocking=True),
+            desc,
+        )
+        # Path log-probs: token t of route r is scored by the prefix row (t == 0)
+        # or by its parent node's row; one gather, one host transfer.
+        r_, d_ = node_paths.shape
+        rows = torch.full((r_, d_), -1, dtype=torch.long)
+        rows[:, 1:] = node_paths[:, :-1].long()
+        toks = torch.tensor([list(x) for x in paths], dtype=torch.long)
+        lp = self.gather_logprobs(logits, rows, toks)
+        return {
+            "logits": logits,
+            "node_count": n,
+            "node_paths": node_paths.tolist(),
+            "parents": parents.tolist(),
+            "path_logprobs": lp,
+        }
+
+    def gather_logprobs(self, logits: torch.Tensor, rows: torch.Tensor, toks: torch.Tensor) -> list[list[float]]:
+        assert self._prefix_logits is not None
+        dev = logits.device
+        allrows = torch.cat((self._prefix_logits.reshape(1, -1).float(), logits.float()), dim=0)
+        lse = torch.logsumexp(allrows, dim=-1)
+        r = (rows + 1).to(dev)
+        t = toks.to(dev)
+        vals = allrows[r, t] - lse[r]
+        return vals.double().cpu().tolist()
+
+    # -------------------------------------------------------------- scoring
+    def _weights_for_depth(self, depth: int) -> tuple[float, ...] | None:
+        if self.score_weights is None:
+            return None
+        if len(self.score_weights) != int(depth):
+            raise ValueError(
+                f"score weights must match verify route depth: weights={len(self.score_weights)}, depth={depth}"
+            )
+        return self.score_weights
+
+    def _score_routes(self, routes, paths, path_lp) -> list[TargetRouteScore]:
+        out: list[TargetRouteScore] = []
+        for route, path, lps in zip(routes, paths, path_lp):
+            lps = [float(v) for v in lps]
+            total = sum(lps)
+            w = self._weights_for_depth(len(lps))
+            sel = total if w is None else sum(a * b for a, b in zip(w, lps))
+            out.append(
+                TargetRouteScore(
+                    route_id=int(route.route_id),
+                    token_ids=tuple(path),
+                    target_logprob=total,
+                    draft_logprob=float(route.draft_logprob),
+                    token_logprobs=tuple(lps),
+                    first_token_logprob=lps[0],
+                    selection_score=sel,
+                    score_weights=() if w is None else tuple(w),
+                    draft_token_logprobs=tuple(float(v) for v in route.draft_token_logprobs),
+                )
+            )
+        return out
+
+    @staticmethod
+    def _best_key(s: TargetRouteScore):
+        return (s.effective_selection_score, s.draft_path_logprob, -s.route_id)
+
+    def _selection_policy_name(self) -> str:
+        if self.route_selection_policy == "first_route":
+            return "diagnostic_first_payload_route"
+        if self.route_selection_policy == "target_sample":
+            return (
+                "sample_target_route_logprob_distribution"
+                if self.score_weights is None
+                else "sample_weighted_target_route_score_distribution"
+            )
+        return "best_of_n_target_path_logprob" if self.score_weights is None else "best_of_n_weighted_target_path_logprob"
+
+    def _sampling_disabled(self) -> dict[str, object]:
+        return {
+            "route_sampling_enabled": False,
+            "route_sampling_scope": "verified_route_level_only",
+            "route_sampling_seed": None,
+            "route_sampling_round": None,
+            "route_sampling_temperature": float(self.route_sampling_temperature),
+        }
+
+    def _select_route_with_metadata(self, scores, *, route_sampling_seed=None, route_sampling_round=None):
+        if not scores:
+            raise ValueError("cannot select from an empty route score list")
+        if self.route_selection_policy == "first_route":
+            return scores[0], self._sampling_disabled()
+        if self.route_selection_policy == "target_sample":
+            return self._sample_route(scores, route_sampling_seed, route_sampling_round)
+        return max(scores, key=self._best_key), self._sampling_disabled()
+
+    def _sample_route(self, scores, seed, rnd):
+        """Seeded route-level draw (host-side, bit-exact replay).
+
+        Candidates are put in a canonical order (token path, draft score,
+        selection score, route id) so the draw does not depend on payload order;
+        the uniform is derived from SHA-256 of the domain, seed and round.
+        """
+        if seed is None or rnd is None:
+            raise ValueError(
+                "target_sample requires explicit route_sampling_seed and route_sampling_round on every verify request"
+            )
+        rnd = int(rnd)
+        if rnd < 0:
+            raise ValueError("route_sampling_round must be non-negative")
+        seed = int(seed)
+        ordered = sorted(
+            scores,
+            key=lambda s: (tuple(s.token_ids), float(s.draft_path_logprob), s.effective_selection_score, int(s.route_id)),
+        )
+        temp = self.route_sampling_temperature
+        logits = [s.effective_selection_score / temp for s in ordered]
+        if any(math.isnan(v) for v in logits):
+            raise ValueError("cannot sample a route from NaN target scores")
+        pos_inf = [math.isinf(v) and v > 0 for v in logits]
+        if any(pos_inf):
+            cnt = sum(pos_inf)
+            probs = [1.0 / cnt if f else 0.0 for f in pos_inf]
+        else:
+            finite = [v for v in logits if math.isfinite(v)]
+            if not finite:
+                probs = [1.0 / len(ordered)] * len(ordered)
+            else:
+                mx = max(finite)
+                ws = [0.0 if v == -math.inf else math.exp(v - mx) for v in logits]
+                tot = sum(ws)
+                probs = [w / tot for w in ws]
+        material = f"{ROUTE_SAMPLE_DOMAIN}:{seed}:{rnd}".encode("utf-8")
+        bits = int.from_bytes(hashlib.sha256(material).digest()[:8], "big")
+        u = (bits + 0.5) / float(1 << 64)
+        chosen, lo, hi, acc = len(ordered) - 1, 0.0, 1.0, 0.0
+        for i, pr in enumerate(probs):
+            nxt = acc + pr
+            if u < nxt or i == len(ordered) - 1:
+                chosen, lo = i, acc
+                hi = nxt if i < len(ordered) - 1 else 1.0
+                break
+            acc = nxt
+        return ordered[chosen], {
+            "route_sampling_enabled": True,
+            "route_sampling_scope": "verified_route_level_only",
+            "route_sampling_seed": seed,
+            "route_sampling_round": rnd,
+            "route_sampling_temperature": temp,
+            "route_sampling_uniform": float(u),
+            "route_sampling_selected_probability": float(probs[chosen]),
+            "route_sampling_selected_cdf_low": float(lo),
+            "route_sampling_selected_cdf_high": float(hi),
+            "route_sampling_boundary_margin": float(min(u - lo, hi - u)),
+            "route_sampling_ordered_candidates": [
+                {"route_id": int(s.route_id), "token_path_hash": token_path_hash(s.token_ids), "probability": float(pr)}
+                for s, pr in zip(ordered, probs)
+            ],
+        }
+
+    def _route_intervention_metadata(self, scores, selected) -> dict[str, object]:
+        if not scores:
+            raise ValueError("route intervention metadata requires non-empty scores")
+        route0 = scores[0]
+        order = sorted(enumerate(scores), key=lambda p: (-float(p[1].draft_path_logprob), int(p[0])))
+        ranks = {int(s.route_id): i for i, (_, s) in enumerate(order, start=1)}
+        top = order[0][1]
+
+        def summary(s: TargetRouteScore) -> dict[str, object]:
+            return {
+                "route_id": int(s.route_id),
+                "token_path_hash": token_path_hash(s.token_ids),
+                "first_token_id": int(s.token_ids[0]),
+                "draft_rank": int(ranks[int(s.route_id)]),
+                "draft_first_token_logprob": s.draft_first_token_logprob,
+                "draft_path_logprob": float(s.draft_path_logprob),
+                "legacy_cumulative_draft_logprob": float(s.draft_logprob),
+                "target_first_token_logprob": None if s.first_token_logprob is None else float(s.first_token_logprob),
+                "target_logprob": float(s.target_logprob),
+                "target_selection_score": float(s.effective_selection_score),
+            }
+
+        def delta(a, b):
+            return None if a is None or b is None else float(a) - float(b)
+
+        def compare(base: TargetRouteScore) -> dict[str, object]:
+            return {
+                "route_changed": tuple(selected.token_ids) != tuple(base.token_ids),
+                "first_token_changed": int(selected.token_ids[0]) != int(base.token_ids[0]),
+                "draft_first_token_logprob_delta": delta(
+                    selected.draft_first_token_logprob, base.draft_first_token_logprob
+                ),
+                "draft_path_logprob_delta": float(selected.draft_path_logprob) - float(base.draft_path_logprob),
+                "legacy_cumulative_draft_logprob_delta": float(selected.draft_logprob) - float(base.draft_logprob),
+                "target_first_token_logprob_delta": delta(selected.first_token_logprob, base.first_token_logprob),
+                "target_path_logprob_delta": float(selected.target_logprob) - float(base.target_logprob),
+                "target_selection_score_delta": selected.effective_selection_score - base.effective_selection_score,
+            }
+
+        v0, vt = compare(route0), compare(top)
+        return {
+            "route_intervention": {
+                "baseline": "route0",
+                "draft_token_logprobs_available": bool(all(s.draft_token_logprobs for s in scores)),
+                "route0_is_draft_top": int(route0.route_id) == int(top.route_id),
+                "route0": summary(route0),
+                "draft_top": summary(top),
+                "selected": summary(selected),
+                "selected_vs_route0": v0,
+                "selected_vs_draft_top": vt,
+            },
+            "selected_draft_rank": int(ranks[int(selected.route_id)]),
+            "route0_route_id": int(route0.route_id),
+            "draft_top_route_id": int(top.route_id),
+            "selected_route_changed_from_route0": bool(v0["route_changed"]),
+            "selected_first_token_changed_from_route0": bool(v0["first_token_changed"]),
+            "selected_minus_route0_draft_first_token_logprob": v0["draft_first_token_logprob_delta"],
+            "selected_minus_route0_draft_logprob": float(v0["draft_path_logprob_delta"]),
+            "selected_minus_route0_target_selection_score": float(v0["target_selection_score_delta"]),
+        }
+
+    @staticmethod
+    def _truncate_selected_path(*, token_ids, node_ids, max_tokens, eos_token_id):
+        if len(token_ids) != len(node_ids) or not token_ids:
+            raise ValueError("selected path tokens and node ids must have equal non-zero length")
+        limit = len(token_ids) if max_tokens is None else min(len(token_ids), int(max_tokens))
+        if limit <= 0:
+            raise ValueError("selected_path_max_tokens must be positive")
+        toks = [int(t) for t in token_ids[:limit]]
+        if eos_token_id is not None:
+            for i, t in enumerate(toks):
+                if t == int(eos_token_id):
+                    toks = toks[: i + 1]
+                    break
+        return tuple(toks), tuple(int(n) for n in node_ids[: len(toks)])
+
+    def _fallback_reason(self, selected: TargetRouteScore) -> str | None:
+        if (
+            self.first_token_threshold is not None
+            and selected.first_token_logprob is not None
+            and float(selected.first_token_logprob) < self.first_token_threshold
+        ):
+            return "first_token_below_threshold"
+        if self.fallback_threshold is not None and selected.effective_selection_score < self.fallback_threshold:
+            return "path_score_below_threshold"
+        return None
+
+    # --------------------------------------------------------------- commit
+    @torch.inference_mode()
+    def _commit_selected_path(self, token_ids, node_ids, logits: torch.Tensor) -> None:
+        if len(token_ids) != len(node_ids) or not node_ids:
+            raise ValueError("selected path tokens and node ids must have equal non-zero length")
+        p = len(self.prefix_token_ids)
+        moves = [(p + int(n), p + j) for j, n in enumerate(node_ids) if int(n) != j]
+        if moves:
+            src = torch.tensor([a for a, _ in moves], dtype=torch.int64)
+            dst = torch.tensor([b for _, b in moves], dtype=torch.int64)
+            src_slots = torch.cat([self.seq.slots_for_positions(int(a), 1) for a in src])
+            dst_slots = torch.cat([self.seq.slots_for_positions(int(b), 1) for b in dst])
+            self.engine.move_slots(src_slots, dst_slots)
+        self.seq.set_prefix_len(p + len(node_ids))
+        self._sync()
+        self.prefix_token_ids = (*self.prefix_token_ids, *(int(t) for t in token_ids))
+        self._prefix_logits = logits[int(node_ids[-1])].detach().clone()
+        self._committed_verify_rounds += 1
+
+    # ------------------------------------------------------------ fallback
+    def _profile_sync(self) -> None:
+        if self.device.type == "cuda":
+            torch.cuda.synchronize(self.device)
+
+    @torch.inference_mode()
+    def _generate_fallback_ar(self, *, max_tokens: int, eos_token_id: int | None) -> list[int]:
+        if self._prefix_logits is None:
+            raise RuntimeError("target fallback AR requires initialized prefix KV")
+        steps = int(max_tokens)
+        if steps <= 0:
+            return []
+        prof = self.profile_fallback_ar
+        t_setup = time.perf_counter()
+        p = len(self.prefix_token_ids)
+        slots = self.seq.reserve_scratch(p + steps)
+        self._sync()
+        if prof:
+            self._profile_sync()
+        setup_s = time.perf_counter() - t_setup
+        dev = self.device
+        toks = torch.empty(steps, dtype=torch.int32, device=dev)
+        all_logits: list[torch.Tensor] = []
+        cur = self._prefix_logits.reshape(1, -1)
+        t_model = time.perf_counter()
+        pages = self.mirror.view()
+        slots_d = slots.to(dev, non_blocking=True)
+        for t in range(steps):
+            toks[t: t + 1] = torch.argmax(cur, dim=-1).to(torch.int32)
+            pos = torch.tensor([p + t], dtype=torch.int32).to(dev, non_blocking=True)
+            desc = single_sequence_desc(pages, pos + 1, shared_len=p + t)
+            cur = self.engine.forward(toks[t: t + 1], pos, slots_d[t: t + 1], desc)
+            all_logits.append(cur)
+        generated = [int(x) for x in toks.cpu().tolist()]
+        if prof:
+            self._profile_sync()
+        model_s = time.perf_counter() - t_model
+        keep = len(generated)
+        if eos_token_id is not None:
+            for i, t in enumerate(generated):
+                if t == int(eos_token_id):
+                    keep = i + 1
+                    break
+        generated = generated[:keep]
+        self.seq.set_prefix_len(p + keep)
+        self._sync()
+        self._prefix_logits = all_logits[keep - 1][0].detach().clone()
+        self.prefix_token_ids = (*self.prefix_token_ids, *generated)
+        self._committed_verify_rounds += 1
+        self._last_fallback_ar_profile = (
+            {
+                "enabled": True,
+                "wrapper_was_cached": True,
+                "wrapper_setup_seconds": setup_s,
+                "decode_plan_seconds": 0.0,
+                "model_forward_seconds": model_s,
+                "token_count": len(generated),
+            }
+            if prof
+            else None
+        )
+        return generated
+
+    # ------------------------------------------------------------- metadata
+    def runtime_metadata(self) -> dict[str, object]:
+        cfg = self.engine.cfg
+        return {
+            "backend": "b200_native_masked_tree_verify",
+            "model": self.model_name,
+            "model_vocab_size": int(cfg.vocab_size),
+            "paged_kv": True,
+            "custom_mask": True,
+            "ancestor_mask_words": "per-node 64-bit words over the node region only",
+            "rope_applied": True,
+            "semantic_correctness_required": True,
+            "page_size": int(self.page_size),
+            "dtype": str(self.engine.dtype).replace("torch.", ""),
+            "device": str(self.device),
+            "persistent_target_paged_kv": True,
+            "deduplicated_tree_nodes": True,
+            "selection_policy": self._selection_policy_name(),
+            "route_selection_policy": self.route_selection_policy,
+            "route_sampling_scope": "verified_route_level_only",
+            "route_sampling_temperature": float(self.route_sampling_temperature),
+            "fallback_ar_sampling": "greedy_argmax",
+            "score_weights": None if self.score_weights is None else [float(v) for v in self.score_weights],
+            "fallback_threshold": self.fallback_threshold,
+            "first_token_threshold": self.first_token_threshold,
+            "fallback_ar_tokens": int(self.fallback_ar_tokens),
+            "profile_fallback_ar": self.profile_fallback_ar,
+            "committed_verify_rounds": self._committed_verify_rounds,
+            "committed_prefix_length": len(self.prefix_token_ids),
+            "k": self.k,
+            "d": self.d,
+        }
+
+    @property
+    def prefix_logits(self) -> torch.Tensor | None:
+        return self._prefix_logits

@@ -1,0 +1,594 @@
+"""Asynchronous tree/forest coordinator (the Edge/Drafter side).
+
+Round structure: send the k stage-1 paths to the Target; while it verifies,
+expand the k^2 forest one decode step at a time, checking for the verify
+result only between steps; then
+- ``select`` + completed forest: promote the selected root's k completed
+  stage-2 routes (zero-copy) -- they are the next stage-1 tree;
+- ``select`` + partial forest: promote the k active stage-2 routes and build
+  the remaining tree depths;
+- ``fallback_ar``: drop speculative routes, EXTEND the prefix with the Target's
+  tokens, build a fresh tree.
+Neither side re-prefills its history.
+
+Parity: reference src/atlas_0709/distributed_system.py:47-1216 (config,
+round traces, result JSON, handoff modes, timeline, warmup and CLI flags).
+"""
+
+from __future__ import annotations
+
+import math
+import time
+from concurrent.futures import ThreadPoolExecutor
+from dataclasses import dataclass, field
+from typing import Any, Sequence
+
+import torch
+
+from ..runtime.builders import (
+    build_forest_one_depth,
+    build_tree_depths,
+    build_tree_one_depth,
+    initialize_forest_routes,
+    initialize_stage1_routes,
+    select_routes_by_stage1_root,
+)
+from ..runtime.drafter import DrafterRuntime
+from ..runtime.sampling import DrafterSamplingConfig, DrafterSamplingContext
+from ..runtime.store import KVTreeStore
+from ..types import BuildDepthsOutput, RouteState
+from ..utils.timeline import EdgeBlackboxTimeline, EdgeRoundTimeline, EdgeSpan
+from .rpc import selected_route_id_from_response
+
+
+@dataclass(frozen=True)
+class DistributedAtlasConfig:
+    k: int = 3
+    d: int = 4
+    max_new_tokens: int = 64
+    eos_token_id: int | None = None
+    fallback_ar_tokens: int = 4
+    generation_seed: int = 0
+    drafter_do_sample: bool = False
+    drafter_temperature: float = 1.0
+    fixed_forest_depth: int | None = None
+    validate_state_alignment: bool = False
+
+    def validate(self) -> None:
+        if self.k <= 0:
+            raise ValueError("k must be positive")
+        if self.d <= 0:
+            raise ValueError("d must be positive")
+        if self.max_new_tokens <= 0:
+            raise ValueError("max_new_tokens must be positive")
+        if self.fallback_ar_tokens <= 0:
+            raise ValueError("fallback_ar_tokens must be positive")
+        t = float(self.drafter_temperature)
+        if not math.isfinite(t) or t <= 0.0:
+            raise ValueError("drafter_temperature must be finite and positive")
+        if self.fixed_forest_depth is not None and not 0 <= int(self.fixed_forest_depth) <= int(self.d):
+            raise ValueError("fixed_forest_depth must be between 0 and d")
+
+
+@dataclass
+class DistributedRoundTrace:
+    round_index: int
+    selected_route_id: int | None
+    committed_tokens: list[int]
+    decision: str
+    fallback_reason: str | None
+    fallback_token_ids: list[int]
+    forest_depth: int
+    verify_returned_before_forest_done: bool
+    target_scores: list[dict[str, object]]
+    handoff_mode: str
+    reused_stage2_routes: int
+    reused_stage2_depth: int
+    remaining_tree_depth: int
+    committed_kv_tokens: int
+    released_route_rows: int
+    released_kv_pages: int
+    target_unique_tree_nodes: int
+    target_unmerged_path_nodes: int
+    target_prefix_len_before: int
+    target_prefix_len_after: int
+    target_decision_metadata: dict[str, object] = field(default_factory=dict)
+
+    def to_dict(self) -> dict[str, object]:
+        return {k: getattr(self, k) for k in self.__dataclass_fields__}
+
+
+@dataclass
+class DistributedGenerationResult:
+    prompt_token_ids: list[int]
+    generated_token_ids: list[int]
+    text: str | None
+    rounds: list[DistributedRoundTrace] = field(default_factory=list)
+    metadata: dict[str, object] = field(default_factory=dict)
+
+    def to_dict(self) -> dict[str, object]:
+        return {
+            "prompt_token_ids": self.prompt_token_ids,
+            "generated_token_ids": self.generated_token_ids,
+            "token_ids": [*self.prompt_token_ids, *self.generated_token_ids],
+            "text": self.text,
+            "rounds": [r.to_dict() for r in self.rounds],
+            "metadata": self.metadata,
+        }
+
+
+@dataclass(frozen=True)
+class StageHandoff:
+    stage1: BuildDepthsOutput
+    mode: str
+    reused_stage2_routes: int
+    reused_stage2_depth: int
+    remaining_tree_depth: int
+    physical_stats: dict[str, int]
+    commit_prune_span: EdgeSpan | None = None
+    tree_step_spans: tuple[EdgeSpan, ...] = ()
+
+
+COMPACT_DECISION_KEYS = (
+    "selection_policy",
+    "route_sampling_enabled",
+    "route_sampling_scope",
+    "route_sampling_seed",
+    "route_sampling_round",
+    "route_sampling_temperature",
+    "route_sampling_uniform",
+    "route_sampling_selected_probability",
+    "route_sampling_selected_cdf_low",
+    "route_sampling_selected_cdf_high",
+    "route_sampling_boundary_margin",
+    "route_sampling_ordered_candidates",
+    "selected_draft_rank",
+    "route0_route_id",
+    "draft_top_route_id",
+    "selected_route_changed_from_route0",
+    "selected_first_token_changed_from_route0",
+    "selected_minus_route0_draft_first_token_logprob",
+    "selected_minus_route0_draft_logprob",
+    "selected_minus_route0_target_selection_score",
+    "route_intervention",
+    "best_selection_score",
+    "best_first_token_logprob",
+)
+
+
+class PagedDistributedAtlasGenerator:
+    """Drives one generation: drafter in this thread, Target through ``target_client``."""
+
+    system_name = "atlas_distributed_two_process"
+
+    def __init__(
+        self,
+        *,
+        config: DistributedAtlasConfig,
+        drafter: DrafterRuntime,
+        target_client: Any,
+        tokenizer=None,
+    ) -> None:
+        config.validate()
+        self.config = config
+        self.drafter = drafter
+        self.target_client = target_client
+        self.tokenizer = tokenizer
+        self.last_timeline: EdgeBlackboxTimeline | None = None
+        self._t0: float | None = None
+
+    # ------------------------------------------------------------ helpers
+    def _now(self) -> float:
+        if self._t0 is None:
+            raise RuntimeError("edge timeline clock has not been initialized")
+        return time.perf_counter() - self._t0
+
+    def _timed(self, name: str, fn, *args):
+        s = self._now()
+        out = fn(*args)
+        return out, EdgeSpan(name, s, self._now())
+
+    def _sampling_config(self) -> DrafterSamplingConfig:
+        c = self.config
+        return DrafterSamplingConfig(bool(c.drafter_do_sample), int(c.generation_seed), float(c.drafter_temperature))
+
+    def _sampling(self, committed: Sequence[int]) -> DrafterSamplingContext:
+        return DrafterSamplingContext(self._sampling_config(), tuple(int(t) for t in committed))
+
+    def _should_build_forest_step(self, *, verify_done: bool, forest_depth: int) -> bool:
+        if forest_depth >= self.config.d:
+            return False
+        if self.config.fixed_forest_depth is not None:
+            return forest_depth < int(self.config.fixed_forest_depth)
+        return not verify_done
+
+    def _should_stop(self, committed_now: Sequence[int], generated: Sequence[int]) -> bool:
+        if len(generated) >= self.config.max_new_tokens:
+            return True
+        eos = self.config.eos_token_id
+        return eos is not None and any(int(t) == int(eos) for t in committed_now)
+
+    def _truncate_commit(self, toks: Sequence[int], generated: Sequence[int]) -> list[int]:
+        out = [int(t) for t in toks[: self.config.max_new_tokens - len(generated)]]
+        eos = self.config.eos_token_id
+        if eos is not None:
+            for i, t in enumerate(out):
+                if t == int(eos):
+                    return out[: i + 1]
+        return out
+
+    def _route_payloads(self, store: KVTreeStore, routes: Sequence[RouteState]) -> list[dict[str, object]]:
+        return [
+            {
+                "route_id": int(r.route_id),
+                "token_ids": [int(t) for t in store.materialized_token_path(r)[: r.stage1_depth]],
+                "draft_logprob": float(r.cumulative_logprob),
+                "draft_token_logprobs": [float(v) for v in r.token_logprobs[: int(r.stage1_depth)]],
+            }
+            for r in routes
+        ]
+
+    @staticmethod
+    def _find_route(stage1: BuildDepthsOutput, route_id: int) -> RouteState:
+        for r in stage1.completed_routes:
+            if int(r.route_id) == int(route_id):
+                return r
+        raise KeyError(f"selected route_id={route_id} is not in the completed stage1 routes")
+
+    def _verify_call(self, committed, routes, remaining, round_index):
+        resp = self.target_client.verify(
+            prefix_token_ids=committed,
+            routes=routes,
+            fallback_max_tokens=min(int(self.config.fallback_ar_tokens), int(remaining)),
+            selected_path_max_tokens=int(remaining),
+            eos_token_id=self.config.eos_token_id,
+            route_sampling_seed=int(self.config.generation_seed),
+            route_sampling_round=int(round_index),
+        )
+        return resp, self._now()
+
+    # ----------------------------------------------------------- generate
+    def generate(self, prompt_token_ids: Sequence[int]) -> DistributedGenerationResult:
+        cfg = self.config
+        committed = [int(t) for t in prompt_token_ids]
+        generated: list[int] = []
+        traces: list[DistributedRoundTrace] = []
+        fallback_profiles: list[dict[str, object]] = []
+        health = self.target_client.health()
+        target_meta = dict(health.get("metadata", {}))
+        self._t0 = time.perf_counter()
+        rounds_tl: list[EdgeRoundTimeline] = []
+        store = KVTreeStore()
+        self.drafter.bind_store(store)
+        pre_frontier = pre_completed = pre_logits = None
+        pre_depth = 0
+        pre_spans: list[EdgeSpan] = []
+        sampling0 = self._sampling(committed)
+
+        with ThreadPoolExecutor(max_workers=1) as pool:
+            tfut = pool.submit(self._timed, "cloud_prompt_blackbox", self.target_client.prefill, committed)
+            _, edge_prefill = self._timed("edge_prompt_prefill", self.drafter.prefill, committed)
+            store.committed_token_ids = list(committed)
+            t_tree = self._now()
+            active = initialize_stage1_routes(
+                self.drafter.prefix_state(), k=cfg.k, route_store=store, sampling=sampling0
+            )
+            stage1 = build_tree_depths(
+                active, depth=cfg.d, k=cfg.k, route_store=store, model_backend=self.drafter, sampling=sampling0
+            )
+            initial_tree = EdgeSpan("edge_initial_stage1_tree", t_tree, self._now())
+            if cfg.fixed_forest_depth is None and not tfut.done():
+                pre_frontier = initialize_forest_routes(
+                    stage1.completed_routes, stage1.last_logits, k=cfg.k, route_store=store, sampling=sampling0
+                )
+                while not tfut.done() and pre_depth < cfg.d:
+                    s0 = self._now()
+                    step = build_forest_one_depth(
+                        pre_frontier, k=cfg.k, route_store=store, model_backend=self.drafter, sampling=sampling0
+                    )
+                    pre_depth += 1
+                    pre_spans.append(EdgeSpan(f"edge_forest_step_{pre_depth}", s0, self._now()))
+                    pre_completed = step.decoded_routes
+                    pre_logits = step.decode_output.next_token_logits
+                    pre_frontier = step.next_routes
+            _, cloud_prefill = tfut.result()
+
+        round_index = 0
+        with ThreadPoolExecutor(max_workers=1) as vpool:
+            while len(generated) < cfg.max_new_tokens:
+                rs = self._sampling(committed)
+                p_round = len(committed)
+                payload = self._route_payloads(store, stage1.completed_routes)
+                v_submit = self._now()
+                remaining = cfg.max_new_tokens - len(generated)
+                vfut = vpool.submit(self._verify_call, list(committed), payload, remaining, round_index)
+                if round_index == 0 and pre_frontier is not None:
+                    f_depth, f_done, f_logits, f_spans, f_front = pre_depth, pre_completed, pre_logits, list(pre_spans), pre_frontier
+                else:
+                    f_depth, f_done, f_logits, f_spans = 0, None, None, []
+                    f_front = initialize_forest_routes(
+                        stage1.completed_routes, stage1.last_logits, k=cfg.k, route_store=store, sampling=rs
+                    )
+                while self._should_build_forest_step(verify_done=vfut.done(), forest_depth=f_depth):
+                    s0 = self._now()
+                    step = build_forest_one_depth(
+                        f_front, k=cfg.k, route_store=store, model_backend=self.drafter, sampling=rs
+                    )
+                    f_depth += 1
+                    f_spans.append(EdgeSpan(f"edge_forest_step_{f_depth}", s0, self._now()))
+                    f_done, f_logits, f_front = step.decoded_routes, step.decode_output.next_token_logits, step.next_routes
+                early = f_depth < cfg.d and vfut.done()
+                resp, v_done = vfut.result()
+                vspan = EdgeSpan("cloud_verify_blackbox", v_submit, v_done)
+                tmeta = dict(resp.get("metadata", {}))
+                prof = tmeta.get("fallback_ar_profile")
+                if isinstance(prof, dict):
+                    fallback_profiles.append({"round_index": round_index, **prof})
+                decision = str(resp.get("decision", "select"))
+                sel_id: int | None = None
+                reason: str | None = None
+                fb_tokens: list[int] = []
+                mode = "stopped"
+                reused = reused_depth = remaining_depth = 0
+                phys = {"committed_kv_tokens": 0, "released_route_rows": 0, "released_kv_pages": 0}
+                handoff_span: EdgeSpan | None = None
+                post_spans: list[EdgeSpan] = []
+                if decision == "fallback_ar":
+                    fb_tokens = [int(t) for t in resp.get("fallback_token_ids", [])]
+                    reason = None if resp.get("fallback_reason") is None else str(resp.get("fallback_reason"))
+                    if len(fb_tokens) > remaining:
+                        raise RuntimeError(
+                            "target fallback returned more tokens than the remaining budget: "
+                            f"returned={len(fb_tokens)}, remaining={remaining}"
+                        )
+                    now = list(fb_tokens)
+                    generated.extend(now)
+                    committed.extend(now)
+                    stop = not now or self._should_stop(now, generated)
+                    mode = "fallback_ar_stopped" if stop else "fallback_ar_extend_prefix_kv"
+                    if not stop:
+                        s0 = self._now()
+                        stage1, phys = self._fallback_extend_handoff(store, now)
+                        handoff_span = EdgeSpan("edge_fallback_extend_then_build_tree", s0, self._now())
+                elif decision == "select":
+                    sel_id = selected_route_id_from_response(resp)
+                    sel = self._find_route(stage1, sel_id)
+                    full = list(store.materialized_token_path(sel)[: cfg.d])
+                    now = self._truncate_commit(full, generated)
+                    generated.extend(now)
+                    committed.extend(now)
+                    stop = not now or self._should_stop(now, generated)
+                    if not stop:
+                        if now != full:
+                            raise RuntimeError("cannot reuse stage-2 KV after a partial stage-1 commit")
+                        h = self._handoff_after_verify(
+                            store=store,
+                            selected_stage1_route=sel,
+                            forest_depth=f_depth,
+                            forest_frontier=f_front,
+                            forest_completed=f_done,
+                            forest_last_logits=f_logits,
+                            sampling=self._sampling(committed),
+                        )
+                        handoff_span, post_spans = h.commit_prune_span, list(h.tree_step_spans)
+                        stage1, mode = h.stage1, h.mode
+                        reused, reused_depth, remaining_depth = (
+                            h.reused_stage2_routes,
+                            h.reused_stage2_depth,
+                            h.remaining_tree_depth,
+                        )
+                        phys = h.physical_stats
+                else:
+                    raise RuntimeError(f"unknown target verify decision: {decision!r}")
+                if cfg.validate_state_alignment:
+                    self._validate_target_prefix_lengths(tmeta, p_round, len(committed))
+                    if not stop:
+                        self._validate_drafter_prefix_state(
+                            store, committed, [*stage1.completed_routes, *stage1.next_frontier_routes]
+                        )
+                traces.append(
+                    DistributedRoundTrace(
+                        round_index=round_index,
+                        selected_route_id=sel_id,
+                        committed_tokens=[int(t) for t in now],
+                        decision=decision,
+                        fallback_reason=reason,
+                        fallback_token_ids=list(fb_tokens),
+                        forest_depth=f_depth,
+                        verify_returned_before_forest_done=early,
+                        target_scores=list(resp.get("scores", [])),
+                        handoff_mode=mode,
+                        reused_stage2_routes=reused,
+                        reused_stage2_depth=reused_depth,
+                        remaining_tree_depth=remaining_depth,
+                        committed_kv_tokens=int(phys["committed_kv_tokens"]),
+                        released_route_rows=int(phys["released_route_rows"]),
+                        released_kv_pages=int(phys["released_kv_pages"]),
+                        target_unique_tree_nodes=int(tmeta.get("node_count", 0)),
+                        target_unmerged_path_nodes=int(tmeta.get("unmerged_path_node_count", 0)),
+                        target_prefix_len_before=int(tmeta.get("prefix_len_before", len(committed) - len(now))),
+                        target_prefix_len_after=int(tmeta.get("prefix_len_after", len(committed))),
+                        target_decision_metadata={k: tmeta[k] for k in COMPACT_DECISION_KEYS if k in tmeta},
+                    )
+                )
+                rounds_tl.append(
+                    EdgeRoundTimeline(
+                        round_index=round_index,
+                        verify_blackbox=vspan,
+                        forest_steps=f_spans,
+                        post_prune_tree_steps=post_spans,
+                        handoff=handoff_span,
+                        forest_depth=f_depth,
+                        accepted_tokens=len(now),
+                        generated_tokens=len(generated),
+                        handoff_mode=mode,
+                        verify_returned_before_forest_done=early,
+                    )
+                )
+                round_index += 1
+                if stop:
+                    break
+
+        elapsed = self._now()
+        timeline = EdgeBlackboxTimeline(edge_prefill, cloud_prefill, initial_tree, rounds_tl, elapsed, len(generated))
+        self.last_timeline = timeline
+        text = self.tokenizer.decode(committed) if self.tokenizer is not None else None
+        fb_rounds = sum(t.decision == "fallback_ar" for t in traces)
+        return DistributedGenerationResult(
+            prompt_token_ids=[int(t) for t in prompt_token_ids],
+            generated_token_ids=generated,
+            text=text,
+            rounds=traces,
+            metadata={
+                "system": self.system_name,
+                "drafter_backend": "b200_native_paged_decode",
+                "target_backend": target_meta.get("backend", "b200_native_masked_tree_verify"),
+                "target_transport": str(health.get("transport", "http")),
+                "target_health": health,
+                "k": cfg.k,
+                "d": cfg.d,
+                "max_new_tokens": cfg.max_new_tokens,
+                "fallback_ar_tokens": int(cfg.fallback_ar_tokens),
+                "generation_seed": int(cfg.generation_seed),
+                "drafter_sampling": self._sampling_config().to_dict(),
+                "fixed_forest_depth": cfg.fixed_forest_depth,
+                "validate_state_alignment": bool(cfg.validate_state_alignment),
+                "rebuild_drafter_prefix_after_commit": False,
+                "rebuild_drafter_prefix_after_fallback": False,
+                "fallback_drafter_handoff": "single_multi_token_extend",
+                "target_fallback_ar_profiles": fallback_profiles,
+                "rebuild_target_prefix_after_commit": False,
+                "cross_round_stage2_kv_reuse": True,
+                "cross_round_target_kv_reuse": True,
+                "target_selection_policy": target_meta.get("selection_policy"),
+                "target_route_selection_policy": target_meta.get("route_selection_policy"),
+                "route_tail_page_cow": True,
+                "branch_safe_page_size": True,
+                "forest_cancel_granularity": "between_decode_steps",
+                "rounds": len(traces),
+                "fallback_rounds": fb_rounds,
+                "fallback_rate": fb_rounds / len(traces) if traces else None,
+                "edge_blackbox_timeline": timeline.summary(),
+                "drafter_hot_path_counters": self.drafter.hot_path_counters(),
+            },
+        )
+
+    # ------------------------------------------------------------ handoffs
+    def _fallback_extend_handoff(self, store: KVTreeStore, tokens: Sequence[int]):
+        suffix = [int(t) for t in tokens]
+        if not suffix:
+            raise ValueError("fallback handoff requires at least one Target token")
+        dropped = self.drafter.drop_speculative()
+        store.committed_token_ids.extend(suffix)
+        self.drafter.append_known_tokens_as_prefix(suffix)
+        rs = self._sampling(store.committed_token_ids)
+        active = initialize_stage1_routes(self.drafter.prefix_state(), k=self.config.k, route_store=store, sampling=rs)
+        stage1 = build_tree_depths(
+            active, depth=self.config.d, k=self.config.k, route_store=store, model_backend=self.drafter, sampling=rs
+        )
+        return stage1, {
+            "committed_kv_tokens": len(suffix),
+            "retained_routes": 0,
+            "released_route_rows": dropped["released_route_rows"],
+            "released_kv_pages": dropped["released_kv_pages"],
+        }
+
+    def _handoff_after_verify(
+        self,
+        *,
+        store: KVTreeStore,
+        selected_stage1_route: RouteState,
+        forest_depth: int,
+        forest_frontier: Sequence[RouteState],
+        forest_completed: Sequence[RouteState] | None,
+        forest_last_logits: torch.Tensor | None,
+        sampling: DrafterSamplingContext,
+    ) -> StageHandoff:
+        cfg = self.config
+        root = int(selected_stage1_route.route_id)
+        clock = self._now if self._t0 is not None else time.perf_counter
+        if forest_depth >= cfg.d:
+            if forest_completed is None or forest_last_logits is None:
+                raise RuntimeError("completed forest is missing its decoded routes or logits")
+            idx = [i for i, r in enumerate(forest_completed) if int(r.stage1_root_id) == root]
+            if len(idx) != cfg.k:
+                raise RuntimeError(
+                    "completed forest does not contain k routes for the selected stage-1 root: "
+                    f"expected={cfg.k}, got={len(idx)}"
+                )
+            s0 = clock()
+            promoted, phys = self.drafter.commit_stage1_and_promote(
+                committed_route=selected_stage1_route, retained_routes=[forest_completed[i] for i in idx]
+            )
+            span = EdgeSpan("edge_commit_prune", s0, clock())
+            sel = torch.tensor(idx, dtype=torch.long, device=forest_last_logits.device)
+            return StageHandoff(
+                stage1=BuildDepthsOutput(promoted, [], forest_last_logits.index_select(0, sel), []),
+                mode="completed_forest_reused",
+                reused_stage2_routes=len(promoted),
+                reused_stage2_depth=cfg.d,
+                remaining_tree_depth=0,
+                physical_stats=phys,
+                commit_prune_span=span,
+            )
+        retained = select_routes_by_stage1_root(forest_frontier, root)
+        if len(retained) != cfg.k:
+            raise RuntimeError(
+                "partial forest does not contain k active routes for the selected stage-1 root: "
+                f"expected={cfg.k}, got={len(retained)}"
+            )
+        s0 = clock()
+        promoted, phys = self.drafter.commit_stage1_and_promote(
+            committed_route=selected_stage1_route, retained_routes=retained
+        )
+        span = EdgeSpan("edge_commit_prune", s0, clock())
+        depths = {int(r.stage1_depth) for r in promoted}
+        if depths != {int(forest_depth)}:
+            raise RuntimeError(
+                f"promoted route depth does not match completed forest depth: route_depths={sorted(depths)}, "
+                f"forest_depth={forest_depth}"
+            )
+        remaining = cfg.d - int(forest_depth)
+        steps = []
+        spans: list[EdgeSpan] = []
+        front = list(promoted)
+        for i in range(remaining):
+            s1 = clock()
+            st = build_tree_one_depth(front, k=cfg.k, route_store=store, model_backend=self.drafter, sampling=sampling)
+            spans.append(EdgeSpan(f"edge_post_prune_tree_step_{i + 1}", s1, clock()))
+            steps.append(st)
+            front = st.next_routes
+        last = steps[-1]
+        return StageHandoff(
+            stage1=BuildDepthsOutput(last.decoded_routes, last.next_routes, last.decode_output.next_token_logits, steps),
+            mode="partial_forest_pruned_then_build_tree",
+            reused_stage2_routes=len(promoted),
+            reused_stage2_depth=int(forest_depth),
+            remaining_tree_depth=remaining,
+            physical_stats=phys,
+            commit_prune_span=span,
+            tree_step_spans=tuple(spans),
+        )
+
+    # ---------------------------------------------------------- validators
+    @staticmethod
+    def _validate_target_prefix_lengths(meta: dict, before: int, after: int) -> None:
+        ob, oa = int(meta.get("prefix_len_before", -1)), int(meta.get("prefix_len_after", -1))
+        if ob != before or oa != after:
+            raise RuntimeError(
+                f"Target committed-prefix length diverged from the coordinator: target={ob}->{oa}, "
+                f"coordinator={before}->{after}"
+            )
+
+    def _validate_drafter_prefix_state(self, store: KVTreeStore, committed, routes) -> None:
+        exp = [int(t) for t in committed]
+        if list(self.drafter.prefix_token_ids) != exp or list(store.committed_token_ids) != exp:
+            raise RuntimeError("Drafter logical committed prefix diverged from the coordinator")
+        if int(self.drafter.route_pool.prefix_len) != len(exp):
+            raise RuntimeError(
+                f"Drafter physical prefix length diverged from the coordinator: "
+                f"slots={int(self.drafter.route_pool.prefix_len)}, tokens={len(exp)}"
+            )
+        for r in routes:
+            if self.drafter.route_pool.has_route(int(r.route_id)):
+                self.drafter.validate_route_physical_state(r)
