@@ -1,0 +1,31 @@
+// Host/device interface of the paged attention kernels (head_dim 128).
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace atlas {
+
+struct AttnParams {
+  const void* q;         // [M, Hq, 128] rotated queries
+  const void* kv;        // cache [L, pages, 2, Hkv, page_size, 128]
+  void* out;             // [M, Hq, 128]
+  const int* dparams;    // device scalars: shared_len, n_shared_pages, mask_base
+  const int* prefix_pages;
+  const int* row_full;   // [M]
+  const int* row_len;    // [M]
+  const int64_t* row_mask;  // [M, mask_words]
+  const int* tail_pages;    // [M, tail_stride]
+  float* part_o;         // [splits, M, Hq, 128]
+  float2* part_ml;       // [splits, M, Hq] (running max in log2 units, sum)
+  int* err;
+  int M, Hq, Hkv, page_size, num_pages, layer;
+  int mask_words, tail_stride, splits, direct_out, bf16;
+  float scale;
+};
+
+void launch_attention(const CUtensorMap& kvmap, const AttnParams& p, bool run_tc, bool run_combine, int row_tiles,
+                      cudaStream_t st);
+
+}  // namespace atlas

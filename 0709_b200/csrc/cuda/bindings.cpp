@@ -1,0 +1,357 @@
+// Python bindings of the sm_100a kernels (torch tensors in, launches on the
+// current CUDA stream).  Also owns TMA descriptor creation: tensor maps are
+// encoded on the host through the driver entry point (no libcuda link) and
+// cached per (address, shape, box).
+
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <cuda.h>
+#include <cudaTypedefs.h>
+#include <torch/extension.h>
+
+#include <cstring>
+#include <mutex>
+#include <unordered_map>
+
+#include "attention.h"
+#include "gemm.h"
+#include "kernels.h"
+
+namespace {
+
+using atlas::AttnParams;
+using atlas::GemmParams;
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    cudaError_t e = cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q);
+    if (e == cudaSuccess && q == cudaDriverEntryPointSuccess) fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  TORCH_CHECK(fn != nullptr, "cuTensorMapEncodeTiled is not available from the CUDA driver");
+  return fn;
+}
+
+struct MapKey {
+  uint64_t ptr;
+  uint64_t d[5];
+  uint32_t box[5];
+  int rank;
+  int dtype;
+  bool operator==(const MapKey& o) const { return std::memcmp(this, &o, sizeof(MapKey)) == 0; }
+};
+struct MapKeyHash {
+  size_t operator()(const MapKey& k) const {
+    size_t h = std::hash<uint64_t>()(k.ptr);
+    for (int i = 0; i < 5; ++i) h = h * 1000003u ^ std::hash<uint64_t>()(k.d[i] * 31 + k.box[i]);
+    return h ^ (k.rank * 7 + k.dtype);
+  }
+};
+
+std::mutex g_map_mu;
+std::unordered_map<MapKey, CUtensorMap, MapKeyHash> g_maps;
+
+CUtensorMapDataType tma_dtype(torch::ScalarType t) {
+  if (t == torch::kBFloat16) return CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+  TORCH_CHECK(t == torch::kHalf, "TMA operands must be fp16 or bf16");
+  return CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+}
+
+// Row-major [outer, inner] with row stride `ld` elements; box {64, box_outer}, 128B swizzle.
+CUtensorMap map_2d(const torch::Tensor& t, int64_t inner, int64_t outer, int64_t ld, int box_outer) {
+  MapKey k{};
+  k.ptr = reinterpret_cast<uint64_t>(t.data_ptr());
+  k.d[0] = inner;
+  k.d[1] = outer;
+  k.d[2] = ld;
+  k.box[0] = 64;
+  k.box[1] = box_outer;
+  k.rank = 2;
+  k.dtype = static_cast<int>(t.scalar_type());
+  std::lock_guard<std::mutex> g(g_map_mu);
+  auto it = g_maps.find(k);
+  if (it != g_maps.end()) return it->second;
+  if (g_maps.size() > 8192) g_maps.clear();
+  CUtensorMap m;
+  cuuint64_t dims[2] = {static_cast<cuuint64_t>(inner), static_cast<cuuint64_t>(outer)};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(ld) * t.element_size()};
+  cuuint32_t box[2] = {64, static_cast<cuuint32_t>(box_outer)};
+  cuuint32_t es[2] = {1, 1};
+  CUresult r = encode_fn()(&m, tma_dtype(t.scalar_type()), 2, t.data_ptr(), dims, strides, box, es,
+                           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  TORCH_CHECK(r == CUDA_SUCCESS, "cuTensorMapEncodeTiled (2d) failed: ", static_cast<int>(r));
+  g_maps.emplace(k, m);
+  return m;
+}
+
+// KV cache [L, NP, 2, Hkv, ps, hd] as 5-D {hd, ps, Hkv, 2, L*NP}; box {64, ps, 1, 1, 1}.
+CUtensorMap map_kv(const torch::Tensor& kv) {
+  TORCH_CHECK(kv.dim() == 6 && kv.is_contiguous(), "kv cache must be a contiguous [L, NP, 2, Hkv, ps, hd] tensor");
+  const int64_t L = kv.size(0), NP = kv.size(1), Hkv = kv.size(3), ps = kv.size(4), hd = kv.size(5);
+  MapKey k{};
+  k.ptr = reinterpret_cast<uint64_t>(kv.data_ptr());
+  k.d[0] = hd;
+  k.d[1] = ps;
+  k.d[2] = Hkv;
+  k.d[3] = 2;
+  k.d[4] = L * NP;
+  k.box[0] = 64;
+  k.box[1] = static_cast<uint32_t>(ps);
+  k.rank = 5;
+  k.dtype = static_cast<int>(kv.scalar_type());
+  std::lock_guard<std::mutex> g(g_map_mu);
+  auto it = g_maps.find(k);
+  if (it != g_maps.end()) return it->second;
+  CUtensorMap m;
+  const int64_t es_b = kv.element_size();
+  cuuint64_t dims[5] = {static_cast<cuuint64_t>(hd), static_cast<cuuint64_t>(ps), static_cast<cuuint64_t>(Hkv), 2,
+                        static_cast<cuuint64_t>(L * NP)};
+  cuuint64_t strides[4] = {static_cast<cuuint64_t>(hd * es_b), static_cast<cuuint64_t>(ps * hd * es_b),
+                           static_cast<cuuint64_t>(Hkv * ps * hd * es_b),
+                           static_cast<cuuint64_t>(2 * Hkv * ps * hd * es_b)};
+  cuuint32_t box[5] = {64, static_cast<cuuint32_t>(ps), 1, 1, 1};
+  cuuint32_t es[5] = {1, 1, 1, 1, 1};
+  CUresult r = encode_fn()(&m, tma_dtype(kv.scalar_type()), 5, kv.data_ptr(), dims, strides, box, es,
+                           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  TORCH_CHECK(r == CUDA_SUCCESS, "cuTensorMapEncodeTiled (kv) failed: ", static_cast<int>(r));
+  g_maps.emplace(k, m);
+  return m;
+}
+
+int pick_bn(int64_t n) {
+  if (n <= 16) return 16;
+  if (n <= 32) return 32;
+  if (n <= 64) return 64;
+  if (n <= 128) return 128;
+  return 256;
+}
+
+int ctas_per_sm(int bn) {
+  const int smem = atlas::gemm_smem_bytes(bn) + 1024;
+  return std::max(1, std::min(2, (228 * 1024) / smem));
+}
+
+// Split-K factor: fill ~all CTA slots when the tile count alone cannot; a
+// function of (M, K, bn) only, so a row's result never depends on batch size
+// within one bn bucket.
+std::pair<int, int> pick_splits(int64_t M, int64_t N, int64_t K, int bn, int num_sms) {
+  const int64_t tiles = ((M + 127) / 128) * ((N + bn - 1) / bn);
+  const int64_t kb = (K + 63) / 64;
+  const int64_t slots = static_cast<int64_t>(num_sms) * ctas_per_sm(bn);
+  int64_t splits = 1;
+  if (tiles * 4 < slots * 3) splits = std::max<int64_t>(1, std::min<int64_t>(kb / 2, slots / tiles));
+  int64_t kbps = (kb + splits - 1) / splits;
+  splits = (kb + kbps - 1) / kbps;
+  return {static_cast<int>(splits), static_cast<int>(kbps)};
+}
+
+int num_sms() {
+  static int n = 0;
+  if (n == 0) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+  }
+  return n;
+}
+
+void check_cuda(const torch::Tensor& t, const char* name) {
+  TORCH_CHECK(t.is_cuda(), name, " must be a CUDA tensor");
+}
+
+// ---------------------------------------------------------------- GEMM
+// out = epilogue(x @ w^T).  w [M, K] contiguous; x [N, K] with unit inner stride.
+std::vector<int64_t> gemm(torch::Tensor w, torch::Tensor x, torch::Tensor out, int64_t epi, torch::Tensor ws,
+                          torch::Tensor counters, torch::Tensor err, int64_t force_splits) {
+  check_cuda(w, "w");
+  check_cuda(x, "x");
+  TORCH_CHECK(w.dim() == 2 && w.is_contiguous(), "w must be contiguous [M, K]");
+  TORCH_CHECK(x.dim() == 2 && x.stride(1) == 1, "x must be [N, K] with unit inner stride");
+  TORCH_CHECK(w.scalar_type() == x.scalar_type(), "w and x must share a dtype");
+  const int64_t M = w.size(0), K = w.size(1), N = x.size(0);
+  TORCH_CHECK(x.size(1) == K, "x inner dimension mismatch");
+  TORCH_CHECK(K % 8 == 0 && x.stride(0) % 8 == 0, "K and the activation row stride must be multiples of 8");
+  const int bn = pick_bn(N);
+  auto sp = pick_splits(M, N, K, bn, num_sms());
+  if (force_splits > 0) {
+    const int64_t kb = (K + 63) / 64;
+    int64_t kbps = (kb + force_splits - 1) / force_splits;
+    sp = {static_cast<int>((kb + kbps - 1) / kbps), static_cast<int>(kbps)};
+  }
+  const int64_t tiles = ((M + 127) / 128) * ((N + bn - 1) / bn);
+  if (sp.first > 1) {
+    TORCH_CHECK(ws.numel() >= sp.first * N * M, "split-K workspace too small: need ", sp.first * N * M);
+    TORCH_CHECK(counters.numel() >= tiles, "split-K counter buffer too small: need ", tiles);
+  }
+  if (epi == atlas::kEpiResidual || epi == atlas::kEpiF32) {
+    TORCH_CHECK(out.scalar_type() == torch::kFloat32, "fp32 output expected for this epilogue");
+  } else {
+    TORCH_CHECK(out.scalar_type() == w.scalar_type(), "activation-dtype output expected");
+  }
+  if (epi == atlas::kEpiSilu) {
+    TORCH_CHECK(M % 128 == 0, "gate/up GEMM needs M % 128 == 0");
+  }
+  TORCH_CHECK(out.stride(-1) == 1, "out must have unit inner stride");
+  const c10::cuda::CUDAGuard guard(w.device());
+  CUtensorMap a = map_2d(w, K, M, K, 128);
+  CUtensorMap b = map_2d(x, K, N, x.stride(0), bn);
+  GemmParams p{};
+  p.M = static_cast<int>(M);
+  p.N = static_cast<int>(N);
+  p.K = static_cast<int>(K);
+  p.ldo = static_cast<int>(out.stride(0));
+  p.splits = sp.first;
+  p.kb_per_split = sp.second;
+  p.bf16 = w.scalar_type() == torch::kBFloat16;
+  p.out = out.data_ptr();
+  p.ws = sp.first > 1 ? ws.data_ptr<float>() : nullptr;
+  p.counters = sp.first > 1 ? counters.data_ptr<int>() : nullptr;
+  p.err = err.data_ptr<int>();
+  atlas::launch_gemm_tn(a, b, p, bn, static_cast<int>(epi), at::cuda::getCurrentCUDAStream());
+  return {bn, sp.first, sp.second};
+}
+
+// ----------------------------------------------------------- attention
+void attention(torch::Tensor q, torch::Tensor kv, int64_t layer, torch::Tensor out, torch::Tensor dparams,
+               torch::Tensor prefix_pages, torch::Tensor row_full, torch::Tensor row_len, torch::Tensor row_mask,
+               torch::Tensor tail_pages, torch::Tensor part_o, torch::Tensor part_ml, torch::Tensor err,
+               int64_t splits, bool run_tc, bool run_combine, bool direct_out, double scale) {
+  check_cuda(q, "q");
+  TORCH_CHECK(q.dim() == 3 && q.size(2) == 128 && q.is_contiguous(), "q must be contiguous [M, Hq, 128]");
+  TORCH_CHECK(kv.scalar_type() == q.scalar_type(), "q and kv dtype mismatch");
+  TORCH_CHECK(kv.size(5) == 128 && kv.size(4) % 8 == 0 && 64 % kv.size(4) == 0,
+              "kernels need head_dim 128 and a page size dividing 64 that is a multiple of 8");
+  TORCH_CHECK(row_mask.dim() == 2 && row_mask.scalar_type() == torch::kInt64, "row_mask must be int64 [M, W]");
+  TORCH_CHECK(tail_pages.dim() == 2, "tail_pages must be [M, T]");
+  const int64_t M = q.size(0), Hq = q.size(1), Hkv = kv.size(3);
+  TORCH_CHECK(Hq % Hkv == 0, "Hq must be a multiple of Hkv");
+  const int64_t G = Hq / Hkv;
+  TORCH_CHECK(128 % G == 0, "GQA group must divide 128");
+  if (!direct_out && run_tc) {
+    TORCH_CHECK(part_o.numel() >= splits * M * Hq * 128 && part_ml.numel() >= splits * M * Hq * 2,
+                "attention split workspace too small");
+  }
+  const c10::cuda::CUDAGuard guard(q.device());
+  CUtensorMap kvmap{};
+  if (run_tc) kvmap = map_kv(kv);
+  AttnParams p{};
+  p.q = q.data_ptr();
+  p.kv = kv.data_ptr();
+  p.out = out.data_ptr();
+  p.dparams = dparams.data_ptr<int>();
+  p.prefix_pages = prefix_pages.data_ptr<int>();
+  p.row_full = row_full.data_ptr<int>();
+  p.row_len = row_len.data_ptr<int>();
+  p.row_mask = row_mask.data_ptr<int64_t>();
+  p.tail_pages = tail_pages.data_ptr<int>();
+  p.part_o = part_o.numel() ? part_o.data_ptr<float>() : nullptr;
+  p.part_ml = part_ml.numel() ? reinterpret_cast<float2*>(part_ml.data_ptr<float>()) : nullptr;
+  p.err = err.data_ptr<int>();
+  p.M = static_cast<int>(M);
+  p.Hq = static_cast<int>(Hq);
+  p.Hkv = static_cast<int>(Hkv);
+  p.page_size = static_cast<int>(kv.size(4));
+  p.num_pages = static_cast<int>(kv.size(1));
+  p.layer = static_cast<int>(layer);
+  p.mask_words = static_cast<int>(row_mask.size(1));
+  p.tail_stride = static_cast<int>(tail_pages.size(1));
+  p.splits = run_tc ? static_cast<int>(splits) : 0;
+  p.direct_out = direct_out ? 1 : 0;
+  p.bf16 = q.scalar_type() == torch::kBFloat16;
+  p.scale = static_cast<float>(scale);
+  const int row_tiles = static_cast<int>((M * G + 127) / 128);
+  atlas::launch_attention(kvmap, p, run_tc, run_combine, row_tiles, at::cuda::getCurrentCUDAStream());
+}
+
+// --------------------------------------------------------- elementwise
+void embed(torch::Tensor tok, torch::Tensor table, torch::Tensor out, torch::Tensor err) {
+  TORCH_CHECK(tok.scalar_type() == torch::kInt32 && out.scalar_type() == torch::kFloat32, "embed dtypes");
+  const c10::cuda::CUDAGuard guard(out.device());
+  atlas::launch_embed(tok.data_ptr<int>(), table.data_ptr(), out.data_ptr<float>(), static_cast<int>(tok.numel()),
+                      static_cast<int>(table.size(1)), static_cast<int>(table.size(0)),
+                      table.scalar_type() == torch::kBFloat16, err.data_ptr<int>(), at::cuda::getCurrentCUDAStream());
+}
+
+void rmsnorm(torch::Tensor x, torch::Tensor w, torch::Tensor out, double eps) {
+  TORCH_CHECK(x.scalar_type() == torch::kFloat32 && x.is_contiguous() && x.size(1) % 4 == 0, "rmsnorm input");
+  const c10::cuda::CUDAGuard guard(x.device());
+  atlas::launch_rmsnorm(x.data_ptr<float>(), w.data_ptr(), out.data_ptr(), static_cast<int>(x.size(0)),
+                        static_cast<int>(x.size(1)), static_cast<float>(eps), w.scalar_type() == torch::kBFloat16,
+                        at::cuda::getCurrentCUDAStream());
+}
+
+void rope_append(torch::Tensor qkv, torch::Tensor table, torch::Tensor pos, torch::Tensor slots, torch::Tensor kv_layer,
+                 torch::Tensor qout, int64_t Hq, int64_t Hkv, torch::Tensor err) {
+  TORCH_CHECK(qkv.is_contiguous() && kv_layer.is_contiguous() && qout.is_contiguous(), "rope_append contiguity");
+  const c10::cuda::CUDAGuard guard(qkv.device());
+  const int hd = static_cast<int>(kv_layer.size(4));
+  atlas::launch_rope_append(qkv.data_ptr(), table.data_ptr<float>(), pos.data_ptr<int>(), slots.data_ptr<int>(),
+                            kv_layer.data_ptr(), qout.data_ptr(), static_cast<int>(qkv.size(0)), static_cast<int>(Hq),
+                            static_cast<int>(Hkv), hd, static_cast<int>(kv_layer.size(3)),
+                            static_cast<int>(kv_layer.size(0)), static_cast<int>(table.size(0)),
+                            qkv.scalar_type() == torch::kBFloat16, err.data_ptr<int>(),
+                            at::cuda::getCurrentCUDAStream());
+}
+
+void kv_copy_pages(torch::Tensor kv, torch::Tensor plan, torch::Tensor err) {
+  TORCH_CHECK(plan.scalar_type() == torch::kInt32 && plan.dim() == 2 && plan.size(1) == 3, "plan must be int32 [n,3]");
+  const c10::cuda::CUDAGuard guard(kv.device());
+  atlas::launch_kv_copy_pages(kv.data_ptr(), plan.data_ptr<int>(), static_cast<int>(plan.size(0)),
+                              static_cast<int>(kv.size(0)), static_cast<int>(kv.size(1)), static_cast<int>(kv.size(3)),
+                              static_cast<int>(kv.size(4)), static_cast<int>(kv.size(5)), err.data_ptr<int>(),
+                              at::cuda::getCurrentCUDAStream());
+}
+
+void kv_move_slots(torch::Tensor kv, torch::Tensor src, torch::Tensor dst, torch::Tensor err) {
+  TORCH_CHECK(src.numel() == dst.numel() && src.numel() <= 64, "at most 64 slot moves per launch");
+  const c10::cuda::CUDAGuard guard(kv.device());
+  atlas::launch_kv_move_slots(kv.data_ptr(), src.data_ptr<int>(), dst.data_ptr<int>(), static_cast<int>(src.numel()),
+                              static_cast<int>(kv.size(0)), static_cast<int>(kv.size(1)), static_cast<int>(kv.size(3)),
+                              static_cast<int>(kv.size(4)), static_cast<int>(kv.size(5)), err.data_ptr<int>(),
+                              at::cuda::getCurrentCUDAStream());
+}
+
+void topk(torch::Tensor logits, int64_t k, c10::optional<torch::Tensor> keys, double inv_temp, torch::Tensor out_lp,
+          torch::Tensor out_id) {
+  TORCH_CHECK(logits.scalar_type() == torch::kFloat32 && logits.is_contiguous(), "logits must be contiguous fp32");
+  TORCH_CHECK(k >= 1 && k <= 8, "top-k supports 1 <= k <= 8");
+  const c10::cuda::CUDAGuard guard(logits.device());
+  atlas::launch_topk(logits.data_ptr<float>(), static_cast<int>(logits.size(0)), static_cast<int>(logits.size(1)),
+                     static_cast<int>(k), keys.has_value() ? keys->data_ptr<int64_t>() : nullptr,
+                     static_cast<float>(inv_temp), out_lp.data_ptr<float>(), out_id.data_ptr<int64_t>(),
+                     at::cuda::getCurrentCUDAStream());
+}
+
+void gather_logprobs(torch::Tensor logits, torch::Tensor rows, torch::Tensor toks, torch::Tensor lse, torch::Tensor out,
+                     torch::Tensor err) {
+  TORCH_CHECK(logits.scalar_type() == torch::kFloat32 && logits.is_contiguous(), "logits must be contiguous fp32");
+  const c10::cuda::CUDAGuard guard(logits.device());
+  atlas::launch_gather_logprobs(logits.data_ptr<float>(), static_cast<int>(logits.size(0)),
+                                static_cast<int>(logits.size(1)), rows.data_ptr<int>(), toks.data_ptr<int>(),
+                                static_cast<int>(rows.numel()), lse.data_ptr<float>(), out.data_ptr<float>(),
+                                err.data_ptr<int>(), at::cuda::getCurrentCUDAStream());
+}
+
+}  // namespace
+
+PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
+  m.doc() = "sm_100a kernels: tcgen05/TMA GEMM and paged attention, fused norm/rope/append, KV copies, top-k";
+  m.def("gemm", &gemm, "tcgen05 GEMM out = epi(x @ w^T); returns [bn, splits, kb_per_split]");
+  m.def("attention", &attention, "paged attention (tensor-core shared range + per-row tail/combine)");
+  m.def("embed", &embed);
+  m.def("rmsnorm", &rmsnorm);
+  m.def("rope_append", &rope_append);
+  m.def("kv_copy_pages", &kv_copy_pages);
+  m.def("kv_move_slots", &kv_move_slots);
+  m.def("topk", &topk);
+  m.def("gather_logprobs", &gather_logprobs);
+  m.attr("EPI_STORE") = static_cast<int>(atlas::kEpiStore);
+  m.attr("EPI_RESIDUAL") = static_cast<int>(atlas::kEpiResidual);
+  m.attr("EPI_SILU") = static_cast<int>(atlas::kEpiSilu);
+  m.attr("EPI_F32") = static_cast<int>(atlas::kEpiF32);
+}

@@ -1,0 +1,132 @@
+// Row-wise kernels around the GEMMs: embedding gather into the fp32 residual
+// stream, RMSNorm (fp32 stream -> activation dtype), and the fused
+// rotary-embedding + paged KV append that follows the QKV projection.
+
+#include "common.cuh"
+#include "kernels.h"
+
+namespace atlas {
+
+template <typename T>
+__global__ void embed_kernel(const int* __restrict__ tok, const T* __restrict__ table, float* __restrict__ out, int H,
+                             int V, int* err) {
+  const int m = blockIdx.x;
+  int t = tok[m];
+  if (t < 0 || t >= V) {
+    if (threadIdx.x == 0) set_error(err, kErrBadIndex);
+    t = 0;
+  }
+  const T* src = table + static_cast<int64_t>(t) * H;
+  float* dst = out + static_cast<int64_t>(m) * H;
+  for (int i = threadIdx.x; i < H; i += blockDim.x) dst[i] = to_f32(src[i]);
+}
+
+template <typename T>
+__global__ void rmsnorm_kernel(const float* __restrict__ x, const T* __restrict__ w, T* __restrict__ out, int H,
+                               float eps) {
+  const int m = blockIdx.x;
+  const float* row = x + static_cast<int64_t>(m) * H;
+  float ss = 0.f;
+  for (int i = threadIdx.x * 4; i < H; i += blockDim.x * 4) {
+    const float4 v = *reinterpret_cast<const float4*>(row + i);
+    ss += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
+  }
+  __shared__ float red[32];
+  ss = warp_sum(ss);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    float v = threadIdx.x < (blockDim.x >> 5) ? red[threadIdx.x] : 0.f;
+    v = warp_sum(v);
+    if (threadIdx.x == 0) red[0] = v;
+  }
+  __syncthreads();
+  const float inv = rsqrtf(red[0] / static_cast<float>(H) + eps);
+  T* o = out + static_cast<int64_t>(m) * H;
+  for (int i = threadIdx.x * 4; i < H; i += blockDim.x * 4) {
+    const float4 v = *reinterpret_cast<const float4*>(row + i);
+    o[i] = from_f32<T>(v.x * inv * to_f32(w[i]));
+    o[i + 1] = from_f32<T>(v.y * inv * to_f32(w[i + 1]));
+    o[i + 2] = from_f32<T>(v.z * inv * to_f32(w[i + 2]));
+    o[i + 3] = from_f32<T>(v.w * inv * to_f32(w[i + 3]));
+  }
+}
+
+// grid (M, Hq + Hkv); block hd/2 threads, thread i rotates the pair (i, i + hd/2).
+template <typename T>
+__global__ void rope_append_kernel(const T* __restrict__ qkv, const float* __restrict__ table,
+                                   const int* __restrict__ pos, const int* __restrict__ slots, T* __restrict__ kv,
+                                   T* __restrict__ qout, int Hq, int Hkv, int hd, int ps, int num_pages,
+                                   int max_pos, int* err) {
+  const int m = blockIdx.x;
+  const int head = blockIdx.y;
+  const int i = threadIdx.x;
+  const int half = hd >> 1;
+  const int qkv_w = (Hq + 2 * Hkv) * hd;
+  int p = pos[m];
+  if (p < 0 || p >= max_pos) {
+    if (i == 0) set_error(err, kErrBadIndex);
+    return;
+  }
+  const float c = table[static_cast<int64_t>(p) * hd + i];
+  const float s = table[static_cast<int64_t>(p) * hd + half + i];
+  const T* row = qkv + static_cast<int64_t>(m) * qkv_w;
+  if (head < Hq) {
+    const T* x = row + head * hd;
+    const float x1 = to_f32(x[i]), x2 = to_f32(x[i + half]);
+    T* o = qout + (static_cast<int64_t>(m) * Hq + head) * hd;
+    o[i] = from_f32<T>(x1 * c - x2 * s);
+    o[i + half] = from_f32<T>(x2 * c + x1 * s);
+    return;
+  }
+  const int kh = head - Hq;
+  const int slot = slots[m];
+  const int page = slot / ps, off = slot % ps;
+  if (slot < 0 || page >= num_pages) {
+    if (i == 0) set_error(err, kErrBadIndex);
+    return;
+  }
+  const int64_t head_stride = static_cast<int64_t>(ps) * hd;
+  T* kdst = kv + ((static_cast<int64_t>(page) * 2 + 0) * Hkv + kh) * head_stride + off * hd;
+  T* vdst = kv + ((static_cast<int64_t>(page) * 2 + 1) * Hkv + kh) * head_stride + off * hd;
+  const T* k = row + (Hq + kh) * hd;
+  const T* v = row + (Hq + Hkv + kh) * hd;
+  const float k1 = to_f32(k[i]), k2 = to_f32(k[i + half]);
+  kdst[i] = from_f32<T>(k1 * c - k2 * s);
+  kdst[i + half] = from_f32<T>(k2 * c + k1 * s);
+  vdst[i] = v[i];
+  vdst[i + half] = v[i + half];
+}
+
+void launch_embed(const int* tok, const void* table, float* out, int M, int H, int V, bool bf16, int* err,
+                  cudaStream_t st) {
+  if (bf16)
+    embed_kernel<__nv_bfloat16><<<M, 256, 0, st>>>(tok, static_cast<const __nv_bfloat16*>(table), out, H, V, err);
+  else
+    embed_kernel<__half><<<M, 256, 0, st>>>(tok, static_cast<const __half*>(table), out, H, V, err);
+}
+
+void launch_rmsnorm(const float* x, const void* w, void* out, int M, int H, float eps, bool bf16, cudaStream_t st) {
+  const int threads = H >= 4096 ? 512 : 256;
+  if (bf16)
+    rmsnorm_kernel<__nv_bfloat16><<<M, threads, 0, st>>>(x, static_cast<const __nv_bfloat16*>(w),
+                                                          static_cast<__nv_bfloat16*>(out), H, eps);
+  else
+    rmsnorm_kernel<__half><<<M, threads, 0, st>>>(x, static_cast<const __half*>(w), static_cast<__half*>(out), H, eps);
+}
+
+void launch_rope_append(const void* qkv, const float* table, const int* pos, const int* slots, void* kv_layer,
+                        void* qout, int M, int Hq, int Hkv, int hd, int ps, int num_pages, int max_pos, bool bf16,
+                        int* err, cudaStream_t st) {
+  dim3 grid(M, Hq + Hkv);
+  if (bf16)
+    rope_append_kernel<__nv_bfloat16><<<grid, hd / 2, 0, st>>>(
+        static_cast<const __nv_bfloat16*>(qkv), table, pos, slots, static_cast<__nv_bfloat16*>(kv_layer),
+        static_cast<__nv_bfloat16*>(qout), Hq, Hkv, hd, ps, num_pages, max_pos, err);
+  else
+    rope_append_kernel<__half><<<grid, hd / 2, 0, st>>>(static_cast<const __half*>(qkv), table, pos, slots,
+                                                         static_cast<__half*>(kv_layer), static_cast<__half*>(qout),
+                                                         Hq, Hkv, hd, ps, num_pages, max_pos, err);
+}
+
+}  // namespace atlas

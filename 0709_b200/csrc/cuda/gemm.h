@@ -1,0 +1,35 @@
+// Host/device interface of the tcgen05 GEMM.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace atlas {
+
+enum GemmEpilogue : int {
+  kEpiStore = 0,     // out[n, m] = acc           (activation dtype)
+  kEpiResidual = 1,  // out[n, m] += acc          (fp32 residual stream)
+  kEpiSilu = 2,      // out[n, f] = silu(gate) * up for 64+64 interleaved rows
+  kEpiF32 = 3,       // out[n, m] = acc           (fp32, e.g. logits)
+};
+
+struct GemmParams {
+  int M;             // output features (rows of A)
+  int N;             // tokens (rows of B)
+  int K;             // reduction length
+  int ldo;           // leading dimension of `out` (elements)
+  int splits;        // split-K factor (1 = no workspace)
+  int kb_per_split;  // 64-wide K blocks per split
+  int bf16;          // operands are bf16 (else fp16)
+  void* out;
+  float* ws;         // split-K partials [splits, N, M]
+  int* counters;     // per-tile tickets, zero between launches
+  int* err;          // device error flag
+};
+
+void launch_gemm_tn(const CUtensorMap& a, const CUtensorMap& b, const GemmParams& p, int bn, int epi,
+                    cudaStream_t st);
+int gemm_smem_bytes(int bn);
+
+}  // namespace atlas

@@ -1,8 +1,10 @@
 """Attention descriptor shared by every paged-attention kernel.
 
-A batch of ``M`` query rows reads one paged KV cache.  Logical page ``j`` of
-row ``r`` is ``prefix_pages[j]`` for ``j < n_shared_pages`` and
-``tail_pages[r, j - n_shared_pages]`` otherwise.  Key position ``x`` is
+A batch of ``M`` query rows reads one paged KV cache.  Position ``x`` of
+row ``r`` lives in ``prefix_pages[x // page]`` when ``x < shared_len`` or
+``x // page < n_shared_pages``, and in ``tail_pages[r, x // page - n_shared_pages]``
+otherwise (a route's private copy of the prefix's partial page holds the same
+committed slots, so both views agree below ``shared_len``).  Key position ``x`` is
 visible to row ``r`` when ``x < row_full[r]``, or when
 ``row_full[r] <= x < row_len[r]`` and bit ``x - mask_base`` of ``row_mask[r]``
 is set (``row_mask`` is [M, W] int64 words, bit ``b`` of word ``b // 64``).  Positions ``[0, shared_len)`` are fully visible to every row and read

@@ -1,0 +1,187 @@
+"""CUDA op table: the engine's ops backed by the sm_100a kernels of ``atlas_cuda``.
+
+Each engine owns one ``CudaOps`` with persistent device buffers: the split-K
+GEMM workspace and tile tickets, the split-KV attention partials, and an
+error flag the kernels set instead of trapping (bad index, bounded wait that
+timed out).  ``check()`` reads the flag.  If the extension cannot be loaded on
+a GPU machine, construction raises -- there is no silent fallback.
+"""
+
+from __future__ import annotations
+
+import math
+
+import torch
+
+from . import _native
+from .attn_desc import AttnDesc
+
+ERROR_NAMES = {1: "mbarrier wait timed out", 2: "index out of range", 3: "unsupported configuration"}
+
+
+class KernelError(RuntimeError):
+    pass
+
+
+def _ext():
+    return _native.cuda()
+
+
+class CudaOps:
+    def __init__(self, engine=None, *, device: torch.device | None = None) -> None:
+        self.ext = _ext()
+        self.engine = engine
+        self.device = engine.device if engine is not None else (device or torch.device("cuda"))
+        dev = self.device
+        self.err = torch.zeros(1, dtype=torch.int32, device=dev)
+        self.ws = torch.empty(16 * 1024 * 1024, dtype=torch.float32, device=dev)
+        self.counters = torch.zeros(65536, dtype=torch.int32, device=dev)
+        self.part_o = torch.empty(0, dtype=torch.float32, device=dev)
+        self.part_ml = torch.empty(0, dtype=torch.float32, device=dev)
+        self.num_sms = torch.cuda.get_device_properties(dev).multi_processor_count
+        self.last_gemm_config: list[int] | None = None
+
+    # ----------------------------------------------------------- errors
+    def check(self) -> None:
+        code = int(self.err.item())
+        if code:
+            self.err.zero_()
+            raise KernelError(f"device kernel reported error {code}: {ERROR_NAMES.get(code, 'unknown')}")
+
+    # ------------------------------------------------------------- GEMM
+    def _gemm(self, x: torch.Tensor, w: torch.Tensor, out: torch.Tensor, epi: int) -> torch.Tensor:
+        self.last_gemm_config = self.ext.gemm(w, x, out, epi, self.ws, self.counters, self.err, 0)
+        return out
+
+    def linear(self, x: torch.Tensor, w: torch.Tensor, out_dtype: torch.dtype | None = None) -> torch.Tensor:
+        out = torch.empty((x.shape[0], w.shape[0]), dtype=w.dtype, device=x.device)
+        return self._gemm(x, w, out, self.ext.EPI_STORE)
+
+    def linear_residual(self, x: torch.Tensor, w: torch.Tensor, resid: torch.Tensor) -> torch.Tensor:
+        return self._gemm(x, w, resid, self.ext.EPI_RESIDUAL)
+
+    def gate_up_silu(self, x: torch.Tensor, wgu: torch.Tensor) -> torch.Tensor:
+        out = torch.empty((x.shape[0], wgu.shape[0] // 2), dtype=wgu.dtype, device=x.device)
+        return self._gemm(x, wgu, out, self.ext.EPI_SILU)
+
+    def lm_head(self, x: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
+        out = torch.empty((x.shape[0], w.shape[0]), dtype=torch.float32, device=x.device)
+        return self._gemm(x, w, out, self.ext.EPI_F32)
+
+    # ------------------------------------------------------ elementwise
+    def embed(self, tokens: torch.Tensor, table: torch.Tensor) -> torch.Tensor:
+        out = torch.empty((tokens.numel(), table.shape[1]), dtype=torch.float32, device=table.device)
+        self.ext.embed(tokens.to(torch.int32), table, out, self.err)
+        return out
+
+    def rmsnorm(self, x: torch.Tensor, w: torch.Tensor, eps: float, out_dtype: torch.dtype) -> torch.Tensor:
+        out = torch.empty(x.shape, dtype=w.dtype, device=x.device)
+        self.ext.rmsnorm(x.contiguous(), w, out, float(eps))
+        return out
+
+    def rope_qkv_append(self, qkv, table, positions, slots, kv_layer, num_heads, num_kv_heads):
+        hd = kv_layer.shape[-1]
+        q = torch.empty((qkv.shape[0], num_heads, hd), dtype=qkv.dtype, device=qkv.device)
+        self.ext.rope_append(
+            qkv, table, positions.to(torch.int32), slots.to(torch.int32), kv_layer, q, num_heads, num_kv_heads, self.err
+        )
+        return q
+
+    # -------------------------------------------------------- attention
+    def _layer_index(self, kv_layer: torch.Tensor) -> tuple[torch.Tensor, int]:
+        kv = self.engine.kv
+        per = kv[0].numel() * kv.element_size()
+        off = kv_layer.data_ptr() - kv.data_ptr()
+        if off % per or not 0 <= off // per < kv.shape[0]:
+            raise ValueError("kv_layer must be a layer view of the engine cache")
+        return kv, off // per
+
+    def _dparams(self, desc: AttnDesc) -> torch.Tensor:
+        cached = getattr(desc, "_dparams", None)
+        if cached is None:
+            cached = torch.tensor(
+                [desc.shared_len, desc.n_shared_pages, desc.mask_base], dtype=torch.int32
+            ).to(self.device, non_blocking=True)
+            desc._dparams = cached  # type: ignore[attr-defined]
+        return cached
+
+    def attention_splits(self, rows: int, hq: int, hkv: int, shared_len: int, page_size: int) -> int:
+        g = hq // hkv
+        row_tiles = max(1, math.ceil(rows * g / 128))
+        chunks = max(1, math.ceil(math.ceil(shared_len / page_size) / (64 // page_size)))
+        return int(max(1, min(64, self.num_sms // (hkv * row_tiles), chunks)))
+
+    def _ensure_parts(self, splits: int, m: int, hq: int) -> None:
+        need = splits * m * hq * 128
+        if self.part_o.numel() < need:
+            self.part_o = torch.empty(need, dtype=torch.float32, device=self.device)
+        if self.part_ml.numel() < 2 * splits * m * hq:
+            self.part_ml = torch.empty(2 * splits * m * hq, dtype=torch.float32, device=self.device)
+
+    def attention(self, q: torch.Tensor, kv_layer: torch.Tensor, desc: AttnDesc, scale: float | None = None,
+                  *, splits: int | None = None) -> torch.Tensor:
+        kv, layer = self._layer_index(kv_layer)
+        m, hq, hd = q.shape
+        scale = 1.0 / math.sqrt(hd) if scale is None else scale
+        out = torch.empty((m, hq * hd), dtype=q.dtype, device=q.device)
+        run_tc = desc.shared_len > 0
+        sp = splits or self.attention_splits(m, hq, kv.shape[3], desc.shared_len, kv.shape[4])
+        if run_tc:
+            self._ensure_parts(sp, m, hq)
+        self.ext.attention(
+            q.contiguous(), kv, layer, out, self._dparams(desc), desc.prefix_pages, desc.row_full, desc.row_len,
+            desc.row_mask, desc.tail_pages, self.part_o, self.part_ml, self.err, sp, run_tc, True, False, float(scale),
+        )
+        return out
+
+    def attention_causal(self, q, kv_layer, desc: AttnDesc, causal_start: int, scale: float | None = None):
+        kv, layer = self._layer_index(kv_layer)
+        m, hq, hd = q.shape
+        scale = 1.0 / math.sqrt(hd) if scale is None else scale
+        out = torch.empty((m, hq * hd), dtype=q.dtype, device=q.device)
+        # All rows of a prefill chunk read one page list; limits are pos + 1 (row_full).
+        total = int(causal_start) + m
+        d2 = AttnDesc(desc.prefix_pages, desc.n_shared_pages, total, 0, desc.row_full, desc.row_len, desc.row_mask,
+                      desc.tail_pages)
+        d2._dparams = torch.tensor([total, desc.n_shared_pages, 0], dtype=torch.int32).to(self.device)  # type: ignore[attr-defined]
+        self.ext.attention(
+            q.contiguous(), kv, layer, out, d2._dparams, desc.prefix_pages, desc.row_full, desc.row_len,  # type: ignore[attr-defined]
+            desc.row_mask, desc.tail_pages, self.part_o, self.part_ml, self.err, 1, True, False, True, float(scale),
+        )
+        return out
+
+    # --------------------------------------------------------- KV cache
+    def kv_copy_pages(self, kv: torch.Tensor, copies: torch.Tensor) -> None:
+        self.ext.kv_copy_pages(kv, copies.to(self.device, torch.int32).contiguous(), self.err)
+
+    def kv_move_slots(self, kv: torch.Tensor, src: torch.Tensor, dst: torch.Tensor) -> None:
+        self.ext.kv_move_slots(kv, src.to(self.device, torch.int32), dst.to(self.device, torch.int32), self.err)
+
+    # ----------------------------------------------------------- vocab
+    def topk_logprobs(self, logits: torch.Tensor, k: int, keys: torch.Tensor | None = None, temperature: float = 1.0):
+        b = logits.shape[0]
+        lp = torch.empty((b, k), dtype=torch.float32, device=logits.device)
+        ids = torch.empty((b, k), dtype=torch.int64, device=logits.device)
+        self.ext.topk(logits.float().contiguous(), k, keys, 1.0 / float(temperature), lp, ids)
+        return lp, ids
+
+    def gather_logprobs(self, logits: torch.Tensor, rows: torch.Tensor, toks: torch.Tensor) -> torch.Tensor:
+        lse = torch.empty(logits.shape[0], dtype=torch.float32, device=logits.device)
+        out = torch.empty(rows.numel(), dtype=torch.float32, device=logits.device)
+        self.ext.gather_logprobs(
+            logits.contiguous(), rows.to(logits.device, torch.int32), toks.to(logits.device, torch.int32), lse, out,
+            self.err,
+        )
+        return out
+
+
+_SHARED: dict[int, CudaOps] = {}
+
+
+def shared_ops(device: torch.device | None = None) -> CudaOps:
+    """Process-wide op table for model-independent kernels (top-k, gathers)."""
+    dev = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
+    idx = dev.index if dev.index is not None else torch.cuda.current_device()
+    if idx not in _SHARED:
+        _SHARED[idx] = CudaOps(device=torch.device("cuda", idx))
+    return _SHARED[idx]

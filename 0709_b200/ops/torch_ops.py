@@ -92,7 +92,7 @@ def _row_positions(desc: AttnDesc, r: int, page_size: int) -> tuple[torch.Tensor
         vis = vis | ((pos >= full) & bit)
     pos = pos[vis]
     j = pos // page_size
-    shared = j < desc.n_shared_pages
+    shared = (j < desc.n_shared_pages) | (pos < desc.shared_len)
     pages = torch.empty_like(j)
     pages[shared] = desc.prefix_pages.long()[j[shared]]
     if (~shared).any():

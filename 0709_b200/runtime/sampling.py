@@ -142,13 +142,23 @@ def batch_parent_token_candidates(
     if len(relative_parent_paths) != batch:
         raise ValueError("relative_parent_paths must contain one semantic path per logits row")
     kk = min(int(k), vocab)
+    do_sample = sampling is not None and sampling.config.do_sample
+    keys = None
+    if do_sample:
+        keys = torch.tensor([sampling.seed_for_parent(p) for p in relative_parent_paths], dtype=torch.int64)
+    if rows.is_cuda and kk <= 8:
+        # Fused log-softmax + top-k (greedy or keyed Gumbel) kernel, one block per row.
+        from ..ops.cuda_ops import shared_ops
+
+        temp = float(sampling.config.temperature) if do_sample else 1.0
+        return shared_ops(rows.device).topk_logprobs(
+            rows, kk, None if keys is None else keys.to(rows.device, non_blocking=True), temp
+        )
     logprobs = torch.log_softmax(rows.float(), dim=-1)
-    if sampling is None or not sampling.config.do_sample:
+    if not do_sample:
         vals, ids = torch.topk(logprobs, k=kk, dim=-1)
         return vals, ids
-    keys = torch.tensor(
-        [sampling.seed_for_parent(p) for p in relative_parent_paths], dtype=torch.int64, device=rows.device
-    )
+    keys = keys.to(rows.device)
     noise = gumbel_from_uniform(keyed_uniform(keys, vocab))
     proposal = rows.float() / float(sampling.config.temperature) + noise
     ids = torch.topk(proposal, k=kk, dim=-1).indices

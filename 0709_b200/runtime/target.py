@@ -310,10 +310,15 @@ class TargetVerifier:
         assert self._prefix_logits is not None
         dev = logits.device
         allrows = torch.cat((self._prefix_logits.reshape(1, -1).float(), logits.float()), dim=0)
-        lse = torch.logsumexp(allrows, dim=-1)
-        r = (rows + 1).to(dev)
-        t = toks.to(dev)
-        vals = allrows[r, t] - lse[r]
+        r = (rows + 1).reshape(-1)
+        t = toks.reshape(-1)
+        if allrows.is_cuda:
+            from ..ops.cuda_ops import shared_ops
+
+            vals = shared_ops(dev).gather_logprobs(allrows, r, t).reshape(rows.shape)
+        else:
+            lse = torch.logsumexp(allrows, dim=-1)
+            vals = (allrows[r, t] - lse[r]).reshape(rows.shape)
         return vals.double().cpu().tolist()
 
     # -------------------------------------------------------------- scoring
@@ -578,8 +583,21 @@ class TargetVerifier:
         t_model = time.perf_counter()
         pages = self.mirror.view()
         slots_d = slots.to(dev, non_blocking=True)
+        if cur.is_cuda:
+            from ..ops.cuda_ops import shared_ops
+
+            sops = shared_ops(dev)
+
+            def argmax_into(row: torch.Tensor, t: int) -> None:
+                _, ids = sops.topk_logprobs(row, 1)
+                toks[t: t + 1] = ids.reshape(-1).to(torch.int32)
+        else:
+
+            def argmax_into(row: torch.Tensor, t: int) -> None:
+                toks[t: t + 1] = torch.argmax(row, dim=-1).to(torch.int32)
+
         for t in range(steps):
-            toks[t: t + 1] = torch.argmax(cur, dim=-1).to(torch.int32)
+            argmax_into(cur, t)
             pos = torch.tensor([p + t], dtype=torch.int32).to(dev, non_blocking=True)
             desc = single_sequence_desc(pages, pos + 1, shared_len=p + t)
             cur = self.engine.forward(toks[t: t + 1], pos, slots_d[t: t + 1], desc)
