@@ -14,6 +14,7 @@ import math
 import torch
 
 from . import _native
+from ..utils import counters
 from .attn_desc import AttnDesc
 
 ERROR_NAMES = {1: "mbarrier wait timed out", 2: "index out of range", 3: "unsupported configuration"}
@@ -51,6 +52,7 @@ class CudaOps:
     # ------------------------------------------------------------- GEMM
     def _gemm(self, x: torch.Tensor, w: torch.Tensor, out: torch.Tensor, epi: int) -> torch.Tensor:
         self.last_gemm_config = self.ext.gemm(w, x, out, epi, self.ws, self.counters, self.err, 0)
+        counters.launches(1)
         return out
 
     def linear(self, x: torch.Tensor, w: torch.Tensor, out_dtype: torch.dtype | None = None) -> torch.Tensor:
@@ -72,11 +74,13 @@ class CudaOps:
     def embed(self, tokens: torch.Tensor, table: torch.Tensor) -> torch.Tensor:
         out = torch.empty((tokens.numel(), table.shape[1]), dtype=torch.float32, device=table.device)
         self.ext.embed(tokens.to(torch.int32), table, out, self.err)
+        counters.launches(1)
         return out
 
     def rmsnorm(self, x: torch.Tensor, w: torch.Tensor, eps: float, out_dtype: torch.dtype) -> torch.Tensor:
         out = torch.empty(x.shape, dtype=w.dtype, device=x.device)
         self.ext.rmsnorm(x.contiguous(), w, out, float(eps))
+        counters.launches(1)
         return out
 
     def rope_qkv_append(self, qkv, table, positions, slots, kv_layer, num_heads, num_kv_heads):
@@ -85,6 +89,7 @@ class CudaOps:
         self.ext.rope_append(
             qkv, table, positions.to(torch.int32), slots.to(torch.int32), kv_layer, q, num_heads, num_kv_heads, self.err
         )
+        counters.launches(1)
         return q
 
     # -------------------------------------------------------- attention
@@ -111,12 +116,27 @@ class CudaOps:
         chunks = max(1, math.ceil(math.ceil(shared_len / page_size) / (64 // page_size)))
         return int(max(1, min(64, self.num_sms // (hkv * row_tiles), chunks)))
 
+    def reserve_attention_workspace(self, max_rows: int, hq: int, hkv: int, max_context: int, page_size: int) -> None:
+        """Allocate split partials for every row count up to ``max_rows`` once (graphs keep the address)."""
+        need_o = need_ml = 0
+        for m in range(1, max_rows + 1):
+            sp = self.attention_splits(m, hq, hkv, max_context, page_size)
+            need_o = max(need_o, sp * m * hq * 128)
+            need_ml = max(need_ml, 2 * sp * m * hq)
+        self._ensure_parts_exact(need_o, need_ml)
+
+    def _ensure_parts_exact(self, need_o: int, need_ml: int) -> None:
+        if self.part_o.numel() < need_o:
+            if torch.cuda.is_current_stream_capturing():
+                raise RuntimeError("attention workspace must be reserved before graph capture")
+            self.part_o = torch.empty(need_o, dtype=torch.float32, device=self.device)
+        if self.part_ml.numel() < need_ml:
+            if torch.cuda.is_current_stream_capturing():
+                raise RuntimeError("attention workspace must be reserved before graph capture")
+            self.part_ml = torch.empty(need_ml, dtype=torch.float32, device=self.device)
+
     def _ensure_parts(self, splits: int, m: int, hq: int) -> None:
-        need = splits * m * hq * 128
-        if self.part_o.numel() < need:
-            self.part_o = torch.empty(need, dtype=torch.float32, device=self.device)
-        if self.part_ml.numel() < 2 * splits * m * hq:
-            self.part_ml = torch.empty(2 * splits * m * hq, dtype=torch.float32, device=self.device)
+        self._ensure_parts_exact(splits * m * hq * 128, 2 * splits * m * hq)
 
     def attention(self, q: torch.Tensor, kv_layer: torch.Tensor, desc: AttnDesc, scale: float | None = None,
                   *, splits: int | None = None) -> torch.Tensor:
@@ -125,13 +145,15 @@ class CudaOps:
         scale = 1.0 / math.sqrt(hd) if scale is None else scale
         out = torch.empty((m, hq * hd), dtype=q.dtype, device=q.device)
         run_tc = desc.shared_len > 0
-        sp = splits or self.attention_splits(m, hq, kv.shape[3], desc.shared_len, kv.shape[4])
+        sp = splits or getattr(desc, "_splits", None) or self.attention_splits(m, hq, kv.shape[3], desc.shared_len,
+                                                                                kv.shape[4])
         if run_tc:
             self._ensure_parts(sp, m, hq)
         self.ext.attention(
             q.contiguous(), kv, layer, out, self._dparams(desc), desc.prefix_pages, desc.row_full, desc.row_len,
             desc.row_mask, desc.tail_pages, self.part_o, self.part_ml, self.err, sp, run_tc, True, False, float(scale),
         )
+        counters.launches(2 if run_tc else 1)
         return out
 
     def attention_causal(self, q, kv_layer, desc: AttnDesc, causal_start: int, scale: float | None = None):
@@ -141,21 +163,25 @@ class CudaOps:
         out = torch.empty((m, hq * hd), dtype=q.dtype, device=q.device)
         # All rows of a prefill chunk read one page list; limits are pos + 1 (row_full).
         total = int(causal_start) + m
-        d2 = AttnDesc(desc.prefix_pages, desc.n_shared_pages, total, 0, desc.row_full, desc.row_len, desc.row_mask,
-                      desc.tail_pages)
-        d2._dparams = torch.tensor([total, desc.n_shared_pages, 0], dtype=torch.int32).to(self.device)  # type: ignore[attr-defined]
+        dp = getattr(desc, "_causal_dparams", None)
+        if dp is None:
+            dp = torch.tensor([total, desc.n_shared_pages, 0], dtype=torch.int32).to(self.device)
+            desc._causal_dparams = dp  # type: ignore[attr-defined]
         self.ext.attention(
-            q.contiguous(), kv, layer, out, d2._dparams, desc.prefix_pages, desc.row_full, desc.row_len,  # type: ignore[attr-defined]
+            q.contiguous(), kv, layer, out, dp, desc.prefix_pages, desc.row_full, desc.row_len,
             desc.row_mask, desc.tail_pages, self.part_o, self.part_ml, self.err, 1, True, False, True, float(scale),
         )
+        counters.launches(1)
         return out
 
     # --------------------------------------------------------- KV cache
     def kv_copy_pages(self, kv: torch.Tensor, copies: torch.Tensor) -> None:
         self.ext.kv_copy_pages(kv, copies.to(self.device, torch.int32).contiguous(), self.err)
+        counters.launches(1)
 
     def kv_move_slots(self, kv: torch.Tensor, src: torch.Tensor, dst: torch.Tensor) -> None:
         self.ext.kv_move_slots(kv, src.to(self.device, torch.int32), dst.to(self.device, torch.int32), self.err)
+        counters.launches(1)
 
     # ----------------------------------------------------------- vocab
     def topk_logprobs(self, logits: torch.Tensor, k: int, keys: torch.Tensor | None = None, temperature: float = 1.0):
@@ -163,6 +189,7 @@ class CudaOps:
         lp = torch.empty((b, k), dtype=torch.float32, device=logits.device)
         ids = torch.empty((b, k), dtype=torch.int64, device=logits.device)
         self.ext.topk(logits.float().contiguous(), k, keys, 1.0 / float(temperature), lp, ids)
+        counters.launches(1)
         return lp, ids
 
     def gather_logprobs(self, logits: torch.Tensor, rows: torch.Tensor, toks: torch.Tensor) -> torch.Tensor:
@@ -172,6 +199,7 @@ class CudaOps:
             logits.contiguous(), rows.to(logits.device, torch.int32), toks.to(logits.device, torch.int32), lse, out,
             self.err,
         )
+        counters.launches(2)
         return out
 
 

@@ -22,12 +22,14 @@ from __future__ import annotations
 import time
 from typing import Any, Sequence
 
+import numpy as np
 import torch
 
 from ..ops import _native
 from ..ops.attn_desc import AttnDesc
+from ..utils import counters
 from ..types import DraftPrefixState, FrontierDecodeOutput, PrefixKVView, RouteState
-from .engine import LlamaEngine
+from .engine import LlamaEngine, row_bucket
 from .store import KVTreeStore
 
 
@@ -35,6 +37,7 @@ class PrefixPageMirror:
     """Device copy of a pool's prefix page list, updated incrementally."""
 
     def __init__(self, capacity: int, device: torch.device) -> None:
+        # Fixed capacity (the pool's page count): captured graphs keep this address.
         self.dev = torch.zeros(int(capacity), dtype=torch.int32, device=device)
         self.host: list[int] = []
         self.h2d_copies = 0
@@ -42,9 +45,7 @@ class PrefixPageMirror:
     def sync(self, pages: torch.Tensor) -> None:
         new = pages.tolist()
         if len(new) > self.dev.numel():
-            grown = torch.zeros(max(len(new), 2 * self.dev.numel()), dtype=torch.int32, device=self.dev.device)
-            grown[: self.dev.numel()].copy_(self.dev)
-            self.dev = grown
+            raise RuntimeError(f"prefix page table of {len(new)} pages exceeds the mirror capacity {self.dev.numel()}")
         start = 0
         n = min(len(new), len(self.host))
         while start < n and new[start] == self.host[start]:
@@ -69,13 +70,14 @@ class DrafterRuntime:
     ) -> None:
         self.engine = engine
         self.host = _native.host()
-        self.page_pool = page_pool if page_pool is not None else self.host.PagePool(engine.num_pages, engine.page_size)
+        # The engine's last page is the trash page for padded graph rows.
+        self.page_pool = page_pool if page_pool is not None else self.host.PagePool(engine.num_pages - 1, engine.page_size)
         self.route_pool = self.host.RoutePool(self.page_pool)
         self.page_size = engine.page_size
         self.prefill_chunk_size = int(prefill_chunk_size)
         self.max_tail_pages = int(max_tail_pages)
         self.device = engine.device
-        self.mirror = PrefixPageMirror(1024, self.device)
+        self.mirror = PrefixPageMirror(engine.num_pages, self.device)
         self.route_store: KVTreeStore | None = None
         self.prefix_token_ids: tuple[int, ...] = ()
         self.prefix_next_token_logits: torch.Tensor | None = None
@@ -157,22 +159,6 @@ class DrafterRuntime:
                     f"route {rid} physical length {rp.route_len(rid)} != logical length {r.kv_view.length}"
                 )
 
-    def row_descriptor(self, rids: Sequence[int]) -> tuple[AttnDesc, torch.Tensor]:
-        tails, lens = self.route_pool.row_tables(list(rids), self.max_tail_pages)
-        dev = self.device
-        lens_d = lens.to(dev, non_blocking=True)
-        desc = AttnDesc(
-            prefix_pages=self.mirror.view(),
-            n_shared_pages=int(self.route_pool.prefix_full_pages),
-            shared_len=int(self.route_pool.prefix_len),
-            mask_base=int(self.route_pool.prefix_len),
-            row_full=lens_d,
-            row_len=lens_d,
-            row_mask=torch.full((len(rids), 1), -1, dtype=torch.int64, device=dev),
-            tail_pages=tails.to(dev, non_blocking=True),
-        )
-        return desc, lens
-
     @torch.inference_mode()
     def decode_frontier_one_token(
         self, active_routes: Sequence[RouteState], attention_backend: Any = None
@@ -184,18 +170,31 @@ class DrafterRuntime:
         rids = [int(r.route_id) for r in active_routes]
         slots, copies = self.route_pool.prepare_append(rids)
         self.engine.copy_pages(copies)
-        desc, lens = self.row_descriptor(rids)
-        dev = self.device
-        tokens = torch.tensor([int(r.pending_token_id) for r in active_routes], dtype=torch.int32)
-        positions = lens - 1
-        logits = self.engine.forward(
-            tokens.to(dev, non_blocking=True), positions.to(dev, non_blocking=True), slots.to(dev, non_blocking=True), desc
+        if copies.numel():
+            counters.h2d(copies.numel() * 4)
+        tails, lens = self.route_pool.row_tables(rids, self.max_tail_pages)
+        lens_np = lens.numpy()
+        plen = int(self.route_pool.prefix_len)
+        logits = self.engine.run_rows(
+            row_bucket(len(rids)),
+            tail_stride=self.max_tail_pages,
+            mask_words=1,
+            prefix_pages=self.mirror.dev,
+            tokens=[int(r.pending_token_id) for r in active_routes],
+            positions=lens_np - 1,
+            slots=slots.numpy(),
+            shared_len=plen,
+            n_shared_pages=int(self.route_pool.prefix_full_pages),
+            mask_base=plen,
+            row_full=lens_np,
+            row_len=lens_np,
+            tail_pages=tails.numpy(),
         )
         node_ids = tuple(self.route_store.reserve_node_ids(len(active_routes)))
         c = self.counters
         c["decode_steps"] += 1
         c["decode_rows"] += len(rids)
-        c["attention_metadata_page_indices"] += int(self.route_pool.prefix_full_pages) + int(desc.tail_pages.numel())
+        c["attention_metadata_page_indices"] += int(self.route_pool.prefix_full_pages) + int(tails.numel())
         return FrontierDecodeOutput(
             route_ids=torch.tensor(rids, dtype=torch.long),
             next_token_logits=logits,
@@ -254,27 +253,52 @@ class DrafterRuntime:
 
     @torch.inference_mode()
     def append_known_tokens_as_prefix(self, token_ids: Sequence[int]) -> torch.Tensor:
-        """Extend the committed prefix by known tokens with one causal EXTEND forward."""
+        """Extend the committed prefix by known tokens with one EXTEND forward.
+
+        Up to 64 tokens run as one graphed masked forward (the tokens see the
+        old prefix fully and each other causally via row masks); longer runs use
+        the chunked causal prefill.
+        """
         suffix = tuple(int(t) for t in token_ids)
         if not suffix:
             raise ValueError("known prefix extension cannot be empty")
         if self.route_pool.num_routes:
             raise RuntimeError("drop speculative routes before extending the prefix")
         start = int(self.route_pool.prefix_len)
-        slots, copies = self.route_pool.append_prefix(len(suffix))
+        n = len(suffix)
+        slots, copies = self.route_pool.append_prefix(n)
         self.engine.copy_pages(copies)
         self._sync_prefix()
-        logits = self.engine.prefill_sequence(
-            torch.tensor(suffix, dtype=torch.int32).to(self.device),
-            start_pos=start,
-            slots=slots.to(self.device),
-            pages=self.mirror.view(),
-            chunk_size=self.prefill_chunk_size,
-        )
+        if n <= 64:
+            masks = np.array([(1 << (r + 1)) - 1 if r < 63 else -1 for r in range(n)], dtype=np.int64)[:, None]
+            logits = self.engine.run_rows(
+                row_bucket(n),
+                tail_stride=1,
+                mask_words=1,
+                prefix_pages=self.mirror.dev,
+                tokens=list(suffix),
+                positions=np.arange(start, start + n),
+                slots=slots.numpy(),
+                shared_len=start,
+                n_shared_pages=len(self.mirror.host),
+                mask_base=start,
+                row_full=np.full(n, start),
+                row_len=np.full(n, start + n),
+                row_mask=masks,
+                pad_front=True,
+            )[-1]
+        else:
+            logits = self.engine.prefill_sequence(
+                torch.tensor(suffix, dtype=torch.int32).to(self.device),
+                start_pos=start,
+                slots=slots.to(self.device),
+                pages=self.mirror.view(),
+                chunk_size=self.prefill_chunk_size,
+            )
         self.prefix_token_ids = (*self.prefix_token_ids, *suffix)
         self.prefix_next_token_logits = logits.unsqueeze(0)
         self.counters["extend_calls"] += 1
-        self.counters["extend_tokens"] += len(suffix)
+        self.counters["extend_tokens"] += n
         return logits
 
     # ---------------------------------------------------------- validation

@@ -16,8 +16,10 @@ SGLang decode forward the drafter uses (fp/flashinfer_backends.py:89-132).
 from __future__ import annotations
 
 import math
+import threading
 from dataclasses import dataclass
 
+import numpy as np
 import torch
 
 from ..models.llama import LlamaWeights, rope_table
@@ -68,9 +70,77 @@ class LlamaEngine:
             else:
                 ops = torch_ops
         self.ops = ops
+        if hasattr(ops, "reserve_attention_workspace"):
+            ops.reserve_attention_workspace(64, c.num_heads, c.num_kv_heads, int(max_positions), self.page_size)
         self.stats = ForwardStats()
+        self.use_graphs = True
+        self._static: dict[tuple[int, int, int], StaticBatch] = {}
+        self._graphs: dict = {}
+        self._graph_pool = torch.cuda.graph_pool_handle() if self.device.type == "cuda" else None
+        # Scratch page for padded rows' KV writes (never part of any sequence).
+        self.trash_slot = (self.num_pages - 1) * self.page_size
 
     # ------------------------------------------------------------------
+    def graph_attention_splits(self, rows: int) -> int | None:
+        """Split-KV count baked into a graph: sized for the longest context the engine holds."""
+        f = getattr(self.ops, "attention_splits", None)
+        if f is None:
+            return None
+        c = self.cfg
+        return f(rows, c.num_heads, c.num_kv_heads, int(self.rope.shape[0]), self.page_size)
+
+    def static_batch(self, rows: int, tail_stride: int = 1, mask_words: int = 1) -> "StaticBatch":
+        key = (int(rows), int(tail_stride), int(mask_words))
+        sb = self._static.get(key)
+        if sb is None:
+            sb = StaticBatch(self, *key)
+            self._static[key] = sb
+        return sb
+
+    @torch.inference_mode()
+    def run_rows(self, rows: int, *, tail_stride: int = 1, mask_words: int = 1, prefix_pages: torch.Tensor, **fields):
+        """Forward ``len(tokens)`` rows through a CUDA graph of the padded row bucket.
+
+        ``fields`` are host arrays (see ``StaticBatch.load``); returns fp32 logits
+        [real rows, V] (a fresh tensor).  On CPU the eager forward runs instead.
+        """
+        sb = self.static_batch(rows, tail_stride, mask_words)
+        n = sb.load(**fields)
+        desc = sb.desc(prefix_pages)
+        if self.device.type != "cuda" or not self.use_graphs:
+            logits = self.forward(sb.tokens, sb.positions, sb.slots, desc)
+            return logits[sb.real_slice(n)].clone()
+        key = (sb.key, prefix_pages.data_ptr())
+        graph = self._graphs.get(key)
+        if graph is None:
+            graph = self._capture(sb, desc)
+            self._graphs[key] = graph
+        g, out, launches = graph
+        g.replay()
+        if launches:
+            from ..utils import counters
+
+            counters.launches(launches)
+        self.stats.calls += 1
+        self.stats.rows += n
+        return out[sb.real_slice(n)].clone()
+
+    def _capture(self, sb: "StaticBatch", desc: AttnDesc):
+        from ..utils import counters
+
+        stream = torch.cuda.Stream(device=self.device)
+        stream.wait_stream(torch.cuda.current_stream(self.device))
+        with torch.cuda.stream(stream):
+            for _ in range(2):
+                self.forward(sb.tokens, sb.positions, sb.slots, desc)
+        torch.cuda.current_stream(self.device).wait_stream(stream)
+        g = torch.cuda.CUDAGraph()
+        before = counters.snapshot()["launches"]
+        with torch.cuda.graph(g, pool=self._graph_pool, capture_error_mode="thread_local"):
+            out = self.forward(sb.tokens, sb.positions, sb.slots, desc)
+        launches = counters.snapshot()["launches"] - before
+        return g, out, launches
+
     @torch.inference_mode()
     def forward(
         self,
@@ -145,3 +215,130 @@ class LlamaEngine:
     def move_slots(self, src: torch.Tensor, dst: torch.Tensor) -> None:
         if src.numel():
             self.ops.kv_move_slots(self.kv, src.to(self.device), dst.to(self.device))
+
+
+class StaticBatch:
+    """Fixed-address inputs of one row bucket, filled by a single host->device copy.
+
+    Layout of the int32 device buffer: dparams[4] (shared_len, n_shared_pages,
+    mask_base, pad), tokens[M], positions[M], slots[M], row_full[M],
+    row_len[M], tail_pages[M*T], then row masks as int64 [M*W].  The host side
+    is a pair of pinned buffers used alternately (an event guards reuse).
+    Rows beyond the real count are padding: token 0 at position 0 writing the
+    engine's trash slot and attending to position 0 only.
+    """
+
+    def __init__(self, engine: LlamaEngine, rows: int, tail_stride: int, mask_words: int) -> None:
+        self.engine = engine
+        self.key = (rows, tail_stride, mask_words)
+        self.M, self.T, self.W = rows, tail_stride, mask_words
+        m, t, w = rows, tail_stride, mask_words
+        self.offs = {}
+        o = 4
+        for name, size in (("tokens", m), ("positions", m), ("slots", m), ("row_full", m), ("row_len", m),
+                           ("tail_pages", m * t)):
+            self.offs[name] = (o, size)
+            o += size
+        o += o % 2
+        self.offs["row_mask"] = (o, 2 * m * w)
+        o += 2 * m * w
+        self.words = o
+        dev = engine.device
+        pin = dev.type == "cuda"
+        self.dev = torch.zeros(o, dtype=torch.int32, device=dev)
+        self.hosts = [torch.zeros(o, dtype=torch.int32, pin_memory=pin) for _ in range(2)]
+        self.events = [None, None]
+        self.turn = 0
+        self.lock = threading.Lock()
+        v = self.dev
+        self.dparams = v[0:4]
+        self.tokens = v[self.offs["tokens"][0]: self.offs["tokens"][0] + m]
+        self.positions = v[self.offs["positions"][0]: self.offs["positions"][0] + m]
+        self.slots = v[self.offs["slots"][0]: self.offs["slots"][0] + m]
+        self.row_full = v[self.offs["row_full"][0]: self.offs["row_full"][0] + m]
+        self.row_len = v[self.offs["row_len"][0]: self.offs["row_len"][0] + m]
+        a = self.offs["tail_pages"][0]
+        self.tail_pages = v[a: a + m * t].view(m, t)
+        a = self.offs["row_mask"][0]
+        self.row_mask = v[a: a + 2 * m * w].view(torch.int64).view(m, w)
+        self.pad_front = False
+
+    def real_slice(self, n: int) -> slice:
+        return slice(self.M - n, self.M) if self.pad_front else slice(0, n)
+
+    def load(self, *, tokens, positions, slots, shared_len, n_shared_pages, mask_base, row_full, row_len,
+             tail_pages=None, row_mask=None, pad_front: bool = False) -> int:
+        from ..utils import counters
+
+        n = len(tokens)
+        if n > self.M:
+            raise ValueError(f"{n} rows exceed the bucket of {self.M}")
+        self.pad_front = bool(pad_front)
+        with self.lock:
+            i = self.turn
+            self.turn ^= 1
+            ev = self.events[i]
+            if ev is not None:
+                ev.synchronize()
+            h = self.hosts[i].numpy()
+            m = self.M
+            r0 = m - n if pad_front else 0
+            rs = slice(r0, r0 + n)
+            h[0:4] = (int(shared_len), int(n_shared_pages), int(mask_base), 0)
+
+            def put(name, vals, pad):
+                a, size = self.offs[name]
+                seg = h[a: a + size]
+                seg[:] = pad
+                seg[rs] = vals
+
+            dev_tokens = isinstance(tokens, torch.Tensor) and tokens.device.type != "cpu"
+            put("tokens", 0 if dev_tokens else tokens, 0)
+            put("positions", positions, 0)
+            put("slots", slots, self.engine.trash_slot)
+            put("row_full", row_full, 1)
+            put("row_len", row_len, 1)
+            a, size = self.offs["tail_pages"]
+            tp = h[a: a + size].reshape(m, self.T)
+            tp[:] = 0
+            if tail_pages is not None:
+                tp[rs, : np.asarray(tail_pages).shape[1]] = tail_pages
+            a, size = self.offs["row_mask"]
+            mk = h[a: a + size].view(np.int64).reshape(m, self.W)
+            mk[:] = -1
+            if row_mask is not None:
+                mk[rs, : np.asarray(row_mask).shape[1]] = row_mask
+            self.dev.copy_(self.hosts[i], non_blocking=True)
+            if dev_tokens:
+                self.tokens[rs].copy_(tokens.reshape(-1).to(torch.int32))
+            if self.dev.is_cuda:
+                ev = torch.cuda.Event()
+                ev.record()
+                self.events[i] = ev
+        counters.h2d(self.words * 4)
+        return n
+
+    def desc(self, prefix_pages: torch.Tensor) -> AttnDesc:
+        d = AttnDesc(
+            prefix_pages=prefix_pages,
+            n_shared_pages=int(self.hosts[self.turn ^ 1][1]),
+            shared_len=max(1, int(self.hosts[self.turn ^ 1][0])),
+            mask_base=int(self.hosts[self.turn ^ 1][2]),
+            row_full=self.row_full,
+            row_len=self.row_len,
+            row_mask=self.row_mask,
+            tail_pages=self.tail_pages,
+        )
+        d._dparams = self.dparams  # type: ignore[attr-defined]
+        d._splits = self.engine.graph_attention_splits(self.M)  # type: ignore[attr-defined]
+        return d
+
+
+ROW_BUCKETS = (1, 2, 4, 8, 16, 32, 64)
+
+
+def row_bucket(n: int) -> int:
+    for b in ROW_BUCKETS:
+        if n <= b:
+            return b
+    raise ValueError(f"{n} rows exceed the largest graph bucket ({ROW_BUCKETS[-1]})")

@@ -32,6 +32,7 @@ from .selection import (
     per_root_topk_candidate_indices,
 )
 from .store import KVTreeStore
+from ..utils import counters
 
 
 class FrontierModelBackend(Protocol):
@@ -165,6 +166,8 @@ def materialize_pending_candidate_batch(
         node_rec[:, 1] = ids
         parts.append(node_rec)
     packed = torch.cat(parts) if len(parts) > 1 else rec
+    if packed.device.type != "cpu":
+        counters.d2h(packed.numel() * 8)
     rows = packed.detach().cpu().tolist()
     cands: list[PendingCandidate] = []
     by_order: list[PendingCandidate | None] = [None] * nsel

@@ -24,13 +24,15 @@ import math
 import time
 from typing import Sequence
 
+import numpy as np
 import torch
 
 from ..ops import _native
 from ..ops.attn_desc import AttnDesc, single_sequence_desc
+from ..utils import counters
 from ..types import PrefixState, TargetRouteScore, TargetVerifyResult, VerifyRoutePayload
 from .drafter import PrefixPageMirror
-from .engine import LlamaEngine
+from .engine import LlamaEngine, row_bucket
 
 ROUTE_SAMPLE_DOMAIN = "atlas0709-target-route-sample-v1"
 
@@ -78,11 +80,12 @@ class TargetVerifier:
         if self.k <= 0 or self.d <= 0:
             raise ValueError("k and d must be positive")
         self.host = _native.host()
-        self.page_pool = page_pool if page_pool is not None else self.host.PagePool(engine.num_pages, engine.page_size)
+        # The engine's last page is the trash page for padded graph rows.
+        self.page_pool = page_pool if page_pool is not None else self.host.PagePool(engine.num_pages - 1, engine.page_size)
         self.seq = self.host.RoutePool(self.page_pool)
         self.device = engine.device
         self.page_size = engine.page_size
-        self.mirror = PrefixPageMirror(1024, self.device)
+        self.mirror = PrefixPageMirror(engine.num_pages, self.device)
         self.score_weights = validate_score_weights(score_weights)
         self.fallback_threshold = None if fallback_threshold is None else float(fallback_threshold)
         self.first_token_threshold = None if first_token_threshold is None else float(first_token_threshold)
@@ -274,22 +277,20 @@ class TargetVerifier:
         p = len(self.prefix_token_ids)
         scratch = self.seq.reserve_scratch(p + n)
         self._sync()
-        dev = self.device
-        lens = torch.full((n,), p + n, dtype=torch.int32)
-        desc = single_sequence_desc(
-            self.mirror.view(),
-            lens.to(dev, non_blocking=True),
+        logits = self.engine.run_rows(
+            row_bucket(n),
+            tail_stride=1,
+            mask_words=int(masks.shape[1]),
+            prefix_pages=self.mirror.dev,
+            tokens=tokens.numpy(),
+            positions=depths.numpy() + p,
+            slots=scratch.numpy(),
             shared_len=p,
+            n_shared_pages=len(self.mirror.host),
             mask_base=p,
-            masks=masks.to(dev, non_blocking=True),
-            full=torch.full((n,), p, dtype=torch.int32).to(dev, non_blocking=True),
-        )
-        positions = (depths + p).to(torch.int32)
-        logits = self.engine.forward(
-            tokens.to(torch.int32).to(dev, non_blocking=True),
-            positions.to(dev, non_blocking=True),
-            scratch.to(dev, non_blocking=True),
-            desc,
+            row_full=np.full(n, p),
+            row_len=np.full(n, p + n),
+            row_mask=masks.numpy(),
         )
         # Path log-probs: token t of route r is scored by the prefix row (t == 0)
         # or by its parent node's row; one gather, one host transfer.
@@ -319,6 +320,8 @@ class TargetVerifier:
         else:
             lse = torch.logsumexp(allrows, dim=-1)
             vals = (allrows[r, t] - lse[r]).reshape(rows.shape)
+        if vals.is_cuda:
+            counters.d2h(vals.numel() * 4)
         return vals.double().cpu().tolist()
 
     # -------------------------------------------------------------- scoring
@@ -581,8 +584,6 @@ class TargetVerifier:
         all_logits: list[torch.Tensor] = []
         cur = self._prefix_logits.reshape(1, -1)
         t_model = time.perf_counter()
-        pages = self.mirror.view()
-        slots_d = slots.to(dev, non_blocking=True)
         if cur.is_cuda:
             from ..ops.cuda_ops import shared_ops
 
@@ -596,12 +597,25 @@ class TargetVerifier:
             def argmax_into(row: torch.Tensor, t: int) -> None:
                 toks[t: t + 1] = torch.argmax(row, dim=-1).to(torch.int32)
 
+        slots_np = slots.numpy()
+        n_pages = len(self.mirror.host)
         for t in range(steps):
             argmax_into(cur, t)
-            pos = torch.tensor([p + t], dtype=torch.int32).to(dev, non_blocking=True)
-            desc = single_sequence_desc(pages, pos + 1, shared_len=p + t)
-            cur = self.engine.forward(toks[t: t + 1], pos, slots_d[t: t + 1], desc)
+            cur = self.engine.run_rows(
+                1,
+                prefix_pages=self.mirror.dev,
+                tokens=toks[t: t + 1],
+                positions=[p + t],
+                slots=slots_np[t: t + 1],
+                shared_len=p + t,
+                n_shared_pages=n_pages,
+                mask_base=p + t,
+                row_full=[p + t + 1],
+                row_len=[p + t + 1],
+            )
             all_logits.append(cur)
+        if toks.is_cuda:
+            counters.d2h(toks.numel() * 4)
         generated = [int(x) for x in toks.cpu().tolist()]
         if prof:
             self._profile_sync()

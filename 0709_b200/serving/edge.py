@@ -249,229 +249,27 @@ class PagedDistributedAtlasGenerator:
 
     # ----------------------------------------------------------- generate
     def generate(self, prompt_token_ids: Sequence[int]) -> DistributedGenerationResult:
-        cfg = self.config
-        committed = [int(t) for t in prompt_token_ids]
-        generated: list[int] = []
-        traces: list[DistributedRoundTrace] = []
-        fallback_profiles: list[dict[str, object]] = []
-        health = self.target_client.health()
-        target_meta = dict(health.get("metadata", {}))
-        self._t0 = time.perf_counter()
-        rounds_tl: list[EdgeRoundTimeline] = []
-        store = KVTreeStore()
-        self.drafter.bind_store(store)
-        pre_frontier = pre_completed = pre_logits = None
-        pre_depth = 0
-        pre_spans: list[EdgeSpan] = []
-        sampling0 = self._sampling(committed)
+        session = self.start(prompt_token_ids)
+        while not session.finished:
+            session.step()
+        return session.result()
 
-        with ThreadPoolExecutor(max_workers=1) as pool:
-            tfut = pool.submit(self._timed, "cloud_prompt_blackbox", self.target_client.prefill, committed)
-            _, edge_prefill = self._timed("edge_prompt_prefill", self.drafter.prefill, committed)
-            store.committed_token_ids = list(committed)
-            t_tree = self._now()
-            active = initialize_stage1_routes(
-                self.drafter.prefix_state(), k=cfg.k, route_store=store, sampling=sampling0
-            )
-            stage1 = build_tree_depths(
-                active, depth=cfg.d, k=cfg.k, route_store=store, model_backend=self.drafter, sampling=sampling0
-            )
-            initial_tree = EdgeSpan("edge_initial_stage1_tree", t_tree, self._now())
-            if cfg.fixed_forest_depth is None and not tfut.done():
-                pre_frontier = initialize_forest_routes(
-                    stage1.completed_routes, stage1.last_logits, k=cfg.k, route_store=store, sampling=sampling0
-                )
-                while not tfut.done() and pre_depth < cfg.d:
-                    s0 = self._now()
-                    step = build_forest_one_depth(
-                        pre_frontier, k=cfg.k, route_store=store, model_backend=self.drafter, sampling=sampling0
-                    )
-                    pre_depth += 1
-                    pre_spans.append(EdgeSpan(f"edge_forest_step_{pre_depth}", s0, self._now()))
-                    pre_completed = step.decoded_routes
-                    pre_logits = step.decode_output.next_token_logits
-                    pre_frontier = step.next_routes
-            _, cloud_prefill = tfut.result()
+    def start(self, prompt_token_ids: Sequence[int]) -> "AtlasSession":
+        """Prefill both sides (concurrently) and build the initial tree; returns a steppable session."""
+        s = AtlasSession(self, prompt_token_ids)
+        s.begin()
+        return s
 
-        round_index = 0
-        with ThreadPoolExecutor(max_workers=1) as vpool:
-            while len(generated) < cfg.max_new_tokens:
-                rs = self._sampling(committed)
-                p_round = len(committed)
-                payload = self._route_payloads(store, stage1.completed_routes)
-                v_submit = self._now()
-                remaining = cfg.max_new_tokens - len(generated)
-                vfut = vpool.submit(self._verify_call, list(committed), payload, remaining, round_index)
-                if round_index == 0 and pre_frontier is not None:
-                    f_depth, f_done, f_logits, f_spans, f_front = pre_depth, pre_completed, pre_logits, list(pre_spans), pre_frontier
-                else:
-                    f_depth, f_done, f_logits, f_spans = 0, None, None, []
-                    f_front = initialize_forest_routes(
-                        stage1.completed_routes, stage1.last_logits, k=cfg.k, route_store=store, sampling=rs
-                    )
-                while self._should_build_forest_step(verify_done=vfut.done(), forest_depth=f_depth):
-                    s0 = self._now()
-                    step = build_forest_one_depth(
-                        f_front, k=cfg.k, route_store=store, model_backend=self.drafter, sampling=rs
-                    )
-                    f_depth += 1
-                    f_spans.append(EdgeSpan(f"edge_forest_step_{f_depth}", s0, self._now()))
-                    f_done, f_logits, f_front = step.decoded_routes, step.decode_output.next_token_logits, step.next_routes
-                early = f_depth < cfg.d and vfut.done()
-                resp, v_done = vfut.result()
-                vspan = EdgeSpan("cloud_verify_blackbox", v_submit, v_done)
-                tmeta = dict(resp.get("metadata", {}))
-                prof = tmeta.get("fallback_ar_profile")
-                if isinstance(prof, dict):
-                    fallback_profiles.append({"round_index": round_index, **prof})
-                decision = str(resp.get("decision", "select"))
-                sel_id: int | None = None
-                reason: str | None = None
-                fb_tokens: list[int] = []
-                mode = "stopped"
-                reused = reused_depth = remaining_depth = 0
-                phys = {"committed_kv_tokens": 0, "released_route_rows": 0, "released_kv_pages": 0}
-                handoff_span: EdgeSpan | None = None
-                post_spans: list[EdgeSpan] = []
-                if decision == "fallback_ar":
-                    fb_tokens = [int(t) for t in resp.get("fallback_token_ids", [])]
-                    reason = None if resp.get("fallback_reason") is None else str(resp.get("fallback_reason"))
-                    if len(fb_tokens) > remaining:
-                        raise RuntimeError(
-                            "target fallback returned more tokens than the remaining budget: "
-                            f"returned={len(fb_tokens)}, remaining={remaining}"
-                        )
-                    now = list(fb_tokens)
-                    generated.extend(now)
-                    committed.extend(now)
-                    stop = not now or self._should_stop(now, generated)
-                    mode = "fallback_ar_stopped" if stop else "fallback_ar_extend_prefix_kv"
-                    if not stop:
-                        s0 = self._now()
-                        stage1, phys = self._fallback_extend_handoff(store, now)
-                        handoff_span = EdgeSpan("edge_fallback_extend_then_build_tree", s0, self._now())
-                elif decision == "select":
-                    sel_id = selected_route_id_from_response(resp)
-                    sel = self._find_route(stage1, sel_id)
-                    full = list(store.materialized_token_path(sel)[: cfg.d])
-                    now = self._truncate_commit(full, generated)
-                    generated.extend(now)
-                    committed.extend(now)
-                    stop = not now or self._should_stop(now, generated)
-                    if not stop:
-                        if now != full:
-                            raise RuntimeError("cannot reuse stage-2 KV after a partial stage-1 commit")
-                        h = self._handoff_after_verify(
-                            store=store,
-                            selected_stage1_route=sel,
-                            forest_depth=f_depth,
-                            forest_frontier=f_front,
-                            forest_completed=f_done,
-                            forest_last_logits=f_logits,
-                            sampling=self._sampling(committed),
-                        )
-                        handoff_span, post_spans = h.commit_prune_span, list(h.tree_step_spans)
-                        stage1, mode = h.stage1, h.mode
-                        reused, reused_depth, remaining_depth = (
-                            h.reused_stage2_routes,
-                            h.reused_stage2_depth,
-                            h.remaining_tree_depth,
-                        )
-                        phys = h.physical_stats
-                else:
-                    raise RuntimeError(f"unknown target verify decision: {decision!r}")
-                if cfg.validate_state_alignment:
-                    self._validate_target_prefix_lengths(tmeta, p_round, len(committed))
-                    if not stop:
-                        self._validate_drafter_prefix_state(
-                            store, committed, [*stage1.completed_routes, *stage1.next_frontier_routes]
-                        )
-                traces.append(
-                    DistributedRoundTrace(
-                        round_index=round_index,
-                        selected_route_id=sel_id,
-                        committed_tokens=[int(t) for t in now],
-                        decision=decision,
-                        fallback_reason=reason,
-                        fallback_token_ids=list(fb_tokens),
-                        forest_depth=f_depth,
-                        verify_returned_before_forest_done=early,
-                        target_scores=list(resp.get("scores", [])),
-                        handoff_mode=mode,
-                        reused_stage2_routes=reused,
-                        reused_stage2_depth=reused_depth,
-                        remaining_tree_depth=remaining_depth,
-                        committed_kv_tokens=int(phys["committed_kv_tokens"]),
-                        released_route_rows=int(phys["released_route_rows"]),
-                        released_kv_pages=int(phys["released_kv_pages"]),
-                        target_unique_tree_nodes=int(tmeta.get("node_count", 0)),
-                        target_unmerged_path_nodes=int(tmeta.get("unmerged_path_node_count", 0)),
-                        target_prefix_len_before=int(tmeta.get("prefix_len_before", len(committed) - len(now))),
-                        target_prefix_len_after=int(tmeta.get("prefix_len_after", len(committed))),
-                        target_decision_metadata={k: tmeta[k] for k in COMPACT_DECISION_KEYS if k in tmeta},
-                    )
-                )
-                rounds_tl.append(
-                    EdgeRoundTimeline(
-                        round_index=round_index,
-                        verify_blackbox=vspan,
-                        forest_steps=f_spans,
-                        post_prune_tree_steps=post_spans,
-                        handoff=handoff_span,
-                        forest_depth=f_depth,
-                        accepted_tokens=len(now),
-                        generated_tokens=len(generated),
-                        handoff_mode=mode,
-                        verify_returned_before_forest_done=early,
-                    )
-                )
-                round_index += 1
-                if stop:
-                    break
+    def close(self) -> None:
+        self._vpool.shutdown(wait=True)
 
-        elapsed = self._now()
-        timeline = EdgeBlackboxTimeline(edge_prefill, cloud_prefill, initial_tree, rounds_tl, elapsed, len(generated))
-        self.last_timeline = timeline
-        text = self.tokenizer.decode(committed) if self.tokenizer is not None else None
-        fb_rounds = sum(t.decision == "fallback_ar" for t in traces)
-        return DistributedGenerationResult(
-            prompt_token_ids=[int(t) for t in prompt_token_ids],
-            generated_token_ids=generated,
-            text=text,
-            rounds=traces,
-            metadata={
-                "system": self.system_name,
-                "drafter_backend": "b200_native_paged_decode",
-                "target_backend": target_meta.get("backend", "b200_native_masked_tree_verify"),
-                "target_transport": str(health.get("transport", "http")),
-                "target_health": health,
-                "k": cfg.k,
-                "d": cfg.d,
-                "max_new_tokens": cfg.max_new_tokens,
-                "fallback_ar_tokens": int(cfg.fallback_ar_tokens),
-                "generation_seed": int(cfg.generation_seed),
-                "drafter_sampling": self._sampling_config().to_dict(),
-                "fixed_forest_depth": cfg.fixed_forest_depth,
-                "validate_state_alignment": bool(cfg.validate_state_alignment),
-                "rebuild_drafter_prefix_after_commit": False,
-                "rebuild_drafter_prefix_after_fallback": False,
-                "fallback_drafter_handoff": "single_multi_token_extend",
-                "target_fallback_ar_profiles": fallback_profiles,
-                "rebuild_target_prefix_after_commit": False,
-                "cross_round_stage2_kv_reuse": True,
-                "cross_round_target_kv_reuse": True,
-                "target_selection_policy": target_meta.get("selection_policy"),
-                "target_route_selection_policy": target_meta.get("route_selection_policy"),
-                "route_tail_page_cow": True,
-                "branch_safe_page_size": True,
-                "forest_cancel_granularity": "between_decode_steps",
-                "rounds": len(traces),
-                "fallback_rounds": fb_rounds,
-                "fallback_rate": fb_rounds / len(traces) if traces else None,
-                "edge_blackbox_timeline": timeline.summary(),
-                "drafter_hot_path_counters": self.drafter.hot_path_counters(),
-            },
-        )
+    @property
+    def _vpool(self) -> ThreadPoolExecutor:
+        pool = getattr(self, "_verify_pool", None)
+        if pool is None:
+            pool = ThreadPoolExecutor(max_workers=1, thread_name_prefix="atlas-verify")
+            self._verify_pool = pool
+        return pool
 
     # ------------------------------------------------------------ handoffs
     def _fallback_extend_handoff(self, store: KVTreeStore, tokens: Sequence[int]):
@@ -592,3 +390,235 @@ class PagedDistributedAtlasGenerator:
         for r in routes:
             if self.drafter.route_pool.has_route(int(r.route_id)):
                 self.drafter.validate_route_physical_state(r)
+
+
+class AtlasSession:
+    """One generation advanced one speculative round per ``step()``."""
+
+    def __init__(self, gen: PagedDistributedAtlasGenerator, prompt_token_ids: Sequence[int]) -> None:
+        self.gen = gen
+        self.prompt = [int(t) for t in prompt_token_ids]
+        self.committed = list(self.prompt)
+        self.generated: list[int] = []
+        self.traces: list[DistributedRoundTrace] = []
+        self.fallback_profiles: list[dict[str, object]] = []
+        self.rounds_tl: list[EdgeRoundTimeline] = []
+        self.finished = False
+        self.round_index = 0
+        self.store = KVTreeStore()
+
+    def begin(self) -> None:
+        g, cfg = self.gen, self.gen.config
+        self.health = g.target_client.health()
+        self.target_meta = dict(self.health.get("metadata", {}))
+        g._t0 = time.perf_counter()
+        g.drafter.bind_store(self.store)
+        self.pre_frontier = self.pre_completed = self.pre_logits = None
+        self.pre_depth = 0
+        self.pre_spans: list[EdgeSpan] = []
+        s0 = g._sampling(self.committed)
+        tfut = g._vpool.submit(g._timed, "cloud_prompt_blackbox", g.target_client.prefill, list(self.committed))
+        _, self.edge_prefill = g._timed("edge_prompt_prefill", g.drafter.prefill, self.committed)
+        self.store.committed_token_ids = list(self.committed)
+        t_tree = g._now()
+        active = initialize_stage1_routes(g.drafter.prefix_state(), k=cfg.k, route_store=self.store, sampling=s0)
+        self.stage1 = build_tree_depths(
+            active, depth=cfg.d, k=cfg.k, route_store=self.store, model_backend=g.drafter, sampling=s0
+        )
+        self.initial_tree = EdgeSpan("edge_initial_stage1_tree", t_tree, g._now())
+        if cfg.fixed_forest_depth is None and not tfut.done():
+            self.pre_frontier = initialize_forest_routes(
+                self.stage1.completed_routes, self.stage1.last_logits, k=cfg.k, route_store=self.store, sampling=s0
+            )
+            while not tfut.done() and self.pre_depth < cfg.d:
+                t0 = g._now()
+                st = build_forest_one_depth(
+                    self.pre_frontier, k=cfg.k, route_store=self.store, model_backend=g.drafter, sampling=s0
+                )
+                self.pre_depth += 1
+                self.pre_spans.append(EdgeSpan(f"edge_forest_step_{self.pre_depth}", t0, g._now()))
+                self.pre_completed = st.decoded_routes
+                self.pre_logits = st.decode_output.next_token_logits
+                self.pre_frontier = st.next_routes
+        _, self.cloud_prefill = tfut.result()
+
+    def step(self) -> DistributedRoundTrace:
+        """One round: verify in the worker while the forest grows; then hand off."""
+        if self.finished:
+            raise RuntimeError("session already finished")
+        g, cfg, store = self.gen, self.gen.config, self.store
+        committed, generated = self.committed, self.generated
+        rs = g._sampling(committed)
+        p_round = len(committed)
+        payload = g._route_payloads(store, self.stage1.completed_routes)
+        v_submit = g._now()
+        remaining = cfg.max_new_tokens - len(generated)
+        vfut = g._vpool.submit(g._verify_call, list(committed), payload, remaining, self.round_index)
+        if self.round_index == 0 and self.pre_frontier is not None:
+            f_depth, f_done, f_logits = self.pre_depth, self.pre_completed, self.pre_logits
+            f_spans, f_front = list(self.pre_spans), self.pre_frontier
+        else:
+            f_depth, f_done, f_logits, f_spans = 0, None, None, []
+            f_front = initialize_forest_routes(
+                self.stage1.completed_routes, self.stage1.last_logits, k=cfg.k, route_store=store, sampling=rs
+            )
+        while g._should_build_forest_step(verify_done=vfut.done(), forest_depth=f_depth):
+            t0 = g._now()
+            st = build_forest_one_depth(f_front, k=cfg.k, route_store=store, model_backend=g.drafter, sampling=rs)
+            f_depth += 1
+            f_spans.append(EdgeSpan(f"edge_forest_step_{f_depth}", t0, g._now()))
+            f_done, f_logits, f_front = st.decoded_routes, st.decode_output.next_token_logits, st.next_routes
+        early = f_depth < cfg.d and vfut.done()
+        resp, v_done = vfut.result()
+        vspan = EdgeSpan("cloud_verify_blackbox", v_submit, v_done)
+        tmeta = dict(resp.get("metadata", {}))
+        prof = tmeta.get("fallback_ar_profile")
+        if isinstance(prof, dict):
+            self.fallback_profiles.append({"round_index": self.round_index, **prof})
+        decision = str(resp.get("decision", "select"))
+        sel_id: int | None = None
+        reason: str | None = None
+        fb_tokens: list[int] = []
+        mode = "stopped"
+        reused = reused_depth = remaining_depth = 0
+        phys = {"committed_kv_tokens": 0, "released_route_rows": 0, "released_kv_pages": 0}
+        handoff_span: EdgeSpan | None = None
+        post_spans: list[EdgeSpan] = []
+        if decision == "fallback_ar":
+            fb_tokens = [int(t) for t in resp.get("fallback_token_ids", [])]
+            reason = None if resp.get("fallback_reason") is None else str(resp.get("fallback_reason"))
+            if len(fb_tokens) > remaining:
+                raise RuntimeError(
+                    "target fallback returned more tokens than the remaining budget: "
+                    f"returned={len(fb_tokens)}, remaining={remaining}"
+                )
+            now = list(fb_tokens)
+            generated.extend(now)
+            committed.extend(now)
+            stop = not now or g._should_stop(now, generated)
+            mode = "fallback_ar_stopped" if stop else "fallback_ar_extend_prefix_kv"
+            if not stop:
+                t0 = g._now()
+                self.stage1, phys = g._fallback_extend_handoff(store, now)
+                handoff_span = EdgeSpan("edge_fallback_extend_then_build_tree", t0, g._now())
+        elif decision == "select":
+            sel_id = selected_route_id_from_response(resp)
+            sel = g._find_route(self.stage1, sel_id)
+            full = list(store.materialized_token_path(sel)[: cfg.d])
+            now = g._truncate_commit(full, generated)
+            generated.extend(now)
+            committed.extend(now)
+            stop = not now or g._should_stop(now, generated)
+            if not stop:
+                if now != full:
+                    raise RuntimeError("cannot reuse stage-2 KV after a partial stage-1 commit")
+                h = g._handoff_after_verify(
+                    store=store,
+                    selected_stage1_route=sel,
+                    forest_depth=f_depth,
+                    forest_frontier=f_front,
+                    forest_completed=f_done,
+                    forest_last_logits=f_logits,
+                    sampling=g._sampling(committed),
+                )
+                handoff_span, post_spans = h.commit_prune_span, list(h.tree_step_spans)
+                self.stage1, mode = h.stage1, h.mode
+                reused, reused_depth, remaining_depth = h.reused_stage2_routes, h.reused_stage2_depth, h.remaining_tree_depth
+                phys = h.physical_stats
+        else:
+            raise RuntimeError(f"unknown target verify decision: {decision!r}")
+        if cfg.validate_state_alignment:
+            g._validate_target_prefix_lengths(tmeta, p_round, len(committed))
+            if not stop:
+                g._validate_drafter_prefix_state(
+                    store, committed, [*self.stage1.completed_routes, *self.stage1.next_frontier_routes]
+                )
+        trace = DistributedRoundTrace(
+            round_index=self.round_index,
+            selected_route_id=sel_id,
+            committed_tokens=[int(t) for t in now],
+            decision=decision,
+            fallback_reason=reason,
+            fallback_token_ids=list(fb_tokens),
+            forest_depth=f_depth,
+            verify_returned_before_forest_done=early,
+            target_scores=list(resp.get("scores", [])),
+            handoff_mode=mode,
+            reused_stage2_routes=reused,
+            reused_stage2_depth=reused_depth,
+            remaining_tree_depth=remaining_depth,
+            committed_kv_tokens=int(phys["committed_kv_tokens"]),
+            released_route_rows=int(phys["released_route_rows"]),
+            released_kv_pages=int(phys["released_kv_pages"]),
+            target_unique_tree_nodes=int(tmeta.get("node_count", 0)),
+            target_unmerged_path_nodes=int(tmeta.get("unmerged_path_node_count", 0)),
+            target_prefix_len_before=int(tmeta.get("prefix_len_before", len(committed) - len(now))),
+            target_prefix_len_after=int(tmeta.get("prefix_len_after", len(committed))),
+            target_decision_metadata={k: tmeta[k] for k in COMPACT_DECISION_KEYS if k in tmeta},
+        )
+        self.traces.append(trace)
+        self.rounds_tl.append(
+            EdgeRoundTimeline(
+                round_index=self.round_index,
+                verify_blackbox=vspan,
+                forest_steps=f_spans,
+                post_prune_tree_steps=post_spans,
+                handoff=handoff_span,
+                forest_depth=f_depth,
+                accepted_tokens=len(now),
+                generated_tokens=len(generated),
+                handoff_mode=mode,
+                verify_returned_before_forest_done=early,
+            )
+        )
+        self.round_index += 1
+        if stop:
+            self.finished = True
+        return trace
+
+    def result(self) -> DistributedGenerationResult:
+        g, cfg = self.gen, self.gen.config
+        elapsed = g._now()
+        timeline = EdgeBlackboxTimeline(
+            self.edge_prefill, self.cloud_prefill, self.initial_tree, self.rounds_tl, elapsed, len(self.generated)
+        )
+        g.last_timeline = timeline
+        fb_rounds = sum(t.decision == "fallback_ar" for t in self.traces)
+        return DistributedGenerationResult(
+            prompt_token_ids=list(self.prompt),
+            generated_token_ids=list(self.generated),
+            text=g.tokenizer.decode(self.committed) if g.tokenizer is not None else None,
+            rounds=self.traces,
+            metadata={
+                "system": g.system_name,
+                "drafter_backend": "b200_native_paged_decode",
+                "target_backend": self.target_meta.get("backend", "b200_native_masked_tree_verify"),
+                "target_transport": str(self.health.get("transport", "http")),
+                "target_health": self.health,
+                "k": cfg.k,
+                "d": cfg.d,
+                "max_new_tokens": cfg.max_new_tokens,
+                "fallback_ar_tokens": int(cfg.fallback_ar_tokens),
+                "generation_seed": int(cfg.generation_seed),
+                "drafter_sampling": g._sampling_config().to_dict(),
+                "fixed_forest_depth": cfg.fixed_forest_depth,
+                "validate_state_alignment": bool(cfg.validate_state_alignment),
+                "rebuild_drafter_prefix_after_commit": False,
+                "rebuild_drafter_prefix_after_fallback": False,
+                "fallback_drafter_handoff": "single_multi_token_extend",
+                "target_fallback_ar_profiles": self.fallback_profiles,
+                "rebuild_target_prefix_after_commit": False,
+                "cross_round_stage2_kv_reuse": True,
+                "cross_round_target_kv_reuse": True,
+                "target_selection_policy": self.target_meta.get("selection_policy"),
+                "target_route_selection_policy": self.target_meta.get("route_selection_policy"),
+                "route_tail_page_cow": True,
+                "branch_safe_page_size": True,
+                "forest_cancel_granularity": "between_decode_steps",
+                "rounds": len(self.traces),
+                "fallback_rounds": fb_rounds,
+                "fallback_rate": fb_rounds / len(self.traces) if self.traces else None,
+                "edge_blackbox_timeline": timeline.summary(),
+                "drafter_hot_path_counters": g.drafter.hot_path_counters(),
+            },
+        )
