@@ -22,6 +22,7 @@
 
 #include "attention.h"
 #include "common.cuh"
+#include "launch.h"
 
 namespace atlas {
 
@@ -77,6 +78,8 @@ __global__ void __launch_bounds__(160, 1)
   for (int i = tid; i < kStages * kStageBytes / 16; i += blockDim.x)
     reinterpret_cast<uint4*>(kv_s)[i] = make_uint4(0, 0, 0, 0);
   __syncthreads();
+  pdl_trigger();
+  pdl_wait();
 
   // ---- load the Q tile (row rho = token * G + g of this kv head) and row limits
   const int rho = tid;
@@ -258,6 +261,8 @@ __global__ void __launch_bounds__(160, 1)
 // One warp per (row, q head): merge split partials, then the row's tail keys.
 template <typename T>
 __global__ void __launch_bounds__(128) attn_combine_tail(AttnParams p) {
+  pdl_wait();
+  pdl_trigger();
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const int64_t pair = static_cast<int64_t>(blockIdx.x) * 4 + warp;
@@ -341,11 +346,11 @@ static void launch_typed(const CUtensorMap& kvmap, const AttnParams& p, bool run
       configured = true;
     }
     dim3 grid(p.Hkv, p.splits, row_tiles);
-    attn_shared_tc<T><<<grid, 160, kSmemBytes, st>>>(kvmap, p);
+    launch_k(attn_shared_tc<T>, grid, dim3(160), kSmemBytes, st, kvmap, p);
   }
   if (run_combine) {
     const int64_t pairs = static_cast<int64_t>(p.M) * p.Hq;
-    attn_combine_tail<T><<<static_cast<unsigned>((pairs + 3) / 4), 128, 0, st>>>(p);
+    launch_k(attn_combine_tail<T>, dim3(static_cast<unsigned>((pairs + 3) / 4)), dim3(128), 0, st, p);
   }
 }
 

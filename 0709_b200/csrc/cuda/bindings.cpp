@@ -321,9 +321,14 @@ void topk(torch::Tensor logits, int64_t k, c10::optional<torch::Tensor> keys, do
   TORCH_CHECK(logits.scalar_type() == torch::kFloat32 && logits.is_contiguous(), "logits must be contiguous fp32");
   TORCH_CHECK(k >= 1 && k <= 8, "top-k supports 1 <= k <= 8");
   const c10::cuda::CUDAGuard guard(logits.device());
-  atlas::launch_topk(logits.data_ptr<float>(), static_cast<int>(logits.size(0)), static_cast<int>(logits.size(1)),
-                     static_cast<int>(k), keys.has_value() ? keys->data_ptr<int64_t>() : nullptr,
-                     static_cast<float>(inv_temp), out_lp.data_ptr<float>(), out_id.data_ptr<int64_t>(),
+  const int64_t B = logits.size(0), V = logits.size(1);
+  // Enough vocabulary chunks to spread the scan over every SM (<= 256 chunks, >= 1024 entries each).
+  const int chunks = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(
+      {256, (V + 1023) / 1024, (2 * num_sms() + B - 1) / B})));
+  auto part = torch::empty({B * chunks * atlas::topk_record_floats()}, logits.options());
+  atlas::launch_topk(logits.data_ptr<float>(), static_cast<int>(B), static_cast<int>(V), static_cast<int>(k),
+                     keys.has_value() ? keys->data_ptr<int64_t>() : nullptr, static_cast<float>(inv_temp),
+                     out_lp.data_ptr<float>(), out_id.data_ptr<int64_t>(), part.data_ptr<float>(), chunks,
                      at::cuda::getCurrentCUDAStream());
 }
 

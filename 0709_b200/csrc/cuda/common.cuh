@@ -96,6 +96,16 @@ __device__ __forceinline__ void tma_load_5d(void* dst, const CUtensorMap* map, u
       : "memory");
 }
 
+// ------------------------------------------------ programmatic dependent launch
+// Kernels are launched with programmatic stream serialization: a kernel may
+// start while its predecessor drains.  `pdl_wait` blocks until the predecessor
+// grid has completed and its writes are visible; every kernel calls it before
+// touching memory that a predecessor may read or write (weights excepted).
+// `pdl_trigger` lets the successor start; kernels issue it only after their
+// own TMEM allocation so a successor can never take columns they still need.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 // ----------------------------------------------------------------- fences
 __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");

@@ -4,12 +4,15 @@
 
 #include "common.cuh"
 #include "kernels.h"
+#include "launch.h"
 
 namespace atlas {
 
 template <typename T>
 __global__ void embed_kernel(const int* __restrict__ tok, const T* __restrict__ table, float* __restrict__ out, int H,
                              int V, int* err) {
+  pdl_wait();
+  pdl_trigger();
   const int m = blockIdx.x;
   int t = tok[m];
   if (t < 0 || t >= V) {
@@ -24,6 +27,8 @@ __global__ void embed_kernel(const int* __restrict__ tok, const T* __restrict__ 
 template <typename T>
 __global__ void rmsnorm_kernel(const float* __restrict__ x, const T* __restrict__ w, T* __restrict__ out, int H,
                                float eps) {
+  pdl_wait();
+  pdl_trigger();
   const int m = blockIdx.x;
   const float* row = x + static_cast<int64_t>(m) * H;
   float ss = 0.f;
@@ -58,6 +63,8 @@ __global__ void rope_append_kernel(const T* __restrict__ qkv, const float* __res
                                    const int* __restrict__ pos, const int* __restrict__ slots, T* __restrict__ kv,
                                    T* __restrict__ qout, int Hq, int Hkv, int hd, int ps, int num_pages,
                                    int max_pos, int* err) {
+  pdl_wait();
+  pdl_trigger();
   const int m = blockIdx.x;
   const int head = blockIdx.y;
   const int i = threadIdx.x;
@@ -101,18 +108,19 @@ __global__ void rope_append_kernel(const T* __restrict__ qkv, const float* __res
 void launch_embed(const int* tok, const void* table, float* out, int M, int H, int V, bool bf16, int* err,
                   cudaStream_t st) {
   if (bf16)
-    embed_kernel<__nv_bfloat16><<<M, 256, 0, st>>>(tok, static_cast<const __nv_bfloat16*>(table), out, H, V, err);
+    launch_k(embed_kernel<__nv_bfloat16>, dim3(M), dim3(256), 0, st, tok, static_cast<const __nv_bfloat16*>(table), out, H, V, err);
   else
-    embed_kernel<__half><<<M, 256, 0, st>>>(tok, static_cast<const __half*>(table), out, H, V, err);
+    launch_k(embed_kernel<__half>, dim3(M), dim3(256), 0, st, tok, static_cast<const __half*>(table), out, H, V, err);
 }
 
 void launch_rmsnorm(const float* x, const void* w, void* out, int M, int H, float eps, bool bf16, cudaStream_t st) {
   const int threads = H >= 4096 ? 512 : 256;
   if (bf16)
-    rmsnorm_kernel<__nv_bfloat16><<<M, threads, 0, st>>>(x, static_cast<const __nv_bfloat16*>(w),
-                                                          static_cast<__nv_bfloat16*>(out), H, eps);
+    launch_k(rmsnorm_kernel<__nv_bfloat16>, dim3(M), dim3(threads), 0, st, x, static_cast<const __nv_bfloat16*>(w),
+             static_cast<__nv_bfloat16*>(out), H, eps);
   else
-    rmsnorm_kernel<__half><<<M, threads, 0, st>>>(x, static_cast<const __half*>(w), static_cast<__half*>(out), H, eps);
+    launch_k(rmsnorm_kernel<__half>, dim3(M), dim3(threads), 0, st, x, static_cast<const __half*>(w),
+             static_cast<__half*>(out), H, eps);
 }
 
 void launch_rope_append(const void* qkv, const float* table, const int* pos, const int* slots, void* kv_layer,
@@ -120,13 +128,12 @@ void launch_rope_append(const void* qkv, const float* table, const int* pos, con
                         int* err, cudaStream_t st) {
   dim3 grid(M, Hq + Hkv);
   if (bf16)
-    rope_append_kernel<__nv_bfloat16><<<grid, hd / 2, 0, st>>>(
-        static_cast<const __nv_bfloat16*>(qkv), table, pos, slots, static_cast<__nv_bfloat16*>(kv_layer),
-        static_cast<__nv_bfloat16*>(qout), Hq, Hkv, hd, ps, num_pages, max_pos, err);
+    launch_k(rope_append_kernel<__nv_bfloat16>, grid, dim3(hd / 2), 0, st, static_cast<const __nv_bfloat16*>(qkv), table,
+             pos, slots, static_cast<__nv_bfloat16*>(kv_layer), static_cast<__nv_bfloat16*>(qout), Hq, Hkv, hd, ps,
+             num_pages, max_pos, err);
   else
-    rope_append_kernel<__half><<<grid, hd / 2, 0, st>>>(static_cast<const __half*>(qkv), table, pos, slots,
-                                                         static_cast<__half*>(kv_layer), static_cast<__half*>(qout),
-                                                         Hq, Hkv, hd, ps, num_pages, max_pos, err);
+    launch_k(rope_append_kernel<__half>, grid, dim3(hd / 2), 0, st, static_cast<const __half*>(qkv), table, pos, slots,
+             static_cast<__half*>(kv_layer), static_cast<__half*>(qout), Hq, Hkv, hd, ps, num_pages, max_pos, err);
 }
 
 }  // namespace atlas

@@ -21,6 +21,7 @@
 
 #include "common.cuh"
 #include "gemm.h"
+#include "launch.h"
 
 namespace atlas {
 
@@ -114,12 +115,23 @@ __global__ void __launch_bounds__(128, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  pdl_trigger();
   bool ok = true;
 
   if (tid == 0) {
-    for (int i = 0; i < nk && ok; ++i) {
+    // Weight tiles do not depend on the previous kernel: stream the first
+    // stages before waiting for it, then the activations.
+    const int pre = min(nk, S::kStages);
+    for (int i = 0; i < pre; ++i) {
+      mbar_arrive_expect_tx(&full[i], S::kStageBytes);
+      tma_load_2d(smem + i * S::kStageBytes, &tmA, &full[i], (kb0 + i) * 64, m0);
+    }
+    pdl_wait();
+    for (int i = 0; i < pre; ++i)
+      tma_load_2d(smem + i * S::kStageBytes + S::kABytes, &tmB, &full[i], (kb0 + i) * 64, n0);
+    for (int i = pre; i < nk && ok; ++i) {
       const int s = i % S::kStages;
-      if (i >= S::kStages) ok = mbar_wait(&empty[s], ((i / S::kStages) - 1) & 1, p.err);
+      ok = mbar_wait(&empty[s], ((i / S::kStages) - 1) & 1, p.err);
       if (!ok) break;
       uint8_t* a = smem + s * S::kStageBytes;
       uint8_t* b = a + S::kABytes;
@@ -148,6 +160,7 @@ __global__ void __launch_bounds__(128, 1)
     umma_commit(done);
   }
   __syncwarp();
+  pdl_wait();
   if (nk > 0) ok = mbar_wait(done, 0, p.err) && ok;
   tc_fence_after();
   if (tid == 0) *flag = ok ? 1 : 0;
@@ -230,7 +243,7 @@ static void launch_bn(const CUtensorMap& a, const CUtensorMap& b, const GemmPara
     cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, S::kBytes);
     configured = true;
   }
-  kern<<<grid, 128, S::kBytes, st>>>(a, b, p);
+  launch_k(kern, grid, dim3(128), S::kBytes, st, a, b, p);
 }
 
 template <int EPI, typename T>

@@ -9,12 +9,15 @@
 
 #include "common.cuh"
 #include "kernels.h"
+#include "launch.h"
 
 namespace atlas {
 
 // grid (copies, layers, 2 * Hkv); cache layout [L, pages, 2, Hkv, ps, hd].
 __global__ void kv_copy_pages_kernel(uint4* __restrict__ kv, const int* __restrict__ plan, int num_pages, int Hkv,
                                      int ps, int hd, int* err) {
+  pdl_wait();
+  pdl_trigger();
   const int ci = blockIdx.x;
   const int layer = blockIdx.y;
   const int kvh = blockIdx.z;  // (k|v) * Hkv + head
@@ -36,6 +39,8 @@ __global__ void kv_copy_pages_kernel(uint4* __restrict__ kv, const int* __restri
 __global__ void kv_move_slots_kernel(uint4* __restrict__ kv, const int* __restrict__ src, const int* __restrict__ dst,
                                      int n, int num_pages, int Hkv, int ps, int hd, int* err) {
   extern __shared__ uint4 buf[];
+  pdl_wait();
+  pdl_trigger();
   const int layer = blockIdx.x;
   const int kvh = blockIdx.y;
   const int per = hd / 8;
@@ -68,7 +73,7 @@ void launch_kv_copy_pages(void* kv, const int* plan, int n, int layers, int num_
                           int* err, cudaStream_t st) {
   if (n == 0) return;
   dim3 grid(n, layers, 2 * Hkv);
-  kv_copy_pages_kernel<<<grid, 128, 0, st>>>(static_cast<uint4*>(kv), plan, num_pages, Hkv, ps, hd, err);
+  launch_k(kv_copy_pages_kernel, grid, dim3(128), 0, st, static_cast<uint4*>(kv), plan, num_pages, Hkv, ps, hd, err);
 }
 
 void launch_kv_move_slots(void* kv, const int* src, const int* dst, int n, int layers, int num_pages, int Hkv, int ps,
@@ -76,7 +81,8 @@ void launch_kv_move_slots(void* kv, const int* src, const int* dst, int n, int l
   if (n == 0) return;
   dim3 grid(layers, 2 * Hkv);
   const size_t smem = static_cast<size_t>(n) * (hd / 8) * sizeof(uint4);
-  kv_move_slots_kernel<<<grid, 256, smem, st>>>(static_cast<uint4*>(kv), src, dst, n, num_pages, Hkv, ps, hd, err);
+  launch_k(kv_move_slots_kernel, grid, dim3(256), smem, st, static_cast<uint4*>(kv), src, dst, n, num_pages, Hkv, ps,
+           hd, err);
 }
 
 }  // namespace atlas
