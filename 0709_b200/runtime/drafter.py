@@ -301,6 +301,12 @@ class DrafterRuntime:
         self.counters["extend_tokens"] += n
         return logits
 
+    def warm_graphs(self, k: int, extend_tokens: int = 4) -> None:
+        """Capture the decode buckets (k and k^2 routes) and the EXTEND bucket up front."""
+        for b in sorted({row_bucket(1), row_bucket(k), row_bucket(k * k)}):
+            self.engine.warm_graph(b, tail_stride=self.max_tail_pages, mask_words=1, prefix_pages=self.mirror.dev)
+        self.engine.warm_graph(row_bucket(extend_tokens), tail_stride=1, mask_words=1, prefix_pages=self.mirror.dev)
+
     # ---------------------------------------------------------- validation
     def validate_route_physical_state(self, route: RouteState) -> None:
         rid = int(route.route_id)

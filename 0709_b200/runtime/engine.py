@@ -125,6 +125,24 @@ class LlamaEngine:
         self.stats.rows += n
         return out[sb.real_slice(n)].clone()
 
+    @torch.inference_mode()
+    def warm_graph(self, rows: int, *, tail_stride: int = 1, mask_words: int = 1, prefix_pages: torch.Tensor) -> None:
+        """Capture the graph of one row bucket now (call before concurrent serving starts).
+
+        Padding-only rows: every row writes the trash slot and attends to
+        position 0, so capture touches no live KV.
+        """
+        if self.device.type != "cuda" or not self.use_graphs:
+            return
+        sb = self.static_batch(rows, tail_stride, mask_words)
+        key = (sb.key, prefix_pages.data_ptr())
+        if key in self._graphs:
+            return
+        sb.load(tokens=[], positions=[], slots=[], shared_len=1, n_shared_pages=1, mask_base=1, row_full=[],
+                row_len=[])
+        self._graphs[key] = self._capture(sb, sb.desc(prefix_pages))
+        torch.cuda.synchronize(self.device)
+
     def _capture(self, sb: "StaticBatch", desc: AttnDesc):
         from ..utils import counters
 

@@ -324,6 +324,12 @@ class TargetVerifier:
             counters.d2h(vals.numel() * 4)
         return vals.double().cpu().tolist()
 
+    def warm_graphs(self) -> None:
+        """Capture the verify bucket (up to k*d nodes) and the AR bucket up front."""
+        n = self.k * self.d
+        self.engine.warm_graph(row_bucket(n), tail_stride=1, mask_words=(n + 63) // 64, prefix_pages=self.mirror.dev)
+        self.engine.warm_graph(1, tail_stride=1, mask_words=1, prefix_pages=self.mirror.dev)
+
     # -------------------------------------------------------------- scoring
     def _weights_for_depth(self, depth: int) -> tuple[float, ...] | None:
         if self.score_weights is None:

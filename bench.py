@@ -149,12 +149,15 @@ def build(args, device):
         model_name=f"random-init {args.target}",
     )
     client = StreamTargetClient(tv, torch.cuda.Stream(device=device))
+    dr = drafter_mod.DrafterRuntime(de)
+    dr.warm_graphs(args.k, args.fallback_ar_tokens)
+    tv.warm_graphs()
     gen = edge.PagedDistributedAtlasGenerator(
         config=edge.DistributedAtlasConfig(
             k=args.k, d=args.d, max_new_tokens=args.max_new_tokens, fallback_ar_tokens=args.fallback_ar_tokens,
             generation_seed=args.seed,
         ),
-        drafter=drafter_mod.DrafterRuntime(de),
+        drafter=dr,
         target_client=client,
     )
     return gen, de, te

@@ -131,6 +131,27 @@ def main() -> int:
         w = torch.ones(4096, device="cuda", dtype=dt)
         us = timeit(lambda: ops.rmsnorm(x, w, 1e-5, dt), args.iters)
         report("rmsnorm rows=12 H=4096", us, x.numel() * 6)
+    if args.only in ("all", "forward"):
+        import numpy as np
+
+        llama = pkg("models.llama")
+        engine_mod = pkg("runtime.engine")
+        for name, rows in (("llama-8b", 12), ("llama-8b", 1), ("llama-1b", 9), ("llama-1b", 3)):
+            cfg = llama.get_config(name)
+            w = llama.random_weights(cfg, seed=1, dtype=dt, device="cuda")
+            eng = engine_mod.LlamaEngine(w, num_pages=512, page_size=16, max_positions=8192)
+            pages = torch.arange(300, dtype=torch.int32, device="cuda")
+            fields = dict(tokens=np.arange(rows), positions=np.arange(2048, 2048 + rows),
+                          slots=np.arange(2048, 2048 + rows), shared_len=2048, n_shared_pages=300, mask_base=2048,
+                          row_full=np.full(rows, 2048), row_len=np.full(rows, 2048 + rows))
+            b = engine_mod.row_bucket(rows)
+            for graphs in (True, False):
+                eng.use_graphs = graphs
+                us = timeit(lambda: eng.run_rows(b, prefix_pages=pages, **fields), max(5, args.iters // 2))
+                report(f"forward {name} rows={rows} P=2048 {'graph+pdl' if graphs else 'eager'}", us,
+                       w.nbytes() + 2 * 2048 * cfg.num_layers * cfg.kv_size * 2)
+            del eng, w
+            torch.cuda.empty_cache()
     with open(os.path.join(ROOT, "gpurun_out", "bench_kernels.json") if os.path.isdir(
             os.path.join(ROOT, "gpurun_out")) else os.devnull, "w") as f:
         json.dump(out, f, indent=1)
