@@ -33,206 +33,272 @@ constexpr int kHd = 128;
 constexpr int kQBytes = 2 * 128 * 128;                     // 2 halves x 128 rows x 128 B
 constexpr int kKVHalfBytes = kChunkKeys * 128;             // 64 keys x 128 B
 constexpr int kStageBytes = 4 * kKVHalfBytes;              // K (2 halves) + V (2 halves)
-constexpr int kPBytes = 128 * 128;                         // 128 rows x 64 keys x 2 B
-constexpr int kSmemBytes = kQBytes + kStages * kStageBytes + kPBytes + 1024 + 256;
+constexpr int kPBytes = 128 * 128;                         // 128 rows x 64 keys x 2 B (one buffer)
+constexpr int kPageIds = 1024;  // page ids of a split staged in shared memory per refill
+constexpr int kSmemBytes = kQBytes + kStages * kStageBytes + 2 * kPBytes + 1024 + 512 + kPageIds * 4;
 constexpr float kLog2e = 1.4426950408889634f;
+constexpr float kRescaleThreshold = 8.0f;  // log2 units: P stays <= 256 between rescales
+constexpr int kThreadsTC = 192;            // warps 0-3 softmax, 4 TMA, 5 MMA
 }  // namespace
 
+// Warp-specialized flash attention over the shared key range.
+//   warp 4  TMA producer: K/V pages of each 64-key chunk into a 4-stage ring
+//           (non-causal: the first stages are issued before the PDL wait --
+//           they read only committed prefix KV);
+//   warp 5  MMA issuer: S(c) = Q K(c)^T into TMEM buffer c%2, then, once the
+//           softmax warps publish P(c-1), O += P(c-1) V(c-1) into TMEM;
+//   warps 0-3  one thread per query row: online softmax with lazy rescaling
+//           (O in TMEM is rescaled only when a row's max grows by more than
+//           2^8), P written to a double-buffered shared tile.
 template <typename T>
-__global__ void __launch_bounds__(160, 1)
+__global__ void __launch_bounds__(kThreadsTC, 1)
     attn_shared_tc(const __grid_constant__ CUtensorMap kvmap, AttnParams p) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* q_s = smem;
   uint8_t* kv_s = q_s + kQBytes;
-  uint8_t* p_s = kv_s + kStages * kStageBytes;
-  uint64_t* full = reinterpret_cast<uint64_t*>(p_s + kPBytes);
+  uint8_t* p_s = kv_s + kStages * kStageBytes;  // two P buffers
+  uint64_t* full = reinterpret_cast<uint64_t*>(p_s + 2 * kPBytes);
   uint64_t* empty = full + kStages;
-  uint64_t* s_bar = empty + kStages;
-  uint64_t* o_bar = s_bar + 1;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(o_bar + 1);
-  int* s_int = reinterpret_cast<int*>(tmem_slot + 1);  // [0] tile max A, [1] ok
+  uint64_t* s_full = empty + kStages;  // [2]
+  uint64_t* p_full = s_full + 2;       // [2], 128 arrivals
+  uint64_t* pv_done = p_full + 2;      // [2]
+  uint64_t* fin = pv_done + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(fin + 1);
+  int* s_int = reinterpret_cast<int*>(tmem_slot + 1);  // [0] tile max A
+  int* page_ids = reinterpret_cast<int*>(reinterpret_cast<uint8_t*>(full) + 256);  // after barriers/slots
 
   const int tid = threadIdx.x;
   const int warp = tid >> 5;
   const int h = blockIdx.x;
   const int split = blockIdx.y;
   const int G = p.Hq / p.Hkv;
-  const int shared_len = p.dparams[0];
   const int ps = p.page_size;
+  const bool causal = p.direct_out != 0;
 
   if (tid == 0) {
     for (int s = 0; s < kStages; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
     }
-    mbar_init(s_bar, 1);
-    mbar_init(o_bar, 1);
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&s_full[b], 1);
+      mbar_init(&p_full[b], 128);
+      mbar_init(&pv_done[b], 1);
+    }
+    mbar_init(fin, 1);
     fence_barrier_init();
     s_int[0] = 0;
-    s_int[1] = 1;
     tma_prefetch_desc(&kvmap);
   }
   if (warp == 0) tmem_alloc(tmem_slot, 256);
-  // Zero the K/V ring so rows past a partial chunk hold finite data.
-  for (int i = tid; i < kStages * kStageBytes / 16; i += blockDim.x)
-    reinterpret_cast<uint4*>(kv_s)[i] = make_uint4(0, 0, 0, 0);
   __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
   pdl_trigger();
-  pdl_wait();
 
-  // ---- load the Q tile (row rho = token * G + g of this kv head) and row limits
+  // Key range of this split (shared_len and the page table are graph inputs
+  // written before the chain started, so they are safe to read before the wait).
+  const int shared_len = p.dparams[0];
+  const int np_total = (shared_len + ps - 1) / ps;
+  const int pps = (np_total + p.splits - 1) / max(p.splits, 1);
+  const int pb = split * pps;
+  const int cp = kChunkKeys / ps;  // pages per chunk
+
+  // Row limits and the Q tile need the previous kernel's output.
   const int rho = tid;
   const int grow = blockIdx.z * 128 + rho;
   const int m = grow / G;
   const int hq = h * G + (grow % G);
+  const int pe0 = min(np_total, pb + pps);
+  const int nch_loaded = pe0 > pb ? (pe0 - pb + cp - 1) / cp : 0;
   int a_lim = 0;
-  if (tid < 128) {
-    const bool valid = m < p.M;
-    if (valid) a_lim = min(p.row_full[m], shared_len);
-    const T* qrow = static_cast<const T*>(p.q) + (static_cast<int64_t>(m) * p.Hq + hq) * kHd;
-#pragma unroll
-    for (int c = 0; c < 16; ++c) {
-      uint4 v = make_uint4(0, 0, 0, 0);
-      if (valid) v = *reinterpret_cast<const uint4*>(qrow + c * 8);
-      *reinterpret_cast<uint4*>(q_s + (c >> 3) * (128 * 128) + sw128_offset(rho, c & 7)) = v;
-    }
-    fence_proxy_async_smem();
-    atomicMax(&s_int[0], a_lim);
-  }
-  __syncthreads();
-  tc_fence_after();
-  const uint32_t tmem = *tmem_slot;
-  const int tile_max = s_int[0];
-
-  const int np_total = (shared_len + ps - 1) / ps;
-  const int pps = (np_total + p.splits - 1) / max(p.splits, 1);
-  const int pb = split * pps;
-  const int pe = min(min(np_total, pb + pps), (tile_max + ps - 1) / ps);
-  const int cp = kChunkKeys / ps;  // pages per chunk
-  const int nchunks = pe > pb ? (pe - pb + cp - 1) / cp : 0;
-
+  int nchunks = 0, pe = pb;
   if (warp == 4) {
-    if (tid == 128) {
-      bool ok = true;
-      for (int c = 0; c < nchunks && ok; ++c) {
-        const int s = c % kStages;
-        if (c >= kStages) ok = mbar_wait(&empty[s], ((c / kStages) - 1) & 1, p.err);
-        if (!ok) break;
-        const int p0 = pb + c * cp;
-        const int npg = min(cp, pe - p0);
-        uint8_t* st = kv_s + s * kStageBytes;
-        mbar_arrive_expect_tx(&full[s], static_cast<uint32_t>(npg * ps * 128 * 4));
-        for (int i = 0; i < npg; ++i) {
-          int page = p.prefix_pages[p0 + i];
-          if (page < 0 || page >= p.num_pages) {
+    // Producer warp: stage the split's page ids in shared memory (all lanes,
+    // in parallel), then lane 0 streams the chunks.  It never joins a block
+    // barrier before the end (the MMA warp frees its ring stages).
+    const int lane = tid & 31;
+    if (causal) pdl_wait();  // causal prefill reads keys the previous kernel wrote
+    bool ok = true;
+    int staged_base = -1;
+    for (int c = 0; c < nch_loaded && ok; ++c) {
+      const int p0 = pb + c * cp;
+      const int npg = min(cp, pe0 - p0);
+      if (staged_base < 0 || p0 + cp > staged_base + kPageIds) {
+        // Refill: pages [p0, p0 + kPageIds) of this split.
+        __syncwarp();
+        staged_base = p0;
+        for (int i = lane; i < kPageIds; i += 32) {
+          const int pi = p0 + i;
+          int page = pi < pe0 ? p.prefix_pages[pi] : -1;
+          if (pi < pe0 && (page < 0 || page >= p.num_pages)) {
             set_error(p.err, kErrBadIndex);
             page = 0;
           }
-          const int zc = p.layer * p.num_pages + page;
-          const int roff = i * ps * 128;
+          page_ids[i] = page;
+        }
+        __syncwarp();
+      }
+      if (lane == 0) {
+        const int s = c % kStages;
+        if (c >= kStages) ok = mbar_wait(&empty[s], ((c / kStages) - 1) & 1, p.err);
+        if (ok) {
+          uint8_t* st = kv_s + s * kStageBytes;
+          mbar_arrive_expect_tx(&full[s], static_cast<uint32_t>(cp * ps * 128 * 4));
+          for (int i = 0; i < cp; ++i) {
+            // Pages past the split's end repeat a valid page: finite data that the
+            // softmax masks to P = 0.
+            const int page = page_ids[p0 - staged_base + (i < npg ? i : 0)];
+            const int zc = p.layer * p.num_pages + page;
+            const int roff = i * ps * 128;
 #pragma unroll
-          for (int half = 0; half < 2; ++half) {
-            tma_load_5d(st + half * kKVHalfBytes + roff, &kvmap, &full[s], half * 64, 0, h, 0, zc);
-            tma_load_5d(st + (2 + half) * kKVHalfBytes + roff, &kvmap, &full[s], half * 64, 0, h, 1, zc);
+            for (int half = 0; half < 2; ++half) {
+              tma_load_5d(st + half * kKVHalfBytes + roff, &kvmap, &full[s], half * 64, 0, h, 0, zc);
+              tma_load_5d(st + (2 + half) * kKVHalfBytes + roff, &kvmap, &full[s], half * 64, 0, h, 1, zc);
+            }
           }
         }
       }
-      if (!ok) s_int[1] = 0;
+      ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
     }
   } else {
-    // ---- softmax / MMA warps (rows 0..127)
-    const bool is_bf16 = p.bf16 != 0;
-    const uint32_t idesc_s = umma_idesc_f16(128, kChunkKeys, is_bf16, false, false);
-    const uint32_t idesc_o = umma_idesc_f16(128, kHd, is_bf16, false, true);
-    const uint32_t lane_base = static_cast<uint32_t>(warp * 32) << 16;
-    const uint32_t tS = tmem;        // columns [0, 64)
-    const uint32_t tO = tmem + 64;   // columns [64, 192)
-    float acc[kHd];
+    if (warp < 4) {
+      pdl_wait();
+      const bool valid = m < p.M;
+      if (valid) a_lim = min(p.row_full[m], shared_len);
+      const T* qrow = static_cast<const T*>(p.q) + (static_cast<int64_t>(m) * p.Hq + hq) * kHd;
 #pragma unroll
-    for (int i = 0; i < kHd; ++i) acc[i] = 0.f;
-    float m_run = -INFINITY, l_run = 0.f;
-    const float sl2 = p.scale * kLog2e;
-    const int lim = min(a_lim, pe * ps);  // keys of later splits / stale ring rows are masked
-    bool ok = true;
-    for (int c = 0; c < nchunks; ++c) {
-      const int s = c % kStages;
-      const uint32_t st = smem_u32(kv_s + s * kStageBytes);
-      if (tid == 0) {
-        ok = mbar_wait(&full[s], (c / kStages) & 1, p.err);
-        tc_fence_after();
-        if (ok) {
+      for (int c = 0; c < 16; ++c) {
+        uint4 v = make_uint4(0, 0, 0, 0);
+        if (valid) v = *reinterpret_cast<const uint4*>(qrow + c * 8);
+        *reinterpret_cast<uint4*>(q_s + (c >> 3) * (128 * 128) + sw128_offset(rho, c & 7)) = v;
+      }
+      fence_proxy_async_smem();
+      atomicMax(&s_int[0], a_lim);
+    }
+    asm volatile("bar.sync 1, 160;" ::: "memory");  // warps 0-3 and 5
+    const int tile_max = s_int[0];
+    pe = min(pe0, (tile_max + ps - 1) / ps);
+    nchunks = pe > pb ? (pe - pb + cp - 1) / cp : 0;
+  }
+
+  if (warp == 5) {
+    if (tid == 160) {
+      const bool is_bf16 = p.bf16 != 0;
+      const uint32_t idesc_s = umma_idesc_f16(128, kChunkKeys, is_bf16, false, false);
+      const uint32_t idesc_o = umma_idesc_f16(128, kHd, is_bf16, false, true);
+      const uint32_t tO = tmem + 128;
+      bool ok = true;
+      for (int c = 0; c <= nchunks && ok; ++c) {
+        if (c < nchunks) {
+          const int s = c % kStages;
+          ok = mbar_wait(&full[s], (c / kStages) & 1, p.err);
+          if (!ok) break;
+          tc_fence_after();
+          const uint32_t st = smem_u32(kv_s + s * kStageBytes);
+          const uint32_t tS = tmem + (c & 1) * 64;
 #pragma unroll
           for (int kk = 0; kk < 8; ++kk) {
             const uint32_t qa = smem_u32(q_s) + (kk >> 2) * (128 * 128) + (kk & 3) * 32;
             const uint32_t kb = st + (kk >> 2) * kKVHalfBytes + (kk & 3) * 32;
             umma_f16_ss(tS, umma_desc_sw128(qa, 16, 1024), umma_desc_sw128(kb, 16, 1024), idesc_s, kk > 0);
           }
+          umma_commit(&s_full[c & 1]);
         }
-        umma_commit(s_bar);
+        if (c >= 1) {
+          const int pc = c - 1;
+          ok = mbar_wait(&p_full[pc & 1], (pc >> 1) & 1, p.err);
+          if (!ok) break;
+          tc_fence_after();
+          const uint32_t pa = smem_u32(p_s + (pc & 1) * kPBytes);
+          const uint32_t vb = smem_u32(kv_s + (pc % kStages) * kStageBytes) + 2 * kKVHalfBytes;
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk) {
+            umma_f16_ss(tO, umma_desc_sw128(pa + kk * 32, 16, 1024),
+                        umma_desc_sw128(vb + kk * 2048, kKVHalfBytes, 1024), idesc_o, (pc > 0 || kk > 0) ? 1u : 0u);
+          }
+          umma_commit(&pv_done[pc & 1]);
+          umma_commit(&empty[pc % kStages]);
+        }
       }
-      __syncwarp();
-      ok = mbar_wait(s_bar, c & 1, p.err) && ok;
+      // Release the stages the producer filled beyond this tile's chunks.
+      for (int c = nchunks; c < nch_loaded && ok; ++c) {
+        ok = mbar_wait(&full[c % kStages], (c / kStages) & 1, p.err);
+        if (ok) mbar_arrive(&empty[c % kStages]);
+      }
+      umma_commit(fin);
+    }
+  } else if (warp < 4) {
+    const uint32_t lane_base = static_cast<uint32_t>(warp * 32) << 16;
+    const uint32_t tO = tmem + 128 + lane_base;
+    float m_run = -INFINITY, l_run = 0.f;
+    const float sl2 = p.scale * kLog2e;
+    const int lim = min(a_lim, pe * ps);
+    bool ok = true;
+    for (int c = 0; c < nchunks; ++c) {
+      ok = mbar_wait(&s_full[c & 1], (c >> 1) & 1, p.err) && ok;
       tc_fence_after();
       float sv[kChunkKeys];
-      tmem_ld32(tS + lane_base, sv);
-      tmem_ld32(tS + lane_base + 32, sv + 32);
+      tmem_ld32(tmem + (c & 1) * 64 + lane_base, sv);
+      tmem_ld32(tmem + (c & 1) * 64 + lane_base + 32, sv + 32);
       const int x0 = (pb + c * cp) * ps;
       float cmax = -INFINITY;
 #pragma unroll
       for (int j = 0; j < kChunkKeys; ++j) {
-        const int x = x0 + j;
-        sv[j] = (x < lim) ? sv[j] * sl2 : -INFINITY;
+        sv[j] = (x0 + j < lim) ? sv[j] * sl2 : -INFINITY;
         cmax = fmaxf(cmax, sv[j]);
       }
-      const float m_new = fmaxf(m_run, cmax);
-      const float alpha = (m_new == -INFINITY) ? 1.f : exp2f(m_run - m_new);
+      const bool grow_max = cmax > m_run + kRescaleThreshold || (m_run == -INFINITY && cmax > -INFINITY);
+      float alpha = 1.f;
+      if (grow_max) {
+        alpha = m_run == -INFINITY ? 0.f : exp2f(m_run - cmax);
+        l_run *= alpha;
+        m_run = cmax;
+      }
+      if (c > 0 && __any_sync(0xffffffffu, grow_max)) {
+        // O must hold P(c-1) V(c-1) before it is rescaled.
+        ok = mbar_wait(&pv_done[(c - 1) & 1], ((c - 1) >> 1) & 1, p.err) && ok;
+        tc_fence_after();
+#pragma unroll
+        for (int q4 = 0; q4 < 4; ++q4) {
+          float ov[32];
+          tmem_ld32(tO + q4 * 32, ov);
+#pragma unroll
+          for (int i = 0; i < 32; ++i) ov[i] *= alpha;
+          tmem_st32(tO + q4 * 32, ov);
+        }
+      }
+      // P buffer c%2 is free once PV(c-2) completed.
+      if (c >= 2) ok = mbar_wait(&pv_done[c & 1], ((c - 2) >> 1) & 1, p.err) && ok;
+      uint8_t* pbuf = p_s + (c & 1) * kPBytes;
       float psum = 0.f;
 #pragma unroll
       for (int cc = 0; cc < 8; ++cc) {
         T pk[8];
 #pragma unroll
         for (int e = 0; e < 8; ++e) {
-          const float pv = (m_new == -INFINITY) ? 0.f : exp2f(sv[cc * 8 + e] - m_new);
+          const float pv = (m_run == -INFINITY) ? 0.f : exp2f(sv[cc * 8 + e] - m_run);
           psum += pv;
           pk[e] = from_f32<T>(pv);
         }
-        *reinterpret_cast<uint4*>(p_s + sw128_offset(rho, cc)) = *reinterpret_cast<uint4*>(pk);
+        *reinterpret_cast<uint4*>(pbuf + sw128_offset(rho, cc)) = *reinterpret_cast<uint4*>(pk);
       }
-      l_run = l_run * alpha + psum;
-      m_run = m_new;
+      l_run += psum;
       fence_proxy_async_smem();
       tc_fence_before();
-      asm volatile("bar.sync 1, 128;" ::: "memory");
-      if (tid == 0) {
-        tc_fence_after();
-        if (ok) {
-          const uint32_t pa = smem_u32(p_s);
-          const uint32_t vb = st + 2 * kKVHalfBytes;
-#pragma unroll
-          for (int kk = 0; kk < 4; ++kk) {
-            umma_f16_ss(tO, umma_desc_sw128(pa + kk * 32, 16, 1024),
-                        umma_desc_sw128(vb + kk * 2048, kKVHalfBytes, 1024), idesc_o, kk > 0);
-          }
-        }
-        umma_commit(o_bar);
-        umma_commit(&empty[s]);
-      }
-      __syncwarp();
-      ok = mbar_wait(o_bar, c & 1, p.err) && ok;
-      tc_fence_after();
-#pragma unroll
-      for (int q4 = 0; q4 < 4; ++q4) {
-        float ov[32];
-        tmem_ld32(tO + lane_base + q4 * 32, ov);
-#pragma unroll
-        for (int i = 0; i < 32; ++i) acc[q4 * 32 + i] = acc[q4 * 32 + i] * alpha + ov[i];
-      }
-      tc_fence_before();
-      asm volatile("bar.sync 1, 128;" ::: "memory");
+      mbar_arrive(&p_full[c & 1]);
     }
-    if (!ok) s_int[1] = 0;
-    // ---- write results
+    ok = mbar_wait(fin, 0, p.err) && ok;
+    tc_fence_after();
+    float acc[kHd];
+    if (nchunks > 0) {
+#pragma unroll
+      for (int q4 = 0; q4 < 4; ++q4) tmem_ld32(tO + q4 * 32, acc + q4 * 32);
+    } else {
+#pragma unroll
+      for (int i = 0; i < kHd; ++i) acc[i] = 0.f;
+    }
     if (m < p.M) {
       const int64_t rowi = static_cast<int64_t>(m) * p.Hq + hq;
       if (p.direct_out) {
@@ -259,6 +325,9 @@ __global__ void __launch_bounds__(160, 1)
 }
 
 // One warp per (row, q head): merge split partials, then the row's tail keys.
+// Lanes fetch the split records and the tail slot ids in parallel and the
+// partial-O and K/V loads are issued in batches, so the warp is not a chain
+// of dependent global loads.
 template <typename T>
 __global__ void __launch_bounds__(128) attn_combine_tail(AttnParams p) {
   pdl_wait();
@@ -276,57 +345,110 @@ __global__ void __launch_bounds__(128) attn_combine_tail(AttnParams p) {
   const int mask_base = p.dparams[2];
   const int ps = p.page_size;
   const float sl2 = p.scale * kLog2e;
+  const int64_t stride_split = static_cast<int64_t>(p.M) * p.Hq;
 
+  // ---- split partials: lane s holds split s and s + 32 (splits <= 64)
   float mx = -INFINITY, l = 0.f;
   float o[4] = {0.f, 0.f, 0.f, 0.f};
-  for (int s = 0; s < p.splits; ++s) {
-    const float2 ml = p.part_ml[static_cast<int64_t>(s) * p.M * p.Hq + pair];
-    if (!(ml.y > 0.f)) continue;
-    const float4 ov = *reinterpret_cast<const float4*>(p.part_o + (static_cast<int64_t>(s) * p.M * p.Hq + pair) * kHd + lane * 4);
-    const float nm = fmaxf(mx, ml.x);
-    const float a = exp2f(mx - nm), b = exp2f(ml.x - nm);
-    o[0] = o[0] * a + ov.x * b;
-    o[1] = o[1] * a + ov.y * b;
-    o[2] = o[2] * a + ov.z * b;
-    o[3] = o[3] * a + ov.w * b;
-    l = l * a + ml.y * b;
-    mx = nm;
+  if (p.splits > 0) {
+    float2 ml0 = make_float2(-INFINITY, 0.f), ml1 = make_float2(-INFINITY, 0.f);
+    if (lane < p.splits) ml0 = p.part_ml[lane * stride_split + pair];
+    if (lane + 32 < p.splits) ml1 = p.part_ml[(lane + 32) * stride_split + pair];
+    if (!(ml0.y > 0.f)) ml0.x = -INFINITY;
+    if (!(ml1.y > 0.f)) ml1.x = -INFINITY;
+    mx = warp_max(fmaxf(ml0.x, ml1.x));
+    if (mx > -INFINITY) {
+      const float w0 = ml0.x > -INFINITY ? exp2f(ml0.x - mx) : 0.f;
+      const float w1 = ml1.x > -INFINITY ? exp2f(ml1.x - mx) : 0.f;
+      l = warp_sum(w0 * ml0.y + w1 * ml1.y);
+      const float* po = p.part_o + pair * kHd + lane * 4;
+      for (int s0 = 0; s0 < p.splits; s0 += 8) {
+        float4 ov[8];
+        float wv[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const int sidx = s0 + j;
+          const float wsrc = sidx < 32 ? __shfl_sync(0xffffffffu, w0, sidx & 31)
+                                       : __shfl_sync(0xffffffffu, w1, sidx & 31);
+          wv[j] = sidx < p.splits ? wsrc : 0.f;
+          ov[j] = (sidx < p.splits && wv[j] > 0.f)
+                      ? *reinterpret_cast<const float4*>(po + static_cast<int64_t>(sidx) * stride_split * kHd)
+                      : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          o[0] += wv[j] * ov[j].x;
+          o[1] += wv[j] * ov[j].y;
+          o[2] += wv[j] * ov[j].z;
+          o[3] += wv[j] * ov[j].w;
+        }
+      }
+    }
   }
+
+  // ---- tail keys [start, row_len): lane t resolves position start + t (+32 ...)
   const T* qp = static_cast<const T*>(p.q) + pair * kHd + lane * 4;
   const float q0 = to_f32(qp[0]), q1 = to_f32(qp[1]), q2 = to_f32(qp[2]), q3 = to_f32(qp[3]);
   const int full = p.row_full[m];
   const int rlen = p.row_len[m];
   const int start = min(full, shared_len);
   const int64_t kv_head = static_cast<int64_t>(ps) * kHd;
-  for (int x = start; x < rlen; ++x) {
-    bool vis = x < full;
-    if (!vis) {
-      const int b = x - mask_base;
-      if (b >= 0 && b < 64 * p.mask_words) {
-        const uint64_t w = static_cast<uint64_t>(p.row_mask[static_cast<int64_t>(m) * p.mask_words + (b >> 6)]);
-        vis = (w >> (b & 63)) & 1ull;
+  for (int t0 = start; t0 < rlen; t0 += 32) {
+    const int x = t0 + lane;
+    int64_t base = -1;
+    if (x < rlen) {
+      bool vis = x < full;
+      if (!vis) {
+        const int b = x - mask_base;
+        if (b >= 0 && b < 64 * p.mask_words) {
+          const uint64_t w = static_cast<uint64_t>(p.row_mask[static_cast<int64_t>(m) * p.mask_words + (b >> 6)]);
+          vis = (w >> (b & 63)) & 1ull;
+        }
+      }
+      if (vis) {
+        const int j = x / ps;
+        const bool in_shared = j < n_shared_pages || x < shared_len;
+        const int page = in_shared ? p.prefix_pages[j]
+                                   : p.tail_pages[static_cast<int64_t>(m) * p.tail_stride + (j - n_shared_pages)];
+        if (page < 0 || page >= p.num_pages) {
+          set_error(p.err, kErrBadIndex);
+        } else {
+          base = ((static_cast<int64_t>(p.layer) * p.num_pages + page) * 2 * p.Hkv + h) * kv_head + (x % ps) * kHd;
+        }
       }
     }
-    if (!vis) continue;
-    const int j = x / ps;
-    int page = j < n_shared_pages ? p.prefix_pages[j] : p.tail_pages[static_cast<int64_t>(m) * p.tail_stride + (j - n_shared_pages)];
-    if (page < 0 || page >= p.num_pages) {
-      set_error(p.err, kErrBadIndex);
-      continue;
+    const int cnt = min(32, rlen - t0);
+    for (int j0 = 0; j0 < cnt; j0 += 4) {
+      int64_t bj[4];
+      float4 kf[4];
+      float2 kh[4], vh[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        bj[u] = (j0 + u < cnt) ? __shfl_sync(0xffffffffu, base, j0 + u) : -1;
+        if (bj[u] >= 0) {
+          const T* kp = static_cast<const T*>(p.kv) + bj[u] + lane * 4;
+          kh[u] = *reinterpret_cast<const float2*>(kp);
+          vh[u] = *reinterpret_cast<const float2*>(kp + static_cast<int64_t>(p.Hkv) * kv_head);
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        if (bj[u] < 0) continue;  // warp-uniform
+        const T* ke = reinterpret_cast<const T*>(&kh[u]);
+        const T* ve = reinterpret_cast<const T*>(&vh[u]);
+        float sc = q0 * to_f32(ke[0]) + q1 * to_f32(ke[1]) + q2 * to_f32(ke[2]) + q3 * to_f32(ke[3]);
+        sc = warp_sum(sc) * sl2;
+        const float nm = fmaxf(mx, sc);
+        const float a = exp2f(mx - nm), w = exp2f(sc - nm);
+        o[0] = o[0] * a + w * to_f32(ve[0]);
+        o[1] = o[1] * a + w * to_f32(ve[1]);
+        o[2] = o[2] * a + w * to_f32(ve[2]);
+        o[3] = o[3] * a + w * to_f32(ve[3]);
+        l = l * a + w;
+        mx = nm;
+        (void)kf;
+      }
     }
-    const int64_t base = ((static_cast<int64_t>(p.layer) * p.num_pages + page) * 2 * p.Hkv + h) * kv_head + (x % ps) * kHd + lane * 4;
-    const T* kp = static_cast<const T*>(p.kv) + base;
-    const T* vp = kp + static_cast<int64_t>(p.Hkv) * kv_head;
-    float sc = q0 * to_f32(kp[0]) + q1 * to_f32(kp[1]) + q2 * to_f32(kp[2]) + q3 * to_f32(kp[3]);
-    sc = warp_sum(sc) * sl2;
-    const float nm = fmaxf(mx, sc);
-    const float a = exp2f(mx - nm), w = exp2f(sc - nm);
-    o[0] = o[0] * a + w * to_f32(vp[0]);
-    o[1] = o[1] * a + w * to_f32(vp[1]);
-    o[2] = o[2] * a + w * to_f32(vp[2]);
-    o[3] = o[3] * a + w * to_f32(vp[3]);
-    l = l * a + w;
-    mx = nm;
   }
   const float inv = l > 0.f ? 1.f / l : 0.f;
   T* op = static_cast<T*>(p.out) + pair * kHd + lane * 4;
@@ -346,7 +468,7 @@ static void launch_typed(const CUtensorMap& kvmap, const AttnParams& p, bool run
       configured = true;
     }
     dim3 grid(p.Hkv, p.splits, row_tiles);
-    launch_k(attn_shared_tc<T>, grid, dim3(160), kSmemBytes, st, kvmap, p);
+    launch_k(attn_shared_tc<T>, grid, dim3(kThreadsTC), kSmemBytes, st, kvmap, p);
   }
   if (run_combine) {
     const int64_t pairs = static_cast<int64_t>(p.M) * p.Hq;

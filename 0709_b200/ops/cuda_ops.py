@@ -139,21 +139,22 @@ class CudaOps:
         self._ensure_parts_exact(splits * m * hq * 128, 2 * splits * m * hq)
 
     def attention(self, q: torch.Tensor, kv_layer: torch.Tensor, desc: AttnDesc, scale: float | None = None,
-                  *, splits: int | None = None) -> torch.Tensor:
+                  *, splits: int | None = None, stages: tuple[bool, bool] = (True, True)) -> torch.Tensor:
         kv, layer = self._layer_index(kv_layer)
         m, hq, hd = q.shape
         scale = 1.0 / math.sqrt(hd) if scale is None else scale
         out = torch.empty((m, hq * hd), dtype=q.dtype, device=q.device)
-        run_tc = desc.shared_len > 0
+        run_tc = desc.shared_len > 0 and stages[0]
         sp = splits or getattr(desc, "_splits", None) or self.attention_splits(m, hq, kv.shape[3], desc.shared_len,
                                                                                 kv.shape[4])
         if run_tc:
             self._ensure_parts(sp, m, hq)
         self.ext.attention(
             q.contiguous(), kv, layer, out, self._dparams(desc), desc.prefix_pages, desc.row_full, desc.row_len,
-            desc.row_mask, desc.tail_pages, self.part_o, self.part_ml, self.err, sp, run_tc, True, False, float(scale),
+            desc.row_mask, desc.tail_pages, self.part_o, self.part_ml, self.err, sp, run_tc, stages[1], False,
+            float(scale),
         )
-        counters.launches(2 if run_tc else 1)
+        counters.launches(int(run_tc) + int(stages[1]))
         return out
 
     def attention_causal(self, q, kv_layer, desc: AttnDesc, causal_start: int, scale: float | None = None):

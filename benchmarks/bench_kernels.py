@@ -122,6 +122,10 @@ def main() -> int:
                 kv_bytes = 2 * (prefix + nodes) * hkv * 128 * 2
                 report(f"attn prefix={prefix} rows={nodes}", us, kv_bytes, 4.0 * nodes * hq * 128 * prefix,
                        splits=ops.attention_splits(nodes, hq, hkv, prefix, ps))
+                us = timeit(lambda: ops.attention(q, kv[0], desc, stages=(True, False)), args.iters)
+                report(f"  tensor-core part only", us, kv_bytes)
+                us = timeit(lambda: ops.attention(q, kv[0], desc, stages=(False, True)), args.iters)
+                report(f"  combine+tail part only", us, kv_bytes)
                 del kv
     if args.only in ("all", "misc"):
         logits = torch.randn(12, 128256, device="cuda")
