@@ -144,7 +144,7 @@ std::pair<int, int> pick_splits(int64_t M, int64_t N, int64_t K, int bn, int num
   const int64_t kb = (K + 63) / 64;
   const int64_t slots = static_cast<int64_t>(num_sms) * ctas_per_sm(bn);
   int64_t splits = 1;
-  if (tiles * 4 < slots * 3) splits = std::max<int64_t>(1, std::min<int64_t>(kb / 2, slots / tiles));
+  if (tiles * 4 < slots * 3) splits = std::max<int64_t>(1, std::min<int64_t>({kb / 2, slots / tiles, 8}));
   int64_t kbps = (kb + splits - 1) / splits;
   splits = (kb + kbps - 1) / kbps;
   return {static_cast<int>(splits), static_cast<int>(kbps)};
@@ -180,13 +180,9 @@ std::vector<int64_t> gemm(torch::Tensor w, torch::Tensor x, torch::Tensor out, i
   auto sp = pick_splits(M, N, K, bn, num_sms());
   if (force_splits > 0) {
     const int64_t kb = (K + 63) / 64;
-    int64_t kbps = (kb + force_splits - 1) / force_splits;
+    const int64_t fs = std::min<int64_t>(force_splits, 8);
+    int64_t kbps = (kb + fs - 1) / fs;
     sp = {static_cast<int>((kb + kbps - 1) / kbps), static_cast<int>(kbps)};
-  }
-  const int64_t tiles = ((M + 127) / 128) * ((N + bn - 1) / bn);
-  if (sp.first > 1) {
-    TORCH_CHECK(ws.numel() >= sp.first * N * M, "split-K workspace too small: need ", sp.first * N * M);
-    TORCH_CHECK(counters.numel() >= tiles, "split-K counter buffer too small: need ", tiles);
   }
   if (epi == atlas::kEpiResidual || epi == atlas::kEpiF32) {
     TORCH_CHECK(out.scalar_type() == torch::kFloat32, "fp32 output expected for this epilogue");
@@ -209,8 +205,6 @@ std::vector<int64_t> gemm(torch::Tensor w, torch::Tensor x, torch::Tensor out, i
   p.kb_per_split = sp.second;
   p.bf16 = w.scalar_type() == torch::kBFloat16;
   p.out = out.data_ptr();
-  p.ws = sp.first > 1 ? ws.data_ptr<float>() : nullptr;
-  p.counters = sp.first > 1 ? counters.data_ptr<int>() : nullptr;
   p.err = err.data_ptr<int>();
   atlas::launch_gemm_tn(a, b, p, bn, static_cast<int>(epi), at::cuda::getCurrentCUDAStream());
   return {bn, sp.first, sp.second};

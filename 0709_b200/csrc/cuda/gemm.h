@@ -19,12 +19,10 @@ struct GemmParams {
   int N;             // tokens (rows of B)
   int K;             // reduction length
   int ldo;           // leading dimension of `out` (elements)
-  int splits;        // split-K factor (1 = no workspace)
+  int splits;        // split-K factor = cluster size along z (1..8)
   int kb_per_split;  // 64-wide K blocks per split
   int bf16;          // operands are bf16 (else fp16)
   void* out;
-  float* ws;         // split-K partials [splits, N, M]
-  int* counters;     // per-tile tickets, zero between launches
   int* err;          // device error flag
 };
 

@@ -13,9 +13,11 @@
 //              a TMEM accumulator, tcgen05.commit releases the stage;
 //   all        epilogue: tcgen05.ld the 128 x BN fp32 accumulator (lane =
 //              output feature) and apply the fused epilogue.
-// Split-K partials go to a fp32 workspace; the last CTA of a tile (atomic
-// ticket) sums the partials in split order, so results are deterministic
-// and independent of the batch composition.
+// Split-K: the S split CTAs of an output tile form one thread-block cluster.
+// Each parks its fp32 partial tile in its own shared memory; after a cluster
+// barrier CTA r reduces columns r, r+S, ... by reading all S partials through
+// distributed shared memory in split order (deterministic, independent of the
+// batch composition) and applies the epilogue.  No global workspace.
 
 #include <cuda.h>
 
@@ -37,46 +39,25 @@ struct GemmSmem {
 
 __device__ __forceinline__ float silu_f(float x) { return x / (1.0f + __expf(-x)); }
 
-template <int BN, int EPI, typename T>
-__device__ __forceinline__ void epilogue_chunk(const GemmParams& p, int m0, int n0, int c0, const float* v,
-                                               float* xchg) {
-  const int tid = threadIdx.x;
-  if constexpr (EPI == kEpiSilu) {
-    // Rows 0..63 of the tile are gate features, 64..127 the matching up features.
-    float* ex = xchg;  // [32 cols][64]
-    if (tid >= 64) {
-#pragma unroll
-      for (int j = 0; j < 32; ++j) ex[j * 64 + (tid - 64)] = v[j];
-    }
-    __syncthreads();
-    if (tid < 64) {
-      const int f = (m0 >> 1) + tid;
-      T* out = reinterpret_cast<T*>(p.out);
-#pragma unroll 4
-      for (int j = 0; j < 32; ++j) {
-        const int n = n0 + c0 + j;
-        if (n < p.N && f < (p.M >> 1)) out[static_cast<int64_t>(n) * p.ldo + f] = from_f32<T>(silu_f(v[j]) * ex[j * 64 + tid]);
-      }
-    }
-    __syncthreads();
-  } else {
-    const int m = m0 + tid;
-    if (m >= p.M) return;
-#pragma unroll 4
-    for (int j = 0; j < 32; ++j) {
-      const int n = n0 + c0 + j;
-      if (n >= p.N) break;
-      const int64_t idx = static_cast<int64_t>(n) * p.ldo + m;
-      if constexpr (EPI == kEpiStore) {
-        reinterpret_cast<T*>(p.out)[idx] = from_f32<T>(v[j]);
-      } else if constexpr (EPI == kEpiResidual) {
-        float* r = reinterpret_cast<float*>(p.out);
-        r[idx] = r[idx] + v[j];
-      } else {  // kEpiF32
-        reinterpret_cast<float*>(p.out)[idx] = v[j];
-      }
-    }
+// Apply the epilogue to one output element (feature m, token n).
+template <int EPI, typename T>
+__device__ __forceinline__ void store_elem(const GemmParams& p, int m, int n, float v) {
+  const int64_t idx = static_cast<int64_t>(n) * p.ldo + m;
+  if constexpr (EPI == kEpiStore) {
+    reinterpret_cast<T*>(p.out)[idx] = from_f32<T>(v);
+  } else if constexpr (EPI == kEpiResidual) {
+    float* r = reinterpret_cast<float*>(p.out);
+    r[idx] = r[idx] + v;
+  } else {  // kEpiF32
+    reinterpret_cast<float*>(p.out)[idx] = v;
   }
+}
+
+// Gate rows 0..63 of a tile pair with up rows 64..127: out[n, f] = silu(g) * u.
+template <typename T>
+__device__ __forceinline__ void store_silu(const GemmParams& p, int m0, int row, int n, float g, float u) {
+  const int f = (m0 >> 1) + row;
+  if (f < (p.M >> 1)) reinterpret_cast<T*>(p.out)[static_cast<int64_t>(n) * p.ldo + f] = from_f32<T>(silu_f(g) * u);
 }
 
 template <int BN, int EPI, typename T>
@@ -167,11 +148,13 @@ __global__ void __launch_bounds__(128, 1)
   __syncthreads();
   ok = *flag != 0;
 
-  float* xchg = reinterpret_cast<float*>(smem);  // stage buffers are free once `done` fired
   const uint32_t lane_base = static_cast<uint32_t>(warp * 32) << 16;
+  const int ncols = min(BN, p.N - n0);
   if (p.splits == 1) {
-    for (int c0 = 0; c0 < BN; c0 += 32) {
-      if (n0 + c0 >= p.N) break;
+    // No split: TMEM -> registers -> global, 32 token columns at a time
+    // (gate/up pairs meet through shared memory).
+    float* ex = reinterpret_cast<float*>(smem);  // [32 cols][64]
+    for (int c0 = 0; c0 < ncols; c0 += 32) {
       float v[32];
       if (ok && nk > 0) {
         tmem_ld32(tmem + lane_base + c0, v);
@@ -179,55 +162,71 @@ __global__ void __launch_bounds__(128, 1)
 #pragma unroll
         for (int j = 0; j < 32; ++j) v[j] = 0.f;
       }
-      epilogue_chunk<BN, EPI, T>(p, m0, n0, c0, v, xchg);
+      if constexpr (EPI == kEpiSilu) {
+        if (tid >= 64) {
+#pragma unroll
+          for (int j = 0; j < 32; ++j) ex[j * 64 + (tid - 64)] = v[j];
+        }
+        __syncthreads();
+        if (tid < 64) {
+#pragma unroll
+          for (int j = 0; j < 32; ++j)
+            if (c0 + j < ncols) store_silu<T>(p, m0, tid, n0 + c0 + j, v[j], ex[j * 64 + tid]);
+        }
+        __syncthreads();
+      } else {
+        if (m0 + tid < p.M) {
+#pragma unroll
+          for (int j = 0; j < 32; ++j)
+            if (c0 + j < ncols) store_elem<EPI, T>(p, m0 + tid, n0 + c0 + j, v[j]);
+        }
+      }
     }
-  } else {
-    // Write this split's partial tile: ws[split][n][m] (fp32).
-    const int m = m0 + tid;
-    for (int c0 = 0; c0 < BN; c0 += 32) {
-      if (n0 + c0 >= p.N) break;
-      float v[32];
-      if (ok && nk > 0) {
-        tmem_ld32(tmem + lane_base + c0, v);
-      } else {
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 0) tmem_dealloc(tmem, S::kTmemCols);
+    return;
+  }
+  // Split-K: stage buffers are free once `done` fired; park the fp32 tile there
+  // as part[n * 128 + m] (column n = token, row m = feature).
+  float* part = reinterpret_cast<float*>(smem);
+  for (int c0 = 0; c0 < BN; c0 += 32) {
+    if (c0 >= ncols) break;
+    float v[32];
+    if (ok && nk > 0) {
+      tmem_ld32(tmem + lane_base + c0, v);
+    } else {
 #pragma unroll
-        for (int j = 0; j < 32; ++j) v[j] = 0.f;
+      for (int j = 0; j < 32; ++j) v[j] = 0.f;
+    }
+#pragma unroll
+    for (int j = 0; j < 32; ++j)
+      if (c0 + j < BN) part[(c0 + j) * 128 + tid] = v[j];
+  }
+  const int NS = p.splits;
+  cluster_sync();
+  const uint32_t rank = cluster_ctarank();
+  for (int c = static_cast<int>(rank); c < ncols; c += NS) {
+    const int n = n0 + c;
+    if constexpr (EPI == kEpiSilu) {
+      if (tid < 64) {
+        float g = 0.f, u = 0.f;
+        for (int s2 = 0; s2 < NS; ++s2) {
+          g += ld_dsmem_f32(part + c * 128 + tid, s2);
+          u += ld_dsmem_f32(part + c * 128 + 64 + tid, s2);
+        }
+        store_silu<T>(p, m0, tid, n, g, u);
       }
+    } else {
+      const int m = m0 + tid;
       if (m < p.M) {
-        for (int j = 0; j < 32; ++j) {
-          const int n = n0 + c0 + j;
-          if (n >= p.N) break;
-          p.ws[(static_cast<int64_t>(split) * p.N + n) * p.M + m] = v[j];
-        }
+        float acc = 0.f;
+        for (int s2 = 0; s2 < NS; ++s2) acc += ld_dsmem_f32(part + c * 128 + tid, s2);
+        store_elem<EPI, T>(p, m, n, acc);
       }
-    }
-    __threadfence();
-    __syncthreads();
-    const int tile = blockIdx.y * gridDim.x + blockIdx.x;
-    if (tid == 0) *flag = (atomicAdd(&p.counters[tile], 1) == p.splits - 1) ? 1 : 0;
-    __syncthreads();
-    if (*flag) {
-      __threadfence();
-      for (int c0 = 0; c0 < BN; c0 += 32) {
-        if (n0 + c0 >= p.N) break;
-        float v[32];
-#pragma unroll
-        for (int j = 0; j < 32; ++j) v[j] = 0.f;
-        if (m < p.M) {
-          for (int s = 0; s < p.splits; ++s) {
-            const float* src = p.ws + (static_cast<int64_t>(s) * p.N) * p.M + m;
-#pragma unroll
-            for (int j = 0; j < 32; ++j) {
-              const int n = n0 + c0 + j;
-              if (n < p.N) v[j] += __ldcg(src + static_cast<int64_t>(n) * p.M);
-            }
-          }
-        }
-        epilogue_chunk<BN, EPI, T>(p, m0, n0, c0, v, xchg);
-      }
-      if (tid == 0) p.counters[tile] = 0;  // ready for the next launch
     }
   }
+  cluster_sync();  // keep every partial alive until all readers are done
   tc_fence_before();
   __syncthreads();
   if (warp == 0) tmem_dealloc(tmem, S::kTmemCols);
@@ -243,7 +242,21 @@ static void launch_bn(const CUtensorMap& a, const CUtensorMap& b, const GemmPara
     cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, S::kBytes);
     configured = true;
   }
-  launch_k(kern, grid, dim3(128), S::kBytes, st, a, b, p);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = dim3(128);
+  cfg.dynamicSmemBytes = S::kBytes;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = pdl_enabled() ? 1 : 0;
+  attr[1].id = cudaLaunchAttributeClusterDimension;
+  attr[1].val.clusterDim.x = 1;
+  attr[1].val.clusterDim.y = 1;
+  attr[1].val.clusterDim.z = static_cast<unsigned>(p.splits);
+  cfg.attrs = attr;
+  cfg.numAttrs = p.splits > 1 ? 2 : 1;  // a cluster only when the K dimension is split
+  cudaLaunchKernelEx(&cfg, kern, a, b, p);
 }
 
 template <int EPI, typename T>

@@ -1,8 +1,9 @@
 """CUDA op table: the engine's ops backed by the sm_100a kernels of ``atlas_cuda``.
 
-Each engine owns one ``CudaOps`` with persistent device buffers: the split-K
-GEMM workspace and tile tickets, the split-KV attention partials, and an
-error flag the kernels set instead of trapping (bad index, bounded wait that
+Each engine owns one ``CudaOps`` with persistent device buffers: the split-KV
+attention partials and an error flag (the GEMM reduces its K splits inside a
+thread-block cluster and needs no workspace; ``ws``/``counters`` are unused
+placeholders kept for the binding signature).  The error flag is set by kernels instead of trapping (bad index, bounded wait that
 timed out).  ``check()`` reads the flag.  If the extension cannot be loaded on
 a GPU machine, construction raises -- there is no silent fallback.
 """
@@ -35,8 +36,8 @@ class CudaOps:
         self.device = engine.device if engine is not None else (device or torch.device("cuda"))
         dev = self.device
         self.err = torch.zeros(1, dtype=torch.int32, device=dev)
-        self.ws = torch.empty(16 * 1024 * 1024, dtype=torch.float32, device=dev)
-        self.counters = torch.zeros(65536, dtype=torch.int32, device=dev)
+        self.ws = torch.empty(0, dtype=torch.float32, device=dev)
+        self.counters = torch.empty(0, dtype=torch.int32, device=dev)
         self.part_o = torch.empty(0, dtype=torch.float32, device=dev)
         self.part_ml = torch.empty(0, dtype=torch.float32, device=dev)
         self.num_sms = torch.cuda.get_device_properties(dev).multi_processor_count

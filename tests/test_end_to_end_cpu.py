@@ -1,0 +1,122 @@
+"""End-to-end CPU plumbing: tiny random-init Llama drafter and target.
+
+Checks against the fp32 oracle:
+- fallback on every round (threshold above any log-prob) == target greedy AR;
+- k=1 with the first-route policy == drafter greedy AR (the reference's own
+  equivalence contract, tools/check_async_greedy_equivalence.py:220-227);
+- the masked tree forward's logits == the oracle with an explicit ancestor mask;
+- the serial generator and the async generator agree token for token.
+"""
+
+from __future__ import annotations
+
+import torch
+import pytest
+
+from conftest import mod
+
+K, D, PAGE = 2, 3, 4
+
+
+@pytest.fixture(scope="module")
+def models():
+    llama = mod("models.llama")
+    dw = llama.random_weights(llama.get_config("tiny-drafter"), seed=1, dtype=torch.float32)
+    tw = llama.random_weights(llama.get_config("tiny-target"), seed=2, dtype=torch.float32)
+    return dw, tw
+
+
+def prompts(n=8, length=64, seed=0):
+    g = torch.Generator().manual_seed(seed)
+    return [torch.randint(0, 1024, (length,), generator=g).tolist() for _ in range(n)]
+
+
+def greedy(w, prompt, n):
+    llama = mod("models.llama")
+    toks = list(prompt)
+    for _ in range(n):
+        toks.append(int(llama.reference_forward(w, toks)[-1].argmax()))
+    return toks[len(prompt):]
+
+
+def make_generator(dw, tw, *, k=K, d=D, serial=False, **target_kw):
+    engine = mod("runtime.engine")
+    drafter = mod("runtime.drafter")
+    target = mod("runtime.target")
+    edge = mod("serving.edge")
+    rpc = mod("serving.rpc")
+    de = engine.LlamaEngine(dw, num_pages=512, page_size=PAGE, max_positions=512)
+    te = engine.LlamaEngine(tw, num_pages=512, page_size=PAGE, max_positions=512)
+    tv = target.TargetVerifier(te, k=k, d=d, **target_kw)
+    cls = mod("serving.serial").SerialAtlasGenerator if serial else edge.PagedDistributedAtlasGenerator
+    cfg = edge.DistributedAtlasConfig(k=k, d=d, max_new_tokens=16, validate_state_alignment=True,
+                                      fixed_forest_depth=None if serial else 2)
+    return cls(config=cfg, drafter=drafter.DrafterRuntime(de), target_client=rpc.InProcessTargetClient(tv))
+
+
+def test_fallback_every_round_equals_target_greedy(models):
+    dw, tw = models
+    p = prompts(2)[1]
+    res = make_generator(dw, tw, fallback_threshold=1e9).generate(p)
+    assert all(r.decision == "fallback_ar" for r in res.rounds)
+    assert {r.fallback_reason for r in res.rounds} == {"path_score_below_threshold"}
+    assert res.generated_token_ids == greedy(tw, p, 16)
+
+
+def test_k1_first_route_equals_drafter_greedy(models):
+    dw, tw = models
+    p = prompts(1, seed=3)[0]
+    res = make_generator(dw, tw, k=1, route_selection_policy="first_route").generate(p)
+    assert res.generated_token_ids == greedy(dw, p, 16)
+
+
+def test_tree_forward_matches_oracle(models):
+    _, tw = models
+    llama = mod("models.llama")
+    engine = mod("runtime.engine")
+    target = mod("runtime.target")
+    te = engine.LlamaEngine(tw, num_pages=512, page_size=PAGE, max_positions=512)
+    tv = target.TargetVerifier(te, k=3, d=3)
+    prompt = prompts(1, length=30)[0]
+    tv.prefill(prompt)
+    out = tv.run_tree([(5, 6, 7), (5, 6, 8), (9, 6, 7)])
+    toks, parents, depth = [5, 6, 7, 8, 9, 6, 7], [-1, 0, 1, 1, -1, 4, 5], [0, 1, 2, 2, 0, 1, 2]
+    p = len(prompt)
+    vis = torch.zeros(p + 7, p + 7, dtype=torch.bool)
+    vis[:p, :p] = torch.tril(torch.ones(p, p, dtype=torch.bool))
+    for i in range(7):
+        vis[p + i, :p] = True
+        a = i
+        while a >= 0:
+            vis[p + i, p + a] = True
+            a = parents[a]
+    ref = llama.reference_forward(tw, prompt + toks, positions=list(range(p)) + [p + x for x in depth], visible=vis)
+    assert torch.allclose(out["logits"], ref[p:], atol=1e-4, rtol=1e-4)
+    assert out["node_count"] == 7
+
+
+def test_config1_async_generation_schema(models):
+    """Config 1: 8 prompts x 64 tokens, k=2 d=3, page 4, greedy; result JSON per the reference schema."""
+    dw, tw = models
+    gen = make_generator(dw, tw)
+    for p in prompts(8):
+        res = gen.generate(p)
+        assert len(res.generated_token_ids) == 16
+        d = res.to_dict()
+        assert set(d) == {"prompt_token_ids", "generated_token_ids", "token_ids", "text", "rounds", "metadata"}
+        r0 = d["rounds"][0]
+        for key in ("decision", "fallback_reason", "handoff_mode", "target_scores", "target_unique_tree_nodes",
+                    "forest_depth", "committed_tokens", "released_kv_pages"):
+            assert key in r0
+        assert r0["handoff_mode"] in {"completed_forest_reused", "partial_forest_pruned_then_build_tree", "stopped"}
+        assert d["metadata"]["edge_blackbox_timeline"]["rounds"] == len(d["rounds"])
+
+
+def test_serial_equals_async_when_target_selects(models):
+    """With no fallback and greedy drafting both schedules commit the same tokens."""
+    dw, tw = models
+    p = prompts(1, seed=5)[0]
+    a = make_generator(dw, tw).generate(p)
+    s = make_generator(dw, tw, serial=True).generate(p)
+    assert a.generated_token_ids == s.generated_token_ids
+    assert all(r.handoff_mode.startswith("serial_") for r in s.rounds)
