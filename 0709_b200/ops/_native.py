@@ -85,6 +85,7 @@ CUDA_SOURCES = [
     "elementwise.cu",
     "kvcache.cu",
     "sampling.cu",
+    "topk_noalloc.cu",
 ]
 
 
