@@ -16,6 +16,7 @@
 #include "attention.h"
 #include "gemm.h"
 #include "kernels.h"
+#include "tp.h"
 
 namespace {
 
@@ -166,8 +167,9 @@ void check_cuda(const torch::Tensor& t, const char* name) {
 
 // ---------------------------------------------------------------- GEMM
 // out = epilogue(x @ w^T).  w [M, K] contiguous; x [N, K] with unit inner stride.
-std::vector<int64_t> gemm(torch::Tensor w, torch::Tensor x, torch::Tensor out, int64_t epi, torch::Tensor ws,
-                          torch::Tensor counters, torch::Tensor err, int64_t force_splits) {
+std::vector<int64_t> gemm_impl(const torch::Tensor& w, const torch::Tensor& x, void* out_ptr, int64_t ldo,
+                               int64_t epi, const torch::Tensor& err, int64_t force_splits,
+                               const atlas::PeerOut* peer) {
   check_cuda(w, "w");
   check_cuda(x, "x");
   TORCH_CHECK(w.dim() == 2 && w.is_contiguous(), "w must be contiguous [M, K]");
@@ -184,15 +186,9 @@ std::vector<int64_t> gemm(torch::Tensor w, torch::Tensor x, torch::Tensor out, i
     int64_t kbps = (kb + fs - 1) / fs;
     sp = {static_cast<int>((kb + kbps - 1) / kbps), static_cast<int>(kbps)};
   }
-  if (epi == atlas::kEpiResidual || epi == atlas::kEpiF32) {
-    TORCH_CHECK(out.scalar_type() == torch::kFloat32, "fp32 output expected for this epilogue");
-  } else {
-    TORCH_CHECK(out.scalar_type() == w.scalar_type(), "activation-dtype output expected");
-  }
   if (epi == atlas::kEpiSilu) {
     TORCH_CHECK(M % 128 == 0, "gate/up GEMM needs M % 128 == 0");
   }
-  TORCH_CHECK(out.stride(-1) == 1, "out must have unit inner stride");
   const c10::cuda::CUDAGuard guard(w.device());
   CUtensorMap a = map_2d(w, K, M, K, 128);
   CUtensorMap b = map_2d(x, K, N, x.stride(0), bn);
@@ -200,14 +196,131 @@ std::vector<int64_t> gemm(torch::Tensor w, torch::Tensor x, torch::Tensor out, i
   p.M = static_cast<int>(M);
   p.N = static_cast<int>(N);
   p.K = static_cast<int>(K);
-  p.ldo = static_cast<int>(out.stride(0));
+  p.ldo = static_cast<int>(ldo);
   p.splits = sp.first;
   p.kb_per_split = sp.second;
   p.bf16 = w.scalar_type() == torch::kBFloat16;
-  p.out = out.data_ptr();
+  p.out = out_ptr;
   p.err = err.data_ptr<int>();
+  if (peer != nullptr) p.peer = *peer;
   atlas::launch_gemm_tn(a, b, p, bn, static_cast<int>(epi), at::cuda::getCurrentCUDAStream());
   return {bn, sp.first, sp.second};
+}
+
+std::vector<int64_t> gemm(torch::Tensor w, torch::Tensor x, torch::Tensor out, int64_t epi, torch::Tensor ws,
+                          torch::Tensor counters, torch::Tensor err, int64_t force_splits) {
+  check_cuda(out, "out");
+  TORCH_CHECK(epi != atlas::kEpiPeer, "use gemm_peer for the peer epilogue");
+  if (epi == atlas::kEpiResidual || epi == atlas::kEpiF32) {
+    TORCH_CHECK(out.scalar_type() == torch::kFloat32, "fp32 output expected for this epilogue");
+  } else {
+    TORCH_CHECK(out.scalar_type() == w.scalar_type(), "activation-dtype output expected");
+  }
+  TORCH_CHECK(out.stride(-1) == 1, "out must have unit inner stride");
+  return gemm_impl(w, x, out.data_ptr(), out.stride(0), epi, err, force_splits, nullptr);
+}
+
+// Row-parallel GEMM whose fp32 output tile is stored into every destination
+// (raw device addresses: local or CUDA-IPC-mapped peer buffers, row stride
+// `ldo` floats), followed by a release of the incremented local sequence
+// number into each destination's flag word.
+std::vector<int64_t> gemm_peer(torch::Tensor w, torch::Tensor x, std::vector<int64_t> dst, int64_t ldo,
+                               std::vector<int64_t> flags, int64_t ticket, int64_t seq, torch::Tensor err) {
+  TORCH_CHECK(!dst.empty() && dst.size() <= static_cast<size_t>(atlas::kMaxPeers) && dst.size() == flags.size(),
+              "gemm_peer needs 1..8 destinations, one flag each");
+  atlas::PeerOut po{};
+  po.ndst = static_cast<int>(dst.size());
+  for (size_t i = 0; i < dst.size(); ++i) {
+    TORCH_CHECK(dst[i] != 0 && flags[i] != 0 && (dst[i] & 3) == 0 && (flags[i] & 3) == 0, "bad peer address");
+    po.dst[i] = reinterpret_cast<float*>(dst[i]);
+    po.flag[i] = reinterpret_cast<uint32_t*>(flags[i]);
+  }
+  TORCH_CHECK(ticket != 0 && seq != 0, "gemm_peer needs ticket and sequence words");
+  po.ticket = reinterpret_cast<uint32_t*>(ticket);
+  po.seq = reinterpret_cast<uint32_t*>(seq);
+  return gemm_impl(w, x, nullptr, ldo, atlas::kEpiPeer, err, 0, &po);
+}
+
+// --------------------------------------------------- tensor parallelism
+void tp_reduce_rmsnorm(int64_t recv, int64_t slot_stride, int64_t flags, int64_t seq, int64_t nsrc, torch::Tensor h,
+                       c10::optional<torch::Tensor> gamma, c10::optional<torch::Tensor> x, double eps,
+                       torch::Tensor err) {
+  TORCH_CHECK(h.scalar_type() == torch::kFloat32 && h.is_contiguous() && h.dim() == 2, "h must be contiguous fp32");
+  const int64_t M = h.size(0), H = h.size(1);
+  TORCH_CHECK(H % 4 == 0 && recv != 0 && (recv & 15) == 0 && slot_stride % 4 == 0, "reduce layout");
+  TORCH_CHECK(nsrc >= 1 && nsrc <= atlas::kMaxPeers, "1..8 sources");
+  TORCH_CHECK(gamma.has_value() == x.has_value(), "gamma and x go together");
+  bool bf16 = false;
+  if (x.has_value()) {
+    TORCH_CHECK(x->is_contiguous() && x->size(0) == M && x->size(1) == H, "x shape");
+    TORCH_CHECK(gamma->scalar_type() == x->scalar_type(), "gamma/x dtype");
+    bf16 = x->scalar_type() == torch::kBFloat16;
+  }
+  const c10::cuda::CUDAGuard guard(h.device());
+  atlas::launch_tp_reduce_rmsnorm(reinterpret_cast<const float*>(recv), slot_stride,
+                                  reinterpret_cast<const uint32_t*>(flags), reinterpret_cast<const uint32_t*>(seq),
+                                  static_cast<int>(nsrc), h.data_ptr<float>(),
+                                  gamma.has_value() ? gamma->data_ptr() : nullptr,
+                                  x.has_value() ? x->data_ptr() : nullptr, static_cast<int>(M), static_cast<int>(H),
+                                  static_cast<float>(eps), bf16, err.data_ptr<int>(), at::cuda::getCurrentCUDAStream());
+}
+
+void tp_wait(int64_t flags, int64_t seq, int64_t nsrc, torch::Tensor err) {
+  const c10::cuda::CUDAGuard guard(err.device());
+  atlas::launch_tp_wait(reinterpret_cast<const uint32_t*>(flags), reinterpret_cast<const uint32_t*>(seq),
+                        static_cast<int>(nsrc), err.data_ptr<int>(), at::cuda::getCurrentCUDAStream());
+}
+
+// CUDA IPC: a plain cudaMalloc region (not the caching allocator, whose blocks
+// share one IPC handle per segment) that peers map into their address space.
+int64_t ipc_malloc(int64_t bytes, int64_t device) {
+  const c10::cuda::CUDAGuard guard(static_cast<c10::DeviceIndex>(device));
+  void* p = nullptr;
+  TORCH_CHECK(cudaMalloc(&p, static_cast<size_t>(bytes)) == cudaSuccess, "cudaMalloc of the symmetric buffer failed");
+  TORCH_CHECK(cudaMemset(p, 0, static_cast<size_t>(bytes)) == cudaSuccess, "cudaMemset failed");
+  return reinterpret_cast<int64_t>(p);
+}
+
+void ipc_free(int64_t ptr, int64_t device) {
+  const c10::cuda::CUDAGuard guard(static_cast<c10::DeviceIndex>(device));
+  cudaFree(reinterpret_cast<void*>(ptr));
+}
+
+py::bytes ipc_handle(int64_t ptr, int64_t device) {
+  const c10::cuda::CUDAGuard guard(static_cast<c10::DeviceIndex>(device));
+  cudaIpcMemHandle_t h;
+  const cudaError_t e = cudaIpcGetMemHandle(&h, reinterpret_cast<void*>(ptr));
+  TORCH_CHECK(e == cudaSuccess, "cudaIpcGetMemHandle failed: ", cudaGetErrorString(e));
+  return py::bytes(reinterpret_cast<const char*>(&h), sizeof(h));
+}
+
+int64_t ipc_open(py::bytes handle, int64_t device) {
+  const c10::cuda::CUDAGuard guard(static_cast<c10::DeviceIndex>(device));
+  std::string s = handle;
+  TORCH_CHECK(s.size() == sizeof(cudaIpcMemHandle_t), "bad IPC handle size");
+  cudaIpcMemHandle_t h;
+  std::memcpy(&h, s.data(), sizeof(h));
+  void* p = nullptr;
+  const cudaError_t e = cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess);
+  TORCH_CHECK(e == cudaSuccess, "cudaIpcOpenMemHandle failed: ", cudaGetErrorString(e));
+  return reinterpret_cast<int64_t>(p);
+}
+
+void ipc_close(int64_t ptr, int64_t device) {
+  const c10::cuda::CUDAGuard guard(static_cast<c10::DeviceIndex>(device));
+  cudaIpcCloseMemHandle(reinterpret_cast<void*>(ptr));
+}
+
+bool can_access_peer(int64_t device, int64_t peer) {
+  int ok = 0;
+  cudaDeviceCanAccessPeer(&ok, static_cast<int>(device), static_cast<int>(peer));
+  return ok != 0;
+}
+
+// View raw device memory owned elsewhere (a symmetric buffer) as a tensor.
+torch::Tensor wrap_ptr(int64_t ptr, std::vector<int64_t> sizes, torch::ScalarType dtype, int64_t device) {
+  auto opts = torch::TensorOptions().dtype(dtype).device(torch::kCUDA, static_cast<c10::DeviceIndex>(device));
+  return torch::from_blob(reinterpret_cast<void*>(ptr), sizes, [](void*) {}, opts);
 }
 
 // ----------------------------------------------------------- attention
@@ -349,8 +462,19 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("kv_move_slots", &kv_move_slots);
   m.def("topk", &topk);
   m.def("gather_logprobs", &gather_logprobs);
+  m.def("gemm_peer", &gemm_peer, "tcgen05 GEMM with the fp32 tile stored into peer buffers, then a release flag");
+  m.def("tp_reduce_rmsnorm", &tp_reduce_rmsnorm, "wait for peers, h += sum of partials, x = rmsnorm(h)");
+  m.def("tp_wait", &tp_wait);
+  m.def("ipc_malloc", &ipc_malloc);
+  m.def("ipc_free", &ipc_free);
+  m.def("ipc_handle", &ipc_handle);
+  m.def("ipc_open", &ipc_open);
+  m.def("ipc_close", &ipc_close);
+  m.def("can_access_peer", &can_access_peer);
+  m.def("wrap_ptr", &wrap_ptr);
   m.attr("EPI_STORE") = static_cast<int>(atlas::kEpiStore);
   m.attr("EPI_RESIDUAL") = static_cast<int>(atlas::kEpiResidual);
   m.attr("EPI_SILU") = static_cast<int>(atlas::kEpiSilu);
   m.attr("EPI_F32") = static_cast<int>(atlas::kEpiF32);
+  m.attr("EPI_PEER") = static_cast<int>(atlas::kEpiPeer);
 }

@@ -22,6 +22,7 @@ enum ErrorCode : int {
   kErrWaitTimeout = 1,   // an mbarrier wait hit its poll limit
   kErrBadIndex = 2,      // an index (page, slot, token) was out of range
   kErrConfig = 3,        // unsupported shape reached a kernel
+  kErrPeerTimeout = 4,   // a peer GPU's flag did not arrive within the time limit
 };
 
 __device__ __forceinline__ void set_error(int* flag, int code) {
@@ -29,6 +30,46 @@ __device__ __forceinline__ void set_error(int* flag, int code) {
 }
 
 constexpr uint32_t kSpinLimit = 1u << 26;  // ~seconds of polling before giving up
+
+// ------------------------------------------------- system-scope (peer) sync
+// Flags written by other GPUs over NVLink: release stores / acquire loads at
+// system scope.  Waits are bounded by wall time (the global timer) and give up
+// at once when the error flag is already set, so one lost peer costs one
+// timeout, not one per wait.
+constexpr uint64_t kPeerWaitNs = 5ull * 1000 * 1000 * 1000;  // 5 s
+
+__device__ __forceinline__ uint64_t global_timer_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+// Wait until *flag >= target (wrap-safe).  Returns false on timeout.
+__device__ __forceinline__ bool wait_flag_geq(const uint32_t* flag, uint32_t target, int* err) {
+  if (err != nullptr && *reinterpret_cast<volatile int*>(err) != 0) return false;
+  const uint64_t t0 = global_timer_ns();
+  uint32_t polls = 0;
+  while (static_cast<int32_t>(ld_acquire_sys(flag) - target) < 0) {
+    if ((++polls & 255u) == 0) {
+      if (global_timer_ns() - t0 > kPeerWaitNs) {
+        set_error(err, kErrPeerTimeout);
+        return false;
+      }
+      if (err != nullptr && *reinterpret_cast<volatile int*>(err) != 0) return false;
+    }
+  }
+  return true;
+}
 
 // ------------------------------------------------------------- addresses
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {

@@ -18,6 +18,10 @@
 // barrier CTA r reduces columns r, r+S, ... by reading all S partials through
 // distributed shared memory in split order (deterministic, independent of the
 // batch composition) and applies the epilogue.  No global workspace.
+// Peer epilogue (tensor parallelism): the fp32 tile is stored straight into
+// every TP rank's receive buffer over NVLink (P2P stores through CUDA IPC
+// mappings) and the grid's last CTA raises a sequence flag on each rank, so
+// the row-parallel GEMM and the all-reduce's data movement are one kernel.
 
 #include <cuda.h>
 
@@ -48,8 +52,32 @@ __device__ __forceinline__ void store_elem(const GemmParams& p, int m, int n, fl
   } else if constexpr (EPI == kEpiResidual) {
     float* r = reinterpret_cast<float*>(p.out);
     r[idx] = r[idx] + v;
+  } else if constexpr (EPI == kEpiPeer) {
+    for (int r = 0; r < p.peer.ndst; ++r) p.peer.dst[r][idx] = v;
   } else {  // kEpiF32
     reinterpret_cast<float*>(p.out)[idx] = v;
+  }
+}
+
+// Peer epilogue completion: every thread's remote stores are fenced at system
+// scope; the last CTA of the grid (ticket) publishes the new sequence number
+// to every destination's flag.
+template <int EPI>
+__device__ __forceinline__ void peer_signal(const GemmParams& p) {
+  if constexpr (EPI == kEpiPeer) {
+    __threadfence_system();
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      const uint32_t total = gridDim.x * gridDim.y * gridDim.z;
+      const uint32_t t = atomicAdd(p.peer.ticket, 1u);
+      if (t == total - 1) {
+        *reinterpret_cast<volatile uint32_t*>(p.peer.ticket) = 0u;
+        __threadfence_system();
+        const uint32_t s = *reinterpret_cast<volatile uint32_t*>(p.peer.seq) + 1u;
+        *reinterpret_cast<volatile uint32_t*>(p.peer.seq) = s;
+        for (int r = 0; r < p.peer.ndst; ++r) st_release_sys(p.peer.flag[r], s);
+      }
+    }
   }
 }
 
@@ -185,6 +213,7 @@ __global__ void __launch_bounds__(128, 1)
     tc_fence_before();
     __syncthreads();
     if (warp == 0) tmem_dealloc(tmem, S::kTmemCols);
+    peer_signal<EPI>(p);
     return;
   }
   // Split-K: stage buffers are free once `done` fired; park the fp32 tile there
@@ -230,6 +259,7 @@ __global__ void __launch_bounds__(128, 1)
   tc_fence_before();
   __syncthreads();
   if (warp == 0) tmem_dealloc(tmem, S::kTmemCols);
+  peer_signal<EPI>(p);
 }
 
 // ------------------------------------------------------------------ host
@@ -279,6 +309,7 @@ void launch_gemm_tn(const CUtensorMap& a, const CUtensorMap& b, const GemmParams
       case kEpiStore: launch_epi<kEpiStore, __nv_bfloat16>(bn, a, b, p, grid, st); break;
       case kEpiResidual: launch_epi<kEpiResidual, __nv_bfloat16>(bn, a, b, p, grid, st); break;
       case kEpiSilu: launch_epi<kEpiSilu, __nv_bfloat16>(bn, a, b, p, grid, st); break;
+      case kEpiPeer: launch_epi<kEpiPeer, __nv_bfloat16>(bn, a, b, p, grid, st); break;
       default: launch_epi<kEpiF32, __nv_bfloat16>(bn, a, b, p, grid, st); break;
     }
   } else {
@@ -286,6 +317,7 @@ void launch_gemm_tn(const CUtensorMap& a, const CUtensorMap& b, const GemmParams
       case kEpiStore: launch_epi<kEpiStore, __half>(bn, a, b, p, grid, st); break;
       case kEpiResidual: launch_epi<kEpiResidual, __half>(bn, a, b, p, grid, st); break;
       case kEpiSilu: launch_epi<kEpiSilu, __half>(bn, a, b, p, grid, st); break;
+      case kEpiPeer: launch_epi<kEpiPeer, __half>(bn, a, b, p, grid, st); break;
       default: launch_epi<kEpiF32, __half>(bn, a, b, p, grid, st); break;
     }
   }

@@ -1,0 +1,120 @@
+// Tensor-parallel reduction kernels (the consumer half of the fused
+// row-parallel GEMM + all-reduce; the producer half is the GEMM's peer
+// epilogue, which stores each rank's fp32 partial tile into every rank's
+// receive buffer over NVLink and raises a sequence flag).
+//
+//  tp_reduce_rmsnorm: wait until every rank's flag has reached this rank's own
+//    sequence number for the call site, then  h += sum_r partial_r  (ranks
+//    summed in rank order, so every rank computes bit-identical residuals)
+//    and  x = RMSNorm(h) * gamma  in the activation dtype -- the residual add
+//    and the next layer's input norm fused with the reduction.
+//  tp_wait: the same wait alone (the root rank before it reads the gathered
+//    vocabulary-parallel logits).
+//
+// All waits are bounded (wait_flag_geq): on timeout the kernel records
+// kErrPeerTimeout and carries on with whatever is in the buffers; the host
+// reads the error flag.
+
+#include "common.cuh"
+#include "launch.h"
+#include "tp.h"
+
+namespace atlas {
+
+__device__ __forceinline__ void wait_all_ranks(const uint32_t* flags, const uint32_t* seq, int nsrc, int* err) {
+  if (flags != nullptr && static_cast<int>(threadIdx.x) < nsrc) {
+    const uint32_t target = *reinterpret_cast<const volatile uint32_t*>(seq);
+    wait_flag_geq(flags + threadIdx.x, target, err);
+  }
+  __syncthreads();
+}
+
+constexpr int kReduceThreads = 256;
+constexpr int kReduceVec = 8;  // float4 per thread kept in registers: H <= 256 * 4 * 8 = 8192 per pass
+
+template <typename T>
+__global__ void __launch_bounds__(kReduceThreads)
+    tp_reduce_rmsnorm_kernel(const float* __restrict__ recv, int64_t slot_stride, const uint32_t* flags,
+                             const uint32_t* seq, int nsrc, float* __restrict__ h, const T* __restrict__ gamma,
+                             T* __restrict__ x, int H, float eps, int* err) {
+  pdl_wait();
+  pdl_trigger();
+  wait_all_ranks(flags, seq, nsrc, err);
+  const int m = blockIdx.x;
+  float* hr = h + static_cast<int64_t>(m) * H;
+  const float* pr = recv + static_cast<int64_t>(m) * H;
+  float ss = 0.f;
+  auto update = [&](int i) -> float4 {
+    float4 acc = __ldcg(reinterpret_cast<const float4*>(pr + i));
+    for (int r = 1; r < nsrc; ++r) {
+      const float4 v = __ldcg(reinterpret_cast<const float4*>(pr + r * slot_stride + i));
+      acc.x += v.x;
+      acc.y += v.y;
+      acc.z += v.z;
+      acc.w += v.w;
+    }
+    float4 o = *reinterpret_cast<const float4*>(hr + i);
+    o.x += acc.x;
+    o.y += acc.y;
+    o.z += acc.z;
+    o.w += acc.w;
+    *reinterpret_cast<float4*>(hr + i) = o;
+    ss += o.x * o.x + o.y * o.y + o.z * o.z + o.w * o.w;
+    return o;
+  };
+  // Pass 1: residual update (first 8192 columns kept in registers) and sum of squares.
+  float4 keep[kReduceVec];
+#pragma unroll
+  for (int j = 0; j < kReduceVec; ++j) {
+    const int i = (j * kReduceThreads + static_cast<int>(threadIdx.x)) * 4;
+    if (i < H) keep[j] = update(i);
+  }
+  for (int i = (kReduceVec * kReduceThreads + static_cast<int>(threadIdx.x)) * 4; i < H; i += kReduceThreads * 4)
+    update(i);
+  if (gamma == nullptr) return;
+  __shared__ float red[kReduceThreads / 32];
+  ss = warp_sum(ss);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+  __syncthreads();
+  float tot = 0.f;
+#pragma unroll
+  for (int w = 0; w < kReduceThreads / 32; ++w) tot += red[w];
+  const float inv = rsqrtf(tot / static_cast<float>(H) + eps);
+  T* xr = x + static_cast<int64_t>(m) * H;
+  auto emit = [&](int i, const float4& o) {
+    xr[i] = from_f32<T>(o.x * inv * to_f32(gamma[i]));
+    xr[i + 1] = from_f32<T>(o.y * inv * to_f32(gamma[i + 1]));
+    xr[i + 2] = from_f32<T>(o.z * inv * to_f32(gamma[i + 2]));
+    xr[i + 3] = from_f32<T>(o.w * inv * to_f32(gamma[i + 3]));
+  };
+#pragma unroll
+  for (int j = 0; j < kReduceVec; ++j) {
+    const int i = (j * kReduceThreads + static_cast<int>(threadIdx.x)) * 4;
+    if (i < H) emit(i, keep[j]);
+  }
+  for (int i = (kReduceVec * kReduceThreads + static_cast<int>(threadIdx.x)) * 4; i < H; i += kReduceThreads * 4)
+    emit(i, *reinterpret_cast<const float4*>(hr + i));
+}
+
+__global__ void tp_wait_kernel(const uint32_t* flags, const uint32_t* seq, int nsrc, int* err) {
+  pdl_wait();
+  pdl_trigger();
+  wait_all_ranks(flags, seq, nsrc, err);
+}
+
+void launch_tp_reduce_rmsnorm(const float* recv, int64_t slot_stride, const uint32_t* flags, const uint32_t* seq,
+                              int nsrc, float* h, const void* gamma, void* x, int M, int H, float eps, bool bf16,
+                              int* err, cudaStream_t st) {
+  if (bf16)
+    launch_k(tp_reduce_rmsnorm_kernel<__nv_bfloat16>, dim3(M), dim3(kReduceThreads), 0, st, recv, slot_stride, flags,
+             seq, nsrc, h, static_cast<const __nv_bfloat16*>(gamma), static_cast<__nv_bfloat16*>(x), H, eps, err);
+  else
+    launch_k(tp_reduce_rmsnorm_kernel<__half>, dim3(M), dim3(kReduceThreads), 0, st, recv, slot_stride, flags, seq,
+             nsrc, h, static_cast<const __half*>(gamma), static_cast<__half*>(x), H, eps, err);
+}
+
+void launch_tp_wait(const uint32_t* flags, const uint32_t* seq, int nsrc, int* err, cudaStream_t st) {
+  launch_k(tp_wait_kernel, dim3(1), dim3(32), 0, st, flags, seq, nsrc, err);
+}
+
+}  // namespace atlas

@@ -1,0 +1,17 @@
+// Launch wrappers of the tensor-parallel reduction kernels.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace atlas {
+
+// h[M, H] += sum over nsrc slots of recv[slot * slot_stride + m * H + i] (rank
+// order), after waiting for flags[0..nsrc) >= *seq when flags != nullptr;
+// then x = rmsnorm(h) * gamma unless gamma == nullptr.
+void launch_tp_reduce_rmsnorm(const float* recv, int64_t slot_stride, const uint32_t* flags, const uint32_t* seq,
+                              int nsrc, float* h, const void* gamma, void* x, int M, int H, float eps, bool bf16,
+                              int* err, cudaStream_t st);
+void launch_tp_wait(const uint32_t* flags, const uint32_t* seq, int nsrc, int* err, cudaStream_t st);
+
+}  // namespace atlas

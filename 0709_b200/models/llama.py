@@ -89,6 +89,11 @@ PRESETS: dict[str, LlamaConfig] = {
     # BASELINE config 1 (CPU plumbing): tiny drafter and target.
     "tiny-drafter": LlamaConfig("tiny-drafter", 2, 256, 4, 2, 64, 512, 1024, rope_theta=10000.0, rope_scaling=None),
     "tiny-target": LlamaConfig("tiny-target", 4, 256, 4, 2, 64, 512, 1024, rope_theta=10000.0, rope_scaling=None),
+    # Small head_dim-128 models for GPU tests (the CUDA attention kernel needs head_dim 128).
+    "small-drafter": LlamaConfig("small-drafter", 2, 512, 8, 2, 128, 1024, 4096),
+    "small-target": LlamaConfig("small-target", 3, 512, 8, 2, 128, 1024, 4096),
+    # Splits over up to 8 tensor-parallel ranks (8 KV heads, FFN 8 x 512).
+    "small-tp-target": LlamaConfig("small-tp-target", 4, 1024, 16, 8, 128, 4096, 8192),
     # Llama-3.2-1B shape as declared by the benchmark (head_dim 128, so q_proj is 2048 -> 4096).
     "llama-1b": LlamaConfig(
         "llama-1b", 16, 2048, 32, 8, 128, 8192, 128256, rope_scaling=RopeScaling(factor=32.0), tie_word_embeddings=True

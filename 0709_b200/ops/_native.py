@@ -86,6 +86,7 @@ CUDA_SOURCES = [
     "kvcache.cu",
     "sampling.cu",
     "topk_noalloc.cu",
+    "tp.cu",
 ]
 
 

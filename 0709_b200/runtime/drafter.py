@@ -41,6 +41,9 @@ class PrefixPageMirror:
         self.dev = torch.zeros(int(capacity), dtype=torch.int32, device=device)
         self.host: list[int] = []
         self.h2d_copies = 0
+        # Called with (start, values) after each device update (tensor-parallel
+        # engines forward the update to the worker ranks' copies).
+        self.on_update = None
 
     def sync(self, pages: torch.Tensor) -> None:
         new = pages.tolist()
@@ -53,6 +56,8 @@ class PrefixPageMirror:
         if start < len(new):
             self.dev[start: len(new)].copy_(pages[start:].to(self.dev.device, non_blocking=True))
             self.h2d_copies += 1
+            if self.on_update is not None:
+                self.on_update(start, new[start:])
         self.host = new
 
     def view(self) -> torch.Tensor:

@@ -223,8 +223,8 @@ class LlamaEngine:
             logits = self.forward(
                 tokens[c0:c1], pos, slots[c0:c1], desc, logits_rows=last, causal_start=start_pos + c0
             )
-        assert logits is not None
-        return logits[0]
+        # Tensor-parallel worker ranks get no logits (they live on the root rank).
+        return None if logits is None else logits[0]
 
     def copy_pages(self, copies: torch.Tensor) -> None:
         if copies.numel():

@@ -86,6 +86,8 @@ class TargetVerifier:
         self.device = engine.device
         self.page_size = engine.page_size
         self.mirror = PrefixPageMirror(engine.num_pages, self.device)
+        if hasattr(engine, "register_mirror"):
+            engine.register_mirror(self.mirror)
         self.score_weights = validate_score_weights(score_weights)
         self.fallback_threshold = None if fallback_threshold is None else float(fallback_threshold)
         self.first_token_threshold = None if first_token_threshold is None else float(first_token_threshold)
@@ -654,9 +656,12 @@ class TargetVerifier:
 
     # ------------------------------------------------------------- metadata
     def runtime_metadata(self) -> dict[str, object]:
-        cfg = self.engine.cfg
+        cfg = getattr(self.engine, "model_cfg", self.engine.cfg)
+        tp = getattr(self.engine, "tp", None)
         return {
             "backend": "b200_native_masked_tree_verify",
+            "tensor_parallel": 1 if tp is None else int(tp.world),
+            "tensor_parallel_comm": None if tp is None else tp.mode,
             "model": self.model_name,
             "model_vocab_size": int(cfg.vocab_size),
             "paged_kv": True,
