@@ -15,6 +15,7 @@
 
 #include "attention.h"
 #include "gemm.h"
+#include "gemm_fp8.h"
 #include "kernels.h"
 #include "tp.h"
 
@@ -61,14 +62,17 @@ CUtensorMapDataType tma_dtype(torch::ScalarType t) {
   return CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
 }
 
-// Row-major [outer, inner] with row stride `ld` elements; box {64, box_outer}, 128B swizzle.
+// Row-major [outer, inner] with row stride `ld` elements; box {128 bytes, box_outer}, 128B swizzle
+// (64 elements of fp16/bf16, 128 of fp8).
 CUtensorMap map_2d(const torch::Tensor& t, int64_t inner, int64_t outer, int64_t ld, int box_outer) {
+  const bool byte = t.element_size() == 1;
+  const uint32_t box_inner = byte ? 128 : 64;
   MapKey k{};
   k.ptr = reinterpret_cast<uint64_t>(t.data_ptr());
   k.d[0] = inner;
   k.d[1] = outer;
   k.d[2] = ld;
-  k.box[0] = 64;
+  k.box[0] = box_inner;
   k.box[1] = box_outer;
   k.rank = 2;
   k.dtype = static_cast<int>(t.scalar_type());
@@ -79,9 +83,9 @@ CUtensorMap map_2d(const torch::Tensor& t, int64_t inner, int64_t outer, int64_t
   CUtensorMap m;
   cuuint64_t dims[2] = {static_cast<cuuint64_t>(inner), static_cast<cuuint64_t>(outer)};
   cuuint64_t strides[1] = {static_cast<cuuint64_t>(ld) * t.element_size()};
-  cuuint32_t box[2] = {64, static_cast<cuuint32_t>(box_outer)};
+  cuuint32_t box[2] = {box_inner, static_cast<cuuint32_t>(box_outer)};
   cuuint32_t es[2] = {1, 1};
-  CUresult r = encode_fn()(&m, tma_dtype(t.scalar_type()), 2, t.data_ptr(), dims, strides, box, es,
+  CUresult r = encode_fn()(&m, byte ? CU_TENSOR_MAP_DATA_TYPE_UINT8 : tma_dtype(t.scalar_type()), 2, t.data_ptr(), dims, strides, box, es,
                            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   TORCH_CHECK(r == CUDA_SUCCESS, "cuTensorMapEncodeTiled (2d) failed: ", static_cast<int>(r));
@@ -239,6 +243,108 @@ std::vector<int64_t> gemm_peer(torch::Tensor w, torch::Tensor x, std::vector<int
   po.ticket = reinterpret_cast<uint32_t*>(ticket);
   po.seq = reinterpret_cast<uint32_t*>(seq);
   return gemm_impl(w, x, nullptr, ldo, atlas::kEpiPeer, err, 0, &po);
+}
+
+// ----------------------------------------------------------------- fp8
+int fp8_pick_bn(int64_t n) { return n <= 16 ? 16 : (n <= 32 ? 32 : 64); }
+
+// Split-K for the fp8 kernel: as for bf16, plus enough splits that one CTA
+// covers at most kFp8MaxKbPerCta K blocks (its scales live in shared memory).
+std::pair<int, int> fp8_pick_splits(int64_t M, int64_t N, int64_t K, int bn) {
+  const int64_t tiles = ((M + 127) / 128) * ((N + bn - 1) / bn);
+  const int64_t kb = K / 128;
+  int64_t splits = 1;
+  if (tiles * 4 < static_cast<int64_t>(num_sms()) * 3)
+    splits = std::max<int64_t>(1, std::min<int64_t>({kb / 2, num_sms() / tiles, 8}));
+  splits = std::max<int64_t>(splits, (kb + atlas::kFp8MaxKbPerCta - 1) / atlas::kFp8MaxKbPerCta);
+  TORCH_CHECK(splits <= 8, "fp8 GEMM: K too long for 8 splits of ", atlas::kFp8MaxKbPerCta, " blocks");
+  int64_t kbps = (kb + splits - 1) / splits;
+  splits = (kb + kbps - 1) / kbps;
+  return {static_cast<int>(splits), static_cast<int>(kbps)};
+}
+
+std::vector<int64_t> gemm_fp8_impl(const torch::Tensor& wq, const torch::Tensor& sw, const torch::Tensor& xq,
+                                   const torch::Tensor& sa, void* out_ptr, int64_t ldo, bool out_bf16, int64_t epi,
+                                   const torch::Tensor& err, const atlas::PeerOut* peer) {
+  check_cuda(wq, "wq");
+  TORCH_CHECK(wq.element_size() == 1 && xq.element_size() == 1, "fp8 operands must be 1-byte tensors");
+  TORCH_CHECK(wq.dim() == 2 && wq.is_contiguous() && xq.dim() == 2 && xq.is_contiguous(), "fp8 operand layout");
+  const int64_t M = wq.size(0), K = wq.size(1), N = xq.size(0);
+  TORCH_CHECK(xq.size(1) == K && K % 128 == 0, "fp8 GEMM needs K % 128 == 0 and matching operands");
+  TORCH_CHECK(sw.scalar_type() == torch::kFloat32 && sw.is_contiguous() && sw.size(0) == (M + 127) / 128 &&
+                  sw.size(1) == K / 128, "weight scales must be fp32 [ceil(M/128), K/128]");
+  TORCH_CHECK(sa.scalar_type() == torch::kFloat32 && sa.is_contiguous() && sa.size(0) == K / 128 && sa.size(1) >= N,
+              "activation scales must be fp32 [K/128, >= N]");
+  if (epi == atlas::kEpiSilu) TORCH_CHECK(M % 128 == 0, "gate/up GEMM needs M % 128 == 0");
+  const int bn = fp8_pick_bn(N);
+  auto sp = fp8_pick_splits(M, N, K, bn);
+  const c10::cuda::CUDAGuard guard(wq.device());
+  CUtensorMap a = map_2d(wq, K, M, K, 128);
+  CUtensorMap b = map_2d(xq, K, N, K, bn);
+  atlas::Fp8GemmParams p{};
+  p.M = static_cast<int>(M);
+  p.N = static_cast<int>(N);
+  p.K = static_cast<int>(K);
+  p.ldo = static_cast<int>(ldo);
+  p.splits = sp.first;
+  p.kb_per_split = sp.second;
+  p.out_bf16 = out_bf16 ? 1 : 0;
+  p.lds = static_cast<int>(sa.size(1));
+  p.sw = sw.data_ptr<float>();
+  p.sa = sa.data_ptr<float>();
+  p.out = out_ptr;
+  p.err = err.data_ptr<int>();
+  if (peer != nullptr) p.peer = *peer;
+  atlas::launch_gemm_fp8(a, b, p, bn, static_cast<int>(epi), at::cuda::getCurrentCUDAStream());
+  return {bn, sp.first, sp.second};
+}
+
+std::vector<int64_t> gemm_fp8(torch::Tensor wq, torch::Tensor sw, torch::Tensor xq, torch::Tensor sa,
+                              torch::Tensor out, int64_t epi, torch::Tensor err) {
+  check_cuda(out, "out");
+  TORCH_CHECK(epi != atlas::kEpiPeer, "use gemm_fp8_peer for the peer epilogue");
+  const bool f32 = epi == atlas::kEpiResidual || epi == atlas::kEpiF32;
+  TORCH_CHECK(f32 ? out.scalar_type() == torch::kFloat32
+                  : (out.scalar_type() == torch::kBFloat16 || out.scalar_type() == torch::kHalf),
+              "output dtype does not match the epilogue");
+  TORCH_CHECK(out.stride(-1) == 1, "out must have unit inner stride");
+  return gemm_fp8_impl(wq, sw, xq, sa, out.data_ptr(), out.stride(0), out.scalar_type() == torch::kBFloat16, epi,
+                       err, nullptr);
+}
+
+std::vector<int64_t> gemm_fp8_peer(torch::Tensor wq, torch::Tensor sw, torch::Tensor xq, torch::Tensor sa,
+                                   std::vector<int64_t> dst, int64_t ldo, std::vector<int64_t> flags, int64_t ticket,
+                                   int64_t seq, torch::Tensor err) {
+  TORCH_CHECK(!dst.empty() && dst.size() <= static_cast<size_t>(atlas::kMaxPeers) && dst.size() == flags.size(),
+              "gemm_fp8_peer needs 1..8 destinations, one flag each");
+  atlas::PeerOut po{};
+  po.ndst = static_cast<int>(dst.size());
+  for (size_t i = 0; i < dst.size(); ++i) {
+    po.dst[i] = reinterpret_cast<float*>(dst[i]);
+    po.flag[i] = reinterpret_cast<uint32_t*>(flags[i]);
+  }
+  po.ticket = reinterpret_cast<uint32_t*>(ticket);
+  po.seq = reinterpret_cast<uint32_t*>(seq);
+  return gemm_fp8_impl(wq, sw, xq, sa, nullptr, ldo, false, atlas::kEpiPeer, err, &po);
+}
+
+void quant_fp8(torch::Tensor x, torch::Tensor xq, torch::Tensor sa) {
+  TORCH_CHECK(x.is_contiguous() && xq.is_contiguous() && x.dim() == 2 && x.size(1) % 128 == 0, "quant_fp8 layout");
+  TORCH_CHECK(sa.size(0) == x.size(1) / 128 && sa.size(1) >= x.size(0), "quant_fp8 scale layout");
+  const c10::cuda::CUDAGuard guard(x.device());
+  atlas::launch_quant_fp8(x.data_ptr(), static_cast<uint8_t*>(xq.data_ptr()), sa.data_ptr<float>(),
+                          static_cast<int>(x.size(0)), static_cast<int>(x.size(1)), static_cast<int>(sa.size(1)),
+                          x.scalar_type() == torch::kBFloat16, at::cuda::getCurrentCUDAStream());
+}
+
+void rmsnorm_fp8(torch::Tensor h, torch::Tensor w, torch::Tensor xq, torch::Tensor sa, double eps) {
+  TORCH_CHECK(h.scalar_type() == torch::kFloat32 && h.is_contiguous() && h.size(1) % 128 == 0, "rmsnorm_fp8 input");
+  TORCH_CHECK(sa.size(0) == h.size(1) / 128 && sa.size(1) >= h.size(0), "rmsnorm_fp8 scale layout");
+  const c10::cuda::CUDAGuard guard(h.device());
+  atlas::launch_rmsnorm_fp8(h.data_ptr<float>(), w.data_ptr(), static_cast<uint8_t*>(xq.data_ptr()),
+                            sa.data_ptr<float>(), static_cast<int>(h.size(0)), static_cast<int>(h.size(1)),
+                            static_cast<int>(sa.size(1)), static_cast<float>(eps), w.scalar_type() == torch::kBFloat16,
+                            at::cuda::getCurrentCUDAStream());
 }
 
 // --------------------------------------------------- tensor parallelism
@@ -465,6 +571,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm_peer", &gemm_peer, "tcgen05 GEMM with the fp32 tile stored into peer buffers, then a release flag");
   m.def("tp_reduce_rmsnorm", &tp_reduce_rmsnorm, "wait for peers, h += sum of partials, x = rmsnorm(h)");
   m.def("tp_wait", &tp_wait);
+  m.def("gemm_fp8", &gemm_fp8, "block-scaled fp8 tcgen05 GEMM; returns [bn, splits, kb_per_split]");
+  m.def("gemm_fp8_peer", &gemm_fp8_peer);
+  m.def("quant_fp8", &quant_fp8, "per-token 1x128 e4m3 quantization");
+  m.def("rmsnorm_fp8", &rmsnorm_fp8, "RMSNorm straight to e4m3 + 1x128 scales");
   m.def("ipc_malloc", &ipc_malloc);
   m.def("ipc_free", &ipc_free);
   m.def("ipc_handle", &ipc_handle);

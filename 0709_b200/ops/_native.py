@@ -87,6 +87,7 @@ CUDA_SOURCES = [
     "sampling.cu",
     "topk_noalloc.cu",
     "tp.cu",
+    "gemm_fp8.cu",
 ]
 
 

@@ -71,6 +71,32 @@ class CudaOps:
         out = torch.empty((x.shape[0], w.shape[0]), dtype=torch.float32, device=x.device)
         return self._gemm(x, w, out, self.ext.EPI_F32)
 
+    # -------------------------------------------------------------- fp8
+    @staticmethod
+    def _scale_ld(n: int) -> int:
+        return (n + 3) // 4 * 4
+
+    def quant_fp8(self, x: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+        n, k = x.shape
+        xq = torch.empty((n, k), dtype=torch.float8_e4m3fn, device=x.device)
+        sa = torch.empty((k // 128, self._scale_ld(n)), dtype=torch.float32, device=x.device)
+        self.ext.quant_fp8(x.contiguous(), xq, sa)
+        counters.launches(1)
+        return xq, sa
+
+    def rmsnorm_fp8(self, h: torch.Tensor, w: torch.Tensor, eps: float) -> tuple[torch.Tensor, torch.Tensor]:
+        n, k = h.shape
+        xq = torch.empty((n, k), dtype=torch.float8_e4m3fn, device=h.device)
+        sa = torch.empty((k // 128, self._scale_ld(n)), dtype=torch.float32, device=h.device)
+        self.ext.rmsnorm_fp8(h.contiguous(), w, xq, sa, float(eps))
+        counters.launches(1)
+        return xq, sa
+
+    def gemm_fp8(self, xq: torch.Tensor, sa: torch.Tensor, w, out: torch.Tensor, epi: int) -> torch.Tensor:
+        self.last_gemm_config = self.ext.gemm_fp8(w.q, w.scale, xq, sa, out, epi, self.err)
+        counters.launches(1)
+        return out
+
     # ------------------------------------------------------ elementwise
     def embed(self, tokens: torch.Tensor, table: torch.Tensor) -> torch.Tensor:
         out = torch.empty((tokens.numel(), table.shape[1]), dtype=torch.float32, device=table.device)

@@ -38,8 +38,9 @@ def parse_args(argv=None):
     p.add_argument("--page-size", type=int, default=4)
     p.add_argument("--prompt-len", type=int, default=40)
     p.add_argument("--new-tokens", type=int, default=16)
-    p.add_argument("--k", type=int, default=2)
-    p.add_argument("--d", type=int, default=3)
+    # (not --k/--d: torchrun's own parser would read "--d" as an abbreviation of its options)
+    p.add_argument("--width", dest="k", type=int, default=2)
+    p.add_argument("--depth", dest="d", type=int, default=3)
     p.add_argument("--seed", type=int, default=0)
     p.add_argument("--fallback-threshold", type=float, default=None)
     p.add_argument("--timing-iters", type=int, default=0, help="Also time this many verify forwards (GPU).")
@@ -130,6 +131,10 @@ def run_root(args, eng, cfg, device, dtype, pages, ctx) -> dict[str, object]:
     for tv in (TargetVerifier(eng, **kw), TargetVerifier(ref, **kw)):
         dr = DrafterRuntime(LlamaEngine(dw, num_pages=pages, page_size=args.page_size, max_positions=ctx + 64))
         conf = DistributedAtlasConfig(k=args.k, d=args.d, max_new_tokens=args.new_tokens, validate_state_alignment=True)
+        if device.type == "cuda":
+            # Capture every graph before the concurrent drafter/target threads start.
+            tv.warm_graphs()
+            dr.warm_graphs(args.k, conf.fallback_ar_tokens)
         gens.append(PagedDistributedAtlasGenerator(config=conf, drafter=dr, target_client=InProcessTargetClient(tv))
                     .generate(prompt))
     res["generated_tp"] = gens[0].generated_token_ids

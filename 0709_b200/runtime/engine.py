@@ -154,8 +154,16 @@ class LlamaEngine:
         torch.cuda.current_stream(self.device).wait_stream(stream)
         g = torch.cuda.CUDAGraph()
         before = counters.snapshot()["launches"]
-        with torch.cuda.graph(g, pool=self._graph_pool, capture_error_mode="thread_local"):
-            out = self.forward(sb.tokens, sb.positions, sb.slots, desc)
+        # Capture on the side stream without the device-wide synchronize that
+        # ``torch.cuda.graph`` performs first: another serving thread may be
+        # capturing or running at the same time (thread-local capture mode).
+        with torch.cuda.stream(stream):
+            g.capture_begin(self._graph_pool, capture_error_mode="thread_local")
+            try:
+                out = self.forward(sb.tokens, sb.positions, sb.slots, desc)
+            finally:
+                g.capture_end()
+        torch.cuda.current_stream(self.device).wait_stream(stream)
         launches = counters.snapshot()["launches"] - before
         return g, out, launches
 
