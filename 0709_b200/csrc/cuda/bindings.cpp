@@ -229,7 +229,10 @@ std::vector<int64_t> gemm(torch::Tensor w, torch::Tensor x, torch::Tensor out, i
 // `ldo` floats), followed by a release of the incremented local sequence
 // number into each destination's flag word.
 std::vector<int64_t> gemm_peer(torch::Tensor w, torch::Tensor x, std::vector<int64_t> dst, int64_t ldo,
-                               std::vector<int64_t> flags, int64_t ticket, int64_t seq, torch::Tensor err) {
+                               std::vector<int64_t> flags, int64_t ticket, int64_t seq, torch::Tensor ws,
+                               torch::Tensor counters, torch::Tensor err) {
+  (void)ws;
+  (void)counters;
   TORCH_CHECK(!dst.empty() && dst.size() <= static_cast<size_t>(atlas::kMaxPeers) && dst.size() == flags.size(),
               "gemm_peer needs 1..8 destinations, one flag each");
   atlas::PeerOut po{};

@@ -80,9 +80,9 @@ __device__ __forceinline__ void fp8_store_silu(const Fp8GemmParams& p, int m0, i
 template <int EPI>
 __device__ __forceinline__ void fp8_peer_signal(const Fp8GemmParams& p) {
   if constexpr (EPI == kEpiPeer) {
-    __threadfence_system();
     __syncthreads();
     if (threadIdx.x == 0) {
+      __threadfence_system();
       const uint32_t total = gridDim.x * gridDim.y * gridDim.z;
       if (atomicAdd(p.peer.ticket, 1u) == total - 1) {
         *reinterpret_cast<volatile uint32_t*>(p.peer.ticket) = 0u;
@@ -281,7 +281,7 @@ __global__ void __launch_bounds__(192, 1)
 __device__ __forceinline__ void quant_block_warp(const float (&v)[4], uint8_t* dst, float* scale_out, int lane) {
   float amax = fmaxf(fmaxf(fabsf(v[0]), fabsf(v[1])), fmaxf(fabsf(v[2]), fabsf(v[3])));
   amax = warp_max(amax);
-  const float scale = fmaxf(amax, 1e-10f) / 448.0f;
+  const float scale = fmaxf(amax, 1e-10f) * (1.0f / 448.0f);
   const float inv = 1.0f / scale;
   uint32_t packed = 0;
 #pragma unroll

@@ -65,9 +65,12 @@ __device__ __forceinline__ void store_elem(const GemmParams& p, int m, int n, fl
 template <int EPI>
 __device__ __forceinline__ void peer_signal(const GemmParams& p) {
   if constexpr (EPI == kEpiPeer) {
-    __threadfence_system();
+    // The CTA barrier orders every thread's stores before thread 0's
+    // system-scope fence, which orders them before the ticket (the
+    // cooperative-groups grid-barrier pattern): one fence per CTA.
     __syncthreads();
     if (threadIdx.x == 0) {
+      __threadfence_system();
       const uint32_t total = gridDim.x * gridDim.y * gridDim.z;
       const uint32_t t = atomicAdd(p.peer.ticket, 1u);
       if (t == total - 1) {

@@ -61,8 +61,8 @@ def quantize_activations(x: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
     """[N, K] -> (e4m3 [N, K], scales [K/128, N]) with one scale per token per 128 columns."""
     n, k = x.shape
     xf = x.float().reshape(n, k // BLOCK, BLOCK)
-    scale = xf.abs().amax(-1).clamp_min(1e-10) / E4M3_MAX
-    # x * (1 / scale), the kernels' arithmetic (bit-identical e4m3 codes).
+    scale = xf.abs().amax(-1).clamp_min(1e-10) * (1.0 / E4M3_MAX)
+    # amax * (1/448) and x * (1 / scale): the kernels' arithmetic.
     q = (xf * (1.0 / scale)[..., None]).clamp(-E4M3_MAX, E4M3_MAX).reshape(n, k).to(torch.float8_e4m3fn)
     return q, scale.t().contiguous()
 

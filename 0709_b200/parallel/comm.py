@@ -146,7 +146,7 @@ class TPGroup:
             dst = [self._recv(self.peers[p], site, self.rank) for p in range(self.world)]
             flags = [self._flag(self.peers[p], site, self.rank) for p in range(self.world)]
             self.ext.gemm_peer(w, a, dst, hid, flags, self.base + TICKET_OFF + 4 * site, self.base + SEQ_OFF + 4 * site,
-                               self.err)
+                               ops.ws, ops.counters, self.err)
             self.ext.tp_reduce_rmsnorm(self._recv(self.base, site, 0), self.max_rows * hid,
                                        self._flag(self.base, site, 0), self.base + SEQ_OFF + 4 * site, self.world, h,
                                        gamma, x, float(eps), self.err)
@@ -175,7 +175,7 @@ class TPGroup:
             root = self.peers[self.root]
             self.ext.gemm_peer(w, x, [root + self.logits_off + self.rank * v * 4], self.vocab,
                                [self._flag(root, SITE_LOGITS, self.rank)], self.base + TICKET_OFF + 4 * SITE_LOGITS,
-                               self.base + SEQ_OFF + 4 * SITE_LOGITS, self.err)
+                               self.base + SEQ_OFF + 4 * SITE_LOGITS, ops.ws, ops.counters, self.err)
             _count(1)
             if not self.is_root:
                 return None

@@ -116,6 +116,7 @@ class TPLlamaEngine(LlamaEngine):
         return self._run_rows_local(rows, tail_stride=tail_stride, mask_words=mask_words, prefix_pages=prefix_pages,
                                     **fields)
 
+    @torch.inference_mode()
     def _run_rows_local(self, rows: int, *, tail_stride: int, mask_words: int, prefix_pages: torch.Tensor, **fields):
         sb = self.static_batch(rows, tail_stride, mask_words)
         n = sb.load(**fields)
@@ -170,16 +171,25 @@ class TPLlamaEngine(LlamaEngine):
             self.mailbox.drain()
 
     # ------------------------------------------------------------ worker
+    @torch.inference_mode()
     def serve(self) -> int:
         """Worker loop: repeat the root's calls until it posts stop; returns the number of calls."""
         assert not self.is_root and self.mailbox is not None
+        import time
+
         calls = 0
+        self.worker_wait_s = 0.0
+        self.worker_handle_s = 0.0
         while True:
+            t0 = time.perf_counter()
             op, payload = self.mailbox.receive()
+            t1 = time.perf_counter()
+            self.worker_wait_s += t1 - t0
             if op == OP_STOP:
                 return calls
             name, kw = payload
             getattr(self, "_w_" + name)(**kw)
+            self.worker_handle_s += time.perf_counter() - t1
             calls += 1
 
     def _w_mirror_new(self, mid: int, capacity: int) -> None:

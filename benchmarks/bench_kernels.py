@@ -135,6 +135,39 @@ def main() -> int:
         w = torch.ones(4096, device="cuda", dtype=dt)
         us = timeit(lambda: ops.rmsnorm(x, w, 1e-5, dt), args.iters)
         report("rmsnorm rows=12 H=4096", us, x.numel() * 6)
+    if args.only in ("all", "chain"):
+        # GEMMs only: 32 layers of (qkv, o + residual, gate/up + SiLU, down + residual) at 8B shapes,
+        # captured in one CUDA graph with PDL -- the weight-streaming ceiling of a forward.
+        llama = pkg("models.llama")
+        cfg = llama.get_config("llama-8b")
+        w = llama.random_weights(cfg, seed=1, dtype=dt, device="cuda")
+        for rows in (1, 12):
+            x = torch.randn(rows, cfg.hidden_size, device="cuda").to(dt)
+            h = torch.zeros(rows, cfg.hidden_size, device="cuda")
+            a = torch.randn(rows, cfg.q_size, device="cuda").to(dt)
+
+            def chain():
+                for lw in w.layers:
+                    ops.linear(x, lw.wqkv)
+                    ops.linear_residual(a, lw.wo, h)
+                    act = ops.gate_up_silu(x, lw.wgu)
+                    ops.linear_residual(act, lw.wd, h)
+
+            chain()
+            g = torch.cuda.CUDAGraph()
+            s_ = torch.cuda.Stream()
+            s_.wait_stream(torch.cuda.current_stream())
+            with torch.cuda.stream(s_):
+                chain()
+                g.capture_begin()
+                chain()
+                g.capture_end()
+            torch.cuda.current_stream().wait_stream(s_)
+            us = timeit(g.replay, max(5, args.iters // 2))
+            nbytes = sum(t.numel() * t.element_size() for lw in w.layers for t in (lw.wqkv, lw.wo, lw.wgu, lw.wd))
+            report(f"gemm chain 8b x32 layers rows={rows}", us, nbytes)
+        del w
+        torch.cuda.empty_cache()
     if args.only in ("all", "forward"):
         import numpy as np
 
