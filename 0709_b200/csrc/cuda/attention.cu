@@ -39,6 +39,11 @@ constexpr int kSmemBytes = kQBytes + kStages * kStageBytes + 2 * kPBytes + 1024 
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kRescaleThreshold = 8.0f;  // log2 units: P stays <= 256 between rescales
 constexpr int kThreadsTC = 192;            // warps 0-3 softmax, 4 TMA, 5 MMA
+// A split covers at least this many pages (4 chunks of 64 keys at page 16):
+// the grid is sized for the longest context a graph may see, and on a short
+// one the surplus splits find no pages and exit instead of each paying the
+// CTA's fixed cost for one chunk and a 64 KB partial round trip.
+constexpr int kMinPagesPerSplit = 16;
 }  // namespace
 
 // Warp-specialized flash attention over the shared key range.
@@ -101,7 +106,7 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
   // written before the chain started, so they are safe to read before the wait).
   const int shared_len = p.dparams[0];
   const int np_total = (shared_len + ps - 1) / ps;
-  const int pps = (np_total + p.splits - 1) / max(p.splits, 1);
+  const int pps = max((np_total + p.splits - 1) / max(p.splits, 1), causal ? 1 : kMinPagesPerSplit);
   const int pb = split * pps;
   const int cp = kChunkKeys / ps;  // pages per chunk
 
@@ -312,9 +317,14 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
           *reinterpret_cast<uint4*>(o + c8 * 8) = *reinterpret_cast<uint4*>(pk);
         }
       } else {
-        float* po = p.part_o + (static_cast<int64_t>(split) * p.M * p.Hq + rowi) * kHd;
+        // A split that saw no key of this row leaves (m, l) = (-inf, 0); the
+        // merge gives it weight 0 and never reads its O.
+        if (l_run > 0.f) {
+          float* po = p.part_o + (static_cast<int64_t>(split) * p.M * p.Hq + rowi) * kHd;
 #pragma unroll
-        for (int i = 0; i < kHd; i += 4) *reinterpret_cast<float4*>(po + i) = make_float4(acc[i], acc[i + 1], acc[i + 2], acc[i + 3]);
+          for (int i = 0; i < kHd; i += 4)
+            *reinterpret_cast<float4*>(po + i) = make_float4(acc[i], acc[i + 1], acc[i + 2], acc[i + 3]);
+        }
         p.part_ml[static_cast<int64_t>(split) * p.M * p.Hq + rowi] = make_float2(m_run, l_run);
       }
     }

@@ -173,7 +173,7 @@ void check_cuda(const torch::Tensor& t, const char* name) {
 // out = epilogue(x @ w^T).  w [M, K] contiguous; x [N, K] with unit inner stride.
 std::vector<int64_t> gemm_impl(const torch::Tensor& w, const torch::Tensor& x, void* out_ptr, int64_t ldo,
                                int64_t epi, const torch::Tensor& err, int64_t force_splits,
-                               const atlas::PeerOut* peer) {
+                               const atlas::PeerOut* peer, const GemmParams* extra = nullptr) {
   check_cuda(w, "w");
   check_cuda(x, "x");
   TORCH_CHECK(w.dim() == 2 && w.is_contiguous(), "w must be contiguous [M, K]");
@@ -197,6 +197,7 @@ std::vector<int64_t> gemm_impl(const torch::Tensor& w, const torch::Tensor& x, v
   CUtensorMap a = map_2d(w, K, M, K, 128);
   CUtensorMap b = map_2d(x, K, N, x.stride(0), bn);
   GemmParams p{};
+  if (extra != nullptr) p = *extra;
   p.M = static_cast<int>(M);
   p.N = static_cast<int>(N);
   p.K = static_cast<int>(K);
@@ -348,6 +349,90 @@ void rmsnorm_fp8(torch::Tensor h, torch::Tensor w, torch::Tensor xq, torch::Tens
                             sa.data_ptr<float>(), static_cast<int>(h.size(0)), static_cast<int>(h.size(1)),
                             static_cast<int>(sa.size(1)), static_cast<float>(eps), w.scalar_type() == torch::kBFloat16,
                             at::cuda::getCurrentCUDAStream());
+}
+
+// --------------------------------------------- GEMM with folded RMSNorm
+// One entry for the epilogues that fold RMSNorm and RoPE into the GEMM:
+//   nin_ss (optional) [K / 128, ld]: per-tile sums of h^2 -> column scale rstd;
+//   kEpiResidualNorm: out = h (fp32, += acc), hb = h in the activation dtype,
+//     nout_ss [M / 128, ld] receives this GEMM's per-tile sums of h^2;
+//   kEpiRope: q_out / kv_layer receive the rotated q/k heads and the v heads.
+std::vector<int64_t> gemm_fused(torch::Tensor w, torch::Tensor x, c10::optional<torch::Tensor> out, int64_t epi,
+                                torch::Tensor err, c10::optional<torch::Tensor> nin_ss, double eps,
+                                c10::optional<torch::Tensor> nout_ss, c10::optional<torch::Tensor> hb,
+                                c10::optional<torch::Tensor> table, c10::optional<torch::Tensor> pos,
+                                c10::optional<torch::Tensor> slots, c10::optional<torch::Tensor> kv_layer,
+                                c10::optional<torch::Tensor> q_out, int64_t Hq, int64_t Hkv) {
+  const int64_t M = w.size(0), K = w.size(1), N = x.size(0);
+  GemmParams ex{};
+  if (nin_ss.has_value()) {
+    TORCH_CHECK(nin_ss->scalar_type() == torch::kFloat32 && nin_ss->is_contiguous() && nin_ss->dim() == 2 &&
+                    nin_ss->size(0) * 128 == K && nin_ss->size(1) >= N,
+                "nin_ss must be fp32 [K / 128, >= N]");
+    ex.nin.ss = nin_ss->data_ptr<float>();
+    ex.nin.tiles = static_cast<int>(nin_ss->size(0));
+    ex.nin.ld = static_cast<int>(nin_ss->size(1));
+    ex.nin.inv_h = 1.0f / static_cast<float>(K);
+    ex.nin.eps = static_cast<float>(eps);
+  }
+  void* out_ptr = nullptr;
+  int64_t ldo = 0;
+  if (epi == atlas::kEpiResidualNorm) {
+    TORCH_CHECK(out.has_value() && nout_ss.has_value() && hb.has_value(), "residual-norm epilogue needs h, hb, ss");
+    TORCH_CHECK(out->scalar_type() == torch::kFloat32 && out->is_contiguous() && out->size(1) == M, "h layout");
+    TORCH_CHECK(hb->scalar_type() == w.scalar_type() && hb->is_contiguous() && hb->size(1) == M, "hb layout");
+    TORCH_CHECK(M % 128 == 0 && nout_ss->scalar_type() == torch::kFloat32 && nout_ss->is_contiguous() &&
+                    nout_ss->size(0) * 128 == M && nout_ss->size(1) >= N,
+                "nout_ss must be fp32 [M / 128, >= N]");
+    ex.nout.ss = nout_ss->data_ptr<float>();
+    ex.nout.ld = static_cast<int>(nout_ss->size(1));
+    ex.nout.hb = hb->data_ptr();
+    out_ptr = out->data_ptr();
+    ldo = out->stride(0);
+  } else if (epi == atlas::kEpiRope) {
+    TORCH_CHECK(table.has_value() && pos.has_value() && slots.has_value() && kv_layer.has_value() &&
+                    q_out.has_value(), "rope epilogue needs table, positions, slots, kv layer and q output");
+    TORCH_CHECK(kv_layer->dim() == 5 && kv_layer->size(4) == 128 && kv_layer->is_contiguous() &&
+                    kv_layer->size(2) == Hkv && kv_layer->scalar_type() == w.scalar_type(),
+                "kv layer must be [pages, 2, Hkv, ps, 128] in the activation dtype");
+    TORCH_CHECK(M == (Hq + 2 * Hkv) * 128 && q_out->is_contiguous() && q_out->numel() >= N * Hq * 128,
+                "rope epilogue: M must be (Hq + 2 Hkv) * 128");
+    TORCH_CHECK(pos->scalar_type() == torch::kInt32 && slots->scalar_type() == torch::kInt32 &&
+                    table->scalar_type() == torch::kFloat32 && table->size(1) == 128, "rope input dtypes");
+    ex.rope.table = table->data_ptr<float>();
+    ex.rope.pos = pos->data_ptr<int>();
+    ex.rope.slots = slots->data_ptr<int>();
+    ex.rope.kv = kv_layer->data_ptr();
+    ex.rope.q = q_out->data_ptr();
+    ex.rope.Hq = static_cast<int>(Hq);
+    ex.rope.Hkv = static_cast<int>(Hkv);
+    ex.rope.ps = static_cast<int>(kv_layer->size(3));
+    ex.rope.num_pages = static_cast<int>(kv_layer->size(0));
+    ex.rope.max_pos = static_cast<int>(table->size(0));
+  } else {
+    TORCH_CHECK(epi == atlas::kEpiStore || epi == atlas::kEpiSilu || epi == atlas::kEpiF32,
+                "gemm_fused: store, SiLU, fp32, residual-norm or rope epilogue");
+    TORCH_CHECK(out.has_value() && out->stride(-1) == 1, "out must have unit inner stride");
+    TORCH_CHECK((epi == atlas::kEpiF32) == (out->scalar_type() == torch::kFloat32), "output dtype vs epilogue");
+    out_ptr = out->data_ptr();
+    ldo = out->stride(0);
+  }
+  return gemm_impl(w, x, out_ptr, ldo, epi, err, 0, nullptr, &ex);
+}
+
+// Embedding gather that also writes the activation-dtype copy and the
+// per-128-feature sums of h^2 that the first folded-norm GEMM needs.
+void embed_norm(torch::Tensor tok, torch::Tensor table, torch::Tensor h, torch::Tensor hb, torch::Tensor ss,
+                torch::Tensor err) {
+  TORCH_CHECK(tok.scalar_type() == torch::kInt32 && h.scalar_type() == torch::kFloat32, "embed dtypes");
+  TORCH_CHECK(table.size(1) % 128 == 0 && ss.size(0) * 128 == table.size(1) && ss.size(1) >= tok.numel(),
+              "ss must be fp32 [H / 128, >= M]");
+  const c10::cuda::CUDAGuard guard(h.device());
+  atlas::launch_embed_norm(tok.data_ptr<int>(), table.data_ptr(), h.data_ptr<float>(), hb.data_ptr(),
+                           ss.data_ptr<float>(), static_cast<int>(ss.size(1)), static_cast<int>(tok.numel()),
+                           static_cast<int>(table.size(1)), static_cast<int>(table.size(0)),
+                           table.scalar_type() == torch::kBFloat16, err.data_ptr<int>(),
+                           at::cuda::getCurrentCUDAStream());
 }
 
 // --------------------------------------------------- tensor parallelism
@@ -571,6 +656,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("kv_move_slots", &kv_move_slots);
   m.def("topk", &topk);
   m.def("gather_logprobs", &gather_logprobs);
+  m.def("gemm_fused", &gemm_fused, "GEMM with folded RMSNorm (residual-norm / rope / scaled epilogues)");
+  m.def("embed_norm", &embed_norm);
+  m.attr("EPI_RESIDUAL_NORM") = static_cast<int>(atlas::kEpiResidualNorm);
+  m.attr("EPI_ROPE") = static_cast<int>(atlas::kEpiRope);
   m.def("gemm_peer", &gemm_peer, "tcgen05 GEMM with the fp32 tile stored into peer buffers, then a release flag");
   m.def("tp_reduce_rmsnorm", &tp_reduce_rmsnorm, "wait for peers, h += sum of partials, x = rmsnorm(h)");
   m.def("tp_wait", &tp_wait);

@@ -24,6 +24,37 @@ __global__ void embed_kernel(const int* __restrict__ tok, const T* __restrict__ 
   for (int i = threadIdx.x; i < H; i += blockDim.x) dst[i] = to_f32(src[i]);
 }
 
+// h = table[token] (fp32), hb = h (activation dtype), ss[t * ss_ld + m] =
+// sum of h^2 over features [128 t, 128 t + 128); one warp per 128 features.
+template <typename T>
+__global__ void embed_norm_kernel(const int* __restrict__ tok, const T* __restrict__ table, float* __restrict__ h,
+                                  T* __restrict__ hb, float* __restrict__ ss, int ss_ld, int H, int V, int* err) {
+  pdl_wait();
+  pdl_trigger();
+  const int m = blockIdx.x;
+  int t = tok[m];
+  if (t < 0 || t >= V) {
+    if (threadIdx.x == 0) set_error(err, kErrBadIndex);
+    t = 0;
+  }
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const T* src = table + static_cast<int64_t>(t) * H;
+  for (int tile = warp; tile < H / 128; tile += blockDim.x >> 5) {
+    const int c = tile * 128 + lane * 4;
+    float sq = 0.f;
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const T v = src[c + e];
+      const float f = to_f32(v);
+      h[static_cast<int64_t>(m) * H + c + e] = f;
+      hb[static_cast<int64_t>(m) * H + c + e] = v;
+      sq += f * f;
+    }
+    sq = warp_sum(sq);
+    if (lane == 0) ss[static_cast<int64_t>(tile) * ss_ld + m] = sq;
+  }
+}
+
 template <typename T>
 __global__ void rmsnorm_kernel(const float* __restrict__ x, const T* __restrict__ w, T* __restrict__ out, int H,
                                float eps) {
@@ -111,6 +142,16 @@ void launch_embed(const int* tok, const void* table, float* out, int M, int H, i
     launch_k(embed_kernel<__nv_bfloat16>, dim3(M), dim3(256), 0, st, tok, static_cast<const __nv_bfloat16*>(table), out, H, V, err);
   else
     launch_k(embed_kernel<__half>, dim3(M), dim3(256), 0, st, tok, static_cast<const __half*>(table), out, H, V, err);
+}
+
+void launch_embed_norm(const int* tok, const void* table, float* h, void* hb, float* ss, int ss_ld, int M, int H, int V,
+                       bool bf16, int* err, cudaStream_t st) {
+  if (bf16)
+    launch_k(embed_norm_kernel<__nv_bfloat16>, dim3(M), dim3(256), 0, st, tok,
+             static_cast<const __nv_bfloat16*>(table), h, static_cast<__nv_bfloat16*>(hb), ss, ss_ld, H, V, err);
+  else
+    launch_k(embed_norm_kernel<__half>, dim3(M), dim3(256), 0, st, tok, static_cast<const __half*>(table), h,
+             static_cast<__half*>(hb), ss, ss_ld, H, V, err);
 }
 
 void launch_rmsnorm(const float* x, const void* w, void* out, int M, int H, float eps, bool bf16, cudaStream_t st) {

@@ -39,6 +39,8 @@ struct GemmSmem {
   static constexpr int kStages = (BN <= 16) ? 6 : (BN <= 32 ? 5 : (BN <= 64 ? 4 : (BN <= 128 ? 4 : 3)));
   static constexpr int kTmemCols = BN < 32 ? 32 : BN;
   static constexpr int kBytes = kStages * kStageBytes + 1024 /*align*/ + 256 /*barriers*/;
+  // Epilogue reuse of the ring: split-K partial tile + exchange + reductions + column scales.
+  static_assert(BN * 128 * 4 + 32 * 64 * 4 + 128 * 4 + BN * 4 <= kStages * kStageBytes, "epilogue scratch");
 };
 
 __device__ __forceinline__ float silu_f(float x) { return x / (1.0f + __expf(-x)); }
@@ -89,6 +91,146 @@ template <typename T>
 __device__ __forceinline__ void store_silu(const GemmParams& p, int m0, int row, int n, float g, float u) {
   const int f = (m0 >> 1) + row;
   if (f < (p.M >> 1)) reinterpret_cast<T*>(p.out)[static_cast<int64_t>(n) * p.ldo + f] = from_f32<T>(silu_f(g) * u);
+}
+
+// Epilogue scratch in shared memory (after the split-K partials).
+struct EpiScratch {
+  float* ex;    // [32 cols][64] pair exchange (gate/up, rotary halves)
+  float* red;   // [4 warps][32 cols] partial sums
+  float* rstd;  // [BN] column norm scales
+};
+
+// Column scales of the folded RMSNorm (all 128 threads; ends with a barrier).
+template <int BN>
+__device__ __forceinline__ void load_rstd(const GemmParams& p, int n0, float* rstd) {
+  if (p.nin.ss != nullptr) {
+    for (int j = threadIdx.x; j < BN; j += 128) {
+      const int n = n0 + j;
+      float acc = 0.f;
+      if (n < p.N)
+        for (int t = 0; t < p.nin.tiles; ++t) acc += p.nin.ss[static_cast<int64_t>(t) * p.nin.ld + n];
+      rstd[j] = rsqrtf(acc * p.nin.inv_h + p.nin.eps);
+    }
+  }
+  __syncthreads();
+}
+
+// Apply epilogue EPI to `cnt` (<= 32) consecutive token columns n_base.. of
+// this CTA's 128-feature tile (thread = feature m0 + tid; v[j] = column j).
+// Every thread of the CTA calls it with the same arguments except v.
+template <int EPI, typename T>
+__device__ __forceinline__ void epi_chunk(const GemmParams& p, int m0, int n_base, int col_off, float (&v)[32],
+                                          int cnt, const EpiScratch& sc) {
+  const int tid = threadIdx.x;
+  const int warp = tid >> 5, lane = tid & 31;
+  if constexpr (EPI == kEpiStore || EPI == kEpiSilu || EPI == kEpiF32 || EPI == kEpiRope) {
+    if (p.nin.ss != nullptr) {
+#pragma unroll
+      for (int j = 0; j < 32; ++j)
+        if (j < cnt) v[j] *= sc.rstd[col_off + j];
+    }
+  }
+  if constexpr (EPI == kEpiSilu) {
+    if (tid >= 64) {
+#pragma unroll
+      for (int j = 0; j < 32; ++j) sc.ex[j * 64 + (tid - 64)] = v[j];
+    }
+    __syncthreads();
+    if (tid < 64) {
+#pragma unroll
+      for (int j = 0; j < 32; ++j)
+        if (j < cnt) store_silu<T>(p, m0, tid, n_base + j, v[j], sc.ex[j * 64 + tid]);
+    }
+    __syncthreads();
+  } else if constexpr (EPI == kEpiResidualNorm) {
+    const int m = m0 + tid;
+    const bool mv = m < p.M;
+    float* hres = reinterpret_cast<float*>(p.out);
+    T* hb = reinterpret_cast<T*>(p.nout.hb);
+#pragma unroll
+    for (int j = 0; j < 32; ++j) {
+      float sq = 0.f;
+      if (j < cnt && mv) {
+        const int64_t idx = static_cast<int64_t>(n_base + j) * p.ldo + m;
+        const float r = hres[idx] + v[j];
+        hres[idx] = r;
+        hb[idx] = from_f32<T>(r);
+        sq = r * r;
+      }
+      sq = warp_sum(sq);
+      if (lane == 0) sc.red[warp * 32 + j] = sq;
+    }
+    __syncthreads();
+    if (tid < cnt)
+      p.nout.ss[static_cast<int64_t>(m0 >> 7) * p.nout.ld + n_base + tid] =
+          (sc.red[tid] + sc.red[32 + tid]) + (sc.red[64 + tid] + sc.red[96 + tid]);
+    __syncthreads();
+  } else if constexpr (EPI == kEpiRope) {
+    const RopeOut& r = p.rope;
+    const int head = m0 >> 7;
+    if (head >= r.Hq + r.Hkv) {
+      // v head: no rotation, append as is.
+      const int vh = head - r.Hq - r.Hkv;
+#pragma unroll
+      for (int j = 0; j < 32; ++j) {
+        if (j >= cnt) continue;
+        const int n = n_base + j;
+        const int slot = r.slots[n];
+        const int page = slot / r.ps, off = slot - page * r.ps;
+        if (slot < 0 || page >= r.num_pages) {
+          set_error(p.err, kErrBadIndex);
+          continue;
+        }
+        T* dst = reinterpret_cast<T*>(r.kv) + ((static_cast<int64_t>(page) * 2 + 1) * r.Hkv + vh) * r.ps * 128 +
+                 off * 128 + tid;
+        *dst = from_f32<T>(v[j]);
+      }
+    } else {
+      if (tid >= 64) {
+#pragma unroll
+        for (int j = 0; j < 32; ++j) sc.ex[j * 64 + (tid - 64)] = v[j];
+      }
+      __syncthreads();
+      if (tid < 64) {
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+          if (j >= cnt) continue;
+          const int n = n_base + j;
+          const int pos = r.pos[n];
+          if (pos < 0 || pos >= r.max_pos) {
+            set_error(p.err, kErrBadIndex);
+            continue;
+          }
+          const float c = r.table[static_cast<int64_t>(pos) * 128 + tid];
+          const float s = r.table[static_cast<int64_t>(pos) * 128 + 64 + tid];
+          const float x1 = v[j], x2 = sc.ex[j * 64 + tid];
+          const float o1 = x1 * c - x2 * s, o2 = x2 * c + x1 * s;
+          T* dst;
+          if (head < r.Hq) {
+            dst = reinterpret_cast<T*>(r.q) + (static_cast<int64_t>(n) * r.Hq + head) * 128;
+          } else {
+            const int slot = r.slots[n];
+            const int page = slot / r.ps, off = slot - page * r.ps;
+            if (slot < 0 || page >= r.num_pages) {
+              set_error(p.err, kErrBadIndex);
+              continue;
+            }
+            dst = reinterpret_cast<T*>(r.kv) +
+                  ((static_cast<int64_t>(page) * 2 + 0) * r.Hkv + (head - r.Hq)) * r.ps * 128 + off * 128;
+          }
+          dst[tid] = from_f32<T>(o1);
+          dst[tid + 64] = from_f32<T>(o2);
+        }
+      }
+      __syncthreads();
+    }
+  } else {
+    if (m0 + tid < p.M) {
+#pragma unroll
+      for (int j = 0; j < 32; ++j)
+        if (j < cnt) store_elem<EPI, T>(p, m0 + tid, n_base + j, v[j]);
+    }
+  }
 }
 
 template <int BN, int EPI, typename T>
@@ -181,10 +323,14 @@ __global__ void __launch_bounds__(128, 1)
 
   const uint32_t lane_base = static_cast<uint32_t>(warp * 32) << 16;
   const int ncols = min(BN, p.N - n0);
+  // Scratch after the (split-K) partial tile: exchange, reductions, column scales.
+  EpiScratch sc;
+  sc.ex = reinterpret_cast<float*>(smem + BN * 128 * 4);
+  sc.red = sc.ex + 32 * 64;
+  sc.rstd = sc.red + 128;
+  load_rstd<BN>(p, n0, sc.rstd);
   if (p.splits == 1) {
-    // No split: TMEM -> registers -> global, 32 token columns at a time
-    // (gate/up pairs meet through shared memory).
-    float* ex = reinterpret_cast<float*>(smem);  // [32 cols][64]
+    // No split: TMEM -> registers -> epilogue, 32 token columns at a time.
     for (int c0 = 0; c0 < ncols; c0 += 32) {
       float v[32];
       if (ok && nk > 0) {
@@ -193,25 +339,7 @@ __global__ void __launch_bounds__(128, 1)
 #pragma unroll
         for (int j = 0; j < 32; ++j) v[j] = 0.f;
       }
-      if constexpr (EPI == kEpiSilu) {
-        if (tid >= 64) {
-#pragma unroll
-          for (int j = 0; j < 32; ++j) ex[j * 64 + (tid - 64)] = v[j];
-        }
-        __syncthreads();
-        if (tid < 64) {
-#pragma unroll
-          for (int j = 0; j < 32; ++j)
-            if (c0 + j < ncols) store_silu<T>(p, m0, tid, n0 + c0 + j, v[j], ex[j * 64 + tid]);
-        }
-        __syncthreads();
-      } else {
-        if (m0 + tid < p.M) {
-#pragma unroll
-          for (int j = 0; j < 32; ++j)
-            if (c0 + j < ncols) store_elem<EPI, T>(p, m0 + tid, n0 + c0 + j, v[j]);
-        }
-      }
+      epi_chunk<EPI, T>(p, m0, n0 + c0, c0, v, min(32, ncols - c0), sc);
     }
     tc_fence_before();
     __syncthreads();
@@ -238,25 +366,16 @@ __global__ void __launch_bounds__(128, 1)
   const int NS = p.splits;
   cluster_sync();
   const uint32_t rank = cluster_ctarank();
+  // CTA `rank` finishes columns rank, rank + NS, ... (one column per pass; all
+  // 128 threads take part, thread = feature).
   for (int c = static_cast<int>(rank); c < ncols; c += NS) {
-    const int n = n0 + c;
-    if constexpr (EPI == kEpiSilu) {
-      if (tid < 64) {
-        float g = 0.f, u = 0.f;
-        for (int s2 = 0; s2 < NS; ++s2) {
-          g += ld_dsmem_f32(part + c * 128 + tid, s2);
-          u += ld_dsmem_f32(part + c * 128 + 64 + tid, s2);
-        }
-        store_silu<T>(p, m0, tid, n, g, u);
-      }
-    } else {
-      const int m = m0 + tid;
-      if (m < p.M) {
-        float acc = 0.f;
-        for (int s2 = 0; s2 < NS; ++s2) acc += ld_dsmem_f32(part + c * 128 + tid, s2);
-        store_elem<EPI, T>(p, m, n, acc);
-      }
-    }
+    float v[32];
+    float acc = 0.f;
+    for (int s2 = 0; s2 < NS; ++s2) acc += ld_dsmem_f32(part + c * 128 + tid, s2);
+    v[0] = acc;
+#pragma unroll
+    for (int j = 1; j < 32; ++j) v[j] = 0.f;
+    epi_chunk<EPI, T>(p, m0, n0 + c, c, v, 1, sc);
   }
   cluster_sync();  // keep every partial alive until all readers are done
   tc_fence_before();
@@ -313,6 +432,8 @@ void launch_gemm_tn(const CUtensorMap& a, const CUtensorMap& b, const GemmParams
       case kEpiResidual: launch_epi<kEpiResidual, __nv_bfloat16>(bn, a, b, p, grid, st); break;
       case kEpiSilu: launch_epi<kEpiSilu, __nv_bfloat16>(bn, a, b, p, grid, st); break;
       case kEpiPeer: launch_epi<kEpiPeer, __nv_bfloat16>(bn, a, b, p, grid, st); break;
+      case kEpiResidualNorm: launch_epi<kEpiResidualNorm, __nv_bfloat16>(bn, a, b, p, grid, st); break;
+      case kEpiRope: launch_epi<kEpiRope, __nv_bfloat16>(bn, a, b, p, grid, st); break;
       default: launch_epi<kEpiF32, __nv_bfloat16>(bn, a, b, p, grid, st); break;
     }
   } else {
@@ -321,6 +442,8 @@ void launch_gemm_tn(const CUtensorMap& a, const CUtensorMap& b, const GemmParams
       case kEpiResidual: launch_epi<kEpiResidual, __half>(bn, a, b, p, grid, st); break;
       case kEpiSilu: launch_epi<kEpiSilu, __half>(bn, a, b, p, grid, st); break;
       case kEpiPeer: launch_epi<kEpiPeer, __half>(bn, a, b, p, grid, st); break;
+      case kEpiResidualNorm: launch_epi<kEpiResidualNorm, __half>(bn, a, b, p, grid, st); break;
+      case kEpiRope: launch_epi<kEpiRope, __half>(bn, a, b, p, grid, st); break;
       default: launch_epi<kEpiF32, __half>(bn, a, b, p, grid, st); break;
     }
   }

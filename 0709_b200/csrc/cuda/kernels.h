@@ -8,6 +8,8 @@ namespace atlas {
 
 void launch_embed(const int* tok, const void* table, float* out, int M, int H, int V, bool bf16, int* err,
                   cudaStream_t st);
+void launch_embed_norm(const int* tok, const void* table, float* h, void* hb, float* ss, int ss_ld, int M, int H, int V,
+                       bool bf16, int* err, cudaStream_t st);
 void launch_rmsnorm(const float* x, const void* w, void* out, int M, int H, float eps, bool bf16, cudaStream_t st);
 void launch_rope_append(const void* qkv, const float* table, const int* pos, const int* slots, void* kv_layer,
                         void* qout, int M, int Hq, int Hkv, int hd, int ps, int num_pages, int max_pos, bool bf16,

@@ -71,6 +71,49 @@ class CudaOps:
         out = torch.empty((x.shape[0], w.shape[0]), dtype=torch.float32, device=x.device)
         return self._gemm(x, w, out, self.ext.EPI_F32)
 
+    # ------------------------------------------------ folded-norm GEMMs
+    # RMSNorm is folded into the GEMMs: the B operand is the residual h in the
+    # activation dtype (``hb``), the norm gain lives in the weight rows, and
+    # the epilogue scales each token column by rstd computed from ``ss``, the
+    # per-128-feature sums of h^2 written by the previous residual epilogue.
+    def embed_norm(self, tokens: torch.Tensor, table: torch.Tensor):
+        m, hdim = tokens.numel(), table.shape[1]
+        h = torch.empty((m, hdim), dtype=torch.float32, device=table.device)
+        hb = torch.empty((m, hdim), dtype=table.dtype, device=table.device)
+        ss = torch.empty((hdim // 128, m), dtype=torch.float32, device=table.device)
+        self.ext.embed_norm(tokens.to(torch.int32), table, h, hb, ss, self.err)
+        counters.launches(1)
+        return h, hb, ss
+
+    def _fused(self, w, x, out, epi, *, ss=None, eps=0.0, ss_out=None, hb=None, rope=None):
+        table = pos = slots = kv = q = None
+        hq = hkv = 0
+        if rope is not None:
+            table, pos, slots, kv, q, hq, hkv = rope
+        self.last_gemm_config = self.ext.gemm_fused(w, x, out, epi, self.err, ss, float(eps), ss_out, hb, table, pos,
+                                                    slots, kv, q, hq, hkv)
+        counters.launches(1)
+
+    def qkv_rope(self, hb, w, ss, eps, table, positions, slots, kv_layer, num_heads, num_kv_heads):
+        q = torch.empty((hb.shape[0], num_heads, 128), dtype=hb.dtype, device=hb.device)
+        self._fused(w, hb, None, self.ext.EPI_ROPE, ss=ss, eps=eps,
+                    rope=(table, positions.to(torch.int32), slots.to(torch.int32), kv_layer, q, num_heads,
+                          num_kv_heads))
+        return q
+
+    def linear_residual_norm(self, x, w, h, hb, ss_out) -> None:
+        self._fused(w, x, h, self.ext.EPI_RESIDUAL_NORM, ss_out=ss_out, hb=hb)
+
+    def gate_up_silu_norm(self, hb, wgu, ss, eps):
+        out = torch.empty((hb.shape[0], wgu.shape[0] // 2), dtype=wgu.dtype, device=hb.device)
+        self._fused(wgu, hb, out, self.ext.EPI_SILU, ss=ss, eps=eps)
+        return out
+
+    def lm_head_norm(self, hb, w, ss, eps):
+        out = torch.empty((hb.shape[0], w.shape[0]), dtype=torch.float32, device=hb.device)
+        self._fused(w, hb, out, self.ext.EPI_F32, ss=ss, eps=eps)
+        return out
+
     # -------------------------------------------------------------- fp8
     @staticmethod
     def _scale_ld(n: int) -> int:

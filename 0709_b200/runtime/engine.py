@@ -16,6 +16,7 @@ SGLang decode forward the drafter uses (fp/flashinfer_backends.py:89-132).
 from __future__ import annotations
 
 import math
+import os
 import threading
 from dataclasses import dataclass
 
@@ -70,6 +71,13 @@ class LlamaEngine:
             else:
                 ops = torch_ops
         self.ops = ops
+        # CUDA: RMSNorm folded into the GEMMs and RoPE + KV append into the QKV
+        # epilogue (needs head_dim 128 and 128-aligned widths).
+        self.fused_norm = (
+            hasattr(ops, "qkv_rope") and c.head_dim == 128 and c.hidden_size % 128 == 0
+            and isinstance(weights, LlamaWeights) and os.environ.get("ATLAS_FUSED_NORM", "1") != "0"
+        )
+        self._folded = self._fold_norms() if self.fused_norm else None
         if hasattr(ops, "reserve_attention_workspace"):
             ops.reserve_attention_workspace(64, c.num_heads, c.num_kv_heads, int(max_positions), self.page_size)
         self.stats = ForwardStats()
@@ -81,6 +89,21 @@ class LlamaEngine:
         self.trash_slot = (self.num_pages - 1) * self.page_size
 
     # ------------------------------------------------------------------
+    def _fold_norms(self):
+        """Weights with the RMSNorm gains multiplied into their input columns.
+
+        With unit gains (random init) the weights are used as they are;
+        otherwise folded copies are made once (the originals are untouched).
+        """
+
+        def fold(wt: torch.Tensor, g: torch.Tensor) -> torch.Tensor:
+            if bool(torch.all(g == 1)):
+                return wt
+            return (wt.float() * g.float()[None, :]).to(wt.dtype).contiguous()
+
+        layers = [(fold(lw.wqkv, lw.attn_norm), fold(lw.wgu, lw.mlp_norm)) for lw in self.w.layers]
+        return layers, fold(self.w.lm_head, self.w.final_norm)
+
     def graph_attention_splits(self, rows: int) -> int | None:
         """Split-KV count baked into a graph: sized for the longest context the engine holds."""
         f = getattr(self.ops, "attention_splits", None)
@@ -183,6 +206,8 @@ class LlamaEngine:
         c = self.cfg
         self.stats.calls += 1
         self.stats.rows += int(tokens.numel())
+        if self.fused_norm:
+            return self._forward_fused(tokens, positions, slots, desc, logits_rows, causal_start)
         h = o.embed(tokens, self.w.embed)
         for li, lw in enumerate(self.w.layers):
             x = o.rmsnorm(h, lw.attn_norm, c.rms_eps, self.dtype)
@@ -202,6 +227,32 @@ class LlamaEngine:
             h = h.index_select(0, logits_rows.long())
         x = o.rmsnorm(h, self.w.final_norm, c.rms_eps, self.dtype)
         return o.lm_head(x, self.w.lm_head)
+
+    def _attend(self, q, li, desc, causal_start):
+        o = self.ops
+        if causal_start is None:
+            return o.attention(q, self.kv[li], desc, self.scale)
+        return o.attention_causal(q, self.kv[li], desc, causal_start, self.scale)
+
+    def _forward_fused(self, tokens, positions, slots, desc, logits_rows, causal_start):
+        """CUDA forward with RMSNorm folded into the GEMMs (no norm or RoPE kernels)."""
+        o = self.ops
+        c = self.cfg
+        layers, lm = self._folded
+        h, hb, ss = o.embed_norm(tokens, self.w.embed)
+        for li, lw in enumerate(self.w.layers):
+            wqkv, wgu = layers[li]
+            q = o.qkv_rope(hb, wqkv, ss, c.rms_eps, self.rope, positions, slots, self.kv[li], c.num_heads,
+                           c.num_kv_heads)
+            a = self._attend(q, li, desc, causal_start)
+            o.linear_residual_norm(a, lw.wo, h, hb, ss)
+            act = o.gate_up_silu_norm(hb, wgu, ss, c.rms_eps)
+            o.linear_residual_norm(act, lw.wd, h, hb, ss)
+        if logits_rows is not None:
+            sel = logits_rows.long()
+            hb = hb.index_select(0, sel)
+            ss = ss.index_select(1, sel).contiguous()
+        return o.lm_head_norm(hb, lm, ss, c.rms_eps)
 
     # ------------------------------------------------------------------
     def prefill_sequence(
