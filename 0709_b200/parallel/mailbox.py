@@ -71,7 +71,10 @@ class Mailbox:
         if create:
             self.words[:] = 0
             self.words[3] = os.getpid()
-        self.seq = int(self.words[0])
+        # Readers start from zero: a message posted before they attached is
+        # still theirs (the writer waits for every reader's acknowledgement
+        # before it overwrites the payload).
+        self.seq = int(self.words[0]) if create else 0
         self.posted = 0
 
     # ------------------------------------------------------------- root
@@ -130,6 +133,16 @@ class Mailbox:
         payload = pickle.loads(bytes(self.mm[PAYLOAD_OFF: PAYLOAD_OFF + n]))
         self.words[HEADER_WORDS + self.rank] = self.seq
         return op, payload
+
+    @classmethod
+    def attach(cls, path: str, *, rank: int, world: int, timeout_s: float = 120.0, **kw) -> "Mailbox":
+        """Wait for the writer to create ``path``, then attach as reader ``rank``."""
+        t0 = time.monotonic()
+        while not (os.path.exists(path) and os.path.getsize(path) > PAYLOAD_OFF):
+            if time.monotonic() - t0 > timeout_s:
+                raise PeerLost(f"mailbox {path} was not created within {timeout_s:.0f} s")
+            time.sleep(0.01)
+        return cls(path, rank=rank, world=world, create=False, **kw)
 
     def close(self) -> None:
         try:

@@ -81,6 +81,7 @@ class LlamaEngine:
         if hasattr(ops, "reserve_attention_workspace"):
             ops.reserve_attention_workspace(64, c.num_heads, c.num_kv_heads, int(max_positions), self.page_size)
         self.stats = ForwardStats()
+        self._run_lock = threading.RLock()
         self.use_graphs = True
         self._static: dict[tuple[int, int, int], StaticBatch] = {}
         self._graphs: dict = {}
@@ -127,6 +128,10 @@ class LlamaEngine:
         ``fields`` are host arrays (see ``StaticBatch.load``); returns fp32 logits
         [real rows, V] (a fresh tensor).  On CPU the eager forward runs instead.
         """
+        with self._run_lock:  # sessions in several threads may share this engine's static inputs
+            return self._run_rows_locked(rows, tail_stride, mask_words, prefix_pages, fields)
+
+    def _run_rows_locked(self, rows, tail_stride, mask_words, prefix_pages, fields):
         sb = self.static_batch(rows, tail_stride, mask_words)
         n = sb.load(**fields)
         desc = sb.desc(prefix_pages)

@@ -114,6 +114,13 @@ class TargetVerifier:
         self._committed_verify_rounds = 0
         self._last_fallback_ar_profile: dict[str, object] | None = None
 
+    def release(self) -> None:
+        """End the session: every page returns to the (possibly shared) pool."""
+        self.seq.clear()
+        self.mirror.host = []
+        self.prefix_token_ids = ()
+        self._prefix_logits = None
+
     # -------------------------------------------------------------- prefill
     def _sync(self) -> None:
         self.mirror.sync(self.seq.prefix_pages())
