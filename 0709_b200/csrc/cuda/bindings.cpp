@@ -441,7 +441,8 @@ void tp_reduce_rmsnorm(int64_t recv, int64_t slot_stride, int64_t flags, int64_t
                        torch::Tensor err) {
   TORCH_CHECK(h.scalar_type() == torch::kFloat32 && h.is_contiguous() && h.dim() == 2, "h must be contiguous fp32");
   const int64_t M = h.size(0), H = h.size(1);
-  TORCH_CHECK(H % 4 == 0 && recv != 0 && (recv & 15) == 0 && slot_stride % 4 == 0, "reduce layout");
+  TORCH_CHECK(H % 32 == 0 && H <= 16384 && recv != 0 && (recv & 15) == 0 && slot_stride % 4 == 0,
+              "reduce layout: H must be a multiple of 32 and at most 16384");
   TORCH_CHECK(nsrc >= 1 && nsrc <= atlas::kMaxPeers, "1..8 sources");
   TORCH_CHECK(gamma.has_value() == x.has_value(), "gamma and x go together");
   bool bf16 = false;

@@ -82,11 +82,11 @@ __device__ __forceinline__ void fp8_peer_signal(const Fp8GemmParams& p) {
   if constexpr (EPI == kEpiPeer) {
     __syncthreads();
     if (threadIdx.x == 0) {
-      __threadfence_system();
+      fence_acq_rel_sys();
       const uint32_t total = gridDim.x * gridDim.y * gridDim.z;
       if (atomicAdd(p.peer.ticket, 1u) == total - 1) {
         *reinterpret_cast<volatile uint32_t*>(p.peer.ticket) = 0u;
-        __threadfence_system();
+        fence_acq_rel_sys();
         const uint32_t s = *reinterpret_cast<volatile uint32_t*>(p.peer.seq) + 1u;
         *reinterpret_cast<volatile uint32_t*>(p.peer.seq) = s;
         for (int r = 0; r < p.peer.ndst; ++r) st_release_sys(p.peer.flag[r], s);

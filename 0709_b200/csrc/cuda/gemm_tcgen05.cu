@@ -68,16 +68,17 @@ template <int EPI>
 __device__ __forceinline__ void peer_signal(const GemmParams& p) {
   if constexpr (EPI == kEpiPeer) {
     // The CTA barrier orders every thread's stores before thread 0's
-    // system-scope fence, which orders them before the ticket (the
-    // cooperative-groups grid-barrier pattern): one fence per CTA.
+    // system-scope release fence, which orders them before the ticket; the
+    // last CTA's acquire-release fence makes all of them visible before the
+    // flags (release/acquire chain; no sequentially consistent fence needed).
     __syncthreads();
     if (threadIdx.x == 0) {
-      __threadfence_system();
+      fence_acq_rel_sys();  // release: this CTA's stores (ordered by the barrier) before the ticket
       const uint32_t total = gridDim.x * gridDim.y * gridDim.z;
       const uint32_t t = atomicAdd(p.peer.ticket, 1u);
       if (t == total - 1) {
         *reinterpret_cast<volatile uint32_t*>(p.peer.ticket) = 0u;
-        __threadfence_system();
+        fence_acq_rel_sys();  // acquire every CTA's release, then release to the peers' flags
         const uint32_t s = *reinterpret_cast<volatile uint32_t*>(p.peer.seq) + 1u;
         *reinterpret_cast<volatile uint32_t*>(p.peer.seq) = s;
         for (int r = 0; r < p.peer.ndst; ++r) st_release_sys(p.peer.flag[r], s);
