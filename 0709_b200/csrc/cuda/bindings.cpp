@@ -231,19 +231,24 @@ std::vector<int64_t> gemm(torch::Tensor w, torch::Tensor x, torch::Tensor out, i
 // number into each destination's flag word.
 std::vector<int64_t> gemm_peer(torch::Tensor w, torch::Tensor x, std::vector<int64_t> dst, int64_t ldo,
                                std::vector<int64_t> flags, int64_t ticket, int64_t seq, torch::Tensor ws,
-                               torch::Tensor counters, torch::Tensor err) {
+                               torch::Tensor counters, torch::Tensor err, bool sentinel) {
   (void)ws;
   (void)counters;
-  TORCH_CHECK(!dst.empty() && dst.size() <= static_cast<size_t>(atlas::kMaxPeers) && dst.size() == flags.size(),
-              "gemm_peer needs 1..8 destinations, one flag each");
+  TORCH_CHECK(!dst.empty() && dst.size() <= static_cast<size_t>(atlas::kMaxPeers) &&
+                  (sentinel || dst.size() == flags.size()),
+              "gemm_peer needs 1..8 destinations, one flag each unless in sentinel mode");
   atlas::PeerOut po{};
   po.ndst = static_cast<int>(dst.size());
+  po.sentinel = sentinel ? 1 : 0;
   for (size_t i = 0; i < dst.size(); ++i) {
-    TORCH_CHECK(dst[i] != 0 && flags[i] != 0 && (dst[i] & 3) == 0 && (flags[i] & 3) == 0, "bad peer address");
+    TORCH_CHECK(dst[i] != 0 && (dst[i] & 3) == 0, "bad peer address");
     po.dst[i] = reinterpret_cast<float*>(dst[i]);
-    po.flag[i] = reinterpret_cast<uint32_t*>(flags[i]);
+    if (!sentinel) {
+      TORCH_CHECK(flags[i] != 0 && (flags[i] & 3) == 0, "bad peer flag address");
+      po.flag[i] = reinterpret_cast<uint32_t*>(flags[i]);
+    }
   }
-  TORCH_CHECK(ticket != 0 && seq != 0, "gemm_peer needs ticket and sequence words");
+  TORCH_CHECK(sentinel || (ticket != 0 && seq != 0), "gemm_peer needs ticket and sequence words");
   po.ticket = reinterpret_cast<uint32_t*>(ticket);
   po.seq = reinterpret_cast<uint32_t*>(seq);
   return gemm_impl(w, x, nullptr, ldo, atlas::kEpiPeer, err, 0, &po);
@@ -438,7 +443,7 @@ void embed_norm(torch::Tensor tok, torch::Tensor table, torch::Tensor h, torch::
 // --------------------------------------------------- tensor parallelism
 void tp_reduce_rmsnorm(int64_t recv, int64_t slot_stride, int64_t flags, int64_t seq, int64_t nsrc, torch::Tensor h,
                        c10::optional<torch::Tensor> gamma, c10::optional<torch::Tensor> x, double eps,
-                       torch::Tensor err) {
+                       torch::Tensor err, bool sentinel) {
   TORCH_CHECK(h.scalar_type() == torch::kFloat32 && h.is_contiguous() && h.dim() == 2, "h must be contiguous fp32");
   const int64_t M = h.size(0), H = h.size(1);
   TORCH_CHECK(H % 32 == 0 && H <= 16384 && recv != 0 && (recv & 15) == 0 && slot_stride % 4 == 0,
@@ -454,7 +459,7 @@ void tp_reduce_rmsnorm(int64_t recv, int64_t slot_stride, int64_t flags, int64_t
   const c10::cuda::CUDAGuard guard(h.device());
   atlas::launch_tp_reduce_rmsnorm(reinterpret_cast<const float*>(recv), slot_stride,
                                   reinterpret_cast<const uint32_t*>(flags), reinterpret_cast<const uint32_t*>(seq),
-                                  static_cast<int>(nsrc), h.data_ptr<float>(),
+                                  static_cast<int>(nsrc), sentinel ? 1 : 0, h.data_ptr<float>(),
                                   gamma.has_value() ? gamma->data_ptr() : nullptr,
                                   x.has_value() ? x->data_ptr() : nullptr, static_cast<int>(M), static_cast<int>(H),
                                   static_cast<float>(eps), bf16, err.data_ptr<int>(), at::cuda::getCurrentCUDAStream());

@@ -48,6 +48,10 @@ struct RopeOut {
 };
 
 constexpr int kMaxPeers = 8;
+// Bit pattern marking an unwritten receive slot: a NaN that IEEE arithmetic
+// on the GPU never produces (its canonical NaN is 0x7fffffff); a computed
+// value with this pattern is stored as the canonical NaN instead.
+constexpr uint32_t kPeerSentinel = 0xffffffffu;
 
 // Destinations of the peer epilogue: the fp32 tile goes to `ndst` buffers
 // (this GPU's or other GPUs' memory, mapped by CUDA IPC), all with row stride
@@ -56,6 +60,7 @@ constexpr int kMaxPeers = 8;
 // destination's flag word for this rank.
 struct PeerOut {
   int ndst;
+  int sentinel;      // 1: receive buffers hold kPeerSentinel until written; no fence, ticket or flags
   float* dst[kMaxPeers];
   uint32_t* flag[kMaxPeers];
   uint32_t* ticket;  // local, zero between launches

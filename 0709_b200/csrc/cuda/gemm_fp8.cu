@@ -65,7 +65,8 @@ __device__ __forceinline__ void fp8_store(const Fp8GemmParams& p, int m, int n, 
     float* r = reinterpret_cast<float*>(p.out);
     r[idx] = r[idx] + v;
   } else if constexpr (EPI == kEpiPeer) {
-    for (int r = 0; r < p.peer.ndst; ++r) p.peer.dst[r][idx] = v;
+    const float w = (__float_as_uint(v) == kPeerSentinel) ? __uint_as_float(0x7fffffffu) : v;
+    for (int r = 0; r < p.peer.ndst; ++r) p.peer.dst[r][idx] = w;
   } else {
     reinterpret_cast<float*>(p.out)[idx] = v;
   }
@@ -80,6 +81,7 @@ __device__ __forceinline__ void fp8_store_silu(const Fp8GemmParams& p, int m0, i
 template <int EPI>
 __device__ __forceinline__ void fp8_peer_signal(const Fp8GemmParams& p) {
   if constexpr (EPI == kEpiPeer) {
+    if (p.peer.sentinel) return;
     __syncthreads();
     if (threadIdx.x == 0) {
       fence_acq_rel_sys();

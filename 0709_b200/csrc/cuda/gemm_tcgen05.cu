@@ -55,7 +55,8 @@ __device__ __forceinline__ void store_elem(const GemmParams& p, int m, int n, fl
     float* r = reinterpret_cast<float*>(p.out);
     r[idx] = r[idx] + v;
   } else if constexpr (EPI == kEpiPeer) {
-    for (int r = 0; r < p.peer.ndst; ++r) p.peer.dst[r][idx] = v;
+    const float w = (__float_as_uint(v) == kPeerSentinel) ? __uint_as_float(0x7fffffffu) : v;
+    for (int r = 0; r < p.peer.ndst; ++r) p.peer.dst[r][idx] = w;
   } else {  // kEpiF32
     reinterpret_cast<float*>(p.out)[idx] = v;
   }
@@ -67,6 +68,7 @@ __device__ __forceinline__ void store_elem(const GemmParams& p, int m, int n, fl
 template <int EPI>
 __device__ __forceinline__ void peer_signal(const GemmParams& p) {
   if constexpr (EPI == kEpiPeer) {
+    if (p.peer.sentinel) return;  // every value is its own arrival flag
     // The CTA barrier orders every thread's stores before thread 0's
     // system-scope release fence, which orders them before the ticket; the
     // last CTA's acquire-release fence makes all of them visible before the

@@ -18,6 +18,7 @@
 
 #include "common.cuh"
 #include "launch.h"
+#include "gemm.h"
 #include "tp.h"
 
 namespace atlas {
@@ -38,11 +39,38 @@ constexpr int kReduceVec = 4;      // float4 per thread kept in registers (H <= 
 // [r H/8, (r+1) H/8), adds the residual and its part of sum(h^2); the 8
 // partial sums meet through distributed shared memory (read in rank order,
 // so every CTA -- and every TP rank -- computes the same rstd).
+// Sentinel mode: poll one float4 of a receive slot until none of its words is
+// the sentinel (bounded by the global timer), then put the sentinel back for
+// the slot's next use.
+__device__ __forceinline__ float4 take_slot(float* ptr, int* err) {
+  float4 v;
+  const uint64_t t0 = global_timer_ns();
+  uint32_t polls = 0;
+  while (true) {
+    asm volatile("ld.volatile.global.v4.f32 {%0, %1, %2, %3}, [%4];"
+                 : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+                 : "l"(ptr)
+                 : "memory");
+    if (__float_as_uint(v.x) != kPeerSentinel && __float_as_uint(v.y) != kPeerSentinel &&
+        __float_as_uint(v.z) != kPeerSentinel && __float_as_uint(v.w) != kPeerSentinel)
+      break;
+    if ((++polls & 63u) == 0) {
+      if (*reinterpret_cast<volatile int*>(err) != 0 || global_timer_ns() - t0 > kPeerWaitNs) {
+        set_error(err, kErrPeerTimeout);
+        break;
+      }
+    }
+  }
+  const float s = __uint_as_float(kPeerSentinel);
+  *reinterpret_cast<float4*>(ptr) = make_float4(s, s, s, s);
+  return v;
+}
+
 template <typename T>
 __global__ void __launch_bounds__(kReduceThreads)
     tp_reduce_rmsnorm_kernel(const float* __restrict__ recv, int64_t slot_stride, const uint32_t* flags,
-                             const uint32_t* seq, int nsrc, float* __restrict__ h, const T* __restrict__ gamma,
-                             T* __restrict__ x, int H, float eps, int* err) {
+                             const uint32_t* seq, int nsrc, int sentinel, float* __restrict__ h,
+                             const T* __restrict__ gamma, T* __restrict__ x, int H, float eps, int* err) {
   __shared__ float red[kReduceThreads / 32];
   __shared__ float part_ss;
   pdl_wait();
@@ -59,13 +87,26 @@ __global__ void __launch_bounds__(kReduceThreads)
   for (int j = 0; j < kReduceVec; ++j) {
     const int i = c0 + (j * kReduceThreads + static_cast<int>(threadIdx.x)) * 4;
     if (i < c0 + chunk) {
-      float4 acc = __ldcg(reinterpret_cast<const float4*>(pr + i));
-      for (int r = 1; r < nsrc; ++r) {
-        const float4 v = __ldcg(reinterpret_cast<const float4*>(pr + r * slot_stride + i));
-        acc.x += v.x;
-        acc.y += v.y;
-        acc.z += v.z;
-        acc.w += v.w;
+      float4 acc;
+      if (sentinel) {
+        float* slot0 = const_cast<float*>(pr) + i;
+        acc = take_slot(slot0, err);
+        for (int r = 1; r < nsrc; ++r) {
+          const float4 v = take_slot(slot0 + r * slot_stride, err);
+          acc.x += v.x;
+          acc.y += v.y;
+          acc.z += v.z;
+          acc.w += v.w;
+        }
+      } else {
+        acc = __ldcg(reinterpret_cast<const float4*>(pr + i));
+        for (int r = 1; r < nsrc; ++r) {
+          const float4 v = __ldcg(reinterpret_cast<const float4*>(pr + r * slot_stride + i));
+          acc.x += v.x;
+          acc.y += v.y;
+          acc.z += v.z;
+          acc.w += v.w;
+        }
       }
       float4 o = *reinterpret_cast<const float4*>(hr + i);
       o.x += acc.x;
@@ -110,8 +151,8 @@ __global__ void tp_wait_kernel(const uint32_t* flags, const uint32_t* seq, int n
 }
 
 void launch_tp_reduce_rmsnorm(const float* recv, int64_t slot_stride, const uint32_t* flags, const uint32_t* seq,
-                              int nsrc, float* h, const void* gamma, void* x, int M, int H, float eps, bool bf16,
-                              int* err, cudaStream_t st) {
+                              int nsrc, int sentinel, float* h, const void* gamma, void* x, int M, int H, float eps,
+                              bool bf16, int* err, cudaStream_t st) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(kReduceCluster, M);
   cfg.blockDim = dim3(kReduceThreads);
@@ -126,10 +167,10 @@ void launch_tp_reduce_rmsnorm(const float* recv, int64_t slot_stride, const uint
   cfg.attrs = attr;
   cfg.numAttrs = 2;
   if (bf16)
-    cudaLaunchKernelEx(&cfg, tp_reduce_rmsnorm_kernel<__nv_bfloat16>, recv, slot_stride, flags, seq, nsrc, h,
+    cudaLaunchKernelEx(&cfg, tp_reduce_rmsnorm_kernel<__nv_bfloat16>, recv, slot_stride, flags, seq, nsrc, sentinel, h,
                        static_cast<const __nv_bfloat16*>(gamma), static_cast<__nv_bfloat16*>(x), H, eps, err);
   else
-    cudaLaunchKernelEx(&cfg, tp_reduce_rmsnorm_kernel<__half>, recv, slot_stride, flags, seq, nsrc, h,
+    cudaLaunchKernelEx(&cfg, tp_reduce_rmsnorm_kernel<__half>, recv, slot_stride, flags, seq, nsrc, sentinel, h,
                        static_cast<const __half*>(gamma), static_cast<__half*>(x), H, eps, err);
 }
 

@@ -9,9 +9,11 @@ namespace atlas {
 // h[M, H] += sum over nsrc slots of recv[slot * slot_stride + m * H + i] (rank
 // order), after waiting for flags[0..nsrc) >= *seq when flags != nullptr;
 // then x = rmsnorm(h) * gamma unless gamma == nullptr.
+// sentinel != 0: no flags; each float4 of a slot is polled until it holds no
+// sentinel word, then reset to the sentinel (see PeerOut::sentinel).
 void launch_tp_reduce_rmsnorm(const float* recv, int64_t slot_stride, const uint32_t* flags, const uint32_t* seq,
-                              int nsrc, float* h, const void* gamma, void* x, int M, int H, float eps, bool bf16,
-                              int* err, cudaStream_t st);
+                              int nsrc, int sentinel, float* h, const void* gamma, void* x, int M, int H, float eps,
+                              bool bf16, int* err, cudaStream_t st);
 void launch_tp_wait(const uint32_t* flags, const uint32_t* seq, int nsrc, int* err, cudaStream_t st);
 
 }  // namespace atlas

@@ -94,8 +94,18 @@ def run_root(args, eng, cfg, device, dtype, pages, ctx) -> dict[str, object]:
     from ..serving.rpc import InProcessTargetClient
 
     world = eng.tp.world
-    ref = LlamaEngine(random_weights(cfg, seed=args.seed + 1, dtype=dtype, device=device), num_pages=pages,
-                      page_size=args.page_size, max_positions=ctx + 64)
+    # The single-GPU reference runs the same unfused layer (separate RMSNorm and
+    # RoPE kernels) as the TP engine, so the comparison isolates the parallelism.
+    prev = os.environ.get("ATLAS_FUSED_NORM")
+    os.environ["ATLAS_FUSED_NORM"] = "0"
+    try:
+        ref = LlamaEngine(random_weights(cfg, seed=args.seed + 1, dtype=dtype, device=device), num_pages=pages,
+                          page_size=args.page_size, max_positions=ctx + 64)
+    finally:
+        if prev is None:
+            os.environ.pop("ATLAS_FUSED_NORM", None)
+        else:
+            os.environ["ATLAS_FUSED_NORM"] = prev
     kw = dict(k=args.k, d=args.d, fallback_threshold=args.fallback_threshold)
     tv_tp, tv_ref = TargetVerifier(eng, **kw), TargetVerifier(ref, **kw)
     g = torch.Generator().manual_seed(args.seed)

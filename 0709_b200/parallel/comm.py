@@ -9,15 +9,18 @@ root" (once per forward):
     One symmetric buffer per rank (plain ``cudaMalloc``, mapped into every
     peer by CUDA IPC; no NVLink multicast objects).  The row-parallel GEMM's
     epilogue stores its fp32 partial tile straight into slot ``rank`` of every
-    rank's receive buffer over NVLink and, once the whole grid is done,
-    release-stores a sequence number into each rank's flag word.  The next
-    kernel (``tp_reduce_rmsnorm``) waits for all ranks' flags (bounded),
-    sums the slots in rank order -- bit-identical on every rank -- adds the
-    residual and applies the following RMSNorm.  The LM head's epilogue
-    stores each rank's vocabulary slice into the root's logits buffer.
-    Receive buffers alternate between two parities (o_proj, down_proj): a rank
-    can only reuse a parity after every peer has passed the other parity's
-    wait, which orders it after their reads of the previous use.
+    rank's receive buffer over NVLink.  Receive slots hold a sentinel NaN
+    pattern until written, so each value is its own arrival flag and the
+    producer needs no fence: the next kernel (``tp_reduce_rmsnorm``) polls
+    every float4 of every slot (bounded wait), restores the sentinel, sums the
+    slots in rank order -- bit-identical on every rank -- adds the residual
+    and applies the following RMSNorm.  The LM head's epilogue stores each
+    rank's vocabulary slice into the root's logits buffer and raises a
+    sequence flag per rank (release/acquire at system scope); the root waits
+    on the flags.  Receive buffers alternate between two sets (o_proj,
+    down_proj): a rank writes a set again only after every peer has consumed
+    the other set, which follows their consumption (and sentinel reset) of
+    the set's previous use.
     Rows beyond ``max_rows`` (prefill chunks) take the NCCL path.
 ``nccl`` (CUDA, the baseline)
     GEMM into a local fp32 buffer, ``all_reduce`` / ``all_gather`` on the
@@ -105,6 +108,11 @@ class TPGroup:
         dist.barrier(group=self.group)
         self.logits_buf = self.ext.wrap_ptr(self.base + self.logits_off, [self.max_rows, self.vocab], torch.float32,
                                             dev)
+        # Receive slots start as the sentinel (all-ones words); readers restore it after each use.
+        recv = self.ext.wrap_ptr(self.base + RECV_OFF, [self.recv_bytes // 4], torch.int32, dev)
+        recv.fill_(-1)
+        torch.cuda.synchronize(self.device)
+        dist.barrier(group=self.group)
 
     def close(self) -> None:
         if self.mode == "fused" and self.base:
@@ -144,19 +152,16 @@ class TPGroup:
         x = torch.empty((m, hid), dtype=a.dtype, device=a.device)
         if self.mode == "fused" and m <= self.max_rows:
             dst = [self._recv(self.peers[p], site, self.rank) for p in range(self.world)]
-            flags = [self._flag(self.peers[p], site, self.rank) for p in range(self.world)]
-            self.ext.gemm_peer(w, a, dst, hid, flags, self.base + TICKET_OFF + 4 * site, self.base + SEQ_OFF + 4 * site,
-                               ops.ws, ops.counters, self.err)
-            self.ext.tp_reduce_rmsnorm(self._recv(self.base, site, 0), self.max_rows * hid,
-                                       self._flag(self.base, site, 0), self.base + SEQ_OFF + 4 * site, self.world, h,
-                                       gamma, x, float(eps), self.err)
+            self.ext.gemm_peer(w, a, dst, hid, [], 0, 0, ops.ws, ops.counters, self.err, True)
+            self.ext.tp_reduce_rmsnorm(self._recv(self.base, site, 0), self.max_rows * hid, 0, 0, self.world, h,
+                                       gamma, x, float(eps), self.err, True)
             _count(2)
             return x
         part = torch.empty((m, hid), dtype=torch.float32, device=a.device)
         ops._gemm(a, w, part, self.ext.EPI_F32)
         if self.world > 1:
             dist.all_reduce(part, group=self.group)
-        self.ext.tp_reduce_rmsnorm(part.data_ptr(), 0, 0, 0, 1, h, gamma, x, float(eps), self.err)
+        self.ext.tp_reduce_rmsnorm(part.data_ptr(), 0, 0, 0, 1, h, gamma, x, float(eps), self.err, False)
         _count(1)
         return x
 
@@ -175,7 +180,7 @@ class TPGroup:
             root = self.peers[self.root]
             self.ext.gemm_peer(w, x, [root + self.logits_off + self.rank * v * 4], self.vocab,
                                [self._flag(root, SITE_LOGITS, self.rank)], self.base + TICKET_OFF + 4 * SITE_LOGITS,
-                               self.base + SEQ_OFF + 4 * SITE_LOGITS, ops.ws, ops.counters, self.err)
+                               self.base + SEQ_OFF + 4 * SITE_LOGITS, ops.ws, ops.counters, self.err, False)
             _count(1)
             if not self.is_root:
                 return None

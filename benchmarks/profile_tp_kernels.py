@@ -54,11 +54,19 @@ def main() -> int:
     dst = [recv.data_ptr() + r * slot * 4 for r in range(tp)]
     flags = [base + 4 * r for r in range(tp)]
 
+    recv.view(torch.int32).fill_(-1)  # sentinel: every slot unwritten
+
     def fused_gemm():
-        ext.gemm_peer(w, a, dst, H, flags, base + 4 * 512, base + 4 * 513, ops.ws, ops.counters, ops.err)
+        ext.gemm_peer(w, a, dst, H, [], 0, 0, ops.ws, ops.counters, ops.err, True)
 
     def fused_reduce():
-        ext.tp_reduce_rmsnorm(recv.data_ptr(), slot, base, base + 4 * 513, tp, h, gamma, x, 1e-5, ops.err)
+        ext.tp_reduce_rmsnorm(recv.data_ptr(), slot, 0, 0, tp, h, gamma, x, 1e-5, ops.err, True)
+
+    def flag_gemm():
+        ext.gemm_peer(w, a, dst, H, flags, base + 4 * 512, base + 4 * 513, ops.ws, ops.counters, ops.err, False)
+
+    def flag_reduce():
+        ext.tp_reduce_rmsnorm(recv.data_ptr(), slot, base, base + 4 * 513, tp, h, gamma, x, 1e-5, ops.err, False)
 
     part = torch.empty(m, H, device="cuda")
 
@@ -66,19 +74,25 @@ def main() -> int:
         ops._gemm(a, w, part, ext.EPI_F32)
 
     def plain_reduce():
-        ext.tp_reduce_rmsnorm(part.data_ptr(), 0, 0, 0, 1, h, gamma, x, 1e-5, ops.err)
+        ext.tp_reduce_rmsnorm(part.data_ptr(), 0, 0, 0, 1, h, gamma, x, 1e-5, ops.err, False)
 
+    ref = a.float() @ w.float().t()
+    fused_gemm()
+    torch.cuda.synchronize()
+    got = recv[:, :m].sum(0) / tp
+    err = float((got - ref).abs().max())
+    fused_reduce()
+    torch.cuda.synchronize()
+    assert bool((recv.view(torch.int32) == -1).all()), "reduce must restore the sentinel"
     for _ in range(args.reps):
         fused_gemm()
         fused_reduce()
     torch.cuda.synchronize()
     ops.check()
-    ref = a.float() @ w.float().t()
-    got = recv[:, :m].sum(0) / tp
-    err = float((got - ref).abs().max())
     out = {"tp": tp, "rows": m, "H": H, "K": K, "max_abs_err_vs_fp32": err,
-           "gemm_peer_us": round(timeit(fused_gemm, 20), 2), "reduce_rmsnorm_tp_us": round(timeit(fused_reduce, 20), 2),
-           "gemm_f32_us": round(timeit(plain_gemm, 20), 2), "reduce_rmsnorm_1src_us": round(timeit(plain_reduce, 20), 2),
+           "sentinel_gemm_peer_plus_reduce_us": round(timeit(lambda: (fused_gemm(), fused_reduce()), 20), 2),
+           "gemm_peer_flags_plus_reduce_us": round(timeit(lambda: (flag_gemm(), flag_reduce()), 20), 2),
+           "gemm_f32_plus_reduce_1src_us": round(timeit(lambda: (plain_gemm(), plain_reduce()), 20), 2),
            "weight_bytes": H * K * 2, "push_bytes_per_rank": (tp - 1) * m * H * 4}
     print(json.dumps(out), flush=True)
     return 0
