@@ -56,9 +56,15 @@ class TPLlamaEngine(LlamaEngine):
         layers = self.w.layers
         h = o.embed(tokens, self.w.embed)
         x = o.rmsnorm(h, layers[0].attn_norm, c.rms_eps, self.dtype)
+        fuse_rope = hasattr(o, "qkv_rope") and c.head_dim == 128
         for li, lw in enumerate(layers):
-            qkv = o.linear(x, lw.wqkv)
-            q = o.rope_qkv_append(qkv, self.rope, positions, slots, self.kv[li], c.num_heads, c.num_kv_heads)
+            if fuse_rope:
+                # RoPE + KV append in the QKV GEMM epilogue (x is already normalized: no rstd scaling).
+                q = o.qkv_rope(x, lw.wqkv, None, 0.0, self.rope, positions, slots, self.kv[li], c.num_heads,
+                               c.num_kv_heads)
+            else:
+                qkv = o.linear(x, lw.wqkv)
+                q = o.rope_qkv_append(qkv, self.rope, positions, slots, self.kv[li], c.num_heads, c.num_kv_heads)
             if causal_start is not None and hasattr(o, "attention_causal"):
                 a = o.attention_causal(q, self.kv[li], desc, causal_start, self.scale)
             else:

@@ -1,0 +1,61 @@
+"""Benchmark helpers and the edge timeline on CPU."""
+
+from __future__ import annotations
+
+import importlib.util
+import json
+import os
+
+import torch
+
+from conftest import REPO, mod
+
+
+def _load(name):
+    spec = importlib.util.spec_from_file_location(name, os.path.join(REPO, "benchmarks", f"{name}.py"))
+    m = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(m)
+    return m
+
+
+def test_matched_batch_ar_keeps_each_routes_greedy_child():
+    bench = _load("bench_isolated_components")
+    llama, engine, drafter = mod("models.llama"), mod("runtime.engine"), mod("runtime.drafter")
+    store_mod, builders, frontier = mod("runtime.store"), mod("runtime.builders"), mod("runtime.frontier")
+    w = llama.random_weights(llama.get_config("tiny-drafter"), seed=1, dtype=torch.float32)
+    dr = drafter.DrafterRuntime(engine.LlamaEngine(w, num_pages=256, page_size=4, max_positions=256))
+    store = store_mod.KVTreeStore()
+    dr.bind_store(store)
+    prompt = list(range(30, 45))
+    dr.prefill(prompt)
+    routes = builders.initialize_stage1_routes(dr.prefix_state(), k=3, route_store=store)
+    firsts = [r.pending_token_id for r in routes]
+    for _ in range(3):
+        routes = frontier.advance_frontier_one_token(routes, k=1, route_store=store, model_backend=dr,
+                                                     selection_policy=bench.PerRouteTop1Selection()).next_routes
+    assert len(routes) == 3
+    for r, f in zip(routes, firsts):
+        path = list(store.materialized_token_path(r)) + [r.pending_token_id]
+        toks = prompt + [f]
+        for _ in range(3):
+            toks.append(int(llama.reference_forward(w, toks)[-1].argmax()))
+        assert path == toks[len(prompt):]
+
+
+def test_timeline_overlap_exposed_wait_json_and_svg(tmp_path):
+    tl = mod("utils.timeline")
+    S = tl.EdgeSpan
+    r = tl.EdgeRoundTimeline(
+        round_index=0, verify_blackbox=S("verify", 0.0, 0.030),
+        forest_steps=[S("forest_1", 0.001, 0.008), S("forest_2", 0.008, 0.020)],
+        post_prune_tree_steps=[], handoff=S("handoff", 0.030, 0.032), forest_depth=2, accepted_tokens=4,
+        generated_tokens=4, handoff_mode="completed_forest_reused", verify_returned_before_forest_done=False)
+    assert abs(r.cloud_edge_overlap_s - 0.019) < 1e-12 and abs(r.exposed_cloud_wait_s - 0.010) < 1e-12
+    t = tl.EdgeBlackboxTimeline(edge_prefill=S("p", 0, 0.01), cloud_prefill_blackbox=S("c", 0, 0.02),
+                                initial_tree=S("t", 0.02, 0.03), rounds=[r], elapsed_s=0.1, generated_tokens=4)
+    s = t.summary()
+    assert s["rounds"] == 1 and abs(s["cloud_hidden_ratio"] - 0.019 / 0.030) < 1e-9
+    tl.write_timeline_json(tmp_path / "t.json", t)
+    tl.write_timeline_svg(tmp_path / "t.svg", t, width=800)
+    assert json.loads((tmp_path / "t.json").read_text())["summary"]["rounds"] == 1
+    assert (tmp_path / "t.svg").read_text().startswith("<svg")
