@@ -9,6 +9,7 @@
 #include <cudaTypedefs.h>
 #include <torch/extension.h>
 
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
 #include <unordered_map>
@@ -136,9 +137,16 @@ int pick_bn(int64_t n) {
   return 256;
 }
 
+// CTA slots per SM the split-K heuristic fills.  ATLAS_GEMM_CTAS_PER_SM=1 leaves
+// half of each SM free so the next kernel (PDL) can become resident and start
+// its prologue and weight prefetch while this one drains.
 int ctas_per_sm(int bn) {
+  static const int cap = [] {
+    const char* v = std::getenv("ATLAS_GEMM_CTAS_PER_SM");
+    return v != nullptr ? std::max(1, std::atoi(v)) : 2;
+  }();
   const int smem = atlas::gemm_smem_bytes(bn) + 1024;
-  return std::max(1, std::min(2, (228 * 1024) / smem));
+  return std::max(1, std::min(cap, (228 * 1024) / smem));
 }
 
 // Split-K factor: fill ~all CTA slots when the tile count alone cannot; a

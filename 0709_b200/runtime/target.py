@@ -161,7 +161,10 @@ class TargetVerifier:
         eos_token_id: int | None = None,
         route_sampling_seed: int | None = None,
         route_sampling_round: int | None = None,
+        on_decision=None,
     ) -> TargetVerifyResult:
+        """Verify the routes; ``on_decision(decision)`` (optional) is called as soon as the
+        decision is known, before the fallback AR tokens are generated or the path is committed."""
         prefix = tuple(int(t) for t in prefix_token_ids)
         if self._prefix_logits is None:
             self.prefill(prefix)
@@ -204,6 +207,8 @@ class TargetVerifier:
                 None if best.first_token_logprob is None else float(best.first_token_logprob)
             ),
         }
+        if on_decision is not None:
+            on_decision("fallback_ar" if reason is not None else "select")
         if reason is not None:
             limit = self.fallback_ar_tokens if fallback_max_tokens is None else min(
                 int(fallback_max_tokens), self.fallback_ar_tokens

@@ -18,6 +18,7 @@ round traces, result JSON, handoff modes, timeline, warmup and CLI flags).
 from __future__ import annotations
 
 import math
+import threading
 import time
 from concurrent.futures import ThreadPoolExecutor
 from dataclasses import dataclass, field
@@ -235,7 +236,10 @@ class PagedDistributedAtlasGenerator:
                 return r
         raise KeyError(f"selected route_id={route_id} is not in the completed stage1 routes")
 
-    def _verify_call(self, committed, routes, remaining, round_index):
+    def _verify_call(self, committed, routes, remaining, round_index, fallback_event=None):
+        kw = {}
+        if fallback_event is not None and getattr(self.target_client, "supports_early_decision", False):
+            kw["on_decision"] = lambda decision: fallback_event.set() if decision == "fallback_ar" else None
         resp = self.target_client.verify(
             prefix_token_ids=committed,
             routes=routes,
@@ -244,6 +248,7 @@ class PagedDistributedAtlasGenerator:
             eos_token_id=self.config.eos_token_id,
             route_sampling_seed=int(self.config.generation_seed),
             route_sampling_round=int(round_index),
+            **kw,
         )
         return resp, self._now()
 
@@ -453,7 +458,11 @@ class AtlasSession:
         payload = g._route_payloads(store, self.stage1.completed_routes)
         v_submit = g._now()
         remaining = cfg.max_new_tokens - len(generated)
-        vfut = g._vpool.submit(g._verify_call, list(committed), payload, remaining, self.round_index)
+        # Set by the target (in-process transports) once it has decided to fall back:
+        # the forest of this round is then discarded, so growing it further would
+        # only compete with the target's AR forwards.
+        fb_decided = threading.Event()
+        vfut = g._vpool.submit(g._verify_call, list(committed), payload, remaining, self.round_index, fb_decided)
         if self.round_index == 0 and self.pre_frontier is not None:
             f_depth, f_done, f_logits = self.pre_depth, self.pre_completed, self.pre_logits
             f_spans, f_front = list(self.pre_spans), self.pre_frontier
@@ -462,7 +471,7 @@ class AtlasSession:
             f_front = initialize_forest_routes(
                 self.stage1.completed_routes, self.stage1.last_logits, k=cfg.k, route_store=store, sampling=rs
             )
-        while g._should_build_forest_step(verify_done=vfut.done(), forest_depth=f_depth):
+        while g._should_build_forest_step(verify_done=vfut.done() or fb_decided.is_set(), forest_depth=f_depth):
             t0 = g._now()
             st = build_forest_one_depth(f_front, k=cfg.k, route_store=store, model_backend=g.drafter, sampling=rs)
             f_depth += 1

@@ -133,9 +133,15 @@ class TargetServerApp:
 
 @dataclass
 class InProcessTargetClient:
-    """Target client with the generator interface, without HTTP or JSON encoding."""
+    """Target client with the generator interface, without HTTP or JSON encoding.
+
+    It reports the verify decision early (``on_decision``), before the target
+    runs its fallback AR, so the generator can stop speculative forest work
+    that a fallback round discards anyway.
+    """
 
     backend: Any
+    supports_early_decision = True
 
     def health(self) -> dict[str, object]:
         return {
@@ -150,7 +156,8 @@ class InProcessTargetClient:
         return {"ok": True, "prompt_len": int(st.committed_length), "metadata": dict(st.metadata)}
 
     def verify(self, *, prefix_token_ids, routes, fallback_max_tokens=None, selected_path_max_tokens=None,
-               eos_token_id=None, route_sampling_seed=None, route_sampling_round=None) -> dict[str, object]:
+               eos_token_id=None, route_sampling_seed=None, route_sampling_round=None,
+               on_decision=None) -> dict[str, object]:
         result = self.backend.verify_payloads(
             prefix_token_ids=prefix_token_ids,
             routes=[verify_payload_from_mapping(dict(r)) for r in routes],
@@ -159,6 +166,7 @@ class InProcessTargetClient:
             eos_token_id=eos_token_id,
             route_sampling_seed=route_sampling_seed,
             route_sampling_round=route_sampling_round,
+            on_decision=on_decision,
         )
         return {"ok": True, **target_verify_result_to_dict(result)}
 

@@ -66,6 +66,8 @@ def parse() -> argparse.Namespace:
     p.add_argument("--fallback-ar-tokens", type=int, default=4)
     p.add_argument("--seed", type=int, default=0)
     p.add_argument("--e2e-prompts", type=int, default=1)
+    p.add_argument("--target-stream-priority", type=int, default=-1,
+                   help="CUDA priority of the target's stream (lower = higher; 0 = same as the drafter)")
     return p.parse_args()
 
 
@@ -94,6 +96,8 @@ def make_prompts(args, rank: int) -> list[list[int]]:
 
 class StreamTargetClient:
     """In-process target client whose calls run on the target's own CUDA stream."""
+
+    supports_early_decision = True
 
     def __init__(self, backend, stream) -> None:
         rpc = _pkg("serving.rpc")
@@ -148,7 +152,9 @@ def build(args, device):
         fallback_ar_tokens=args.fallback_ar_tokens,
         model_name=f"random-init {args.target}",
     )
-    client = StreamTargetClient(tv, torch.cuda.Stream(device=device))
+    # The target is on the critical path of every round (verify, then fallback AR);
+    # the drafter's forest only fills the wait, so the target stream gets priority.
+    client = StreamTargetClient(tv, torch.cuda.Stream(device=device, priority=args.target_stream_priority))
     dr = drafter_mod.DrafterRuntime(de)
     dr.warm_graphs(args.k, args.fallback_ar_tokens)
     tv.warm_graphs()
@@ -174,6 +180,7 @@ class Driver:
         self.rounds = 0
         self.fallback_rounds = 0
         self.prompts_started = 0
+        self.breakdown: list[tuple[float, float, float, float]] = []  # round, verify, forest, handoff (s)
 
     def step(self) -> int:
         if self.session is None or self.session.finished:
@@ -181,7 +188,14 @@ class Driver:
             self.next += 1
             self.prompts_started += 1
             self.session = self.gen.start(p)
+        t0 = time.perf_counter()
         tr = self.session.step()
+        dt = time.perf_counter() - t0
+        rt = self.session.rounds_tl[-1]
+        forest = sum(sp.elapsed_s for sp in rt.forest_steps)
+        handoff = (rt.handoff.elapsed_s if rt.handoff is not None else 0.0) + sum(
+            sp.elapsed_s for sp in rt.post_prune_tree_steps)
+        self.breakdown.append((dt, rt.verify_blackbox.elapsed_s, forest, handoff))
         self.rounds += 1
         self.fallback_rounds += int(tr.decision == "fallback_ar")
         return len(tr.committed_tokens)
@@ -312,6 +326,10 @@ def main() -> int:
                 "step": "one speculative round (verify || forest, handoff); next prompt's prefill inside its step",
                 "l2": "weights (~17 GB) stream every step; working set far above L2",
                 "rounds_timed": drv.rounds - r0,
+                "round_breakdown_ms": {
+                    k: round(1e3 * sum(b[i] for b in drv.breakdown[r0:]) / max(1, drv.rounds - r0), 3)
+                    for i, k in enumerate(("round_host", "target_verify_blackbox", "drafter_forest", "drafter_handoff"))
+                },
                 "fallback_rate_timed": round((drv.fallback_rounds - f0) / max(1, drv.rounds - r0), 3),
                 "tokens_timed": int(total_tokens),
             },
