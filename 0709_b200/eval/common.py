@@ -1,0 +1,150 @@
+"""Shared pieces of the evaluation drivers: JSONL I/O with resume, generator construction."""
+
+from __future__ import annotations
+
+import hashlib
+import json
+import math
+import time
+from pathlib import Path
+from typing import Any, Iterable, Mapping, Sequence
+
+import torch
+
+
+def read_jsonl(path: str | Path) -> list[dict[str, Any]]:
+    out = []
+    with Path(path).open(encoding="utf-8") as f:
+        for n, line in enumerate(f, 1):
+            if line.strip():
+                try:
+                    out.append(json.loads(line))
+                except json.JSONDecodeError as exc:
+                    raise RuntimeError(f"{path}:{n}: invalid JSON: {exc}") from exc
+    return out
+
+
+def append_jsonl(path: str | Path, row: Mapping[str, Any]) -> None:
+    p = Path(path)
+    p.parent.mkdir(parents=True, exist_ok=True)
+    with p.open("a", encoding="utf-8") as f:
+        f.write(json.dumps(row, ensure_ascii=False, sort_keys=True) + "\n")
+
+
+def done_indices(path: str | Path) -> set[int]:
+    p = Path(path)
+    return {int(r["index"]) for r in read_jsonl(p)} if p.exists() else set()
+
+
+def token_ids_sha256(ids: Sequence[int]) -> str:
+    return hashlib.sha256(json.dumps([int(t) for t in ids], separators=(",", ":")).encode()).hexdigest()
+
+
+def optional_float(v: str) -> float | None:
+    if v.strip().lower() in {"none", "off", "disabled"}:
+        return None
+    x = float(v)
+    if not math.isfinite(x):
+        raise ValueError("value must be finite or none/off/disabled")
+    return x
+
+
+def add_generation_flags(p) -> None:
+    p.add_argument("--backend", choices=["ar", "atlas", "atlas_serial"], required=True)
+    p.add_argument("--model", required=True, help="AR model, or the ATLAS drafter (preset or checkpoint dir)")
+    p.add_argument("--target-model", default=None, help="in-process target (preset or checkpoint dir)")
+    p.add_argument("--target-url", default=None, help="remote target server (HTTP)")
+    p.add_argument("--tokenizer", default=None, help="tokenizer.json or its directory (bytes if absent)")
+    p.add_argument("--max-new-tokens", type=int, default=512)
+    p.add_argument("--eos-token-id", type=int, default=None)
+    p.add_argument("--dtype", choices=["float16", "bfloat16", "float32"], default="float16")
+    p.add_argument("--page-size", type=int, default=16)
+    p.add_argument("--context-length", type=int, default=4096)
+    p.add_argument("--k", type=int, default=3)
+    p.add_argument("--d", type=int, default=4)
+    p.add_argument("--path-score-weights", default="0.45,0.30,0.17,0.08")
+    p.add_argument("--fallback-threshold", type=optional_float, default=-0.5)
+    p.add_argument("--first-token-threshold", type=optional_float, default=-0.7)
+    p.add_argument("--fallback-ar-tokens", type=int, default=4)
+    p.add_argument("--route-selection-policy", choices=["target_best", "target_sample", "first_route"],
+                   default="target_best")
+    p.add_argument("--generation-seed", type=int, default=0)
+    p.add_argument("--seed", type=int, default=0, help="seed of random-init presets")
+    p.add_argument("--device", default=None)
+    p.add_argument("--resume", action="store_true")
+
+
+def make_generate(args):
+    """Return ``generate(prompt_ids) -> (token ids, metadata, rounds)`` for the chosen backend."""
+    from ..models.loader import resolve_model
+    from ..runtime.drafter import DrafterRuntime
+    from ..runtime.engine import LlamaEngine
+
+    dev = torch.device(args.device or ("cuda" if torch.cuda.is_available() else "cpu"))
+    ctx = int(args.context_length) + int(args.max_new_tokens) + 8 * args.k * args.d + 64
+    pages = 2 * math.ceil(ctx / args.page_size) + 64
+
+    def engine(spec, seed):
+        return LlamaEngine(resolve_model(spec, dtype=args.dtype, device=dev, seed=seed), num_pages=pages,
+                           page_size=args.page_size, max_positions=ctx + 64)
+
+    drafter = DrafterRuntime(engine(args.model, args.seed))
+    if args.backend == "ar":
+        from ..serving.ar import PagedGreedyARGenerator
+
+        gen = PagedGreedyARGenerator(drafter=drafter)
+
+        def run(ids):
+            r = gen.generate(ids, max_new_tokens=args.max_new_tokens, eos_token_id=args.eos_token_id)
+            return r.generated_token_ids, dict(r.metadata), []
+
+        return run
+    from ..serving.edge import DistributedAtlasConfig, PagedDistributedAtlasGenerator
+    from ..serving.rpc import InProcessTargetClient, RemoteTargetClient
+    from ..serving.serial import SerialAtlasGenerator
+    from ..runtime.target import TargetVerifier
+
+    if args.target_url:
+        client = RemoteTargetClient(args.target_url)
+    else:
+        if not args.target_model:
+            raise SystemExit("ATLAS backends need --target-model or --target-url")
+        weights = [float(x) for x in args.path_score_weights.split(",")] if args.path_score_weights else None
+        tv = TargetVerifier(engine(args.target_model, args.seed + 1), k=args.k, d=args.d, score_weights=weights,
+                            fallback_threshold=args.fallback_threshold,
+                            first_token_threshold=args.first_token_threshold,
+                            fallback_ar_tokens=args.fallback_ar_tokens,
+                            route_selection_policy=args.route_selection_policy, model_name=str(args.target_model))
+        if dev.type == "cuda":
+            tv.warm_graphs()
+        client = InProcessTargetClient(tv)
+    if dev.type == "cuda":
+        drafter.warm_graphs(args.k, args.fallback_ar_tokens)
+    cls = SerialAtlasGenerator if args.backend == "atlas_serial" else PagedDistributedAtlasGenerator
+    cfg = DistributedAtlasConfig(k=args.k, d=args.d, max_new_tokens=args.max_new_tokens,
+                                 eos_token_id=args.eos_token_id, fallback_ar_tokens=args.fallback_ar_tokens,
+                                 generation_seed=args.generation_seed,
+                                 fixed_forest_depth=None)
+    gen = cls(config=cfg, drafter=drafter, target_client=client)
+
+    def run(ids):
+        r = gen.generate(ids)
+        return r.generated_token_ids, dict(r.metadata), list(r.rounds)
+
+    return run
+
+
+def timed(fn, *a):
+    t0 = time.perf_counter()
+    out = fn(*a)
+    if torch.cuda.is_available():
+        torch.cuda.synchronize()
+    return out, time.perf_counter() - t0
+
+
+def rows_summary(rows: Iterable[Mapping[str, Any]]) -> dict[str, Any]:
+    rows = list(rows)
+    toks = sum(int(r.get("generated_tokens", 0)) for r in rows)
+    secs = sum(float(r.get("elapsed_s", 0.0)) for r in rows)
+    return {"samples": len(rows), "generated_tokens": toks, "elapsed_s": secs,
+            "tokens_per_s": toks / secs if secs > 0 else None}

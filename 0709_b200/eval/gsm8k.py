@@ -1,0 +1,125 @@
+"""GSM8K exact-match evaluation: ``python -m 0709_b200.eval.gsm8k --backend atlas ...``.
+
+Reads a local GSM8K-format JSONL (``question``, ``answer`` with ``#### N``),
+generates with the chosen backend (drafter AR, asynchronous ATLAS, or serial
+ATLAS), extracts the final number, and appends one row per sample to
+``predictions.jsonl`` (``--resume`` skips done indices).  ATLAS rows carry the
+per-sample target-intervention summary (``utils.interventions``) and the
+prompt's token hash so paired runs can be aligned; ``summary.json`` holds
+accuracy, throughput and the aggregated intervention statistics.
+
+Prompts: zero-shot with an answer-format instruction, or few-shot from
+``--fewshot-file`` (JSONL of question/answer pairs).  There is no network
+here, so the dataset must be a local file.  Parity: reference
+scripts/gsm8k_eval.py (backends, resume, interventions, summary).
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import re
+from pathlib import Path
+
+from ..serving.prompts import decode, encode, load_tokenizer
+from ..utils.interventions import aggregate_prediction_interventions, summarize_generation_interventions
+from .common import add_generation_flags, append_jsonl, done_indices, make_generate, read_jsonl, rows_summary, \
+    timed, token_ids_sha256
+
+GOLD_RE = re.compile(r"####\s*([^\n\r]+)")
+FINAL_RE = re.compile(r"final answer is\s*\$?\s*(-?[\d,]*\.?\d+)", re.IGNORECASE)
+NUM_RE = re.compile(r"-?\d[\d,]*\.?\d*")
+INSTRUCTION = "Solve the problem step by step. End with the sentence: The final answer is <number>."
+
+
+def normalize(x: str | None) -> str | None:
+    if x is None:
+        return None
+    s = x.strip().replace(",", "").replace("$", "").rstrip(".")
+    try:
+        v = float(s)
+    except ValueError:
+        return None
+    return str(int(v)) if v == int(v) else repr(v)
+
+
+def gold_answer(row: dict) -> str | None:
+    m = GOLD_RE.search(str(row.get("answer", "")))
+    return normalize(m.group(1)) if m else None
+
+
+def extract(text: str, *, strict: bool = False) -> str | None:
+    m = FINAL_RE.search(text or "")
+    if m:
+        return normalize(m.group(1))
+    if strict:
+        return None
+    nums = NUM_RE.findall(text or "")
+    return normalize(nums[-1]) if nums else None
+
+
+def build_prompt(question: str, fewshot: list[dict]) -> str:
+    parts = [INSTRUCTION, ""]
+    for ex in fewshot:
+        parts += [f"Question: {ex['question']}", f"Answer: {ex['answer']}", ""]
+    parts += [f"Question: {question}", "Answer:"]
+    return "\n".join(parts)
+
+
+def build_parser() -> argparse.ArgumentParser:
+    p = argparse.ArgumentParser(description="GSM8K exact match")
+    add_generation_flags(p)
+    p.add_argument("--data-file", required=True)
+    p.add_argument("--fewshot-file", default=None)
+    p.add_argument("--output-dir", required=True)
+    p.add_argument("--start", type=int, default=0)
+    p.add_argument("--end", type=int, default=None)
+    p.add_argument("--max-examples", type=int, default=None)
+    p.add_argument("--strict-marker", action="store_true", help="require 'The final answer is'")
+    return p
+
+
+def main(argv=None) -> int:
+    args = build_parser().parse_args(argv)
+    out = Path(args.output_dir)
+    out.mkdir(parents=True, exist_ok=True)
+    pred_path = out / "predictions.jsonl"
+    rows = read_jsonl(args.data_file)[args.start:args.end]
+    if args.max_examples is not None:
+        rows = rows[: args.max_examples]
+    fewshot = read_jsonl(args.fewshot_file) if args.fewshot_file else []
+    tok = load_tokenizer(args.tokenizer)
+    done = done_indices(pred_path) if args.resume else set()
+    if not args.resume and pred_path.exists():
+        pred_path.unlink()
+    generate = make_generate(args)
+    for i, row in enumerate(rows, start=args.start):
+        if i in done:
+            continue
+        ids = encode(tok, build_prompt(str(row["question"]), fewshot))
+        (gen_ids, meta, rounds), secs = timed(generate, ids)
+        text = decode(tok, gen_ids) or ""
+        pred, gold = extract(text, strict=args.strict_marker), gold_answer(row)
+        rec = {"index": i, "question": row["question"], "gold": gold, "prediction": pred,
+               "correct": pred is not None and pred == gold, "response": text, "model": args.model,
+               "backend": args.backend, "prompt_tokens": len(ids), "prompt_token_ids_sha256": token_ids_sha256(ids),
+               "generated_tokens": len(gen_ids), "elapsed_s": secs}
+        if rounds:
+            rec["target_intervention"] = {k: v for k, v in summarize_generation_interventions(
+                [r.to_dict() if hasattr(r, "to_dict") else r for r in rounds]).items() if k != "rounds"}
+            rec["rounds"] = len(rounds)
+            rec["fallback_rounds"] = sum(getattr(r, "decision", "") == "fallback_ar" for r in rounds)
+        append_jsonl(pred_path, rec)
+    preds = read_jsonl(pred_path)
+    acc = sum(bool(r["correct"]) for r in preds) / len(preds) if preds else None
+    summary = {"accuracy": acc, "correct": sum(bool(r["correct"]) for r in preds), **rows_summary(preds),
+               "extraction_failures": sum(r["prediction"] is None for r in preds), "backend": args.backend,
+               "model": args.model, "target": args.target_model or args.target_url,
+               "target_intervention": aggregate_prediction_interventions(preds)}
+    (out / "summary.json").write_text(json.dumps(summary, indent=2, sort_keys=True) + "\n")
+    print(json.dumps({k: summary[k] for k in ("accuracy", "samples", "tokens_per_s")}))
+    return 0
+
+
+if __name__ == "__main__":
+    raise SystemExit(main())
