@@ -158,6 +158,17 @@ std::pair<int, int> pick_splits(int64_t M, int64_t N, int64_t K, int bn, int num
   const int64_t slots = static_cast<int64_t>(num_sms) * ctas_per_sm(bn);
   int64_t splits = 1;
   if (tiles * 4 < slots * 3) splits = std::max<int64_t>(1, std::min<int64_t>({kb / 2, slots / tiles, 8}));
+  // Power-of-two cluster sizes pack into the GPCs without stranded SMs
+  // (ATLAS_GEMM_POW2_SPLITS=0 keeps any size).
+  static const bool pow2 = [] {
+    const char* v = std::getenv("ATLAS_GEMM_POW2_SPLITS");
+    return v == nullptr || v[0] != '0';
+  }();
+  if (pow2) {
+    int64_t p = 1;
+    while (p * 2 <= splits) p *= 2;
+    splits = p;
+  }
   int64_t kbps = (kb + splits - 1) / splits;
   splits = (kb + kbps - 1) / kbps;
   return {static_cast<int>(splits), static_cast<int>(kbps)};
