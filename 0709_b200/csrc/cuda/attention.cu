@@ -39,11 +39,6 @@ constexpr int kSmemBytes = kQBytes + kStages * kStageBytes + 2 * kPBytes + 1024 
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kRescaleThreshold = 8.0f;  // log2 units: P stays <= 256 between rescales
 constexpr int kThreadsTC = 192;            // warps 0-3 softmax, 4 TMA, 5 MMA
-// A split covers at least this many pages (4 chunks of 64 keys at page 16):
-// the grid is sized for the longest context a graph may see, and on a short
-// one the surplus splits find no pages and exit instead of each paying the
-// CTA's fixed cost for one chunk and a 64 KB partial round trip.
-constexpr int kMinPagesPerSplit = 16;
 }  // namespace
 
 // Warp-specialized flash attention over the shared key range.
@@ -106,7 +101,7 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
   // written before the chain started, so they are safe to read before the wait).
   const int shared_len = p.dparams[0];
   const int np_total = (shared_len + ps - 1) / ps;
-  const int pps = max((np_total + p.splits - 1) / max(p.splits, 1), causal ? 1 : kMinPagesPerSplit);
+  const int pps = max((np_total + p.splits - 1) / max(p.splits, 1), causal ? 1 : p.min_pages_per_split);
   const int pb = split * pps;
   const int cp = kChunkKeys / ps;  // pages per chunk
 
@@ -265,7 +260,7 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
         // O must hold P(c-1) V(c-1) before it is rescaled.
         ok = mbar_wait(&pv_done[(c - 1) & 1], ((c - 1) >> 1) & 1, p.err) && ok;
         tc_fence_after();
-#pragma unroll
+#pragma unroll 1
         for (int q4 = 0; q4 < 4; ++q4) {
           float ov[32];
           tmem_ld32(tO + q4 * 32, ov);

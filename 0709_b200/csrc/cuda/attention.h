@@ -22,6 +22,7 @@ struct AttnParams {
   int* err;
   int M, Hq, Hkv, page_size, num_pages, layer;
   int mask_words, tail_stride, splits, direct_out, bf16;
+  int min_pages_per_split;  // a split covers at least this many pages (surplus splits exit at once)
   float scale;
 };
 
