@@ -282,10 +282,15 @@ std::pair<int, int> fp8_pick_splits(int64_t M, int64_t N, int64_t K, int bn) {
   const int64_t tiles = ((M + 127) / 128) * ((N + bn - 1) / bn);
   const int64_t kb = K / 128;
   int64_t splits = 1;
-  if (tiles * 4 < static_cast<int64_t>(num_sms()) * 3)
-    splits = std::max<int64_t>(1, std::min<int64_t>({kb / 2, num_sms() / tiles, 8}));
+  const int64_t slots = static_cast<int64_t>(num_sms()) * (bn <= 32 ? 2 : 1);  // CTAs resident per SM
+  if (tiles * 4 < slots * 3) splits = std::max<int64_t>(1, std::min<int64_t>({kb / 2, slots / tiles, 8}));
   splits = std::max<int64_t>(splits, (kb + atlas::kFp8MaxKbPerCta - 1) / atlas::kFp8MaxKbPerCta);
   TORCH_CHECK(splits <= 8, "fp8 GEMM: K too long for 8 splits of ", atlas::kFp8MaxKbPerCta, " blocks");
+  {  // power-of-two cluster sizes (see pick_splits); round up so the scale table still fits
+    int64_t p = 1;
+    while (p < splits) p *= 2;
+    splits = std::min<int64_t>(p, 8);
+  }
   int64_t kbps = (kb + splits - 1) / splits;
   splits = (kb + kbps - 1) / kbps;
   return {static_cast<int>(splits), static_cast<int>(kbps)};

@@ -32,12 +32,16 @@ struct Fp8Smem {
   static constexpr int kABytes = 128 * 128;  // 128 rows x 128 K x 1 B
   static constexpr int kBBytes = BN * 128;
   static constexpr int kStageBytes = kABytes + kBBytes;
-  static constexpr int kStages = BN <= 32 ? 8 : 6;
+  // BN <= 32: ~96 KB of shared memory and 256 TMEM columns, so two CTAs share an SM.
+  static constexpr int kStages = BN <= 16 ? 5 : (BN <= 32 ? 4 : 6);
   static constexpr int kAccStride = BN < 32 ? 32 : BN;  // TMEM columns per accumulator
-  static constexpr int kTmemCols = 2 * kAccStride;      // 64 or 128
+  // Accumulators in flight: the MMA warp runs up to kAccBufs K blocks ahead of
+  // the promotion warps, so promotion latency does not throttle the stream.
+  static constexpr int kAccBufs = 256 / kAccStride;     // 8 (BN <= 32) or 4 (BN = 64)
+  static constexpr int kTmemCols = kAccBufs * kAccStride;  // 256
   static constexpr int kScaleBytes = kFp8MaxKbPerCta * (BN + 1) * 4;
   static constexpr int kPartBytes = BN * 128 * 4;       // split-K partial (reuses the stages)
-  static constexpr int kBytes = kStages * kStageBytes + kScaleBytes + 1024 /*align*/ + 256 /*barriers*/;
+  static constexpr int kBytes = kStages * kStageBytes + kScaleBytes + 1024 /*align*/ + 512 /*barriers*/;
   static_assert(kPartBytes <= kStages * kStageBytes, "partial tile must fit in the stage ring");
 };
 
@@ -98,7 +102,7 @@ __device__ __forceinline__ void fp8_peer_signal(const Fp8GemmParams& p) {
 }
 
 template <int BN, int EPI, typename T>
-__global__ void __launch_bounds__(192, 1)
+__global__ void __launch_bounds__(192, BN <= 32 ? 2 : 1)
     gemm_fp8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                     Fp8GemmParams p) {
   using S = Fp8Smem<BN>;
@@ -109,8 +113,8 @@ __global__ void __launch_bounds__(192, 1)
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + S::kStages * S::kStageBytes + S::kScaleBytes);
   uint64_t* empty = full + S::kStages;
   uint64_t* tfull = empty + S::kStages;
-  uint64_t* tempty = tfull + 2;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
+  uint64_t* tempty = tfull + S::kAccBufs;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + S::kAccBufs);
 
   const int tid = threadIdx.x;
   const int warp = tid >> 5;
@@ -127,7 +131,7 @@ __global__ void __launch_bounds__(192, 1)
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
     }
-    for (int b = 0; b < 2; ++b) {
+    for (int b = 0; b < S::kAccBufs; ++b) {
       mbar_init(&tfull[b], 1);
       mbar_init(&tempty[b], 4);  // one arrival per promotion warp
     }
@@ -174,9 +178,10 @@ __global__ void __launch_bounds__(192, 1)
       bool ok = true;
       for (int i = 0; i < nk && ok; ++i) {
         const int s = i % S::kStages;
-        const int b = i & 1;
+        const int b = i % S::kAccBufs;
+        const int u = i / S::kAccBufs;
         ok = mbar_wait(&full[s], (i / S::kStages) & 1, p.err);
-        if (ok && i >= 2) ok = mbar_wait(&tempty[b], ((i >> 1) - 1) & 1, p.err);
+        if (ok && u >= 1) ok = mbar_wait(&tempty[b], (u - 1) & 1, p.err);
         if (!ok) break;
         tc_fence_after();
         const uint32_t a = smem_u32(smem + s * S::kStageBytes);
@@ -202,8 +207,8 @@ __global__ void __launch_bounds__(192, 1)
     epi_bar();
     const uint32_t lane_base = static_cast<uint32_t>(warp * 32) << 16;
     for (int i = 0; i < nk; ++i) {
-      const int b = i & 1;
-      if (!mbar_wait(&tfull[b], (i >> 1) & 1, p.err)) break;
+      const int b = i % S::kAccBufs;
+      if (!mbar_wait(&tfull[b], (i / S::kAccBufs) & 1, p.err)) break;
       tc_fence_after();
       float v[BN < 32 ? 32 : BN];
 #pragma unroll

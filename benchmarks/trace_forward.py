@@ -37,13 +37,20 @@ def main() -> int:
     ap.add_argument("--prefix", type=int, default=2048)
     ap.add_argument("--replays", type=int, default=3)
     ap.add_argument("--json-out", default=None)
+    ap.add_argument("--fp8", action="store_true", help="block-scaled fp8 weights (Fp8LlamaEngine)")
     args = ap.parse_args()
     llama = importlib.import_module("0709_b200.models.llama")
     engine_mod = importlib.import_module("0709_b200.runtime.engine")
     cfg = llama.get_config(args.model)
-    w = llama.random_weights(cfg, seed=1, dtype=torch.float16, device="cuda")
     npages = (args.prefix + args.rows) // 16 + 4
-    eng = engine_mod.LlamaEngine(w, num_pages=npages + 8, page_size=16, max_positions=args.prefix + 4096)
+    if args.fp8:
+        fp8 = importlib.import_module("0709_b200.models.fp8")
+        w = fp8.random_weights_fp8(cfg, seed=1, dtype=torch.bfloat16, device="cuda")
+        eng = importlib.import_module("0709_b200.runtime.engine_fp8").Fp8LlamaEngine(
+            w, num_pages=npages + 8, page_size=16, max_positions=args.prefix + 4096)
+    else:
+        w = llama.random_weights(cfg, seed=1, dtype=torch.float16, device="cuda")
+        eng = engine_mod.LlamaEngine(w, num_pages=npages + 8, page_size=16, max_positions=args.prefix + 4096)
     pages = torch.arange(npages, dtype=torch.int32, device="cuda")
     r, p = args.rows, args.prefix
     fields = dict(tokens=np.arange(r), positions=np.arange(p, p + r), slots=np.arange(p, p + r), shared_len=p,
