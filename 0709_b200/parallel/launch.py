@@ -33,8 +33,9 @@ def build_tp_target(cfg: LlamaConfig, *, mode: str, seed: int, dtype: torch.dtyp
     world = dist.get_world_size(group)
     path = mailbox_path(tag)
     mb = None
+    ack_timeout = float(os.environ.get("ATLAS_TP_ACK_TIMEOUT", "120"))
     if world > 1 and rank == 0:
-        mb = Mailbox(path, rank=0, world=world, create=True)
+        mb = Mailbox(path, rank=0, world=world, create=True, ack_timeout_s=ack_timeout)
     dist.barrier(group=group)
     if world > 1 and rank != 0:
         mb = Mailbox(path, rank=rank, world=world, create=False)

@@ -24,6 +24,8 @@ configuration's TP=2/4/8 target.
 
 from __future__ import annotations
 
+import os
+
 import numpy as np
 import torch
 
@@ -186,7 +188,12 @@ class TPLlamaEngine(LlamaEngine):
         calls = 0
         self.worker_wait_s = 0.0
         self.worker_handle_s = 0.0
+        # Host-side fault injection for tests: leave between two calls, as a crashed
+        # rank would (never inside a kernel or collective).
+        exit_after = int(os.environ.get("ATLAS_TP_FAULT_EXIT_AFTER", "-1"))
         while True:
+            if 0 <= exit_after <= calls:
+                os._exit(0)
             t0 = time.perf_counter()
             op, payload = self.mailbox.receive()
             t1 = time.perf_counter()

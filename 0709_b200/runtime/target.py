@@ -30,6 +30,7 @@ import torch
 from ..ops import _native
 from ..ops.attn_desc import AttnDesc, single_sequence_desc
 from ..utils import counters
+from ..utils.nvtx import nvtx_range
 from ..types import PrefixState, TargetRouteScore, TargetVerifyResult, VerifyRoutePayload
 from .drafter import PrefixPageMirror
 from .engine import LlamaEngine, row_bucket
@@ -174,7 +175,8 @@ class TargetVerifier:
                 f"request_len={len(prefix)}, target_len={len(self.prefix_token_ids)}"
             )
         paths, depth = self._validate_routes(routes)
-        tree = self.run_tree(paths)
+        with nvtx_range("target_tree_verify"):
+            tree = self.run_tree(paths)
         scores = self._score_routes(routes, paths, tree["path_logprobs"])
         best = max(scores, key=self._best_key)
         selected, sampling_meta = self._select_route_with_metadata(
@@ -213,7 +215,8 @@ class TargetVerifier:
             limit = self.fallback_ar_tokens if fallback_max_tokens is None else min(
                 int(fallback_max_tokens), self.fallback_ar_tokens
             )
-            generated = self._generate_fallback_ar(max_tokens=limit, eos_token_id=eos_token_id)
+            with nvtx_range("target_fallback_ar"):
+                generated = self._generate_fallback_ar(max_tokens=limit, eos_token_id=eos_token_id)
             return TargetVerifyResult(
                 selected_route_id=None,
                 scores=scores,
@@ -281,12 +284,37 @@ class TargetVerifier:
         return paths, depth
 
     # ------------------------------------------------------- tree forward
+    @staticmethod
+    def linear_tree(paths: Sequence[Sequence[int]]):
+        """The same outputs as ``build_tree`` with no prefix sharing: every route keeps
+        its own chain of nodes (block-diagonal causal mask).  Used by the linear
+        verify baseline (reference src/atlas_0709/flashinfer_full_verify.py:742-784)."""
+        r, d = len(paths), len(paths[0])
+        n = r * d
+        tokens = torch.tensor([int(t) for p in paths for t in p], dtype=torch.int64)
+        depths = torch.arange(d, dtype=torch.int32).repeat(r)
+        parents = torch.arange(n, dtype=torch.int32) - 1
+        parents[::d] = -1
+        node_paths = torch.arange(n, dtype=torch.int32).reshape(r, d)
+        w = (n + 63) // 64
+        masks = np.zeros((n, w), dtype=np.uint64)
+        for i in range(n):
+            for a in range(i - i % d, i + 1):
+                masks[i, a // 64] |= np.uint64(1) << np.uint64(a % 64)
+        return tokens, parents, depths, node_paths, torch.from_numpy(masks.view(np.int64))
+
     @torch.inference_mode()
-    def run_tree(self, paths: Sequence[Sequence[int]]) -> dict[str, object]:
-        """One masked forward over the deduplicated trie; returns logits and path log-probs."""
-        tokens, parents, depths, node_paths, masks = self.host.build_tree(
-            torch.tensor([list(p) for p in paths], dtype=torch.int64)
-        )
+    def run_tree(self, paths: Sequence[Sequence[int]], *, deduplicate: bool = True) -> dict[str, object]:
+        """One masked forward over the deduplicated trie; returns logits and path log-probs.
+
+        ``deduplicate=False`` runs every route's tokens as its own chain (linear verify baseline).
+        """
+        if deduplicate:
+            tokens, parents, depths, node_paths, masks = self.host.build_tree(
+                torch.tensor([list(p) for p in paths], dtype=torch.int64)
+            )
+        else:
+            tokens, parents, depths, node_paths, masks = self.linear_tree(paths)
         n = int(tokens.numel())
         p = len(self.prefix_token_ids)
         scratch = self.seq.reserve_scratch(p + n)
@@ -668,10 +696,13 @@ class TargetVerifier:
 
     # ------------------------------------------------------------- metadata
     def runtime_metadata(self) -> dict[str, object]:
+        from .metadata import runtime_info
+
         cfg = getattr(self.engine, "model_cfg", self.engine.cfg)
         tp = getattr(self.engine, "tp", None)
         return {
             "backend": "b200_native_masked_tree_verify",
+            "framework": runtime_info(self.device),
             "tensor_parallel": 1 if tp is None else int(tp.world),
             "tensor_parallel_comm": None if tp is None else tp.mode,
             "model": self.model_name,

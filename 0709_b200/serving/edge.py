@@ -38,6 +38,7 @@ from ..runtime.drafter import DrafterRuntime
 from ..runtime.sampling import DrafterSamplingConfig, DrafterSamplingContext
 from ..runtime.store import KVTreeStore
 from ..types import BuildDepthsOutput, RouteState
+from ..utils.nvtx import nvtx_range
 from ..utils.timeline import EdgeBlackboxTimeline, EdgeRoundTimeline, EdgeSpan
 from .rpc import selected_route_id_from_response
 
@@ -473,7 +474,9 @@ class AtlasSession:
             )
         while g._should_build_forest_step(verify_done=vfut.done() or fb_decided.is_set(), forest_depth=f_depth):
             t0 = g._now()
-            st = build_forest_one_depth(f_front, k=cfg.k, route_store=store, model_backend=g.drafter, sampling=rs)
+            with nvtx_range(f"edge_forest_depth_{f_depth + 1}"):
+                st = build_forest_one_depth(f_front, k=cfg.k, route_store=store, model_backend=g.drafter,
+                                            sampling=rs)
             f_depth += 1
             f_spans.append(EdgeSpan(f"edge_forest_step_{f_depth}", t0, g._now()))
             f_done, f_logits, f_front = st.decoded_routes, st.decode_output.next_token_logits, st.next_routes
@@ -508,7 +511,8 @@ class AtlasSession:
             mode = "fallback_ar_stopped" if stop else "fallback_ar_extend_prefix_kv"
             if not stop:
                 t0 = g._now()
-                self.stage1, phys = g._fallback_extend_handoff(store, now)
+                with nvtx_range("edge_fallback_extend_then_build_tree"):
+                    self.stage1, phys = g._fallback_extend_handoff(store, now)
                 handoff_span = EdgeSpan("edge_fallback_extend_then_build_tree", t0, g._now())
         elif decision == "select":
             sel_id = selected_route_id_from_response(resp)

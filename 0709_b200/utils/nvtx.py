@@ -1,0 +1,25 @@
+"""Optional NVTX ranges (``ATLAS_NVTX=1``) around serving phases, for Nsight timelines.
+
+Zero cost when disabled: the context manager does nothing.
+"""
+
+from __future__ import annotations
+
+import contextlib
+import os
+
+import torch
+
+ENABLED = os.environ.get("ATLAS_NVTX", "0") == "1"
+
+
+@contextlib.contextmanager
+def nvtx_range(name: str):
+    if ENABLED and torch.cuda.is_available():
+        torch.cuda.nvtx.range_push(name)
+        try:
+            yield
+        finally:
+            torch.cuda.nvtx.range_pop()
+    else:
+        yield

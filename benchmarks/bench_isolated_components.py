@@ -36,7 +36,8 @@ sys.path.insert(0, ROOT)
 
 # Reference (1x H800, P=8192, k=3 d=4, eager): HANDOFF numbers quoted in the survey.
 REFERENCE_H800_MS = {"batch_ar_k": 25.096, "tree": 28.978, "batch_ar_k2": 26.806, "forest": 31.686,
-                     "target_verify": 24.224, "target_ar1": 18.402}
+                     "target_verify": 24.224, "target_ar1": 18.402, "target_ar2": 34.734,
+                     "target_linear_verify": 28.484}
 
 
 def pkg(name):
@@ -170,6 +171,28 @@ def main() -> int:
                                                 slots=slots[:1], shared_len=p, n_shared_pages=len(tv.mirror.host),
                                                 mask_base=p, row_full=[p + 1], row_len=[p + 1])))
         ver, ar = ver[2:], ar[2:]
+        # Two dependent one-token forwards (the second token fed on the device) and the
+        # linear (non-deduplicated) verify of the same kind of routes, without commit.
+        ar2, lin, tree_fwd = [], [], []
+        for i in range(args.pairs + 2):
+            p = len(tv.prefix_token_ids)
+            slots = tv.seq.reserve_scratch(p + 2).numpy()
+            tv._sync()
+            tok = torch.zeros(2, dtype=torch.int32, device=dev)
+
+            def two():
+                for j in range(2):
+                    te.run_rows(1, prefix_pages=tv.mirror.dev, tokens=tok[j:j + 1], positions=[p + j],
+                                slots=slots[j:j + 1], shared_len=p + j, n_shared_pages=len(tv.mirror.host),
+                                mask_base=p + j, row_full=[p + j + 1], row_len=[p + j + 1])
+
+            ar2.append(timed(two))
+            paths = [list(r.token_ids) for r in synthetic_routes()]
+            lin.append(timed(lambda: tv.run_tree(paths, deduplicate=False)))
+            tree_fwd.append(timed(lambda: tv.run_tree(paths)))
+        out["target_ar2_ms"] = round(statistics.mean(v[0] for v in ar2[2:]), 3)
+        out["target_linear_verify_ms"] = round(statistics.mean(v[0] for v in lin[2:]), 3)
+        out["target_tree_forward_ms"] = round(statistics.mean(v[0] for v in tree_fwd[2:]), 3)
         out["target_verify_ms"] = round(statistics.mean(v[0] for v in ver), 3)
         out["target_verify_host_ms"] = round(statistics.mean(v[1] for v in ver), 3)
         out["target_ar1_ms"] = round(statistics.mean(v[0] for v in ar), 3)

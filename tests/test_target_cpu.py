@@ -160,3 +160,16 @@ def test_intervention_metadata_in_verify_result(tw):
     md = res.metadata
     assert md["route_count"] == 2
     assert any("intervention" in key or "draft" in key for key in md), sorted(md)
+
+
+def test_linear_verify_matches_deduplicated_tree(tw):
+    tv = verifier(tw)
+    prompt = list(range(60, 73))
+    tv.prefill(prompt)
+    paths = [[4, 5, 6], [4, 5, 9], [1, 7, 7]]
+    a = tv.run_tree(paths)
+    b = tv.run_tree(paths, deduplicate=False)
+    assert b["node_count"] == 9 and a["node_count"] == 7
+    for ra, rb in zip(a["path_logprobs"], b["path_logprobs"]):
+        for x, y in zip(ra, rb):
+            assert abs(x - y) < 1e-4

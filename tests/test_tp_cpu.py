@@ -127,3 +127,16 @@ def test_worker_detects_dead_root(tmp_path):
     assert time.monotonic() - t0 < 30
     w.close()
     os.unlink(path)
+
+
+def test_root_detects_a_worker_that_left():
+    # The worker exits (between calls) after its first few commands; the root's next
+    # command is never acknowledged and it raises PeerLost instead of hanging.
+    cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes", "1", "--nproc-per-node", "2",
+           "--master-addr", "127.0.0.1", "--master-port", str(free_port()), os.path.join(REPO, "tests", "tp_fault_job.py")]
+    env = dict(os.environ, OMP_NUM_THREADS="1", ATLAS_TP_FAULT_EXIT_AFTER="4", ATLAS_TP_ACK_TIMEOUT="3")
+    r = subprocess.run(cmd, cwd=REPO, env=env, capture_output=True, text=True, timeout=240)
+    d = last_json(r.stdout)
+    assert d["peer_lost"], r.stdout[-2000:] + r.stderr[-2000:]
+    assert d["kind"] in ("PeerLost", "RuntimeError")
+    assert "did not acknowledge" in d["message"] or "Connection" in d["message"] or "closed" in d["message"]
