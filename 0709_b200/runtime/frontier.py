@@ -8,6 +8,7 @@ reserved on the host by the model backend, so they never ride the transfer.
 
 from __future__ import annotations
 
+import os
 import struct
 from collections import Counter
 from dataclasses import dataclass
@@ -224,6 +225,9 @@ def advance_frontier_one_token(
     if not active_routes:
         raise ValueError("active_routes cannot be empty")
     out = model_backend.decode_frontier_one_token(active_routes, attention_backend=attention_backend)
+    if HOST_SELECTION and out.new_node_ids_cpu is not None and hasattr(selection_policy, "select"):
+        return _advance_host_selection(active_routes, out, k=k, route_store=route_store,
+                                       selection_policy=selection_policy, sampling=sampling)
     batch = build_pending_candidate_batch(
         active_routes,
         out.next_token_logits,
@@ -247,6 +251,45 @@ def advance_frontier_one_token(
         decode_output=out,
         selection_stats=stats,
     )
+
+
+# Host selection: after the top-k kernel, one transfer brings the k candidates of
+# every parent to the host, where ranking (<= k^3 candidates) and route
+# bookkeeping run in Python -- the same order as the device path
+# (score desc, parent, rank, token), without its dozens of small GPU launches.
+HOST_SELECTION = os.environ.get("ATLAS_DEVICE_SELECTION", "0") != "1"
+
+
+def _advance_host_selection(active_routes, out, *, k, route_store, selection_policy, sampling) -> FrontierStepOutput:
+    rel = [route_store.pending_token_path(r) for r in active_routes]
+    lp, ids = batch_parent_token_candidates(out.next_token_logits, k=k, sampling=sampling,
+                                            relative_parent_paths=rel)
+    packed = torch.stack((ids.to(torch.float64), lp.to(torch.float64)), dim=-1)
+    is_transfer = packed.device.type != "cpu"
+    if is_transfer:
+        counters.d2h(packed.numel() * 8)
+    rows = packed.cpu().tolist()
+    cands: list[PendingCandidate] = []
+    for r, row in zip(active_routes, rows):
+        base = float(r.cumulative_logprob)
+        for rank, (tok, tlp) in enumerate(row):
+            cands.append(PendingCandidate(parent_route_id=int(r.route_id), stage1_root_id=int(r.stage1_root_id),
+                                          pending_token_id=int(tok), cumulative_logprob=base + float(tlp),
+                                          rank_in_parent=rank, parent_logprob=base))
+    chosen = selection_policy.select(cands, k=k, active_routes=active_routes)
+    node_ids = [int(x) for x in out.new_node_ids_cpu]
+    if len(node_ids) != len(active_routes):
+        raise ValueError("new_node_ids_cpu must have one id per active route")
+    stats = FrontierSelectionStats(
+        candidate_count=len(cands), selected_count=len(chosen), host_materialization_batches=1,
+        host_materialization_elements=int(packed.numel()), host_transfer_batches=int(is_transfer),
+        host_transfer_elements=int(packed.numel()) if is_transfer else 0, selection_device="cpu",
+        new_node_ids_source="decode_output_cpu")
+    decoded = route_store.mark_routes_materialized(list(active_routes), node_ids, phase=selection_policy.phase)
+    nxt = route_store.materialize_route_descriptors(chosen, parent_routes=decoded)
+    route_store.release_routes_without_descendants(decoded, nxt)
+    return FrontierStepOutput(decoded_routes=decoded, next_routes=nxt, candidates=cands, selected_candidates=chosen,
+                              decode_output=out, selection_stats=stats)
 
 
 def _resolve_new_node_ids(out: FrontierDecodeOutput, *, expected: int):

@@ -54,6 +54,9 @@ class PerRouteTop1Selection:
         n = len(active_routes)
         return torch.arange(n, device=candidates.pending_token_ids.device) * candidates.candidates_per_parent
 
+    def select(self, candidates, *, k, active_routes):
+        return [c for c in candidates if c.rank_in_parent == 0]
+
 
 def timed(fn):
     torch.cuda.synchronize()
