@@ -188,6 +188,8 @@ def make_target_handler(app: TargetServerApp) -> type[BaseHTTPRequestHandler]:
                     resp = app.prefill(body)
                 elif self.path == "/verify":
                     resp = app.verify(body)
+                elif self.path == "/release" and hasattr(app, "release"):
+                    resp = app.release(body)  # multi-session servers: end a session, free its pages
                 else:
                     self._write(404, {"ok": False, "error": f"unknown endpoint: {self.path}"})
                     return
@@ -220,8 +222,9 @@ def make_server(app: TargetServerApp, *, host: str, port: int) -> ThreadingHTTPS
 
 def serve_target(app: TargetServerApp, *, host: str, port: int) -> None:
     server = make_server(app, host=host, port=port)
+    meta = app.backend.runtime_metadata() if hasattr(app, "backend") else app.health()
     print(json.dumps({"service": "atlas_0709_target", "host": host, "port": int(server.server_address[1]),
-                      "metadata": app.backend.runtime_metadata()}, indent=2, sort_keys=True), flush=True)
+                      "metadata": meta}, indent=2, sort_keys=True), flush=True)
     try:
         server.serve_forever()
     except KeyboardInterrupt:
@@ -231,9 +234,12 @@ def serve_target(app: TargetServerApp, *, host: str, port: int) -> None:
 
 
 class RemoteTargetClient:
-    def __init__(self, base_url: str, *, timeout: float = 600.0) -> None:
+    """HTTP client; ``session_id`` (optional) addresses one session of a multi-session server."""
+
+    def __init__(self, base_url: str, *, timeout: float = 600.0, session_id: str | None = None) -> None:
         self.base_url = base_url.rstrip("/")
         self.timeout = float(timeout)
+        self.session_id = session_id
 
     def health(self) -> dict[str, object]:
         with urllib.request.urlopen(f"{self.base_url}/health", timeout=self.timeout) as r:
@@ -259,7 +265,12 @@ class RemoteTargetClient:
                 payload[key] = int(val)
         return self._post("/verify", payload)
 
+    def release(self) -> dict[str, object]:
+        return self._post("/release", {})
+
     def _post(self, path: str, payload: Mapping[str, object]) -> dict[str, object]:
+        if self.session_id is not None:
+            payload = {**payload, "session_id": self.session_id}
         req = urllib.request.Request(
             f"{self.base_url}{path}",
             data=json.dumps(payload).encode("utf-8"),

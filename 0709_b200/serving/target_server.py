@@ -57,6 +57,8 @@ def build_parser() -> argparse.ArgumentParser:
                    default="target_best")
     p.add_argument("--route-sampling-temperature", type=float, default=1.0)
     p.add_argument("--verbose", action="store_true", help="Log every HTTP request.")
+    p.add_argument("--sessions", type=int, default=1,
+                   help="Serve up to this many concurrent sessions (requests carry session_id; POST /release ends one).")
     return p
 
 
@@ -84,9 +86,40 @@ def build_backend(args: argparse.Namespace) -> TargetVerifier:
     return tv
 
 
+def build_multi_session_app(args: argparse.Namespace):
+    """One engine and page pool shared by up to ``--sessions`` target sessions."""
+    from .. import ops  # noqa: F401
+    from ..ops import _native
+    from .sessions import MultiSessionTargetApp
+
+    device = torch.device(args.device if torch.cuda.is_available() or not args.device.startswith("cuda") else "cpu")
+    w = resolve_model(args.model, dtype=args.dtype, device=device, seed=args.seed)
+    ctx = int(args.prefix_len) + int(args.max_new_tokens_capacity) + 4 * int(args.k) * int(args.d) + 64
+    pages = int(args.sessions) * (2 * math.ceil(ctx / args.page_size) + 64)
+    engine = LlamaEngine(w, num_pages=pages, page_size=args.page_size, max_positions=ctx + 64)
+    pool = _native.host().PagePool(engine.num_pages - 1, args.page_size)
+
+    def make(sid: str) -> TargetVerifier:
+        tv = TargetVerifier(engine, k=args.k, d=args.d, page_pool=pool,
+                            score_weights=parse_score_weights(args.path_score_weights),
+                            fallback_threshold=args.fallback_threshold,
+                            first_token_threshold=args.first_token_threshold,
+                            fallback_ar_tokens=args.fallback_ar_tokens, profile_fallback_ar=args.profile_fallback_ar,
+                            route_selection_policy=args.route_selection_policy,
+                            route_sampling_temperature=args.route_sampling_temperature, model_name=args.model)
+        if device.type == "cuda":
+            tv.warm_graphs()
+        return tv
+
+    return MultiSessionTargetApp(make, max_sessions=int(args.sessions))
+
+
 def main(argv=None) -> int:
     args = build_parser().parse_args(argv)
-    app = TargetServerApp(build_backend(args))
+    if int(args.sessions) > 1:
+        app = build_multi_session_app(args)
+    else:
+        app = TargetServerApp(build_backend(args))
     app.verbose = bool(args.verbose)
     serve_target(app, host=args.host, port=args.port)
     return 0

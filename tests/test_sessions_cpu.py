@@ -81,3 +81,31 @@ def test_two_sessions_over_shm_match_single_session(tmp_path):
         assert g.generated_token_ids == w.generated_token_ids
         assert [r.decision for r in g.rounds] == [r.decision for r in w.rounds]
     assert server_box["served"] >= 2 * 2
+
+
+def test_multi_session_http_server(tmp_path):
+    import threading as th
+
+    ts = mod("serving.target_server")
+    rpc = mod("serving.rpc")
+    args = ts.build_parser().parse_args(["--model", "tiny-target", "--port", "0", "--device", "cpu", "--dtype",
+                                         "float32", "--page-size", "4", "--k", "2", "--d", "2", "--prefix-len", "64",
+                                         "--max-new-tokens-capacity", "64", "--sessions", "3"])
+    app = ts.build_multi_session_app(args)
+    server = rpc.make_server(app, host="127.0.0.1", port=0)
+    t = th.Thread(target=server.serve_forever, daemon=True)
+    t.start()
+    try:
+        url = f"http://127.0.0.1:{server.server_address[1]}"
+        dw, _ = _weights()
+        outs = []
+        for sid in ("a", "b"):
+            c = rpc.RemoteTargetClient(url, timeout=60, session_id=sid)
+            outs.append(_generate(dw, c, list(range(5, 25))))
+        assert outs[0].generated_token_ids == outs[1].generated_token_ids
+        h = rpc.RemoteTargetClient(url).health()
+        assert h["sessions"] == ["a", "b"]
+        assert rpc.RemoteTargetClient(url, session_id="a").release()["released"]
+    finally:
+        server.shutdown()
+        server.server_close()
