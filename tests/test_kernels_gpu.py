@@ -314,3 +314,61 @@ def test_graph_replay_matches_eager(rows):
     eng.ops.check()
     assert torch.equal(out_graph[0], out_graph[1])
     assert torch.equal(out_graph[1], out_eager)
+
+
+def _causal_oracle(w, tokens, q_chunk: int = 2048) -> torch.Tensor:
+    """fp32 causal forward with query-chunked attention (long contexts); returns the final hidden rows."""
+    llama = mod("models.llama")
+    cfg = w.config
+    toks = torch.as_tensor(tokens, dtype=torch.long, device=w.device)
+    t = int(toks.numel())
+    pos = torch.arange(t, device=w.device)
+    table = llama.rope_table(cfg, t, device=w.device)
+    hd = cfg.head_dim
+    x = w.embed[toks].float()
+    for lw in w.layers:
+        a = llama.rmsnorm_ref(x, lw.attn_norm, cfg.rms_eps)
+        qkv = a @ lw.wqkv.float().t()
+        q = llama.apply_rope(qkv[:, : cfg.q_size].reshape(t, cfg.num_heads, hd), table, pos)
+        k = llama.apply_rope(qkv[:, cfg.q_size: cfg.q_size + cfg.kv_size].reshape(t, cfg.num_kv_heads, hd), table, pos)
+        v = qkv[:, cfg.q_size + cfg.kv_size:].reshape(t, cfg.num_kv_heads, hd)
+        k = k.repeat_interleave(cfg.group, dim=1).transpose(0, 1)
+        v = v.repeat_interleave(cfg.group, dim=1).transpose(0, 1)
+        o = torch.empty(t, cfg.num_heads, hd, device=w.device)
+        for c0 in range(0, t, q_chunk):
+            c1 = min(t, c0 + q_chunk)
+            s = torch.einsum("qhd,hkd->hqk", q[c0:c1], k[:, :c1]) / math.sqrt(hd)
+            s = s.masked_fill(torch.arange(c1, device=w.device)[None, None, :] > pos[c0:c1][None, :, None],
+                              float("-inf"))
+            o[c0:c1] = torch.einsum("hqk,hkd->qhd", torch.softmax(s, -1), v[:, :c1])
+        x = x + o.reshape(t, cfg.q_size) @ lw.wo.float().t()
+        m = llama.rmsnorm_ref(x, lw.mlp_norm, cfg.rms_eps)
+        gate, up = llama.split_gate_up(lw.wgu.float())
+        x = x + (torch.nn.functional.silu(m @ gate.t()) * (m @ up.t())) @ lw.wd.float().t()
+    return x
+
+
+@pytest.mark.parametrize("prefill_chunk", [8192, 4096])
+def test_long_context_prefill_and_verify(prefill_chunk):
+    """A 16K-token prompt prefilled in chunks, then a tree verified on top of it (split-KV attention path)."""
+    llama = mod("models.llama")
+    engine_mod = mod("runtime.engine")
+    target_mod = mod("runtime.target")
+    cfg = llama.LlamaConfig("gpu-small", 2, 512, 8, 2, 128, 1024, 4096)
+    w32 = llama.random_weights(cfg, seed=11, dtype=torch.float32, device="cuda")
+    w = llama.weights_to(w32, dtype=torch.bfloat16)
+    p = 16384 + 37
+    eng = engine_mod.LlamaEngine(w, num_pages=p // 16 + 64, page_size=16, max_positions=p + 64)
+    tv = target_mod.TargetVerifier(eng, k=2, d=3, prefill_chunk_size=prefill_chunk)
+    prompt = torch.randint(0, 4096, (p,), generator=torch.Generator().manual_seed(5)).tolist()
+    tv.prefill(prompt)
+    paths = [(5, 6, 7), (5, 8, 9)]
+    out = tv.run_tree(paths)
+    wf = llama.weights_to(w, dtype=torch.float32)
+    nodes = {(5, 6, 7): [0, 1, 2], (5, 8, 9): [0, 3, 4]}
+    for path in paths:
+        hid = _causal_oracle(wf, prompt + list(path))[p - 1:]
+        lo = llama.rmsnorm_ref(hid, wf.final_norm, cfg.rms_eps) @ wf.lm_head.float().t()
+        assert rel_err(tv.prefix_logits, lo[0]) < 3e-2
+        assert rel_err(out["logits"][nodes[path]], lo[1:]) < 3e-2
+    eng.ops.check()
