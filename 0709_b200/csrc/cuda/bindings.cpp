@@ -184,6 +184,17 @@ int num_sms() {
   return n;
 }
 
+// Load streamed weight tiles with the evict-first L2 policy: weights are read
+// once per forward, so they should not displace activations, KV pages and
+// split partials (ATLAS_L2_EVICT_FIRST=0 disables).
+int stream_hint() {
+  static const int v = [] {
+    const char* e = std::getenv("ATLAS_L2_EVICT_FIRST");
+    return (e == nullptr || e[0] != '0') ? 1 : 0;
+  }();
+  return v;
+}
+
 void check_cuda(const torch::Tensor& t, const char* name) {
   TORCH_CHECK(t.is_cuda(), name, " must be a CUDA tensor");
 }
@@ -227,6 +238,7 @@ std::vector<int64_t> gemm_impl(const torch::Tensor& w, const torch::Tensor& x, v
   p.out = out_ptr;
   p.err = err.data_ptr<int>();
   if (peer != nullptr) p.peer = *peer;
+  p.stream_hint = stream_hint();
   atlas::launch_gemm_tn(a, b, p, bn, static_cast<int>(epi), at::cuda::getCurrentCUDAStream());
   return {bn, sp.first, sp.second};
 }
@@ -328,6 +340,7 @@ std::vector<int64_t> gemm_fp8_impl(const torch::Tensor& wq, const torch::Tensor&
   p.out = out_ptr;
   p.err = err.data_ptr<int>();
   if (peer != nullptr) p.peer = *peer;
+  p.stream_hint = stream_hint();
   atlas::launch_gemm_fp8(a, b, p, bn, static_cast<int>(epi), at::cuda::getCurrentCUDAStream());
   return {bn, sp.first, sp.second};
 }

@@ -81,6 +81,7 @@ struct GemmParams {
   NormIn nin;        // optional rstd column scaling (store, SiLU, fp32, rope epilogues)
   NormOut nout;      // kEpiResidualNorm only
   RopeOut rope;      // kEpiRope only
+  int stream_hint;   // load weight tiles with the evict-first L2 policy (read once per forward)
 };
 
 void launch_gemm_tn(const CUtensorMap& a, const CUtensorMap& b, const GemmParams& p, int bn, int epi,

@@ -152,10 +152,15 @@ __global__ void __launch_bounds__(192, BN <= 32 ? 2 : 1)
   if (warp == 4) {
     if (lane == 0) {
       bool ok = true;
+      const bool hint = p.stream_hint != 0;
+      const uint64_t pol = l2_policy_evict_first();
       const int pre = min(nk, S::kStages);
       for (int i = 0; i < pre; ++i) {
         mbar_arrive_expect_tx(&full[i], S::kStageBytes);
-        tma_load_2d(smem + i * S::kStageBytes, &tmA, &full[i], (kb0 + i) * 128, m0);
+        if (hint)
+          tma_load_2d_hint(smem + i * S::kStageBytes, &tmA, &full[i], (kb0 + i) * 128, m0, pol);
+        else
+          tma_load_2d(smem + i * S::kStageBytes, &tmA, &full[i], (kb0 + i) * 128, m0);
       }
       pdl_wait();
       for (int i = 0; i < pre; ++i)
@@ -166,7 +171,10 @@ __global__ void __launch_bounds__(192, BN <= 32 ? 2 : 1)
         if (!ok) break;
         uint8_t* a = smem + s * S::kStageBytes;
         mbar_arrive_expect_tx(&full[s], S::kStageBytes);
-        tma_load_2d(a, &tmA, &full[s], (kb0 + i) * 128, m0);
+        if (hint)
+          tma_load_2d_hint(a, &tmA, &full[s], (kb0 + i) * 128, m0, pol);
+        else
+          tma_load_2d(a, &tmA, &full[s], (kb0 + i) * 128, m0);
         tma_load_2d(a + S::kABytes, &tmB, &full[s], (kb0 + i) * 128, n0);
       }
     }

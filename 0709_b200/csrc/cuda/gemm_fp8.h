@@ -25,6 +25,7 @@ struct Fp8GemmParams {
   void* out;
   int* err;
   PeerOut peer;      // kEpiPeer only
+  int stream_hint;   // load weight tiles with the evict-first L2 policy (read once per forward)
 };
 
 void launch_gemm_fp8(const CUtensorMap& a, const CUtensorMap& b, const Fp8GemmParams& p, int bn, int epi,

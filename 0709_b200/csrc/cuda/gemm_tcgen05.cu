@@ -278,10 +278,15 @@ __global__ void __launch_bounds__(128, 1)
   if (tid == 0) {
     // Weight tiles do not depend on the previous kernel: stream the first
     // stages before waiting for it, then the activations.
+    const bool hint = p.stream_hint != 0;
+    const uint64_t pol = l2_policy_evict_first();
     const int pre = min(nk, S::kStages);
     for (int i = 0; i < pre; ++i) {
       mbar_arrive_expect_tx(&full[i], S::kStageBytes);
-      tma_load_2d(smem + i * S::kStageBytes, &tmA, &full[i], (kb0 + i) * 64, m0);
+      if (hint)
+        tma_load_2d_hint(smem + i * S::kStageBytes, &tmA, &full[i], (kb0 + i) * 64, m0, pol);
+      else
+        tma_load_2d(smem + i * S::kStageBytes, &tmA, &full[i], (kb0 + i) * 64, m0);
     }
     pdl_wait();
     for (int i = 0; i < pre; ++i)
@@ -293,7 +298,10 @@ __global__ void __launch_bounds__(128, 1)
       uint8_t* a = smem + s * S::kStageBytes;
       uint8_t* b = a + S::kABytes;
       mbar_arrive_expect_tx(&full[s], S::kStageBytes);
-      tma_load_2d(a, &tmA, &full[s], (kb0 + i) * 64, m0);
+      if (hint)
+        tma_load_2d_hint(a, &tmA, &full[s], (kb0 + i) * 64, m0, pol);
+      else
+        tma_load_2d(a, &tmA, &full[s], (kb0 + i) * 64, m0);
       tma_load_2d(b, &tmB, &full[s], (kb0 + i) * 64, n0);
     }
   } else if (tid == 32) {
