@@ -9,7 +9,11 @@ result only between steps; then
   the remaining tree depths;
 - ``fallback_ar``: drop speculative routes, EXTEND the prefix with the Target's
   tokens, build a fresh tree.
-Neither side re-prefills its history.
+Neither side re-prefills its history.  A tree built by a handoff stops one
+decode step short: the paths (with the depth-d tokens still pending) are
+enough for the verify request, and the step that decodes the depth-d tokens
+runs first in the next round, while the Target verifies.  The reference
+decodes it before sending; the requests are identical.
 
 Parity: reference src/atlas_0709/distributed_system.py:47-1216 (config,
 round traces, result JSON, handoff modes, timeline, warmup and CLI flags).
@@ -119,9 +123,25 @@ class DistributedGenerationResult:
         }
 
 
+@dataclass
+class DeferredTree:
+    """A stage-1 tree whose last depth is not decoded yet.
+
+    ``routes`` carry ``d - 1`` materialized tokens and the depth-``d`` token as
+    their pending token (with its draft log-prob), which is all the verify
+    request needs.  The step that decodes the pending tokens -- KV for the
+    forest and the logits its roots start from -- then runs while the target
+    verifies instead of before the request is sent.  The tokens sent are the
+    ones a fully decoded tree would send.
+    """
+
+    routes: list[RouteState]
+    steps: list
+
+
 @dataclass(frozen=True)
 class StageHandoff:
-    stage1: BuildDepthsOutput
+    stage1: BuildDepthsOutput | DeferredTree
     mode: str
     reused_stage2_routes: int
     reused_stage2_depth: int
@@ -219,16 +239,32 @@ class PagedDistributedAtlasGenerator:
                     return out[: i + 1]
         return out
 
-    def _route_payloads(self, store: KVTreeStore, routes: Sequence[RouteState]) -> list[dict[str, object]]:
-        return [
-            {
+    def _route_payloads(self, store: KVTreeStore, routes: Sequence[RouteState], *,
+                        pending: bool = False) -> list[dict[str, object]]:
+        """Verify payloads; ``pending`` routes contribute their pending token as the last one."""
+        out = []
+        for r in routes:
+            depth = int(r.stage1_depth) + (1 if pending else 0)
+            path = store.pending_token_path(r) if pending else store.materialized_token_path(r)
+            out.append({
                 "route_id": int(r.route_id),
-                "token_ids": [int(t) for t in store.materialized_token_path(r)[: r.stage1_depth]],
+                "token_ids": [int(t) for t in path[:depth]],
                 "draft_logprob": float(r.cumulative_logprob),
-                "draft_token_logprobs": [float(v) for v in r.token_logprobs[: int(r.stage1_depth)]],
-            }
-            for r in routes
-        ]
+                "draft_token_logprobs": [float(v) for v in r.token_logprobs[:depth]],
+            })
+        return out
+
+    def _tree_for_verify(self, active: Sequence[RouteState], *, depth: int, store: KVTreeStore,
+                         sampling) -> DeferredTree:
+        """Decode ``depth - 1`` tree depths; the last one is left to run during the verify."""
+        steps: list = []
+        front = list(active)
+        for _ in range(int(depth) - 1):
+            st = build_tree_one_depth(front, k=self.config.k, route_store=store, model_backend=self.drafter,
+                                      sampling=sampling)
+            steps.append(st)
+            front = st.next_routes
+        return DeferredTree(front, steps)
 
     @staticmethod
     def _find_route(stage1: BuildDepthsOutput, route_id: int) -> RouteState:
@@ -287,9 +323,7 @@ class PagedDistributedAtlasGenerator:
         self.drafter.append_known_tokens_as_prefix(suffix)
         rs = self._sampling(store.committed_token_ids)
         active = initialize_stage1_routes(self.drafter.prefix_state(), k=self.config.k, route_store=store, sampling=rs)
-        stage1 = build_tree_depths(
-            active, depth=self.config.d, k=self.config.k, route_store=store, model_backend=self.drafter, sampling=rs
-        )
+        stage1 = self._tree_for_verify(active, depth=self.config.d, store=store, sampling=rs)
         return stage1, {
             "committed_kv_tokens": len(suffix),
             "retained_routes": 0,
@@ -356,15 +390,15 @@ class PagedDistributedAtlasGenerator:
         steps = []
         spans: list[EdgeSpan] = []
         front = list(promoted)
-        for i in range(remaining):
+        # The last depth is decoded during the next verify (see DeferredTree).
+        for i in range(remaining - 1):
             s1 = clock()
             st = build_tree_one_depth(front, k=cfg.k, route_store=store, model_backend=self.drafter, sampling=sampling)
             spans.append(EdgeSpan(f"edge_post_prune_tree_step_{i + 1}", s1, clock()))
             steps.append(st)
             front = st.next_routes
-        last = steps[-1]
         return StageHandoff(
-            stage1=BuildDepthsOutput(last.decoded_routes, last.next_routes, last.decode_output.next_token_logits, steps),
+            stage1=DeferredTree(front, steps),
             mode="partial_forest_pruned_then_build_tree",
             reused_stage2_routes=len(promoted),
             reused_stage2_depth=int(forest_depth),
@@ -456,7 +490,11 @@ class AtlasSession:
         committed, generated = self.committed, self.generated
         rs = g._sampling(committed)
         p_round = len(committed)
-        payload = g._route_payloads(store, self.stage1.completed_routes)
+        deferred = self.stage1 if isinstance(self.stage1, DeferredTree) else None
+        if deferred is not None:
+            payload = g._route_payloads(store, deferred.routes, pending=True)
+        else:
+            payload = g._route_payloads(store, self.stage1.completed_routes)
         v_submit = g._now()
         remaining = cfg.max_new_tokens - len(generated)
         # Set by the target (in-process transports) once it has decided to fall back:
@@ -464,11 +502,20 @@ class AtlasSession:
         # only compete with the target's AR forwards.
         fb_decided = threading.Event()
         vfut = g._vpool.submit(g._verify_call, list(committed), payload, remaining, self.round_index, fb_decided)
+        tree_spans: list[EdgeSpan] = []
+        if deferred is not None:
+            t0 = g._now()
+            with nvtx_range("edge_tree_last_depth"):
+                st = build_tree_one_depth(deferred.routes, k=cfg.k, route_store=store, model_backend=g.drafter,
+                                          sampling=rs)
+            self.stage1 = BuildDepthsOutput(st.decoded_routes, st.next_routes, st.decode_output.next_token_logits,
+                                            [*deferred.steps, st])
+            tree_spans.append(EdgeSpan("edge_tree_last_depth", t0, g._now()))
         if self.round_index == 0 and self.pre_frontier is not None:
             f_depth, f_done, f_logits = self.pre_depth, self.pre_completed, self.pre_logits
             f_spans, f_front = list(self.pre_spans), self.pre_frontier
         else:
-            f_depth, f_done, f_logits, f_spans = 0, None, None, []
+            f_depth, f_done, f_logits, f_spans = 0, None, None, list(tree_spans)
             f_front = initialize_forest_routes(
                 self.stage1.completed_routes, self.stage1.last_logits, k=cfg.k, route_store=store, sampling=rs
             )
@@ -543,9 +590,9 @@ class AtlasSession:
         if cfg.validate_state_alignment:
             g._validate_target_prefix_lengths(tmeta, p_round, len(committed))
             if not stop:
-                g._validate_drafter_prefix_state(
-                    store, committed, [*self.stage1.completed_routes, *self.stage1.next_frontier_routes]
-                )
+                live = (self.stage1.routes if isinstance(self.stage1, DeferredTree)
+                        else [*self.stage1.completed_routes, *self.stage1.next_frontier_routes])
+                g._validate_drafter_prefix_state(store, committed, live)
         trace = DistributedRoundTrace(
             round_index=self.round_index,
             selected_route_id=sel_id,
