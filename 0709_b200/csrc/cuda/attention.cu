@@ -330,35 +330,76 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
 }
 
 // One warp per (row, q head): merge split partials, then the row's tail keys.
-// Lanes fetch the split records and the tail slot ids in parallel and the
-// partial-O and K/V loads are issued in batches, so the warp is not a chain
-// of dependent global loads.
+// Latency-bound, so the kernel is arranged as few dependent round trips as
+// possible: the row's metadata and the first 32 tail keys' KV addresses are
+// resolved before the PDL wait (they come from graph inputs, not from the
+// kernels before this one); after it the split records, the query, all
+// non-empty partial O rows (16 splits per batch) and then up to 8 tail keys'
+// K/V per batch are loaded with every load of a batch in flight at once.
+// The arithmetic (split order, then keys in position order) is unchanged.
 template <typename T>
 __global__ void __launch_bounds__(128) attn_combine_tail(AttnParams p) {
-  pdl_wait();
-  pdl_trigger();
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const int64_t pair = static_cast<int64_t>(blockIdx.x) * 4 + warp;
-  if (pair >= static_cast<int64_t>(p.M) * p.Hq) return;
+  if (pair >= static_cast<int64_t>(p.M) * p.Hq) {
+    pdl_trigger();
+    return;
+  }
   const int m = static_cast<int>(pair / p.Hq);
   const int hq = static_cast<int>(pair % p.Hq);
   const int G = p.Hq / p.Hkv;
   const int h = hq / G;
-  const int shared_len = p.dparams[0];
-  const int n_shared_pages = p.dparams[1];
-  const int mask_base = p.dparams[2];
   const int ps = p.page_size;
   const float sl2 = p.scale * kLog2e;
   const int64_t stride_split = static_cast<int64_t>(p.M) * p.Hq;
+  const int64_t kv_head = static_cast<int64_t>(ps) * kHd;
 
-  // ---- split partials: lane s holds split s and s + 32 (splits <= 64)
+  // ---- before the wait: graph inputs only (metadata, masks, page tables)
+  const int shared_len = p.dparams[0];
+  const int n_shared_pages = p.dparams[1];
+  const int mask_base = p.dparams[2];
+  const int full = p.row_full[m];
+  const int rlen = p.row_len[m];
+  const int start = min(full, shared_len);
+  // Element offset of key x of this row in the cache, or -1 if x is not visible.
+  auto resolve = [&](int x) -> int64_t {
+    if (x >= rlen) return -1;
+    bool vis = x < full;
+    if (!vis) {
+      const int b = x - mask_base;
+      if (b >= 0 && b < 64 * p.mask_words) {
+        const uint64_t w = static_cast<uint64_t>(p.row_mask[static_cast<int64_t>(m) * p.mask_words + (b >> 6)]);
+        vis = (w >> (b & 63)) & 1ull;
+      }
+    }
+    if (!vis) return -1;
+    const int j = x / ps;
+    const bool in_shared = j < n_shared_pages || x < shared_len;
+    const int page = in_shared ? p.prefix_pages[j]
+                               : p.tail_pages[static_cast<int64_t>(m) * p.tail_stride + (j - n_shared_pages)];
+    if (page < 0 || page >= p.num_pages) {
+      set_error(p.err, kErrBadIndex);
+      return -1;
+    }
+    return ((static_cast<int64_t>(p.layer) * p.num_pages + page) * 2 * p.Hkv + h) * kv_head + (x % ps) * kHd;
+  };
+  const int64_t base_first = start < rlen ? resolve(start + lane) : -1;
+
+  pdl_wait();
+  pdl_trigger();
+
+  // ---- split records and the query (one round trip)
+  float2 ml0 = make_float2(-INFINITY, 0.f), ml1 = make_float2(-INFINITY, 0.f);
+  if (lane < p.splits) ml0 = p.part_ml[lane * stride_split + pair];
+  if (lane + 32 < p.splits) ml1 = p.part_ml[(lane + 32) * stride_split + pair];
+  const T* qp = static_cast<const T*>(p.q) + pair * kHd + lane * 4;
+  const float q0 = to_f32(qp[0]), q1 = to_f32(qp[1]), q2 = to_f32(qp[2]), q3 = to_f32(qp[3]);
+
+  // ---- merge the splits (lane s holds split s and s + 32; splits <= 64)
   float mx = -INFINITY, l = 0.f;
   float o[4] = {0.f, 0.f, 0.f, 0.f};
   if (p.splits > 0) {
-    float2 ml0 = make_float2(-INFINITY, 0.f), ml1 = make_float2(-INFINITY, 0.f);
-    if (lane < p.splits) ml0 = p.part_ml[lane * stride_split + pair];
-    if (lane + 32 < p.splits) ml1 = p.part_ml[(lane + 32) * stride_split + pair];
     if (!(ml0.y > 0.f)) ml0.x = -INFINITY;
     if (!(ml1.y > 0.f)) ml1.x = -INFINITY;
     mx = warp_max(fmaxf(ml0.x, ml1.x));
@@ -367,21 +408,20 @@ __global__ void __launch_bounds__(128) attn_combine_tail(AttnParams p) {
       const float w1 = ml1.x > -INFINITY ? exp2f(ml1.x - mx) : 0.f;
       l = warp_sum(w0 * ml0.y + w1 * ml1.y);
       const float* po = p.part_o + pair * kHd + lane * 4;
-      for (int s0 = 0; s0 < p.splits; s0 += 8) {
-        float4 ov[8];
-        float wv[8];
+      for (int s0 = 0; s0 < p.splits; s0 += 16) {
+        float4 ov[16];
+        float wv[16];
 #pragma unroll
-        for (int j = 0; j < 8; ++j) {
+        for (int j = 0; j < 16; ++j) {
           const int sidx = s0 + j;
           const float wsrc = sidx < 32 ? __shfl_sync(0xffffffffu, w0, sidx & 31)
                                        : __shfl_sync(0xffffffffu, w1, sidx & 31);
           wv[j] = sidx < p.splits ? wsrc : 0.f;
-          ov[j] = (sidx < p.splits && wv[j] > 0.f)
-                      ? *reinterpret_cast<const float4*>(po + static_cast<int64_t>(sidx) * stride_split * kHd)
-                      : make_float4(0.f, 0.f, 0.f, 0.f);
+          ov[j] = wv[j] > 0.f ? *reinterpret_cast<const float4*>(po + static_cast<int64_t>(sidx) * stride_split * kHd)
+                              : make_float4(0.f, 0.f, 0.f, 0.f);
         }
 #pragma unroll
-        for (int j = 0; j < 8; ++j) {
+        for (int j = 0; j < 16; ++j) {
           o[0] += wv[j] * ov[j].x;
           o[1] += wv[j] * ov[j].y;
           o[2] += wv[j] * ov[j].z;
@@ -391,44 +431,15 @@ __global__ void __launch_bounds__(128) attn_combine_tail(AttnParams p) {
     }
   }
 
-  // ---- tail keys [start, row_len): lane t resolves position start + t (+32 ...)
-  const T* qp = static_cast<const T*>(p.q) + pair * kHd + lane * 4;
-  const float q0 = to_f32(qp[0]), q1 = to_f32(qp[1]), q2 = to_f32(qp[2]), q3 = to_f32(qp[3]);
-  const int full = p.row_full[m];
-  const int rlen = p.row_len[m];
-  const int start = min(full, shared_len);
-  const int64_t kv_head = static_cast<int64_t>(ps) * kHd;
+  // ---- tail keys [start, rlen): lane t resolves key t0 + t; K/V of 8 keys per batch
   for (int t0 = start; t0 < rlen; t0 += 32) {
-    const int x = t0 + lane;
-    int64_t base = -1;
-    if (x < rlen) {
-      bool vis = x < full;
-      if (!vis) {
-        const int b = x - mask_base;
-        if (b >= 0 && b < 64 * p.mask_words) {
-          const uint64_t w = static_cast<uint64_t>(p.row_mask[static_cast<int64_t>(m) * p.mask_words + (b >> 6)]);
-          vis = (w >> (b & 63)) & 1ull;
-        }
-      }
-      if (vis) {
-        const int j = x / ps;
-        const bool in_shared = j < n_shared_pages || x < shared_len;
-        const int page = in_shared ? p.prefix_pages[j]
-                                   : p.tail_pages[static_cast<int64_t>(m) * p.tail_stride + (j - n_shared_pages)];
-        if (page < 0 || page >= p.num_pages) {
-          set_error(p.err, kErrBadIndex);
-        } else {
-          base = ((static_cast<int64_t>(p.layer) * p.num_pages + page) * 2 * p.Hkv + h) * kv_head + (x % ps) * kHd;
-        }
-      }
-    }
+    const int64_t base = t0 == start ? base_first : resolve(t0 + lane);
     const int cnt = min(32, rlen - t0);
-    for (int j0 = 0; j0 < cnt; j0 += 4) {
-      int64_t bj[4];
-      float4 kf[4];
-      float2 kh[4], vh[4];
+    for (int j0 = 0; j0 < cnt; j0 += 8) {
+      int64_t bj[8];
+      float2 kh[8], vh[8];
 #pragma unroll
-      for (int u = 0; u < 4; ++u) {
+      for (int u = 0; u < 8; ++u) {
         bj[u] = (j0 + u < cnt) ? __shfl_sync(0xffffffffu, base, j0 + u) : -1;
         if (bj[u] >= 0) {
           const T* kp = static_cast<const T*>(p.kv) + bj[u] + lane * 4;
@@ -437,7 +448,7 @@ __global__ void __launch_bounds__(128) attn_combine_tail(AttnParams p) {
         }
       }
 #pragma unroll
-      for (int u = 0; u < 4; ++u) {
+      for (int u = 0; u < 8; ++u) {
         if (bj[u] < 0) continue;  // warp-uniform
         const T* ke = reinterpret_cast<const T*>(&kh[u]);
         const T* ve = reinterpret_cast<const T*>(&vh[u]);
@@ -451,7 +462,6 @@ __global__ void __launch_bounds__(128) attn_combine_tail(AttnParams p) {
         o[3] = o[3] * a + w * to_f32(ve[3]);
         l = l * a + w;
         mx = nm;
-        (void)kf;
       }
     }
   }

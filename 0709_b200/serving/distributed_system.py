@@ -41,6 +41,10 @@ def build_parser() -> argparse.ArgumentParser:
     p.add_argument("--k", type=int, default=3)
     p.add_argument("--d", type=int, default=4)
     p.add_argument("--fixed-forest-depth", type=int, default=None)
+    p.add_argument("--forest-gate", choices=["overlap", "adaptive"], default="adaptive",
+                   help="overlap: always grow the forest during the verify (reference schedule); adaptive: wait for "
+                        "the target's decision while most recent rounds fell back.")
+    p.add_argument("--forest-gate-threshold", type=float, default=0.75)
     p.add_argument("--validate-state-alignment", action="store_true")
     p.add_argument("--max-new-tokens", type=int, default=16)
     p.add_argument("--eos-token-id", type=int, default=None)
@@ -119,7 +123,8 @@ def main(argv=None) -> int:
             k=args.k, d=args.d, max_new_tokens=max_new, eos_token_id=eos, fallback_ar_tokens=args.fallback_ar_tokens,
             generation_seed=args.generation_seed, drafter_do_sample=args.drafter_do_sample,
             drafter_temperature=args.drafter_temperature, fixed_forest_depth=args.fixed_forest_depth,
-            validate_state_alignment=args.validate_state_alignment)
+            validate_state_alignment=args.validate_state_alignment, forest_gate=args.forest_gate,
+            forest_gate_threshold=args.forest_gate_threshold)
 
     warm_s = 0.0
     for i in range(args.warmup_runs):

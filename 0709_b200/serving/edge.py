@@ -59,6 +59,14 @@ class DistributedAtlasConfig:
     drafter_temperature: float = 1.0
     fixed_forest_depth: int | None = None
     validate_state_alignment: bool = False
+    # "overlap": the drafter decodes the rest of the tree and the forest while the
+    # target verifies (the reference schedule).  "adaptive": the same, except while
+    # the moving average of fallback decisions is >= forest_gate_threshold; then
+    # the drafter first waits for the target's decision, and on a fallback spends
+    # nothing on a tree and forest that the fallback discards (they would only
+    # compete with the target's AR steps for the GPU).  Tokens are identical.
+    forest_gate: str = "adaptive"
+    forest_gate_threshold: float = 0.75
 
     def validate(self) -> None:
         if self.k <= 0:
@@ -74,6 +82,10 @@ class DistributedAtlasConfig:
             raise ValueError("drafter_temperature must be finite and positive")
         if self.fixed_forest_depth is not None and not 0 <= int(self.fixed_forest_depth) <= int(self.d):
             raise ValueError("fixed_forest_depth must be between 0 and d")
+        if self.forest_gate not in ("overlap", "adaptive"):
+            raise ValueError("forest_gate must be 'overlap' or 'adaptive'")
+        if not 0.0 < float(self.forest_gate_threshold) <= 1.0:
+            raise ValueError("forest_gate_threshold must be in (0, 1]")
 
 
 @dataclass
@@ -198,6 +210,8 @@ class PagedDistributedAtlasGenerator:
         self.tokenizer = tokenizer
         self.last_timeline: EdgeBlackboxTimeline | None = None
         self._t0: float | None = None
+        # Moving average of fallback decisions (forest_gate="adaptive"); kept across prompts.
+        self.fallback_ema = 0.0
 
     # ------------------------------------------------------------ helpers
     def _now(self) -> float:
@@ -273,10 +287,16 @@ class PagedDistributedAtlasGenerator:
                 return r
         raise KeyError(f"selected route_id={route_id} is not in the completed stage1 routes")
 
-    def _verify_call(self, committed, routes, remaining, round_index, fallback_event=None):
+    def _verify_call(self, committed, routes, remaining, round_index, fallback_event=None, decision_event=None):
         kw = {}
         if fallback_event is not None and getattr(self.target_client, "supports_early_decision", False):
-            kw["on_decision"] = lambda decision: fallback_event.set() if decision == "fallback_ar" else None
+            def on_decision(decision):
+                if decision == "fallback_ar":
+                    fallback_event.set()
+                if decision_event is not None:
+                    decision_event.set()
+
+            kw["on_decision"] = on_decision
         resp = self.target_client.verify(
             prefix_token_ids=committed,
             routes=routes,
@@ -446,6 +466,7 @@ class AtlasSession:
         self.finished = False
         self.round_index = 0
         self.store = KVTreeStore()
+        self.gated_rounds = 0
 
     def begin(self) -> None:
         g, cfg = self.gen, self.gen.config
@@ -501,9 +522,20 @@ class AtlasSession:
         # the forest of this round is then discarded, so growing it further would
         # only compete with the target's AR forwards.
         fb_decided = threading.Event()
-        vfut = g._vpool.submit(g._verify_call, list(committed), payload, remaining, self.round_index, fb_decided)
+        decided = threading.Event()
+        vfut = g._vpool.submit(g._verify_call, list(committed), payload, remaining, self.round_index, fb_decided,
+                               decided)
+        vfut.add_done_callback(lambda _f: decided.set())
+        gated = (cfg.forest_gate == "adaptive" and cfg.fixed_forest_depth is None
+                 and g.fallback_ema >= float(cfg.forest_gate_threshold))
+        if gated:
+            self.gated_rounds += 1
+            while not decided.wait(0.05) and not vfut.done():
+                pass
+        # A gated round that falls back builds nothing: the fallback drops this tree.
+        skip = gated and fb_decided.is_set()
         tree_spans: list[EdgeSpan] = []
-        if deferred is not None:
+        if deferred is not None and not skip:
             t0 = g._now()
             with nvtx_range("edge_tree_last_depth"):
                 st = build_tree_one_depth(deferred.routes, k=cfg.k, route_store=store, model_backend=g.drafter,
@@ -511,7 +543,9 @@ class AtlasSession:
             self.stage1 = BuildDepthsOutput(st.decoded_routes, st.next_routes, st.decode_output.next_token_logits,
                                             [*deferred.steps, st])
             tree_spans.append(EdgeSpan("edge_tree_last_depth", t0, g._now()))
-        if self.round_index == 0 and self.pre_frontier is not None:
+        if skip:
+            f_depth, f_done, f_logits, f_spans, f_front = 0, None, None, [], []
+        elif self.round_index == 0 and self.pre_frontier is not None:
             f_depth, f_done, f_logits = self.pre_depth, self.pre_completed, self.pre_logits
             f_spans, f_front = list(self.pre_spans), self.pre_frontier
         else:
@@ -519,7 +553,8 @@ class AtlasSession:
             f_front = initialize_forest_routes(
                 self.stage1.completed_routes, self.stage1.last_logits, k=cfg.k, route_store=store, sampling=rs
             )
-        while g._should_build_forest_step(verify_done=vfut.done() or fb_decided.is_set(), forest_depth=f_depth):
+        while not skip and g._should_build_forest_step(verify_done=vfut.done() or fb_decided.is_set(),
+                                                       forest_depth=f_depth):
             t0 = g._now()
             with nvtx_range(f"edge_forest_depth_{f_depth + 1}"):
                 st = build_forest_one_depth(f_front, k=cfg.k, route_store=store, model_backend=g.drafter,
@@ -535,6 +570,7 @@ class AtlasSession:
         if isinstance(prof, dict):
             self.fallback_profiles.append({"round_index": self.round_index, **prof})
         decision = str(resp.get("decision", "select"))
+        g.fallback_ema = 0.7 * g.fallback_ema + 0.3 * (1.0 if decision == "fallback_ar" else 0.0)
         sel_id: int | None = None
         reason: str | None = None
         fb_tokens: list[int] = []
@@ -675,6 +711,9 @@ class AtlasSession:
                 "route_tail_page_cow": True,
                 "branch_safe_page_size": True,
                 "forest_cancel_granularity": "between_decode_steps",
+                "forest_gate": cfg.forest_gate,
+                "forest_gate_threshold": float(cfg.forest_gate_threshold),
+                "forest_gated_rounds": self.gated_rounds,
                 "rounds": len(self.traces),
                 "fallback_rounds": fb_rounds,
                 "fallback_rate": fb_rounds / len(self.traces) if self.traces else None,

@@ -66,6 +66,8 @@ def parse() -> argparse.Namespace:
     p.add_argument("--fallback-ar-tokens", type=int, default=4)
     p.add_argument("--seed", type=int, default=0)
     p.add_argument("--e2e-prompts", type=int, default=1)
+    p.add_argument("--forest-gate", choices=["overlap", "adaptive"], default="adaptive",
+                   help="drafter forest schedule (see DistributedAtlasConfig.forest_gate)")
     p.add_argument("--target-stream-priority", type=int, default=-1,
                    help="CUDA priority of the target's stream (lower = higher; 0 = same as the drafter)")
     return p.parse_args()
@@ -161,7 +163,7 @@ def build(args, device):
     gen = edge.PagedDistributedAtlasGenerator(
         config=edge.DistributedAtlasConfig(
             k=args.k, d=args.d, max_new_tokens=args.max_new_tokens, fallback_ar_tokens=args.fallback_ar_tokens,
-            generation_seed=args.seed,
+            generation_seed=args.seed, forest_gate=args.forest_gate,
         ),
         drafter=dr,
         target_client=client,
@@ -323,6 +325,7 @@ def main() -> int:
                 "fallback_threshold": args.fallback_threshold,
                 "first_token_threshold": args.first_token_threshold,
                 "fallback_ar_tokens": args.fallback_ar_tokens,
+                "forest_gate": args.forest_gate,
                 "step": "one speculative round (verify || forest, handoff); next prompt's prefill inside its step",
                 "l2": "weights (~17 GB) stream every step; working set far above L2",
                 "rounds_timed": drv.rounds - r0,

@@ -39,7 +39,7 @@ def greedy(w, prompt, n):
     return toks[len(prompt):]
 
 
-def make_generator(dw, tw, *, k=K, d=D, serial=False, **target_kw):
+def make_generator(dw, tw, *, k=K, d=D, serial=False, cfg_kw=None, **target_kw):
     engine = mod("runtime.engine")
     drafter = mod("runtime.drafter")
     target = mod("runtime.target")
@@ -49,8 +49,9 @@ def make_generator(dw, tw, *, k=K, d=D, serial=False, **target_kw):
     te = engine.LlamaEngine(tw, num_pages=512, page_size=PAGE, max_positions=512)
     tv = target.TargetVerifier(te, k=k, d=d, **target_kw)
     cls = mod("serving.serial").SerialAtlasGenerator if serial else edge.PagedDistributedAtlasGenerator
-    cfg = edge.DistributedAtlasConfig(k=k, d=d, max_new_tokens=16, validate_state_alignment=True,
-                                      fixed_forest_depth=None if serial else 2)
+    kw = dict(k=k, d=d, max_new_tokens=16, validate_state_alignment=True, fixed_forest_depth=None if serial else 2)
+    kw.update(cfg_kw or {})
+    cfg = edge.DistributedAtlasConfig(**kw)
     return cls(config=cfg, drafter=drafter.DrafterRuntime(de), target_client=rpc.InProcessTargetClient(tv))
 
 
@@ -120,3 +121,30 @@ def test_serial_equals_async_when_target_selects(models):
     s = make_generator(dw, tw, serial=True).generate(p)
     assert a.generated_token_ids == s.generated_token_ids
     assert all(r.handoff_mode.startswith("serial_") for r in s.rounds)
+
+
+def test_adaptive_forest_gate_keeps_tokens(models):
+    """Gated rounds (after repeated fallbacks) build no tree or forest; the tokens do not change."""
+    dw, tw = models
+    p = prompts(3)[2]
+    out = {}
+    for gate in ("overlap", "adaptive"):
+        cfg = dict(fixed_forest_depth=None, forest_gate=gate, max_new_tokens=32)
+        res = make_generator(dw, tw, cfg_kw=cfg, fallback_threshold=1e9).generate(p)
+        assert all(r.decision == "fallback_ar" for r in res.rounds)
+        out[gate] = res
+    assert out["adaptive"].generated_token_ids == out["overlap"].generated_token_ids == greedy(tw, p, 32)
+    assert out["overlap"].metadata["forest_gated_rounds"] == 0
+    gated = out["adaptive"].metadata["forest_gated_rounds"]
+    assert gated >= 3
+    # Gated fallback rounds grew no forest.
+    assert sum(r.forest_depth == 0 for r in out["adaptive"].rounds) >= gated
+
+
+def test_forest_gate_stays_open_when_routes_are_selected(models):
+    dw, tw = models
+    p = prompts(4)[3]
+    cfg = dict(fixed_forest_depth=None, forest_gate="adaptive", max_new_tokens=16)
+    res = make_generator(dw, tw, k=1, cfg_kw=cfg, route_selection_policy="first_route").generate(p)
+    assert all(r.decision == "select" for r in res.rounds)
+    assert res.metadata["forest_gated_rounds"] == 0
