@@ -141,7 +141,7 @@ class DrafterRuntime:
     def prefix_state(self) -> DraftPrefixState:
         assert self.prefix_next_token_logits is not None
         return DraftPrefixState(
-            token_ids=torch.tensor(self.prefix_token_ids, dtype=torch.long),
+            token_tuple=tuple(self.prefix_token_ids),
             prefix_kv_view=PrefixKVView(committed_length=len(self.prefix_token_ids)),
             next_token_logits=self.prefix_next_token_logits,
             committed_length=len(self.prefix_token_ids),

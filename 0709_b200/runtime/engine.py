@@ -134,14 +134,13 @@ class LlamaEngine:
     def _run_rows_locked(self, rows, tail_stride, mask_words, prefix_pages, fields):
         sb = self.static_batch(rows, tail_stride, mask_words)
         n = sb.load(**fields)
-        desc = sb.desc(prefix_pages)
         if self.device.type != "cuda" or not self.use_graphs:
-            logits = self.forward(sb.tokens, sb.positions, sb.slots, desc)
+            logits = self.forward(sb.tokens, sb.positions, sb.slots, sb.desc(prefix_pages))
             return logits[sb.real_slice(n)].clone()
         key = (sb.key, prefix_pages.data_ptr())
         graph = self._graphs.get(key)
-        if graph is None:
-            graph = self._capture(sb, desc)
+        if graph is None:  # a replay reads the static inputs directly; only a capture needs the descriptor
+            graph = self._capture(sb, sb.desc(prefix_pages))
             self._graphs[key] = graph
         g, out, launches = graph
         g.replay()

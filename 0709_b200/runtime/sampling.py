@@ -65,18 +65,25 @@ class DrafterSamplingContext:
 
     def __post_init__(self) -> None:
         self.config.validate()
-        toks = tuple(int(t) for t in self.committed_token_ids)
-        object.__setattr__(self, "committed_token_ids", toks)
-        h = hashlib.blake2b(digest_size=8)
-        h.update(_DOMAIN)
-        h.update(struct.pack("<Q", int(self.config.seed) & _M64))
-        h.update(_pack_tokens(toks))
-        object.__setattr__(self, "_prefix_state", h)
+        if not isinstance(self.committed_token_ids, tuple):
+            object.__setattr__(self, "committed_token_ids", tuple(int(t) for t in self.committed_token_ids))
+
+    def _prefix_hash(self):
+        """Hash state of (domain, seed, committed prefix); built on first use -- greedy
+        drafting never needs it, and the prefix grows to thousands of tokens."""
+        h = self._prefix_state
+        if h is None:
+            h = hashlib.blake2b(digest_size=8)
+            h.update(_DOMAIN)
+            h.update(struct.pack("<Q", int(self.config.seed) & _M64))
+            h.update(_pack_tokens(self.committed_token_ids))
+            object.__setattr__(self, "_prefix_state", h)
+        return h
 
     def seed_for_parent(self, relative_parent_path: Sequence[int]) -> int:
         """63-bit key for the parent whose absolute history is prefix + relative path."""
         rel = tuple(int(t) for t in relative_parent_path)
-        h = self._prefix_state.copy()  # type: ignore[union-attr]
+        h = self._prefix_hash().copy()
         h.update(_pack_tokens(rel))
         h.update(struct.pack("<Q", len(self.committed_token_ids) + len(rel)))
         return int.from_bytes(h.digest(), "little") & KEY_MASK

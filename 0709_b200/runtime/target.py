@@ -166,9 +166,9 @@ class TargetVerifier:
     ) -> TargetVerifyResult:
         """Verify the routes; ``on_decision(decision)`` (optional) is called as soon as the
         decision is known, before the fallback AR tokens are generated or the path is committed."""
-        prefix = tuple(int(t) for t in prefix_token_ids)
+        prefix = tuple(prefix_token_ids)  # element-wise == also accepts numpy integers
         if self._prefix_logits is None:
-            self.prefill(prefix)
+            self.prefill([int(t) for t in prefix])
         elif prefix != self.prefix_token_ids:
             raise RuntimeError(
                 "target committed prefix mismatch; incremental verify cannot silently rebuild KV: "
@@ -184,7 +184,64 @@ class TargetVerifier:
         )
         reason = self._fallback_reason(selected)
         p_before = len(self.prefix_token_ids)
-        common = {
+        if on_decision is not None:
+            on_decision("fallback_ar" if reason is not None else "select")
+        meta: dict[str, object] = {}
+
+        def build_metadata() -> None:
+            meta.update(self._verify_metadata(routes, depth, tree, p_before, scores, best, selected, sampling_meta))
+
+        if reason is not None:
+            limit = self.fallback_ar_tokens if fallback_max_tokens is None else min(
+                int(fallback_max_tokens), self.fallback_ar_tokens
+            )
+            # The response metadata is assembled while the AR steps run on the GPU.
+            with nvtx_range("target_fallback_ar"):
+                generated = self._generate_fallback_ar(max_tokens=limit, eos_token_id=eos_token_id,
+                                                       while_running=build_metadata)
+            return TargetVerifyResult(
+                selected_route_id=None,
+                scores=scores,
+                decision="fallback_ar",
+                fallback_token_ids=tuple(generated),
+                fallback_reason=reason,
+                metadata={
+                    **meta,
+                    "prefix_len_after": int(len(self.prefix_token_ids)),
+                    "target_kv_commit": "fallback_ar_in_place",
+                    "target_reprefill_after_verify": False,
+                    "fallback_triggered": True,
+                    "fallback_reason": reason,
+                    "fallback_token_count": int(len(generated)),
+                    "fallback_ar_profile": self._last_fallback_ar_profile,
+                },
+            )
+        build_metadata()
+        idx = next(i for i, r in enumerate(routes) if int(r.route_id) == int(selected.route_id))
+        node_path = tree["node_paths"][idx]
+        committed_path, committed_nodes = self._truncate_selected_path(
+            token_ids=paths[idx], node_ids=node_path, max_tokens=selected_path_max_tokens, eos_token_id=eos_token_id
+        )
+        self._commit_selected_path(committed_path, committed_nodes, tree["logits"])
+        return TargetVerifyResult(
+            selected_route_id=selected.route_id,
+            scores=scores,
+            metadata={
+                **meta,
+                "prefix_len_after": int(len(self.prefix_token_ids)),
+                "target_kv_commit": "selected_tree_path_in_place",
+                "target_reprefill_after_verify": False,
+                "fallback_triggered": False,
+                "selected_route_id": int(selected.route_id),
+                "selected_selection_score": float(selected.effective_selection_score),
+                "selected_path_committed_tokens": int(len(committed_path)),
+                "selected_path_was_truncated": bool(len(committed_path) != len(paths[idx])),
+            },
+        )
+
+    def _verify_metadata(self, routes, depth, tree, p_before, scores, best, selected, sampling_meta) -> dict:
+        """Response metadata of one verify (state as of before its commit)."""
+        return {
             **self.runtime_metadata(),
             "route_count": len(routes),
             "path_depth": int(depth),
@@ -201,62 +258,12 @@ class TargetVerifier:
             "fallback_ar_tokens": int(self.fallback_ar_tokens),
             **sampling_meta,
             **self._route_intervention_metadata(scores, selected),
-        }
-        best_fields = {
             "best_route_id": int(best.route_id),
             "best_selection_score": float(best.effective_selection_score),
             "best_first_token_logprob": (
                 None if best.first_token_logprob is None else float(best.first_token_logprob)
             ),
         }
-        if on_decision is not None:
-            on_decision("fallback_ar" if reason is not None else "select")
-        if reason is not None:
-            limit = self.fallback_ar_tokens if fallback_max_tokens is None else min(
-                int(fallback_max_tokens), self.fallback_ar_tokens
-            )
-            with nvtx_range("target_fallback_ar"):
-                generated = self._generate_fallback_ar(max_tokens=limit, eos_token_id=eos_token_id)
-            return TargetVerifyResult(
-                selected_route_id=None,
-                scores=scores,
-                decision="fallback_ar",
-                fallback_token_ids=tuple(generated),
-                fallback_reason=reason,
-                metadata={
-                    **common,
-                    "prefix_len_after": int(len(self.prefix_token_ids)),
-                    "target_kv_commit": "fallback_ar_in_place",
-                    "target_reprefill_after_verify": False,
-                    "fallback_triggered": True,
-                    "fallback_reason": reason,
-                    "fallback_token_count": int(len(generated)),
-                    **best_fields,
-                    "fallback_ar_profile": self._last_fallback_ar_profile,
-                },
-            )
-        idx = next(i for i, r in enumerate(routes) if int(r.route_id) == int(selected.route_id))
-        node_path = tree["node_paths"][idx]
-        committed_path, committed_nodes = self._truncate_selected_path(
-            token_ids=paths[idx], node_ids=node_path, max_tokens=selected_path_max_tokens, eos_token_id=eos_token_id
-        )
-        self._commit_selected_path(committed_path, committed_nodes, tree["logits"])
-        return TargetVerifyResult(
-            selected_route_id=selected.route_id,
-            scores=scores,
-            metadata={
-                **common,
-                "prefix_len_after": int(len(self.prefix_token_ids)),
-                "target_kv_commit": "selected_tree_path_in_place",
-                "target_reprefill_after_verify": False,
-                "fallback_triggered": False,
-                **best_fields,
-                "selected_route_id": int(selected.route_id),
-                "selected_selection_score": float(selected.effective_selection_score),
-                "selected_path_committed_tokens": int(len(committed_path)),
-                "selected_path_was_truncated": bool(len(committed_path) != len(paths[idx])),
-            },
-        )
 
     def _validate_routes(self, routes: Sequence[VerifyRoutePayload]) -> tuple[list[tuple[int, ...]], int]:
         if not routes:
@@ -613,7 +620,9 @@ class TargetVerifier:
             torch.cuda.synchronize(self.device)
 
     @torch.inference_mode()
-    def _generate_fallback_ar(self, *, max_tokens: int, eos_token_id: int | None) -> list[int]:
+    def _generate_fallback_ar(self, *, max_tokens: int, eos_token_id: int | None, while_running=None) -> list[int]:
+        """Greedy AR from the committed prefix; ``while_running`` (optional) is called after
+        every step is enqueued and before the host waits for the tokens."""
         if self._prefix_logits is None:
             raise RuntimeError("target fallback AR requires initialized prefix KV")
         steps = int(max_tokens)
@@ -662,6 +671,8 @@ class TargetVerifier:
                 row_len=[p + t + 1],
             )
             all_logits.append(cur)
+        if while_running is not None:
+            while_running()
         if toks.is_cuda:
             counters.d2h(toks.numel() * 4)
         generated = [int(x) for x in toks.cpu().tolist()]

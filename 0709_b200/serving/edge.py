@@ -229,7 +229,7 @@ class PagedDistributedAtlasGenerator:
         return DrafterSamplingConfig(bool(c.drafter_do_sample), int(c.generation_seed), float(c.drafter_temperature))
 
     def _sampling(self, committed: Sequence[int]) -> DrafterSamplingContext:
-        return DrafterSamplingContext(self._sampling_config(), tuple(int(t) for t in committed))
+        return DrafterSamplingContext(self._sampling_config(), tuple(committed))
 
     def _should_build_forest_step(self, *, verify_done: bool, forest_depth: int) -> bool:
         if forest_depth >= self.config.d:

@@ -117,10 +117,15 @@ class FrontierSelectionStats:
 
 @dataclass(frozen=True)
 class DraftPrefixState:
-    token_ids: torch.Tensor
+    token_tuple: tuple[int, ...]
     prefix_kv_view: PrefixKVView
     next_token_logits: torch.Tensor
     committed_length: int
+
+    @property
+    def token_ids(self) -> torch.Tensor:
+        """The committed prefix as an int64 tensor (built on request: prefixes are long)."""
+        return torch.tensor(self.token_tuple, dtype=torch.long)
 
 
 @dataclass(frozen=True)
