@@ -137,8 +137,9 @@ class TPLlamaEngine(LlamaEngine):
         if graph is None:
             graph = self._capture(sb, desc)
             self._graphs[key] = graph
-        g, out, launches = graph
-        g.replay()
+        graphs, out, launches = graph[0], graph[1], graph[2]
+        for g in graphs:
+            g.replay()
         if launches:
             from ..utils import counters
 

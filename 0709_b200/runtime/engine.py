@@ -86,6 +86,11 @@ class LlamaEngine:
         self._static: dict[tuple[int, int, int], StaticBatch] = {}
         self._graphs: dict = {}
         self._graph_pool = torch.cuda.graph_pool_handle() if self.device.type == "cuda" else None
+        # A forward's graph is captured as a short head (embedding + the first
+        # layers) and the rest: launching a graph costs the host ~1 us per node,
+        # and with one graph the GPU would wait for all of it; with two it starts
+        # on the head while the host still launches the tail.
+        self.graph_head_layers = int(os.environ.get("ATLAS_GRAPH_HEAD_LAYERS", "2"))
         # Scratch page for padded rows' KV writes (never part of any sequence).
         self.trash_slot = (self.num_pages - 1) * self.page_size
 
@@ -142,8 +147,9 @@ class LlamaEngine:
         if graph is None:  # a replay reads the static inputs directly; only a capture needs the descriptor
             graph = self._capture(sb, sb.desc(prefix_pages))
             self._graphs[key] = graph
-        g, out, launches = graph
-        g.replay()
+        graphs, out, launches = graph[0], graph[1], graph[2]
+        for g in graphs:
+            g.replay()
         if launches:
             from ..utils import counters
 
@@ -179,20 +185,45 @@ class LlamaEngine:
             for _ in range(2):
                 self.forward(sb.tokens, sb.positions, sb.slots, desc)
         torch.cuda.current_stream(self.device).wait_stream(stream)
-        g = torch.cuda.CUDAGraph()
         before = counters.snapshot()["launches"]
+        split = self._graph_split()
+        keep = ()
         # Capture on the side stream without the device-wide synchronize that
         # ``torch.cuda.graph`` performs first: another serving thread may be
         # capturing or running at the same time (thread-local capture mode).
         with torch.cuda.stream(stream):
-            g.capture_begin(self._graph_pool, capture_error_mode="thread_local")
-            try:
-                out = self.forward(sb.tokens, sb.positions, sb.slots, desc)
-            finally:
-                g.capture_end()
+            if split:
+                # Head: embedding + layers [0, split).  The residual stream and
+                # its norm statistics carry over to the tail graph; they stay
+                # referenced so no other capture reuses their memory.
+                g1 = self._capture_one(lambda: self._fused_layers(
+                    self.ops.embed_norm(sb.tokens, self.w.embed), sb.positions, sb.slots, desc, None, 0, split))
+                keep = g1[1]
+                g2 = self._capture_one(lambda: self._fused_end(
+                    self._fused_layers(keep, sb.positions, sb.slots, desc, None, split, self.cfg.num_layers), None))
+                graphs, out = [g1[0], g2[0]], g2[1]
+            else:
+                g, out = self._capture_one(lambda: self.forward(sb.tokens, sb.positions, sb.slots, desc))
+                graphs = [g]
         torch.cuda.current_stream(self.device).wait_stream(stream)
         launches = counters.snapshot()["launches"] - before
-        return g, out, launches
+        return graphs, out, launches, keep
+
+    def _capture_one(self, fn):
+        g = torch.cuda.CUDAGraph()
+        g.capture_begin(self._graph_pool, capture_error_mode="thread_local")
+        try:
+            out = fn()
+        finally:
+            g.capture_end()
+        return g, out
+
+    def _graph_split(self) -> int:
+        """Layers in the head graph (0: one graph), for the folded-norm forward of this class."""
+        if not self.fused_norm or type(self).forward is not LlamaEngine.forward:
+            return 0
+        k = self.graph_head_layers
+        return k if 0 < k < self.cfg.num_layers else 0
 
     @torch.inference_mode()
     def forward(
@@ -240,11 +271,19 @@ class LlamaEngine:
 
     def _forward_fused(self, tokens, positions, slots, desc, logits_rows, causal_start):
         """CUDA forward with RMSNorm folded into the GEMMs (no norm or RoPE kernels)."""
+        state = self.ops.embed_norm(tokens, self.w.embed)
+        state = self._fused_layers(state, positions, slots, desc, causal_start, 0, self.cfg.num_layers)
+        return self._fused_end(state, logits_rows)
+
+    def _fused_layers(self, state, positions, slots, desc, causal_start, l0: int, l1: int):
+        """Layers [l0, l1) on the residual stream ``state`` = (h fp32, hb activation copy,
+        per-128-feature sums of h^2), updated in place; returns ``state``."""
         o = self.ops
         c = self.cfg
-        layers, lm = self._folded
-        h, hb, ss = o.embed_norm(tokens, self.w.embed)
-        for li, lw in enumerate(self.w.layers):
+        h, hb, ss = state
+        layers = self._folded[0]
+        for li in range(l0, l1):
+            lw = self.w.layers[li]
             wqkv, wgu = layers[li]
             q = o.qkv_rope(hb, wqkv, ss, c.rms_eps, self.rope, positions, slots, self.kv[li], c.num_heads,
                            c.num_kv_heads)
@@ -252,6 +291,14 @@ class LlamaEngine:
             o.linear_residual_norm(a, lw.wo, h, hb, ss)
             act = o.gate_up_silu_norm(hb, wgu, ss, c.rms_eps)
             o.linear_residual_norm(act, lw.wd, h, hb, ss)
+        return state
+
+    def _fused_end(self, state, logits_rows):
+        """Final norm (folded into the LM head) on the rows ``logits_rows`` (default: all)."""
+        o = self.ops
+        c = self.cfg
+        _, hb, ss = state
+        lm = self._folded[1]
         if logits_rows is not None:
             sel = logits_rows.long()
             hb = hb.index_select(0, sel)
