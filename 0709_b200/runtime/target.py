@@ -112,6 +112,9 @@ class TargetVerifier:
         self.prefill_chunk_size = int(prefill_chunk_size)
         self.prefix_token_ids: tuple[int, ...] = ()
         self._prefix_logits: torch.Tensor | None = None
+        # Last committed token whose forward has not run yet (after a fallback AR): its
+        # KV slot is committed, its KV and the prefix logits come with the next forward.
+        self._pending_token: int | None = None
         self._committed_verify_rounds = 0
         self._last_fallback_ar_profile: dict[str, object] | None = None
 
@@ -121,6 +124,7 @@ class TargetVerifier:
         self.mirror.host = []
         self.prefix_token_ids = ()
         self._prefix_logits = None
+        self._pending_token = None
 
     # -------------------------------------------------------------- prefill
     def _sync(self) -> None:
@@ -144,6 +148,7 @@ class TargetVerifier:
         )
         self.prefix_token_ids = toks
         self._prefix_logits = logits
+        self._pending_token = None
         self._committed_verify_rounds = 0
         self._last_fallback_ar_profile = None
         return PrefixState(
@@ -167,7 +172,7 @@ class TargetVerifier:
         """Verify the routes; ``on_decision(decision)`` (optional) is called as soon as the
         decision is known, before the fallback AR tokens are generated or the path is committed."""
         prefix = tuple(prefix_token_ids)  # element-wise == also accepts numpy integers
-        if self._prefix_logits is None:
+        if self._prefix_logits is None and self._pending_token is None:
             self.prefill([int(t) for t in prefix])
         elif prefix != self.prefix_token_ids:
             raise RuntimeError(
@@ -316,6 +321,10 @@ class TargetVerifier:
 
         ``deduplicate=False`` runs every route's tokens as its own chain (linear verify baseline).
         """
+        if self._pending_token is not None:
+            if deduplicate:
+                return self._run_tree_with_pending(paths)
+            self._flush_pending()
         if deduplicate:
             tokens, parents, depths, node_paths, masks = self.host.build_tree(
                 torch.tensor([list(p) for p in paths], dtype=torch.int64)
@@ -356,11 +365,90 @@ class TargetVerifier:
             "path_logprobs": lp,
         }
 
-    def gather_logprobs(self, logits: torch.Tensor, rows: torch.Tensor, toks: torch.Tensor) -> list[list[float]]:
-        assert self._prefix_logits is not None
+    def _run_tree_with_pending(self, paths: Sequence[Sequence[int]]) -> dict[str, object]:
+        """``run_tree`` when the last prefix token's forward is still pending.
+
+        That token becomes the root of the trie (every path is prefixed with it),
+        at its own position and KV slot: the masked forward writes its KV, its row
+        gives the prefix logits, and the routes' first tokens are scored by that
+        row -- one forward instead of a one-row forward followed by the verify.
+        Its key is read as a masked node (the tensor-core pass covers the keys
+        before it), since this forward writes it.
+        """
+        lead = int(self._pending_token)
+        tokens, parents, depths, node_paths, masks = self.host.build_tree(
+            torch.tensor([[lead, *p] for p in paths], dtype=torch.int64)
+        )
+        n = int(tokens.numel())
+        p = len(self.prefix_token_ids)
+        base = p - 1  # the lead token's position
+        scratch = self.seq.reserve_scratch(p + n - 1)
+        slots = torch.cat((self.seq.slots_for_positions(base, 1), scratch))
+        self._sync()
+        logits = self.engine.run_rows(
+            row_bucket(n),
+            tail_stride=1,
+            mask_words=int(masks.shape[1]),
+            prefix_pages=self.mirror.dev,
+            tokens=tokens.numpy(),
+            positions=depths.numpy() + base,
+            slots=slots.numpy(),
+            shared_len=base,
+            n_shared_pages=len(self.mirror.host),
+            mask_base=base,
+            row_full=np.full(n, base),
+            row_len=np.full(n, base + n),
+            row_mask=masks.numpy(),
+        )
+        self._prefix_logits = logits[0].detach().clone()
+        self._pending_token = None
+        # Token t of a route is scored by its parent's row: the lead row for t == 0.
+        toks = torch.tensor([list(x) for x in paths], dtype=torch.long)
+        lp = self.gather_logprobs(logits, node_paths[:, :-1].long(), toks, prefix_row=False)
+        real = node_paths[:, 1:] - 1  # node i >= 1 of this trie is node i - 1 of the routes' trie
+        return {
+            "logits": logits[1:],
+            "node_count": n - 1,
+            "node_paths": real.tolist(),
+            "parents": [int(x) - 1 if int(x) > 0 else -1 for x in parents[1:].tolist()],
+            "path_logprobs": lp,
+        }
+
+    @torch.inference_mode()
+    def _flush_pending(self) -> None:
+        """Run the pending token's one-row forward (KV and prefix logits) on its own."""
+        if self._pending_token is None:
+            return
+        p = len(self.prefix_token_ids)
+        q = p - 1
+        slot = self.seq.slots_for_positions(q, 1).numpy()
+        logits = self.engine.run_rows(
+            1,
+            prefix_pages=self.mirror.dev,
+            tokens=np.array([self._pending_token]),
+            positions=[q],
+            slots=slot,
+            shared_len=q,
+            n_shared_pages=len(self.mirror.host),
+            mask_base=q,
+            row_full=[q + 1],
+            row_len=[q + 1],
+        )
+        self._prefix_logits = logits[0].detach().clone()
+        self._pending_token = None
+
+    def gather_logprobs(self, logits: torch.Tensor, rows: torch.Tensor, toks: torch.Tensor, *,
+                        prefix_row: bool = True) -> list[list[float]]:
+        """Log-probs of ``toks`` under the rows ``rows`` of ``logits``; with ``prefix_row``
+        the prefix logits are row -1."""
         dev = logits.device
-        allrows = torch.cat((self._prefix_logits.reshape(1, -1).float(), logits.float()), dim=0)
-        r = (rows + 1).reshape(-1)
+        if prefix_row:
+            assert self._prefix_logits is not None
+            allrows = torch.cat((self._prefix_logits.reshape(1, -1).float(), logits.float()), dim=0)
+            r = (rows + 1).reshape(-1)
+        else:
+            allrows = logits.float()
+            r = rows.reshape(-1)
         t = toks.reshape(-1)
         if allrows.is_cuda:
             from ..ops.cuda_ops import shared_ops
@@ -623,6 +711,7 @@ class TargetVerifier:
     def _generate_fallback_ar(self, *, max_tokens: int, eos_token_id: int | None, while_running=None) -> list[int]:
         """Greedy AR from the committed prefix; ``while_running`` (optional) is called after
         every step is enqueued and before the host waits for the tokens."""
+        self._flush_pending()
         if self._prefix_logits is None:
             raise RuntimeError("target fallback AR requires initialized prefix KV")
         steps = int(max_tokens)
@@ -658,6 +747,8 @@ class TargetVerifier:
         n_pages = len(self.mirror.host)
         for t in range(steps):
             argmax_into(cur, t)
+            if t == steps - 1:
+                break  # the last token's forward runs with the next verify (or on demand)
             cur = self.engine.run_rows(
                 1,
                 prefix_pages=self.mirror.dev,
@@ -688,7 +779,11 @@ class TargetVerifier:
         generated = generated[:keep]
         self.seq.set_prefix_len(p + keep)
         self._sync()
-        self._prefix_logits = all_logits[keep - 1][0].detach().clone()
+        if keep == steps:
+            self._pending_token = int(generated[-1])
+            self._prefix_logits = None
+        else:
+            self._prefix_logits = all_logits[keep - 1][0].detach().clone()
         self.prefix_token_ids = (*self.prefix_token_ids, *generated)
         self._committed_verify_rounds += 1
         self._last_fallback_ar_profile = (
@@ -746,4 +841,5 @@ class TargetVerifier:
 
     @property
     def prefix_logits(self) -> torch.Tensor | None:
+        self._flush_pending()
         return self._prefix_logits

@@ -173,3 +173,56 @@ def test_linear_verify_matches_deduplicated_tree(tw):
     for ra, rb in zip(a["path_logprobs"], b["path_logprobs"]):
         for x, y in zip(ra, rb):
             assert abs(x - y) < 1e-4
+
+
+def test_pending_fallback_token_is_resolved_by_the_next_verify(tw):
+    """After a fallback the last AR token's forward is deferred; the next verify runs it as
+    the trie root.  Scores, the committed path's KV and the prefix logits match a recompute."""
+    tv = verifier(tw, route_selection_policy="first_route")
+    prompt = list(range(30, 47))
+    tv.prefill(prompt)
+    tv.fallback_threshold = 1e9
+    tv.route_selection_policy = "target_best"
+    res = tv.verify_payloads(prefix_token_ids=prompt, routes=[payload(i, [i + 1, 2, 3]) for i in range(3)],
+                             fallback_max_tokens=4)
+    assert res.decision == "fallback_ar" and len(res.fallback_token_ids) == 4
+    ar = list(res.fallback_token_ids)
+    # The target's greedy tokens.
+    toks = list(prompt)
+    for _ in range(4):
+        toks.append(int(greedy_logits(tw, toks)[-1].argmax()))
+    assert ar == toks[len(prompt):]
+    assert tv._pending_token == ar[-1]
+    # Next round selects: the pending token rides along as the trie root.
+    tv.fallback_threshold = None
+    tv.route_selection_policy = "first_route"
+    prefix = prompt + ar
+    routes = [payload(0, [9, 8, 7]), payload(1, [9, 8, 1]), payload(2, [4, 4, 4])]
+    res2 = tv.verify_payloads(prefix_token_ids=prefix, routes=routes)
+    assert res2.decision == "select" and res2.selected_route_id == 0
+    assert tv._pending_token is None
+    ref = torch.log_softmax(greedy_logits(tw, prefix + [9, 8, 7]), dim=-1)
+    want = [float(ref[len(prefix) - 1 + j, t]) for j, t in enumerate([9, 8, 7])]
+    got = list(res2.scores[0].token_logprobs)
+    assert got == pytest.approx(want, abs=1e-4)
+    torch.testing.assert_close(tv.prefix_logits, greedy_logits(tw, prefix + [9, 8, 7])[-1], rtol=1e-4, atol=1e-4)
+    # And one more round on top sees correct KV for every committed token.
+    tv.verify_payloads(prefix_token_ids=list(tv.prefix_token_ids),
+                       routes=[payload(5, [1, 2, 3]), payload(6, [1, 2, 4]), payload(7, [6, 6, 6])])
+    torch.testing.assert_close(tv.prefix_logits, greedy_logits(tw, prefix + [9, 8, 7, 1, 2, 3])[-1],
+                               rtol=1e-4, atol=1e-4)
+    tv.seq.validate()
+
+
+def test_pending_fallback_token_flushes_on_demand(tw):
+    tv = verifier(tw)
+    prompt = list(range(60, 71))
+    tv.prefill(prompt)
+    tv.fallback_threshold = 1e9
+    res = tv.verify_payloads(prefix_token_ids=prompt, routes=[payload(i, [i + 1, 2, 3]) for i in range(3)],
+                             fallback_max_tokens=2)
+    assert tv._pending_token is not None
+    # Reading the prefix logits (or a linear verify) runs the pending forward on its own.
+    want = greedy_logits(tw, prompt + list(res.fallback_token_ids))[-1]
+    torch.testing.assert_close(tv.prefix_logits, want, rtol=1e-4, atol=1e-4)
+    assert tv._pending_token is None
