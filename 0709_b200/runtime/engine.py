@@ -390,6 +390,17 @@ class StaticBatch:
         a = self.offs["row_mask"][0]
         self.row_mask = v[a: a + 2 * m * w].view(torch.int64).view(m, w)
         self.pad_front = False
+        # numpy views of each pinned host buffer, made once (load runs for every forward)
+        self._host_views = []
+        for hb in self.hosts:
+            h = hb.numpy()
+            views = {name: h[a: a + size] for name, (a, size) in self.offs.items() if name != "row_mask"}
+            views["tail_pages"] = views["tail_pages"].reshape(m, t)
+            a, size = self.offs["row_mask"]
+            views["row_mask"] = h[a: a + size].view(np.int64).reshape(m, w)
+            views["head"] = h[0:4]
+            self._host_views.append(views)
+        self._pad = {"tokens": 0, "positions": 0, "slots": engine.trash_slot, "row_full": 1, "row_len": 1}
 
     def real_slice(self, n: int) -> slice:
         return slice(self.M - n, self.M) if self.pad_front else slice(0, n)
@@ -408,31 +419,23 @@ class StaticBatch:
             ev = self.events[i]
             if ev is not None:
                 ev.synchronize()
-            h = self.hosts[i].numpy()
+            hv = self._host_views[i]
             m = self.M
             r0 = m - n if pad_front else 0
             rs = slice(r0, r0 + n)
-            h[0:4] = (int(shared_len), int(n_shared_pages), int(mask_base), 0)
-
-            def put(name, vals, pad):
-                a, size = self.offs[name]
-                seg = h[a: a + size]
-                seg[:] = pad
-                seg[rs] = vals
-
+            hv["head"][:] = (int(shared_len), int(n_shared_pages), int(mask_base), 0)
             dev_tokens = isinstance(tokens, torch.Tensor) and tokens.device.type != "cpu"
-            put("tokens", 0 if dev_tokens else tokens, 0)
-            put("positions", positions, 0)
-            put("slots", slots, self.engine.trash_slot)
-            put("row_full", row_full, 1)
-            put("row_len", row_len, 1)
-            a, size = self.offs["tail_pages"]
-            tp = h[a: a + size].reshape(m, self.T)
+            for name, vals in (("tokens", 0 if dev_tokens else tokens), ("positions", positions), ("slots", slots),
+                               ("row_full", row_full), ("row_len", row_len)):
+                seg = hv[name]
+                if n < m:
+                    seg[:] = self._pad[name]
+                seg[rs] = vals
+            tp = hv["tail_pages"]
             tp[:] = 0
             if tail_pages is not None:
                 tp[rs, : np.asarray(tail_pages).shape[1]] = tail_pages
-            a, size = self.offs["row_mask"]
-            mk = h[a: a + size].view(np.int64).reshape(m, self.W)
+            mk = hv["row_mask"]
             mk[:] = -1
             if row_mask is not None:
                 mk[rs, : np.asarray(row_mask).shape[1]] = row_mask

@@ -24,7 +24,7 @@ from __future__ import annotations
 import math
 import threading
 import time
-from concurrent.futures import ThreadPoolExecutor
+from concurrent.futures import Future, ThreadPoolExecutor
 from dataclasses import dataclass, field
 from typing import Any, Sequence
 
@@ -523,15 +523,19 @@ class AtlasSession:
         # only compete with the target's AR forwards.
         fb_decided = threading.Event()
         decided = threading.Event()
-        vfut = g._vpool.submit(g._verify_call, list(committed), payload, remaining, self.round_index, fb_decided,
-                               decided)
-        vfut.add_done_callback(lambda _f: decided.set())
         gated = (cfg.forest_gate == "adaptive" and cfg.fixed_forest_depth is None
                  and g.fallback_ema >= float(cfg.forest_gate_threshold))
         if gated:
+            # Nothing overlaps the verify of a gated round: run it on this thread
+            # (no hand-off to the worker and back).
             self.gated_rounds += 1
-            while not decided.wait(0.05) and not vfut.done():
-                pass
+            vfut = Future()
+            vfut.set_result(g._verify_call(list(committed), payload, remaining, self.round_index, fb_decided,
+                                           decided))
+        else:
+            vfut = g._vpool.submit(g._verify_call, list(committed), payload, remaining, self.round_index,
+                                   fb_decided, decided)
+            vfut.add_done_callback(lambda _f: decided.set())
         # A gated round that falls back builds nothing: the fallback drops this tree.
         skip = gated and fb_decided.is_set()
         tree_spans: list[EdgeSpan] = []
