@@ -27,18 +27,6 @@ _CACHE: dict[str, object] = {}
 CUDA_ARCH_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 
-def _cutlass_include() -> list[str]:
-    import importlib.util
-
-    out: list[str] = []
-    spec = importlib.util.find_spec("flashinfer")
-    if spec and spec.submodule_search_locations:
-        inc = Path(list(spec.submodule_search_locations)[0]) / "data" / "cutlass" / "include"
-        if inc.is_dir():
-            out.append(str(inc))
-    return out
-
-
 def _load(name: str, sources: list[Path], *, cuda: bool, verbose: bool = False):
     with _LOCK:
         if name in _CACHE:
@@ -94,12 +82,3 @@ CUDA_SOURCES = [
 def cuda():
     """The sm_100a kernel extension.  Raises if it cannot be built or loaded."""
     return _load("atlas_cuda", [_CSRC / "cuda" / s for s in CUDA_SOURCES], cuda=True)
-
-
-def cuda_available() -> bool:
-    return torch.cuda.is_available()
-
-
-def build_all(verbose: bool = False) -> None:
-    host()
-    cuda()
