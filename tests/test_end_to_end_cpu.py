@@ -148,3 +148,18 @@ def test_forest_gate_stays_open_when_routes_are_selected(models):
     res = make_generator(dw, tw, k=1, cfg_kw=cfg, route_selection_policy="first_route").generate(p)
     assert all(r.decision == "select" for r in res.rounds)
     assert res.metadata["forest_gated_rounds"] == 0
+
+
+@pytest.mark.parametrize("forest_depth", [0, 1, 2, 3])
+def test_every_handoff_depth_keeps_greedy_equivalence(models, forest_depth):
+    """k=1 first-route selection with the forest stopped at each depth (completed at d):
+    every handoff -- including a deferred last tree depth of zero to d-1 prebuilt steps --
+    commits the drafter's greedy tokens and passes the state-alignment checks."""
+    dw, tw = models
+    p = prompts(1, seed=7)[0]
+    cfg = dict(fixed_forest_depth=forest_depth, max_new_tokens=14)
+    res = make_generator(dw, tw, k=1, cfg_kw=cfg, route_selection_policy="first_route").generate(p)
+    assert res.generated_token_ids == greedy(dw, p, 14)
+    modes = {r.handoff_mode for r in res.rounds[:-1]}
+    want = "completed_forest_reused" if forest_depth == D else "partial_forest_pruned_then_build_tree"
+    assert modes == {want}
