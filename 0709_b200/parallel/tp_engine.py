@@ -137,16 +137,15 @@ class TPLlamaEngine(LlamaEngine):
         if graph is None:
             graph = self._capture(sb, desc)
             self._graphs[key] = graph
-        graphs, out, launches = graph[0], graph[1], graph[2]
-        for g in graphs:
+        for g in graph.graphs:
             g.replay()
-        if launches:
+        if graph.launches:
             from ..utils import counters
 
-            counters.launches(launches)
+            counters.launches(graph.launches)
         self.stats.calls += 1
         self.stats.rows += n
-        return None if out is None else out[sb.real_slice(n)].clone()
+        return None if graph.out is None else graph.out[sb.real_slice(n)].clone()
 
     @torch.inference_mode()
     def warm_graph(self, rows: int, *, tail_stride: int = 1, mask_words: int = 1, prefix_pages: torch.Tensor) -> None:

@@ -19,6 +19,7 @@ import math
 import os
 import threading
 from dataclasses import dataclass
+from typing import NamedTuple
 
 import numpy as np
 import torch
@@ -147,16 +148,15 @@ class LlamaEngine:
         if graph is None:  # a replay reads the static inputs directly; only a capture needs the descriptor
             graph = self._capture(sb, sb.desc(prefix_pages))
             self._graphs[key] = graph
-        graphs, out, launches = graph[0], graph[1], graph[2]
-        for g in graphs:
+        for g in graph.graphs:
             g.replay()
-        if launches:
+        if graph.launches:
             from ..utils import counters
 
-            counters.launches(launches)
+            counters.launches(graph.launches)
         self.stats.calls += 1
         self.stats.rows += n
-        return out[sb.real_slice(n)].clone()
+        return graph.out[sb.real_slice(n)].clone()
 
     @torch.inference_mode()
     def warm_graph(self, rows: int, *, tail_stride: int = 1, mask_words: int = 1, prefix_pages: torch.Tensor) -> None:
@@ -207,7 +207,7 @@ class LlamaEngine:
                 graphs = [g]
         torch.cuda.current_stream(self.device).wait_stream(stream)
         launches = counters.snapshot()["launches"] - before
-        return graphs, out, launches, keep
+        return CapturedForward(graphs, out, launches, keep)
 
     def _capture_one(self, fn):
         g = torch.cuda.CUDAGraph()
@@ -343,6 +343,16 @@ class LlamaEngine:
     def move_slots(self, src: torch.Tensor, dst: torch.Tensor) -> None:
         if src.numel():
             self.ops.kv_move_slots(self.kv, src.to(self.device), dst.to(self.device))
+
+
+class CapturedForward(NamedTuple):
+    """CUDA graphs of one forward (replayed in order), its static output, the kernel
+    launches they contain, and the tensors carried from one graph to the next."""
+
+    graphs: list
+    out: torch.Tensor | None
+    launches: int
+    keep: tuple
 
 
 class StaticBatch:
