@@ -33,6 +33,60 @@ def short(name: str) -> str:
     return re.sub(r"\(.*", "", name).replace("void ", "")[:60]
 
 
+def analyze_rounds(events, bounds, walls, *, top_gaps: int = 12) -> dict:
+    """Busy/idle accounting of GPU activity records.
+
+    ``events``: (start_us, end_us, name) of every kernel / copy, any order;
+    ``bounds``: (start_us, end_us) of each round; ``walls``: host seconds per round.
+    Busy time is the union of the intervals that start inside the round; each
+    idle gap is attributed to the pair of activities on either side of it.
+    """
+    events = sorted(events)
+    out_rounds = []
+    gap_kinds: dict[str, list[float]] = collections.defaultdict(list)
+    for ri, (lo, hi) in enumerate(bounds[: len(walls)]):
+        ks = [e for e in events if lo <= e[0] < hi]
+        busy = 0.0
+        gaps = []
+        end = lo
+        prev = "(round start)"
+        for s, t, name in ks:
+            if s > end:
+                gaps.append((s - end, prev, short(name)))
+            busy += max(0.0, t - max(s, end))
+            if t > end:
+                end = t
+                prev = short(name)
+        if hi > end:
+            gaps.append((hi - end, prev, "(round end)"))
+        gaps.sort(reverse=True)
+        for g, a, b in gaps:
+            gap_kinds[f"{a}  ->  {b}"].append(g)
+        per = collections.Counter(short(e[2]) for e in ks)
+        out_rounds.append({
+            "round": ri,
+            "wall_us": round(walls[ri] * 1e6, 1),
+            "span_us": round(hi - lo, 1),
+            "gpu_busy_us": round(busy, 1),
+            "gpu_idle_us": round(hi - lo - busy, 1),
+            "gpu_events": len(ks),
+            "largest_gaps_us": [[round(g, 1), a, b] for g, a, b in gaps[:top_gaps]],
+            "top_kernels": per.most_common(8),
+        })
+    n = max(1, len(out_rounds))
+    return {
+        "rounds": len(out_rounds),
+        "mean_wall_us": round(1e6 * sum(walls) / max(1, len(walls)), 1),
+        "mean_span_us": round(sum(r["span_us"] for r in out_rounds) / n, 1),
+        "mean_gpu_busy_us": round(sum(r["gpu_busy_us"] for r in out_rounds) / n, 1),
+        "mean_gpu_idle_us": round(sum(r["gpu_idle_us"] for r in out_rounds) / n, 1),
+        "idle_by_boundary_us_per_round": {
+            k: round(sum(v) / n, 1) for k, v in sorted(gap_kinds.items(), key=lambda kv: -sum(kv[1]))[:20]
+        },
+        "per_round": out_rounds,
+    }
+
+
 def main() -> int:
     ap = argparse.ArgumentParser(add_help=False)
     ap.add_argument("--rounds", type=int, default=6)
@@ -70,52 +124,10 @@ def main() -> int:
     marks = [i for i, e in enumerate(evs) if "spin_kernel" in e.name]
     gpu = [e for e in evs if "spin_kernel" not in e.name]
     bounds = [(evs[a].time_range.end, evs[b].time_range.start) for a, b in zip(marks, marks[1:])]
-    out_rounds = []
-    gap_kinds: dict[str, list[float]] = collections.defaultdict(list)
-    for ri, (lo, hi) in enumerate(bounds[: len(walls)]):
-        ks = [e for e in gpu if lo <= e.time_range.start < hi]
-        busy = 0.0
-        gaps = []
-        end = lo
-        prev = "(round start)"
-        for e in ks:
-            s, t = e.time_range.start, e.time_range.end
-            if s > end:
-                gaps.append((s - end, prev, short(e.name)))
-            busy += max(0.0, t - max(s, end))
-            if t > end:
-                end = t
-                prev = short(e.name)
-        if hi > end:
-            gaps.append((hi - end, prev, "(round end)"))
-        gaps.sort(reverse=True)
-        for g, a, b in gaps:
-            gap_kinds[f"{a}  ->  {b}"].append(g)
-        per = collections.Counter(short(e.name) for e in ks)
-        out_rounds.append({
-            "round": ri,
-            "wall_us": round(walls[ri] * 1e6, 1),
-            "span_us": round(hi - lo, 1),
-            "gpu_busy_us": round(busy, 1),
-            "gpu_idle_us": round(hi - lo - busy, 1),
-            "gpu_events": len(ks),
-            "largest_gaps_us": [[round(g, 1), a, b] for g, a, b in gaps[: own.top_gaps]],
-            "top_kernels": per.most_common(8),
-        })
     if len(bounds) < len(walls):
         print(f"warning: found {len(marks)} round markers for {len(walls)} rounds", file=sys.stderr)
-    summary = {
-        "rounds": len(out_rounds),
-        "mean_wall_us": round(1e6 * sum(walls) / max(1, len(walls)), 1),
-        "mean_span_us": round(sum(r["span_us"] for r in out_rounds) / max(1, len(out_rounds)), 1),
-        "mean_gpu_busy_us": round(sum(r["gpu_busy_us"] for r in out_rounds) / max(1, len(out_rounds)), 1),
-        "mean_gpu_idle_us": round(sum(r["gpu_idle_us"] for r in out_rounds) / max(1, len(out_rounds)), 1),
-        "idle_by_boundary_us_per_round": {
-            k: round(sum(v) / max(1, len(out_rounds)), 1)
-            for k, v in sorted(gap_kinds.items(), key=lambda kv: -sum(kv[1]))[:20]
-        },
-        "per_round": out_rounds,
-    }
+    summary = analyze_rounds([(e.time_range.start, e.time_range.end, e.name) for e in gpu], bounds, walls,
+                             top_gaps=own.top_gaps)
     print(json.dumps({k: v for k, v in summary.items() if k != "per_round"}, indent=1))
     if own.json_out:
         with open(own.json_out, "w") as f:

@@ -59,3 +59,19 @@ def test_timeline_overlap_exposed_wait_json_and_svg(tmp_path):
     tl.write_timeline_svg(tmp_path / "t.svg", t, width=800)
     assert json.loads((tmp_path / "t.json").read_text())["summary"]["rounds"] == 1
     assert (tmp_path / "t.svg").read_text().startswith("<svg")
+
+
+def test_round_trace_accounting():
+    tr = _load("trace_round")
+    # Round 0 spans [0, 100): kernels A [10, 40), B [30, 60) overlap; copy C [80, 90).
+    events = [(30.0, 60.0, "void B<float>(int)"), (10.0, 40.0, "A"), (80.0, 90.0, "Memcpy HtoD"),
+              (120.0, 150.0, "A")]
+    out = tr.analyze_rounds(events, [(0.0, 100.0), (100.0, 200.0)], [1e-4, 1e-4])
+    r0, r1 = out["per_round"]
+    assert r0["gpu_busy_us"] == 60.0 and r0["gpu_idle_us"] == 40.0
+    assert r0["largest_gaps_us"][0] == [20.0, "B<float>", "Memcpy HtoD"]
+    assert {tuple(g) for g in r0["largest_gaps_us"]} == {(20.0, "B<float>", "Memcpy HtoD"),
+                                                         (10.0, "(round start)", "A"),
+                                                         (10.0, "Memcpy HtoD", "(round end)")}
+    assert r1["gpu_busy_us"] == 30.0 and r1["gpu_idle_us"] == 70.0
+    assert out["mean_gpu_idle_us"] == 55.0
