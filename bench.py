@@ -326,7 +326,8 @@ def main() -> int:
                 "first_token_threshold": args.first_token_threshold,
                 "fallback_ar_tokens": args.fallback_ar_tokens,
                 "forest_gate": args.forest_gate,
-                "step": "one speculative round (verify || forest, handoff); next prompt's prefill inside its step",
+                "step": ("one speculative round (verify, with the forest overlapped unless the adaptive gate is closed; "
+                         "handoff); next prompt's prefill inside its step"),
                 "l2": "weights (~17 GB) stream every step; working set far above L2",
                 "rounds_timed": drv.rounds - r0,
                 "round_breakdown_ms": {
