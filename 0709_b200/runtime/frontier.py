@@ -253,8 +253,8 @@ def advance_frontier_one_token(
     )
 
 
-# Host selection: after the top-k kernel, one transfer brings the k candidates of
-# every parent to the host, where ranking (<= k^3 candidates) and route
+# Host selection: after the top-k kernel, one wait and two small copies bring the
+# k candidates of every parent (ids, log-probs) to the host, where ranking (<= k^3 candidates) and route
 # bookkeeping run in Python -- the same order as the device path
 # (score desc, parent, rank, token), without its dozens of small GPU launches.
 HOST_SELECTION = os.environ.get("ATLAS_DEVICE_SELECTION", "0") != "1"
@@ -264,15 +264,17 @@ def _advance_host_selection(active_routes, out, *, k, route_store, selection_pol
     rel = [route_store.pending_token_path(r) for r in active_routes]
     lp, ids = batch_parent_token_candidates(out.next_token_logits, k=k, sampling=sampling,
                                             relative_parent_paths=rel)
-    packed = torch.stack((ids.to(torch.float64), lp.to(torch.float64)), dim=-1)
-    is_transfer = packed.device.type != "cpu"
+    # Two plain transfers (the first waits for the top-k kernel), no packing kernels.
+    is_transfer = ids.device.type != "cpu"
     if is_transfer:
-        counters.d2h(packed.numel() * 8)
-    rows = packed.cpu().tolist()
+        counters.d2h(ids.numel() * ids.element_size() + lp.numel() * lp.element_size())
+    id_rows = ids.cpu().tolist()
+    lp_rows = lp.cpu().tolist()
+    n_elems = 2 * ids.numel()
     cands: list[PendingCandidate] = []
-    for r, row in zip(active_routes, rows):
+    for r, row_ids, row_lp in zip(active_routes, id_rows, lp_rows):
         base = float(r.cumulative_logprob)
-        for rank, (tok, tlp) in enumerate(row):
+        for rank, (tok, tlp) in enumerate(zip(row_ids, row_lp)):
             cands.append(PendingCandidate(parent_route_id=int(r.route_id), stage1_root_id=int(r.stage1_root_id),
                                           pending_token_id=int(tok), cumulative_logprob=base + float(tlp),
                                           rank_in_parent=rank, parent_logprob=base))
@@ -282,8 +284,8 @@ def _advance_host_selection(active_routes, out, *, k, route_store, selection_pol
         raise ValueError("new_node_ids_cpu must have one id per active route")
     stats = FrontierSelectionStats(
         candidate_count=len(cands), selected_count=len(chosen), host_materialization_batches=1,
-        host_materialization_elements=int(packed.numel()), host_transfer_batches=int(is_transfer),
-        host_transfer_elements=int(packed.numel()) if is_transfer else 0, selection_device="cpu",
+        host_materialization_elements=n_elems, host_transfer_batches=int(is_transfer),
+        host_transfer_elements=n_elems if is_transfer else 0, selection_device="cpu",
         new_node_ids_source="decode_output_cpu")
     decoded = route_store.mark_routes_materialized(list(active_routes), node_ids, phase=selection_policy.phase)
     nxt = route_store.materialize_route_descriptors(chosen, parent_routes=decoded)
