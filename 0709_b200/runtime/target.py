@@ -204,6 +204,8 @@ class TargetVerifier:
             with nvtx_range("target_fallback_ar"):
                 generated = self._generate_fallback_ar(max_tokens=limit, eos_token_id=eos_token_id,
                                                        while_running=build_metadata)
+            if not meta:  # no AR step ran (a budget of zero tokens)
+                build_metadata()
             return TargetVerifyResult(
                 selected_route_id=None,
                 scores=scores,

@@ -226,3 +226,14 @@ def test_pending_fallback_token_flushes_on_demand(tw):
     want = greedy_logits(tw, prompt + list(res.fallback_token_ids))[-1]
     torch.testing.assert_close(tv.prefix_logits, want, rtol=1e-4, atol=1e-4)
     assert tv._pending_token is None
+
+
+def test_fallback_with_zero_token_budget_keeps_metadata(tw):
+    tv = verifier(tw)
+    prompt = list(range(70, 81))
+    tv.prefill(prompt)
+    tv.fallback_threshold = 1e9
+    res = tv.verify_payloads(prefix_token_ids=prompt, routes=[payload(i, [i + 1, 2, 3]) for i in range(3)],
+                             fallback_max_tokens=0)
+    assert res.decision == "fallback_ar" and res.fallback_token_ids == ()
+    assert res.metadata["prefix_len_before"] == len(prompt) and res.metadata["node_count"] > 0
