@@ -138,3 +138,20 @@ def test_prompt_helpers():
     assert prompts.parse_token_ids(None, tokenizer=None, prompt="x", prefix_len=5, repeat_token_id=7) == [7] * 5
     ids = prompts.parse_token_ids(None, tokenizer=None, prompt="hé")
     assert prompts.decode(None, ids) == "hé"
+
+
+def test_forest_gate_flags_and_validation(tmp_path):
+    ds = mod("serving.distributed_system")
+    edge = mod("serving.edge")
+    out = tmp_path / "res.json"
+    rc = ds.main(["--drafter-model", "tiny-drafter", "--target-model", "tiny-target", "--dtype", "float32",
+                  "--prompt-token-ids", ",".join(str(i) for i in range(40, 60)), "--k", "2", "--d", "2",
+                  "--max-new-tokens", "6", "--page-size", "4", "--max-total-tokens", "2048",
+                  "--forest-gate", "overlap", "--json-out", str(out)])
+    assert rc == 0
+    meta = json.loads(out.read_text())["metadata"]
+    assert meta["forest_gate"] == "overlap" and meta["forest_gated_rounds"] == 0
+    with pytest.raises(ValueError):
+        edge.DistributedAtlasConfig(forest_gate="sometimes").validate()
+    with pytest.raises(ValueError):
+        edge.DistributedAtlasConfig(forest_gate_threshold=0.0).validate()
