@@ -67,6 +67,7 @@ def main() -> int:
     ap.add_argument("--only", default="all")
     ap.add_argument("--iters", type=int, default=20)
     ap.add_argument("--dtype", default="float16")
+    ap.add_argument("--json-out", default=None, help="also write every row to this JSON file")
     args = ap.parse_args()
     dt = {"float16": torch.float16, "bfloat16": torch.bfloat16}[args.dtype]
     hbm, tflops, src = peaks()
@@ -189,9 +190,9 @@ def main() -> int:
                        w.nbytes() + 2 * 2048 * cfg.num_layers * cfg.kv_size * 2)
             del eng, w
             torch.cuda.empty_cache()
-    with open(os.path.join(ROOT, "gpurun_out", "bench_kernels.json") if os.path.isdir(
-            os.path.join(ROOT, "gpurun_out")) else os.devnull, "w") as f:
-        json.dump(out, f, indent=1)
+    if args.json_out:
+        with open(args.json_out, "w") as f:
+            json.dump(out, f, indent=1)
     return 0
 
 
