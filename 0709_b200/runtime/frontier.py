@@ -261,7 +261,11 @@ HOST_SELECTION = os.environ.get("ATLAS_DEVICE_SELECTION", "0") != "1"
 
 
 def _advance_host_selection(active_routes, out, *, k, route_store, selection_policy, sampling) -> FrontierStepOutput:
-    rel = [route_store.pending_token_path(r) for r in active_routes]
+    # Semantic parent paths key the sampling noise; greedy drafting does not read them.
+    if sampling is not None and sampling.config.do_sample:
+        rel = [route_store.pending_token_path(r) for r in active_routes]
+    else:
+        rel = [()] * len(active_routes)
     lp, ids = batch_parent_token_candidates(out.next_token_logits, k=k, sampling=sampling,
                                             relative_parent_paths=rel)
     # Two plain transfers (the first waits for the top-k kernel), no packing kernels.
