@@ -82,9 +82,9 @@ def per_root_topk_candidate_indices(
 
 
 def topk_pairs_to_python(token_ids: torch.Tensor, token_logprobs: torch.Tensor) -> list[tuple[int, float]]:
-    """One host transfer for a top-k result (ids exactly representable in float64)."""
+    """A top-k result as host (token, log-prob) pairs: one wait, two small copies, no packing kernels."""
     if token_ids.shape != token_logprobs.shape:
         raise ValueError("token ids and logprobs must have matching shapes")
-    packed = torch.stack((token_ids.to(torch.float64), token_logprobs.to(torch.float64)), dim=-1)
-    rows = packed.detach().cpu().reshape(-1, 2).tolist()
-    return [(int(t), float(lp)) for t, lp in rows]
+    ids = token_ids.detach().reshape(-1).cpu().tolist()
+    lps = token_logprobs.detach().reshape(-1).cpu().tolist()
+    return [(int(t), float(lp)) for t, lp in zip(ids, lps)]
