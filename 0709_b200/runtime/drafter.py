@@ -49,10 +49,13 @@ class PrefixPageMirror:
         new = pages.tolist()
         if len(new) > self.dev.numel():
             raise RuntimeError(f"prefix page table of {len(new)} pages exceeds the mirror capacity {self.dev.numel()}")
-        start = 0
         n = min(len(new), len(self.host))
-        while start < n and new[start] == self.host[start]:
-            start += 1
+        if new[:n] == self.host[:n]:  # the usual case: pages only appended or dropped at the end
+            start = n
+        else:
+            start = 0
+            while new[start] == self.host[start]:
+                start += 1
         if start < len(new):
             self.dev[start: len(new)].copy_(pages[start:].to(self.dev.device, non_blocking=True))
             self.h2d_copies += 1
