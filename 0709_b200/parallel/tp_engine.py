@@ -25,6 +25,7 @@ configuration's TP=2/4/8 target.
 from __future__ import annotations
 
 import os
+import time
 
 import numpy as np
 import torch
@@ -33,6 +34,16 @@ from ..models.llama import LlamaConfig, LlamaWeights
 from ..runtime.engine import LlamaEngine
 from .comm import SITE_DOWN, SITE_O, TPGroup
 from .mailbox import OP_CALL, OP_STOP, Mailbox
+
+
+class HostMark:
+    """A host timestamp with the ``elapsed_time`` of a CUDA event (CPU ranks)."""
+
+    def __init__(self) -> None:
+        self.t = time.perf_counter()
+
+    def elapsed_time(self, other: "HostMark") -> float:
+        return (other.t - self.t) * 1e3
 
 
 class TPLlamaEngine(LlamaEngine):
@@ -46,6 +57,11 @@ class TPLlamaEngine(LlamaEngine):
         self._mirrors: dict[int, torch.Tensor] = {}   # worker: root mirror id -> local page table
         self._root_mirrors: dict[int, object] = {}    # root: id -> mirror
         self.posted_calls = 0
+        # Timing marks: CUDA events recorded by every rank at the same point of the
+        # call stream (``mark``); ``mark_hook(tag)`` runs on each rank right after.
+        self.marks: dict[str, torch.cuda.Event] = {}
+        self.mark_launches: dict[str, int] = {}
+        self.mark_hook = None
 
     # ---------------------------------------------------------- forward
     @torch.inference_mode()
@@ -173,6 +189,27 @@ class TPLlamaEngine(LlamaEngine):
             self._post("move_slots", src=src.cpu().numpy(), dst=dst.cpu().numpy())
         super().move_slots(src, dst)
 
+    def mark(self, tag: str, *, barrier: bool = False) -> None:
+        """Record a CUDA event named ``tag`` on every rank at this point of the call stream.
+
+        With ``barrier`` each rank first drains its GPU work and meets the others, so
+        the events open a region that every rank starts together; without it the
+        event follows the rank's previously issued work (the end of a region).
+        ``elapsed_ms(a, b)`` then gives each rank's device time between two marks.
+        """
+        self._post("mark", tag=str(tag), barrier=bool(barrier))
+        self._w_mark(str(tag), bool(barrier))
+
+    def elapsed_ms(self, start: str, end: str) -> float:
+        if self.device.type == "cuda":
+            torch.cuda.synchronize(self.device)
+        return float(self.marks[start].elapsed_time(self.marks[end]))
+
+    def set_comm_mode(self, mode: str) -> None:
+        """Switch every rank's collectives (``fused`` or ``nccl``); captured graphs are dropped."""
+        self._post("set_comm_mode", mode=str(mode))
+        self._w_set_comm_mode(str(mode))
+
     def stop_workers(self) -> None:
         if self.is_root and self.mailbox is not None and self.tp.world > 1:
             self.mailbox.post(OP_STOP, None)
@@ -183,8 +220,6 @@ class TPLlamaEngine(LlamaEngine):
     def serve(self) -> int:
         """Worker loop: repeat the root's calls until it posts stop; returns the number of calls."""
         assert not self.is_root and self.mailbox is not None
-        import time
-
         calls = 0
         self.worker_wait_s = 0.0
         self.worker_handle_s = 0.0
@@ -204,6 +239,41 @@ class TPLlamaEngine(LlamaEngine):
             getattr(self, "_w_" + name)(**kw)
             self.worker_handle_s += time.perf_counter() - t1
             calls += 1
+
+    def _w_mark(self, tag: str, barrier: bool) -> None:
+        from ..utils import counters
+
+        cuda = self.device.type == "cuda"
+        if barrier:
+            if cuda:
+                torch.cuda.synchronize(self.device)
+            if self.tp.world > 1:
+                import torch.distributed as dist
+
+                dist.barrier(group=self.tp.group)
+                if cuda:
+                    torch.cuda.synchronize(self.device)
+        if cuda:
+            ev = torch.cuda.Event(enable_timing=True)
+            ev.record()
+        else:
+            ev = HostMark()
+        self.marks[tag] = ev
+        self.mark_launches[tag] = counters.snapshot()["launches"]
+        if self.mark_hook is not None:
+            self.mark_hook(tag)
+
+    def _w_set_comm_mode(self, mode: str) -> None:
+        from .comm import MODES
+
+        if mode not in MODES:
+            raise ValueError(f"comm mode must be one of {MODES}")
+        if mode == "fused" and not self.tp.base:
+            raise ValueError("fused collectives need the peer buffers mapped at start-up (build in fused mode)")
+        if self.device.type == "cuda":
+            torch.cuda.synchronize(self.device)
+        self._graphs.clear()
+        self.tp.mode = mode
 
     def _w_mirror_new(self, mid: int, capacity: int) -> None:
         self._mirrors[mid] = torch.zeros(capacity, dtype=torch.int32, device=self.device)

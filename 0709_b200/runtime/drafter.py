@@ -28,6 +28,7 @@ import torch
 from ..ops import _native
 from ..ops.attn_desc import AttnDesc
 from ..utils import counters
+from ..utils.transfer import ids_to_device
 from ..types import DraftPrefixState, FrontierDecodeOutput, PrefixKVView, RouteState
 from .engine import LlamaEngine, row_bucket
 from .store import KVTreeStore
@@ -129,7 +130,7 @@ class DrafterRuntime:
         self.engine.copy_pages(copies)
         self._sync_prefix()
         logits = self.engine.prefill_sequence(
-            torch.tensor(toks, dtype=torch.int32).to(self.device),
+            ids_to_device(toks, self.device),
             start_pos=0,
             slots=slots.to(self.device),
             pages=self.mirror.view(),
@@ -297,7 +298,7 @@ class DrafterRuntime:
             )[-1]
         else:
             logits = self.engine.prefill_sequence(
-                torch.tensor(suffix, dtype=torch.int32).to(self.device),
+                ids_to_device(suffix, self.device),
                 start_pos=start,
                 slots=slots.to(self.device),
                 pages=self.mirror.view(),

@@ -30,6 +30,7 @@ import torch
 from ..ops import _native
 from ..ops.attn_desc import AttnDesc, single_sequence_desc
 from ..utils import counters
+from ..utils.transfer import ids_to_device
 from ..utils.nvtx import nvtx_range
 from ..types import PrefixState, TargetRouteScore, TargetVerifyResult, VerifyRoutePayload
 from .drafter import PrefixPageMirror
@@ -140,7 +141,7 @@ class TargetVerifier:
         slots, _ = self.seq.append_prefix(len(toks))
         self._sync()
         logits = self.engine.prefill_sequence(
-            torch.tensor(toks, dtype=torch.int32).to(self.device),
+            ids_to_device(toks, self.device),
             start_pos=0,
             slots=slots.to(self.device),
             pages=self.mirror.view(),
