@@ -16,13 +16,26 @@ import torch
 
 from . import _native
 from ..utils import counters
+from ..utils.transfer import ERROR_NAMES, KernelError  # noqa: F401  (re-exported)
 from .attn_desc import AttnDesc
 
-ERROR_NAMES = {1: "mbarrier wait timed out", 2: "index out of range", 3: "unsupported configuration"}
+_FLAGS: dict[int, torch.Tensor] = {}
 
 
-class KernelError(RuntimeError):
-    pass
+def device_error_flag(device: torch.device) -> torch.Tensor:
+    """The device's error flag (int32[1]), shared by every op table and TP group on it.
+
+    Kernels record a code here instead of trapping; one read of this flag (packed
+    into a result copy the serving path makes anyway) covers every kernel that
+    ran on the device before it.
+    """
+    dev = torch.device(device)
+    idx = dev.index if dev.index is not None else torch.cuda.current_device()
+    flag = _FLAGS.get(idx)
+    if flag is None:
+        flag = torch.zeros(1, dtype=torch.int32, device=torch.device("cuda", idx))
+        _FLAGS[idx] = flag
+    return flag
 
 
 def _ext():
@@ -35,7 +48,7 @@ class CudaOps:
         self.engine = engine
         self.device = engine.device if engine is not None else (device or torch.device("cuda"))
         dev = self.device
-        self.err = torch.zeros(1, dtype=torch.int32, device=dev)
+        self.err = device_error_flag(dev)
         self.ws = torch.empty(0, dtype=torch.float32, device=dev)
         self.counters = torch.empty(0, dtype=torch.int32, device=dev)
         self.part_o = torch.empty(0, dtype=torch.float32, device=dev)
@@ -48,7 +61,7 @@ class CudaOps:
         code = int(self.err.item())
         if code:
             self.err.zero_()
-            raise KernelError(f"device kernel reported error {code}: {ERROR_NAMES.get(code, 'unknown')}")
+            raise KernelError(code)
 
     # ------------------------------------------------------------- GEMM
     def _gemm(self, x: torch.Tensor, w: torch.Tensor, out: torch.Tensor, epi: int) -> torch.Tensor:

@@ -76,8 +76,10 @@ class TPGroup:
         if self.mode in ("fused", "nccl"):
             from ..ops import _native
 
+            from ..ops.cuda_ops import device_error_flag
+
             self.ext = _native.cuda()
-            self.err = torch.zeros(1, dtype=torch.int32, device=self.device)
+            self.err = device_error_flag(self.device)
         if self.mode == "fused":
             self._setup_symmetric()
 

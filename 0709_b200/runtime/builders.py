@@ -1,10 +1,18 @@
-"""Stage-1 tree and stage-2 forest construction over a frontier model backend.
+"""Stage-1 trees and stage-2 forests built from frontier depths.
 
-Parity: reference src/atlas_0709/flashinfer_paged/builders.py:31-261.
-- stage-1 tree: ``k`` routes, global top-k per depth (batch-k decode);
-- stage-2 forest: ``k`` children per completed stage-1 route (``k^2`` routes),
-  per-root top-k per depth (batch-k^2 decode);
-- ``select_routes_by_stage1_root`` keeps the selected root's ``k`` routes.
+Everything here is one of two moves over ``KVTreeStore``:
+
+* ``seed``: open ``k`` routes per parent from already decoded logits -- the
+  committed prefix's logits for a stage-1 tree (the parent is the prefix), or
+  the last logits of the ``k`` completed stage-1 routes for a forest (each
+  completed route becomes the stage-1 root of its ``k`` children);
+* ``grow``: one frontier depth (``frontier.advance_frontier_one_token``) with
+  the tree's or the forest's selection policy, repeated ``depth`` times.
+
+Shapes: a tree keeps ``k`` routes at every depth (batch-``k`` decodes), a
+forest ``k^2`` (batch-``k^2`` decodes, best ``k`` per root).
+
+Behaviour matches the reference's builders (src/atlas_0709/flashinfer_paged/builders.py:31-261).
 """
 
 from __future__ import annotations
@@ -13,17 +21,14 @@ from typing import Any, Sequence
 
 import torch
 
-from ..types import BuildDepthsOutput, DecodePhase, DraftPrefixState, FrontierStepOutput, PendingCandidate, RouteState
-from .frontier import (
-    FrontierModelBackend,
-    GlobalTopKSelection,
-    PerStage1RootTopKSelection,
-    advance_frontier_one_token,
-    collect_pending_candidates,
-)
-from .sampling import DrafterSamplingContext, batch_parent_token_candidates, single_parent_token_candidates
-from .selection import topk_pairs_to_python
+from ..types import BuildDepthsOutput, DecodePhase, DraftPrefixState, FrontierStepOutput, RouteState
+from .frontier import (BestKOverall, BestKPerRoot, FrontierModelBackend, advance_frontier_one_token,
+                       backend_status, propose_children)
+from .sampling import DrafterSamplingContext
 from .store import KVTreeStore
+
+TREE = BestKOverall()
+FOREST = BestKPerRoot()
 
 
 def initialize_stage1_routes(
@@ -32,93 +37,14 @@ def initialize_stage1_routes(
     k: int,
     route_store: KVTreeStore,
     sampling: DrafterSamplingContext | None = None,
+    model_backend: FrontierModelBackend | None = None,
 ) -> list[RouteState]:
-    lp, ids = single_parent_token_candidates(draft_prefix_state.next_token_logits, k=k, sampling=sampling)
-    routes: list[RouteState] = []
-    for tok, tlp in topk_pairs_to_python(ids, lp):
-        rid = route_store.allocate_route_id()
-        routes.append(
-            route_store.register_route(
-                RouteState(
-                    route_id=rid,
-                    stage1_root_id=rid,
-                    parent_route_id=None,
-                    materialized_leaf_node_id=None,
-                    pending_token_id=tok,
-                    cumulative_logprob=tlp,
-                    stage1_depth=0,
-                    stage2_depth=0,
-                    kv_view=draft_prefix_state.prefix_kv_view.fork(),
-                    token_logprobs=(float(tlp),),
-                )
-            )
-        )
-    return routes
-
-
-def build_tree_one_depth(
-    active_routes: Sequence[RouteState],
-    *,
-    k: int,
-    route_store: KVTreeStore,
-    model_backend: FrontierModelBackend,
-    attention_backend: Any = None,
-    phase: DecodePhase = DecodePhase.STAGE1,
-    sampling: DrafterSamplingContext | None = None,
-) -> FrontierStepOutput:
-    if len(active_routes) != k:
-        raise ValueError(f"build_tree_one_depth expects {k} active routes, got {len(active_routes)}")
-    return advance_frontier_one_token(
-        active_routes,
-        k=k,
-        route_store=route_store,
-        model_backend=model_backend,
-        selection_policy=GlobalTopKSelection(phase=phase),
-        attention_backend=attention_backend,
-        sampling=sampling,
-    )
-
-
-def _depths(step_fn, active_routes, depth: int, **kw) -> BuildDepthsOutput:
-    if depth <= 0:
-        raise ValueError("depth must be positive")
-    steps: list[FrontierStepOutput] = []
-    frontier = list(active_routes)
-    for _ in range(depth):
-        step = step_fn(frontier, **kw)
-        steps.append(step)
-        frontier = step.next_routes
-    last = steps[-1]
-    return BuildDepthsOutput(
-        completed_routes=last.decoded_routes,
-        next_frontier_routes=last.next_routes,
-        last_logits=last.decode_output.next_token_logits,
-        steps=steps,
-    )
-
-
-def build_tree_depths(
-    active_routes: Sequence[RouteState],
-    *,
-    depth: int,
-    k: int,
-    route_store: KVTreeStore,
-    model_backend: FrontierModelBackend,
-    attention_backend: Any = None,
-    phase: DecodePhase = DecodePhase.STAGE1,
-    sampling: DrafterSamplingContext | None = None,
-) -> BuildDepthsOutput:
-    return _depths(
-        build_tree_one_depth,
-        active_routes,
-        depth,
-        k=k,
-        route_store=route_store,
-        model_backend=model_backend,
-        attention_backend=attention_backend,
-        phase=phase,
-        sampling=sampling,
-    )
+    """``k`` stage-1 routes seeded from the committed prefix's next-token logits (one pending token each)."""
+    cands, _ = propose_children([None], draft_prefix_state.next_token_logits, k=k, sampling=sampling,
+                                history=lambda _p: (), status=backend_status(model_backend))
+    prefix = draft_prefix_state.prefix_kv_view
+    return [route_store.new_route(root=None, parent=None, token=c.pending_token_id,
+                                  token_logprob=c.cumulative_logprob, prefix=prefix) for c in cands]
 
 
 def initialize_forest_routes(
@@ -128,83 +54,76 @@ def initialize_forest_routes(
     k: int,
     route_store: KVTreeStore,
     sampling: DrafterSamplingContext | None = None,
+    model_backend: FrontierModelBackend | None = None,
 ) -> list[RouteState]:
+    """``k`` stage-2 children of every completed stage-1 route; each completed route is their root."""
     if len(stage1_routes) != int(stage1_last_logits.shape[0]):
-        raise ValueError("stage1_routes and stage1_last_logits must have the same batch size")
-    rel = [route_store.materialized_token_path(r) for r in stage1_routes]
-    lp, ids = batch_parent_token_candidates(stage1_last_logits, k=k, sampling=sampling, relative_parent_paths=rel)
-    kk = int(ids.shape[-1])
-    pairs = topk_pairs_to_python(ids, lp)
-    out: list[RouteState] = []
-    for row, parent in enumerate(stage1_routes):
-        for rank in range(kk):
-            tok, tlp = pairs[row * kk + rank]
-            out.append(
-                route_store.register_route(
-                    RouteState(
-                        route_id=route_store.allocate_route_id(),
-                        stage1_root_id=parent.route_id,
-                        parent_route_id=parent.route_id,
-                        materialized_leaf_node_id=parent.materialized_leaf_node_id,
-                        pending_token_id=tok,
-                        cumulative_logprob=parent.cumulative_logprob + tlp,
-                        stage1_depth=parent.stage1_depth,
-                        stage2_depth=0,
-                        kv_view=parent.kv_view.fork(),
-                        token_logprobs=(*parent.token_logprobs, float(tlp)),
-                    )
-                )
-            )
-    return out
+        raise ValueError(f"{len(stage1_routes)} completed stage-1 routes but {int(stage1_last_logits.shape[0])} "
+                         "rows of last logits")
+    cands, _ = propose_children(list(stage1_routes), stage1_last_logits, k=k, sampling=sampling,
+                                history=route_store.materialized_token_path, status=backend_status(model_backend),
+                                root_of=lambda r: r.route_id)
+    by_id = {int(r.route_id): r for r in stage1_routes}
+    return [route_store.new_route(root=c.stage1_root_id, parent=by_id[c.parent_route_id], token=c.pending_token_id,
+                                  token_logprob=c.cumulative_logprob - c.parent_logprob) for c in cands]
 
 
-def build_forest_one_depth(
-    active_routes: Sequence[RouteState],
-    *,
-    k: int,
-    route_store: KVTreeStore,
-    model_backend: FrontierModelBackend,
-    attention_backend: Any = None,
-    sampling: DrafterSamplingContext | None = None,
-) -> FrontierStepOutput:
-    if len(active_routes) != k * k:
-        raise ValueError(f"build_forest_one_depth expects {k * k} active routes, got {len(active_routes)}")
-    return advance_frontier_one_token(
-        active_routes,
-        k=k,
-        route_store=route_store,
-        model_backend=model_backend,
-        selection_policy=PerStage1RootTopKSelection(phase=DecodePhase.STAGE2),
-        attention_backend=attention_backend,
-        sampling=sampling,
-    )
+def _grow(routes, depth: int, *, k: int, width: int, policy, route_store, model_backend, attention_backend,
+          sampling) -> BuildDepthsOutput:
+    if int(depth) < 1:
+        raise ValueError(f"cannot build {depth} depths")
+    steps: list[FrontierStepOutput] = []
+    front = list(routes)
+    for _ in range(int(depth)):
+        if len(front) != width:
+            raise ValueError(f"a depth of this build decodes {width} routes; {len(front)} are active")
+        step = advance_frontier_one_token(front, k=k, route_store=route_store, model_backend=model_backend,
+                                          selection_policy=policy, attention_backend=attention_backend,
+                                          sampling=sampling)
+        steps.append(step)
+        front = step.next_routes
+    last = steps[-1]
+    return BuildDepthsOutput(completed_routes=last.decoded_routes, next_frontier_routes=last.next_routes,
+                             last_logits=last.decode_output.next_token_logits, steps=steps)
 
 
-def build_forest_depths(
-    active_routes: Sequence[RouteState],
-    *,
-    depth: int,
-    k: int,
-    route_store: KVTreeStore,
-    model_backend: FrontierModelBackend,
-    attention_backend: Any = None,
-    sampling: DrafterSamplingContext | None = None,
-) -> BuildDepthsOutput:
-    return _depths(
-        build_forest_one_depth,
-        active_routes,
-        depth,
-        k=k,
-        route_store=route_store,
-        model_backend=model_backend,
-        attention_backend=attention_backend,
-        sampling=sampling,
-    )
+def _tree_policy(phase: DecodePhase) -> BestKOverall:
+    return TREE if phase == DecodePhase.STAGE1 else BestKOverall(phase=phase)
+
+
+def build_tree_one_depth(active_routes: Sequence[RouteState], *, k: int, route_store: KVTreeStore,
+                         model_backend: FrontierModelBackend, attention_backend: Any = None,
+                         phase: DecodePhase = DecodePhase.STAGE1,
+                         sampling: DrafterSamplingContext | None = None) -> FrontierStepOutput:
+    """One stage-1 depth: decode the ``k`` routes and keep the best ``k`` children overall."""
+    return _grow(active_routes, 1, k=k, width=k, policy=_tree_policy(phase), route_store=route_store,
+                 model_backend=model_backend, attention_backend=attention_backend, sampling=sampling).steps[0]
+
+
+def build_tree_depths(active_routes: Sequence[RouteState], *, depth: int, k: int, route_store: KVTreeStore,
+                      model_backend: FrontierModelBackend, attention_backend: Any = None,
+                      phase: DecodePhase = DecodePhase.STAGE1,
+                      sampling: DrafterSamplingContext | None = None) -> BuildDepthsOutput:
+    return _grow(active_routes, depth, k=k, width=k, policy=_tree_policy(phase), route_store=route_store,
+                 model_backend=model_backend, attention_backend=attention_backend, sampling=sampling)
+
+
+def build_forest_one_depth(active_routes: Sequence[RouteState], *, k: int, route_store: KVTreeStore,
+                           model_backend: FrontierModelBackend, attention_backend: Any = None,
+                           sampling: DrafterSamplingContext | None = None) -> FrontierStepOutput:
+    """One stage-2 depth: decode the ``k^2`` routes and keep the best ``k`` children per root."""
+    return _grow(active_routes, 1, k=k, width=k * k, policy=FOREST, route_store=route_store,
+                 model_backend=model_backend, attention_backend=attention_backend, sampling=sampling).steps[0]
+
+
+def build_forest_depths(active_routes: Sequence[RouteState], *, depth: int, k: int, route_store: KVTreeStore,
+                        model_backend: FrontierModelBackend, attention_backend: Any = None,
+                        sampling: DrafterSamplingContext | None = None) -> BuildDepthsOutput:
+    return _grow(active_routes, depth, k=k, width=k * k, policy=FOREST, route_store=route_store,
+                 model_backend=model_backend, attention_backend=attention_backend, sampling=sampling)
 
 
 def select_routes_by_stage1_root(routes: Sequence[RouteState], selected_stage1_root_id: int) -> list[RouteState]:
-    return [r for r in routes if r.stage1_root_id == selected_stage1_root_id]
-
-
-def collect_final_pending_candidates(completed_routes, last_logits, *, k: int) -> list[PendingCandidate]:
-    return collect_pending_candidates(completed_routes, last_logits, k=k)
+    """The routes under one stage-1 root (the forest part that survives a selection)."""
+    root = int(selected_stage1_root_id)
+    return [r for r in routes if int(r.stage1_root_id) == root]

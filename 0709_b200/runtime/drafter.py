@@ -103,12 +103,18 @@ class DrafterRuntime:
     # ---------------------------------------------------------------- store
     def bind_store(self, store: KVTreeStore) -> None:
         self.route_store = store
-        store.add_route_release_hook(self._fork_children)
+        store.on_spawn(self._fork_children)
 
-    def _fork_children(self, previous: Sequence[RouteState], nxt: Sequence[RouteState]) -> None:
-        for child in nxt:
-            if child.parent_route_id is not None and not self.route_pool.has_route(child.route_id):
-                self.route_pool.fork(int(child.route_id), int(child.parent_route_id))
+    def _fork_children(self, children: Sequence[RouteState]) -> None:
+        """New child routes share their parent's pages (the tail page is copied on their first append)."""
+        rp = self.route_pool
+        for child in children:
+            if child.parent_route_id is not None and not rp.has_route(child.route_id):
+                rp.fork(int(child.route_id), int(child.parent_route_id))
+
+    def status_flag(self) -> torch.Tensor | None:
+        """The drafter device's kernel error flag (None for op tables that raise directly)."""
+        return getattr(self.engine.ops, "err", None)
 
     # -------------------------------------------------------------- prefix
     def _sync_prefix(self) -> None:
@@ -229,26 +235,23 @@ class DrafterRuntime:
     ) -> tuple[list[RouteState], dict[str, int]]:
         store = self.route_store
         assert store is not None
-        nodes = store.node_path_for_route(committed_route)
-        if not nodes:
-            raise ValueError("cannot commit a stage-1 route with no materialized nodes")
+        n_nodes = len(committed_route.kv_view.node_ids)
+        if not n_nodes:
+            raise ValueError(f"stage-1 route {committed_route.route_id} has no decoded tokens to commit")
         self._ensure_views([committed_route, *retained_routes])
         keep = [int(r.route_id) for r in retained_routes]
+        # Physical: keep the survivors' views, then turn the committed route's view into the prefix.
         released_routes, freed = self.route_pool.retain([*keep, int(committed_route.route_id)])
         freed += self.route_pool.commit(int(committed_route.route_id))
-        tokens = store.commit_route(committed_route)
+        # Logical: the same commit on the node arena, survivors rebased onto the new prefix.
+        tokens, promoted = store.advance_prefix(committed_route, retained_routes)
         self.prefix_token_ids = (*self.prefix_token_ids, *tokens)
         if self.route_pool.prefix_len != len(self.prefix_token_ids):
-            raise RuntimeError("drafter physical prefix diverged from the logical prefix")
-        promoted = store.promote_routes_after_commit(
-            committed_route, retained_routes, PrefixKVView(committed_length=len(self.prefix_token_ids))
-        )
+            raise RuntimeError(f"drafter pages hold {self.route_pool.prefix_len} committed tokens, the route "
+                               f"store {len(self.prefix_token_ids)}")
         self._sync_prefix()
-        live = {n for r in promoted for n in r.kv_view.node_ids}
-        for nid in [n for n in store.nodes if n not in live]:
-            del store.nodes[nid]
         return promoted, {
-            "committed_kv_tokens": len(nodes),
+            "committed_kv_tokens": n_nodes,
             "retained_routes": len(promoted),
             "released_route_rows": int(released_routes) + 1,
             "released_kv_pages": int(freed),

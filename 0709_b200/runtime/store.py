@@ -1,216 +1,225 @@
-"""Logical route/tree topology.
+"""Speculative tree state of one drafter session: a node arena plus the live routes.
 
-Tracks tree nodes (token, parent, depth, stage-1 root) and live routes. Physical
-KV placement is owned by the native page pool (``runtime.kv_pool``); the store
-only hands out node ids and route ids and rebases routes after a commit.
+Nodes are the drafted tokens whose KV has been written.  They live in an
+append-only arena of parallel lists (token, parent node, depth, stage-1 root)
+addressed by ``node_id - base``; a depth's node ids are reserved in one block
+when the drafter launches its decode, and filled in when the step's routes
+``grow``.  Nothing is deleted while a round runs: dead branches simply stop
+being referenced, and on a commit the arena is cut below the survivors'
+oldest node -- a few hundred list entries per round instead of per-node
+objects that are created and freed.  Node ids never repeat.
 
-Behavioural parity: reference src/atlas_0709/flashinfer_paged/kv.py:21-258
-(node materialization, descriptor fork with per-token log-probs, commit, and
-promotion that rebases ``stage2_depth -> stage1_depth``).
+Routes are ``RouteState`` records (the public route type).  The store gives
+them ids, grows them by one node, spawns children from selected candidates,
+and on a commit moves the committed route's tokens into the prefix and
+rebases the surviving stage-2 routes onto it.  Physical KV (pages, tail
+copy-on-write) is the native ``RoutePool``'s business; listeners registered
+with ``on_spawn`` learn about new children so the pool can fork their views.
+
+Behaviour matches the reference's tree store (src/atlas_0709/flashinfer_paged/kv.py:21-258):
+the same ids, per-token draft log-probs relative to the committed prefix,
+commit semantics and stage-2 -> stage-1 rebasing.
 """
 
 from __future__ import annotations
 
-from dataclasses import dataclass
 from typing import Callable, Iterable, Sequence
 
 from ..types import DecodePhase, PendingCandidate, PrefixKVView, RouteKVView, RouteState
 
-
-@dataclass
-class TreeNode:
-    node_id: int
-    token_id: int
-    parent_node_id: int | None
-    stage1_root_id: int
-    depth: int
-    owner_route_id: int | None = None
-    committed: bool = False
-
-
-ReleaseHook = Callable[[Sequence[RouteState], Sequence[RouteState]], None]
+SpawnListener = Callable[[Sequence[RouteState]], None]
+_HOLE = -1  # arena slot reserved for a node that has not grown yet
 
 
 class KVTreeStore:
     def __init__(self) -> None:
-        self._next_route_id = 1
-        self._next_node_id = 1
-        self.nodes: dict[int, TreeNode] = {}
-        self.routes: dict[int, RouteState] = {}
         self.committed_token_ids: list[int] = []
-        self._release_hooks: list[ReleaseHook] = []
+        self.routes: dict[int, RouteState] = {}
+        self._route_ids = 0
+        self._base = 1          # node id of arena slot 0
+        self._tok: list[int] = []
+        self._parent: list[int] = []
+        self._depth: list[int] = []
+        self._root: list[int] = []
+        self._listeners: list[SpawnListener] = []
 
-    # ---------------------------------------------------------------- ids
+    # ------------------------------------------------------------- ids
     def allocate_route_id(self) -> int:
-        rid = self._next_route_id
-        self._next_route_id += 1
-        return rid
-
-    def allocate_node_id(self) -> int:
-        nid = self._next_node_id
-        self._next_node_id += 1
-        return nid
+        self._route_ids += 1
+        return self._route_ids
 
     def reserve_node_ids(self, count: int) -> list[int]:
-        start = self._next_node_id
-        self._next_node_id += int(count)
-        return list(range(start, start + int(count)))
+        """Reserve ``count`` consecutive node ids (one decode step's nodes)."""
+        first = self._base + len(self._tok)
+        n = int(count)
+        self._tok.extend([_HOLE] * n)
+        self._parent.extend([_HOLE] * n)
+        self._depth.extend([0] * n)
+        self._root.extend([0] * n)
+        return list(range(first, first + n))
 
-    def peek_next_node_id(self) -> int:
-        return self._next_node_id
+    @property
+    def arena_size(self) -> int:
+        return len(self._tok)
 
-    # ------------------------------------------------------------ routes
-    def reset_speculative(self) -> None:
-        self.nodes.clear()
-        self.routes.clear()
+    def on_spawn(self, listener: SpawnListener) -> None:
+        self._listeners.append(listener)
 
-    def add_route_release_hook(self, hook: ReleaseHook) -> None:
-        self._release_hooks.append(hook)
-
+    # ------------------------------------------------------------ views
     def prefix_view(self, committed_length: int | None = None) -> PrefixKVView:
         n = len(self.committed_token_ids) if committed_length is None else int(committed_length)
         return PrefixKVView(committed_length=n)
 
-    def register_route(self, route: RouteState) -> RouteState:
-        self.routes[int(route.route_id)] = route
+    def node_token(self, node_id: int) -> int:
+        tok = self._tok[int(node_id) - self._base]
+        if tok == _HOLE:
+            raise KeyError(f"node {node_id} was reserved but never grown")
+        return tok
+
+    def node_parent(self, node_id: int) -> int | None:
+        p = self._parent[int(node_id) - self._base]
+        return None if p == _HOLE else p
+
+    def tokens_for_node_ids(self, node_ids: Iterable[int]) -> tuple[int, ...]:
+        base, tok = self._base, self._tok
+        return tuple(tok[int(n) - base] for n in node_ids)
+
+    def materialized_token_path(self, route: RouteState) -> tuple[int, ...]:
+        """Tokens of the route's grown nodes (relative to the committed prefix)."""
+        return self.tokens_for_node_ids(route.kv_view.node_ids)
+
+    def pending_token_path(self, route: RouteState) -> tuple[int, ...]:
+        """Grown tokens followed by the route's pending token."""
+        return (*self.materialized_token_path(route), int(route.pending_token_id))
+
+    # ----------------------------------------------------------- routes
+    def new_route(self, *, root: int | None, parent: RouteState | None, token: int, token_logprob: float,
+                  prefix: PrefixKVView | None = None) -> RouteState:
+        """A route one pending token beyond ``parent`` (or beyond the committed prefix when ``parent`` is None).
+
+        A route without a parent is its own stage-1 root; a child takes ``root``
+        (default: its parent's root).
+        """
+        rid = self.allocate_route_id()
+        if parent is None:
+            view = (prefix or self.prefix_view()).fork()
+            route = RouteState(route_id=rid, stage1_root_id=rid if root is None else int(root), parent_route_id=None,
+                               materialized_leaf_node_id=None, pending_token_id=int(token),
+                               cumulative_logprob=float(token_logprob), stage1_depth=0, stage2_depth=0, kv_view=view,
+                               token_logprobs=(float(token_logprob),))
+        else:
+            route = RouteState(
+                route_id=rid,
+                stage1_root_id=int(parent.stage1_root_id if root is None else root),
+                parent_route_id=int(parent.route_id),
+                materialized_leaf_node_id=parent.materialized_leaf_node_id,
+                pending_token_id=int(token),
+                cumulative_logprob=float(parent.cumulative_logprob) + float(token_logprob),
+                stage1_depth=int(parent.stage1_depth),
+                stage2_depth=int(parent.stage2_depth),
+                kv_view=parent.kv_view.fork(),
+                token_logprobs=(*parent.token_logprobs, float(token_logprob)) if parent.token_logprobs else (),
+            )
+        self.routes[rid] = route
         return route
 
     def get_route(self, route_id: int) -> RouteState:
         return self.routes[int(route_id)]
 
-    def get_routes(self, route_ids: Iterable[int]) -> list[RouteState]:
-        return [self.get_route(r) for r in route_ids]
-
-    def mark_routes_materialized(
-        self,
-        routes: Sequence[RouteState],
-        new_node_ids: Sequence[int],
-        phase: DecodePhase,
-    ) -> list[RouteState]:
-        """Turn each route's pending token into a tree node (its KV was just written)."""
-        if len(routes) != len(new_node_ids):
-            raise ValueError("routes and new_node_ids must have the same length")
-        out: list[RouteState] = []
-        for route, raw in zip(routes, new_node_ids):
-            nid = int(raw)
-            next_depth = route.total_materialized_depth() + 1
-            if route.token_logprobs and len(route.token_logprobs) != next_depth:
+    def grow(self, routes: Sequence[RouteState], node_ids: Sequence[int], phase: DecodePhase) -> list[RouteState]:
+        """Each route's pending token became node ``node_ids[i]`` (its KV is written); extend the routes."""
+        if len(routes) != len(node_ids):
+            raise ValueError(f"{len(routes)} routes grew but {len(node_ids)} node ids were reserved")
+        stage2 = phase == DecodePhase.STAGE2
+        if not stage2 and phase != DecodePhase.STAGE1:
+            raise ValueError(f"unknown decode phase {phase!r}")
+        base = self._base
+        for route, nid in zip(routes, node_ids):
+            depth = int(route.stage1_depth) + int(route.stage2_depth) + 1
+            if route.token_logprobs and len(route.token_logprobs) != depth:
                 raise ValueError(
-                    "frontier route token_logprobs must include exactly its pending token: "
-                    f"route_id={route.route_id}, logprobs={len(route.token_logprobs)}, "
-                    f"next_materialized_depth={next_depth}"
-                )
-            parent = route.kv_view.node_ids[-1] if route.kv_view.node_ids else None
-            self.nodes[nid] = TreeNode(
-                node_id=nid,
-                token_id=int(route.pending_token_id),
-                parent_node_id=parent,
-                stage1_root_id=route.stage1_root_id,
-                depth=next_depth,
-                owner_route_id=route.route_id,
-            )
-            route.materialized_leaf_node_id = nid
-            route.kv_view = route.kv_view.append_node(nid)
-            if phase == DecodePhase.STAGE1:
-                route.stage1_depth += 1
-            elif phase == DecodePhase.STAGE2:
+                    f"route {route.route_id} carries {len(route.token_logprobs)} draft log-probs; growing it to "
+                    f"depth {depth} needs exactly one per token including the pending one")
+            slot = int(nid) - base
+            if not 0 <= slot < len(self._tok) or self._tok[slot] != _HOLE:
+                raise ValueError(f"node id {nid} is not a reserved, unused slot")
+            leaf = route.materialized_leaf_node_id
+            self._tok[slot] = int(route.pending_token_id)
+            self._parent[slot] = _HOLE if leaf is None else int(leaf)
+            self._depth[slot] = depth
+            self._root[slot] = int(route.stage1_root_id)
+            route.materialized_leaf_node_id = int(nid)
+            route.kv_view = route.kv_view.append_node(int(nid))
+            if stage2:
                 route.stage2_depth += 1
-            else:  # pragma: no cover - enum exhausted
-                raise ValueError(f"unsupported decode phase: {phase}")
-            self.register_route(route)
-            out.append(route)
-        return out
+            else:
+                route.stage1_depth += 1
+        return list(routes)
 
-    def materialize_route_descriptors(
-        self,
-        selected: Sequence[PendingCandidate],
-        parent_routes: Sequence[RouteState],
-    ) -> list[RouteState]:
-        """Create one child route per selected candidate, forking its parent's view."""
-        parents = {r.route_id: r for r in parent_routes}
-        out: list[RouteState] = []
-        for cand in selected:
-            parent = parents.get(cand.parent_route_id) or self.get_route(cand.parent_route_id)
-            if parent.token_logprobs and len(parent.token_logprobs) != parent.total_materialized_depth():
-                raise ValueError(
-                    "decoded parent token_logprobs must match its materialized path: "
-                    f"route_id={parent.route_id}, logprobs={len(parent.token_logprobs)}, "
-                    f"materialized_depth={parent.total_materialized_depth()}"
-                )
-            local = float(cand.cumulative_logprob - cand.parent_logprob)
-            child = RouteState(
-                route_id=self.allocate_route_id(),
-                stage1_root_id=cand.stage1_root_id,
-                parent_route_id=parent.route_id,
-                materialized_leaf_node_id=parent.materialized_leaf_node_id,
-                pending_token_id=int(cand.pending_token_id),
-                cumulative_logprob=float(cand.cumulative_logprob),
-                stage1_depth=parent.stage1_depth,
-                stage2_depth=parent.stage2_depth,
-                kv_view=parent.kv_view.fork(),
-                token_logprobs=(*parent.token_logprobs, local) if parent.token_logprobs else (),
-            )
-            out.append(self.register_route(child))
-        return out
+    def spawn(self, picks: Sequence[PendingCandidate], parents: Sequence[RouteState]) -> list[RouteState]:
+        """One child route per picked candidate, forked from its (just grown) parent."""
+        by_id = {int(r.route_id): r for r in parents}
+        children: list[RouteState] = []
+        for c in picks:
+            parent = by_id.get(int(c.parent_route_id))
+            if parent is None:
+                parent = self.get_route(c.parent_route_id)
+            grown = int(parent.stage1_depth) + int(parent.stage2_depth)
+            if parent.token_logprobs and len(parent.token_logprobs) != grown:
+                raise ValueError(f"parent route {parent.route_id} has {len(parent.token_logprobs)} draft "
+                                 f"log-probs for {grown} grown tokens")
+            children.append(self.new_route(root=c.stage1_root_id, parent=parent, token=c.pending_token_id,
+                                           token_logprob=float(c.cumulative_logprob) - float(c.parent_logprob)))
+        for listener in self._listeners:
+            listener(children)
+        return children
 
-    def release_routes_without_descendants(
-        self, previous_routes: Sequence[RouteState], next_routes: Sequence[RouteState]
-    ) -> None:
-        """Notify physical backends that parents without selected children can go."""
-        for hook in self._release_hooks:
-            hook(previous_routes, next_routes)
+    # -------------------------------------------------- commit / rebase
+    def advance_prefix(self, route: RouteState, survivors: Sequence[RouteState], *,
+                       max_tokens: int | None = None) -> tuple[tuple[int, ...], list[RouteState]]:
+        """Commit ``route``'s grown tokens and rebase ``survivors`` (its stage-2 descendants) onto them.
 
-    # ------------------------------------------------------------- paths
-    def tokens_for_node_ids(self, node_ids: Sequence[int]) -> tuple[int, ...]:
-        return tuple(self.nodes[int(n)].token_id for n in node_ids)
-
-    def materialized_token_path(self, route: RouteState) -> tuple[int, ...]:
-        return self.tokens_for_node_ids(route.kv_view.node_ids)
-
-    def node_path_for_route(self, route: RouteState) -> tuple[int, ...]:
-        return tuple(route.kv_view.node_ids)
-
-    def pending_token_path(self, route: RouteState) -> tuple[int, ...]:
-        return (*self.materialized_token_path(route), int(route.pending_token_id))
-
-    # ------------------------------------------------------ commit/promote
-    def commit_route(self, route: RouteState, max_tokens: int | None = None) -> tuple[int, ...]:
-        nodes = self.node_path_for_route(route)
+        Returns the committed tokens and the rebased routes, which are now
+        stage-1 routes of the longer prefix: their node paths, depths and draft
+        log-probs lose the committed part, and each becomes its own root.
+        Every other route is forgotten and the arena below the survivors'
+        oldest node is released.
+        """
+        path = tuple(route.kv_view.node_ids)
         if max_tokens is not None:
-            nodes = nodes[: int(max_tokens)]
-        for n in nodes:
-            self.nodes[n].committed = True
-        tokens = self.tokens_for_node_ids(nodes)
+            path = path[: int(max_tokens)]
+        tokens = self.tokens_for_node_ids(path)
         self.committed_token_ids.extend(tokens)
-        return tokens
+        cut = len(path)
+        prefix = self.prefix_view()
+        for r in survivors:
+            nodes = tuple(r.kv_view.node_ids)
+            if nodes[:cut] != path:
+                raise ValueError(f"route {r.route_id} does not descend from the committed route {route.route_id}")
+            if r.token_logprobs:
+                grown = int(r.stage1_depth) + int(r.stage2_depth)
+                if len(r.token_logprobs) - grown not in (0, 1):
+                    raise ValueError(f"route {r.route_id}: {len(r.token_logprobs)} draft log-probs for {grown} "
+                                     "grown tokens")
+                r.token_logprobs = tuple(r.token_logprobs[cut:])
+            rest = nodes[cut:]
+            r.kv_view = RouteKVView(prefix=prefix, node_ids=rest)
+            r.materialized_leaf_node_id = rest[-1] if rest else None
+            r.stage1_depth, r.stage2_depth = int(r.stage2_depth), 0
+            r.stage1_root_id = int(r.route_id)
+            r.parent_route_id = None
+        self._release_below(survivors)
+        self.routes = {int(r.route_id): r for r in survivors}
+        return tokens, list(survivors)
 
-    def promote_routes_after_commit(
-        self,
-        committed_route: RouteState,
-        routes: Sequence[RouteState],
-        new_prefix: PrefixKVView,
-    ) -> list[RouteState]:
-        """Rebase stage-2 routes of the selected root so they become stage-1 routes."""
-        committed = self.node_path_for_route(committed_route)
-        out: list[RouteState] = []
-        for route in routes:
-            nodes = route.kv_view.node_ids
-            if nodes[: len(committed)] != committed:
-                raise ValueError("cannot promote a route outside the committed branch")
-            if route.token_logprobs:
-                depth = route.total_materialized_depth()
-                if len(route.token_logprobs) not in (depth, depth + 1):
-                    raise ValueError(
-                        "promoted route token_logprobs do not match its token path: "
-                        f"route_id={route.route_id}, logprobs={len(route.token_logprobs)}"
-                    )
-                route.token_logprobs = tuple(route.token_logprobs[len(committed):])
-            suffix = tuple(nodes[len(committed):])
-            route.kv_view = RouteKVView(prefix=new_prefix, node_ids=suffix)
-            route.materialized_leaf_node_id = suffix[-1] if suffix else None
-            route.stage1_depth = route.stage2_depth
-            route.stage2_depth = 0
-            route.stage1_root_id = route.route_id
-            route.parent_route_id = None
-            out.append(self.register_route(route))
-        return out
+    def reset_speculative(self) -> None:
+        """Forget every route and node (the committed prefix stays)."""
+        self.routes.clear()
+        self._release_below(())
+
+    def _release_below(self, survivors: Sequence[RouteState]) -> None:
+        oldest = min((int(n) for r in survivors for n in r.kv_view.node_ids), default=None)
+        cut = len(self._tok) if oldest is None else oldest - self._base
+        if cut > 0:
+            del self._tok[:cut], self._parent[:cut], self._depth[:cut], self._root[:cut]
+            self._base += cut

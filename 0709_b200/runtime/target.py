@@ -30,7 +30,7 @@ import torch
 from ..ops import _native
 from ..ops.attn_desc import AttnDesc, single_sequence_desc
 from ..utils import counters
-from ..utils.transfer import ids_to_device
+from ..utils.transfer import KernelError, ids_to_device, read_back
 from ..utils.nvtx import nvtx_range
 from ..types import PrefixState, TargetRouteScore, TargetVerifyResult, VerifyRoutePayload
 from .drafter import PrefixPageMirror
@@ -181,8 +181,15 @@ class TargetVerifier:
                 f"request_len={len(prefix)}, target_len={len(self.prefix_token_ids)}"
             )
         paths, depth = self._validate_routes(routes)
-        with nvtx_range("target_tree_verify"):
-            tree = self.run_tree(paths)
+        p_committed = len(self.prefix_token_ids)
+        try:
+            with nvtx_range("target_tree_verify"):
+                tree = self.run_tree(paths)
+        except KernelError:
+            # Nothing is scored, selected or committed: drop the nodes' scratch slots.
+            self.seq.set_prefix_len(p_committed)
+            self._sync()
+            raise
         scores = self._score_routes(routes, paths, tree["path_logprobs"])
         best = max(scores, key=self._best_key)
         selected, sampling_meta = self._select_route_with_metadata(
@@ -403,11 +410,11 @@ class TargetVerifier:
             row_len=np.full(n, base + n),
             row_mask=masks.numpy(),
         )
-        self._prefix_logits = logits[0].detach().clone()
-        self._pending_token = None
         # Token t of a route is scored by its parent's row: the lead row for t == 0.
         toks = torch.tensor([list(x) for x in paths], dtype=torch.long)
         lp = self.gather_logprobs(logits, node_paths[:, :-1].long(), toks, prefix_row=False)
+        self._prefix_logits = logits[0].detach().clone()
+        self._pending_token = None
         real = node_paths[:, 1:] - 1  # node i >= 1 of this trie is node i - 1 of the routes' trie
         return {
             "logits": logits[1:],
@@ -459,10 +466,14 @@ class TargetVerifier:
             vals = shared_ops(dev).gather_logprobs(allrows, r, t).reshape(rows.shape)
         else:
             lse = torch.logsumexp(allrows, dim=-1)
-            vals = (allrows[r, t] - lse[r]).reshape(rows.shape)
-        if vals.is_cuda:
-            counters.d2h(vals.numel() * 4)
-        return vals.double().cpu().tolist()
+            vals = (allrows[r, t] - lse[r]).reshape(rows.shape).float()
+        # The one transfer of the verify also brings back the device error flag.
+        (host,) = read_back([vals], self.status_flag(), where="target tree verify")
+        return host.astype(np.float64).tolist()
+
+    def status_flag(self) -> torch.Tensor | None:
+        """The target device's kernel error flag (None for op tables that raise directly)."""
+        return getattr(self.engine.ops, "err", None)
 
     def warm_graphs(self) -> None:
         """Capture the verify bucket (up to k*d nodes) and the AR bucket up front."""
@@ -767,9 +778,13 @@ class TargetVerifier:
             all_logits.append(cur)
         if while_running is not None:
             while_running()
-        if toks.is_cuda:
-            counters.d2h(toks.numel() * 4)
-        generated = [int(x) for x in toks.cpu().tolist()]
+        try:
+            (host_toks,) = read_back([toks], self.status_flag(), where="target fallback AR")
+        except KernelError:
+            self.seq.set_prefix_len(p)
+            self._sync()
+            raise
+        generated = [int(x) for x in host_toks.tolist()]
         if prof:
             self._profile_sync()
         model_s = time.perf_counter() - t_model

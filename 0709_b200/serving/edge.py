@@ -342,7 +342,8 @@ class PagedDistributedAtlasGenerator:
         store.committed_token_ids.extend(suffix)
         self.drafter.append_known_tokens_as_prefix(suffix)
         rs = self._sampling(store.committed_token_ids)
-        active = initialize_stage1_routes(self.drafter.prefix_state(), k=self.config.k, route_store=store, sampling=rs)
+        active = initialize_stage1_routes(self.drafter.prefix_state(), k=self.config.k, route_store=store, sampling=rs,
+                                          model_backend=self.drafter)
         stage1 = self._tree_for_verify(active, depth=self.config.d, store=store, sampling=rs)
         return stage1, {
             "committed_kv_tokens": len(suffix),
@@ -482,14 +483,16 @@ class AtlasSession:
         _, self.edge_prefill = g._timed("edge_prompt_prefill", g.drafter.prefill, self.committed)
         self.store.committed_token_ids = list(self.committed)
         t_tree = g._now()
-        active = initialize_stage1_routes(g.drafter.prefix_state(), k=cfg.k, route_store=self.store, sampling=s0)
+        active = initialize_stage1_routes(g.drafter.prefix_state(), k=cfg.k, route_store=self.store, sampling=s0,
+                                          model_backend=g.drafter)
         self.stage1 = build_tree_depths(
             active, depth=cfg.d, k=cfg.k, route_store=self.store, model_backend=g.drafter, sampling=s0
         )
         self.initial_tree = EdgeSpan("edge_initial_stage1_tree", t_tree, g._now())
         if cfg.fixed_forest_depth is None and not tfut.done():
             self.pre_frontier = initialize_forest_routes(
-                self.stage1.completed_routes, self.stage1.last_logits, k=cfg.k, route_store=self.store, sampling=s0
+                self.stage1.completed_routes, self.stage1.last_logits, k=cfg.k, route_store=self.store, sampling=s0,
+                model_backend=g.drafter,
             )
             while not tfut.done() and self.pre_depth < cfg.d:
                 t0 = g._now()
@@ -555,7 +558,8 @@ class AtlasSession:
         else:
             f_depth, f_done, f_logits, f_spans = 0, None, None, list(tree_spans)
             f_front = initialize_forest_routes(
-                self.stage1.completed_routes, self.stage1.last_logits, k=cfg.k, route_store=store, sampling=rs
+                self.stage1.completed_routes, self.stage1.last_logits, k=cfg.k, route_store=store, sampling=rs,
+                model_backend=g.drafter,
             )
         while not skip and g._should_build_forest_step(verify_done=vfut.done() or fb_decided.is_set(),
                                                        forest_depth=f_depth):

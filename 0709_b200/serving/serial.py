@@ -55,7 +55,8 @@ class SerialAtlasGenerator(PagedDistributedAtlasGenerator):
         while len(generated) < cfg.max_new_tokens:
             rs = self._sampling(committed)
             t = time.perf_counter()
-            active = initialize_stage1_routes(self.drafter.prefix_state(), k=cfg.k, route_store=store, sampling=rs)
+            active = initialize_stage1_routes(self.drafter.prefix_state(), k=cfg.k, route_store=store, sampling=rs,
+                                              model_backend=self.drafter)
             stage1 = build_tree_depths(
                 active, depth=cfg.d, k=cfg.k, route_store=store, model_backend=self.drafter, sampling=rs
             )

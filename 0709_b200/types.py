@@ -86,24 +86,6 @@ class PendingCandidate:
 
 
 @dataclass(frozen=True)
-class PendingCandidateBatch:
-    """Device-resident candidate descriptors for one frontier depth (one row per candidate)."""
-
-    parent_route_ids: torch.Tensor
-    stage1_root_ids: torch.Tensor
-    parent_row_indices: torch.Tensor
-    pending_token_ids: torch.Tensor
-    cumulative_logprobs: torch.Tensor
-    parent_logprobs: torch.Tensor
-    ranks_in_parent: torch.Tensor
-    candidates_per_parent: int
-
-    @property
-    def candidate_count(self) -> int:
-        return int(self.pending_token_ids.numel())
-
-
-@dataclass(frozen=True)
 class FrontierSelectionStats:
     candidate_count: int = 0
     selected_count: int = 0
