@@ -508,6 +508,22 @@ void tp_wait(int64_t flags, int64_t seq, int64_t nsrc, torch::Tensor err) {
                         static_cast<int>(nsrc), err.data_ptr<int>(), at::cuda::getCurrentCUDAStream());
 }
 
+// Wall-time limit of the cross-GPU waits (tp_reduce_rmsnorm, tp_wait) on one device.
+void set_peer_wait_ns(int64_t ns, int64_t device) {
+  TORCH_CHECK(ns > 0, "the peer wait limit must be positive");
+  const c10::cuda::CUDAGuard guard(static_cast<c10::DeviceIndex>(device));
+  const cudaError_t e = atlas::set_peer_wait_ns(static_cast<uint64_t>(ns));
+  TORCH_CHECK(e == cudaSuccess, "set_peer_wait_ns: ", cudaGetErrorString(e));
+}
+
+int64_t peer_wait_ns(int64_t device) {
+  const c10::cuda::CUDAGuard guard(static_cast<c10::DeviceIndex>(device));
+  uint64_t ns = 0;
+  const cudaError_t e = atlas::get_peer_wait_ns(&ns);
+  TORCH_CHECK(e == cudaSuccess, "peer_wait_ns: ", cudaGetErrorString(e));
+  return static_cast<int64_t>(ns);
+}
+
 // CUDA IPC: a plain cudaMalloc region (not the caching allocator, whose blocks
 // share one IPC handle per segment) that peers map into their address space.
 int64_t ipc_malloc(int64_t bytes, int64_t device) {
@@ -714,6 +730,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm_peer", &gemm_peer, "tcgen05 GEMM with the fp32 tile stored into peer buffers, then a release flag");
   m.def("tp_reduce_rmsnorm", &tp_reduce_rmsnorm, "wait for peers, h += sum of partials, x = rmsnorm(h)");
   m.def("tp_wait", &tp_wait);
+  m.def("set_peer_wait_ns", &set_peer_wait_ns, "wall-time limit (ns) of cross-GPU waits on a device");
+  m.def("peer_wait_ns", &peer_wait_ns);
   m.def("gemm_fp8", &gemm_fp8, "block-scaled fp8 tcgen05 GEMM; returns [bn, splits, kb_per_split]");
   m.def("gemm_fp8_peer", &gemm_fp8_peer);
   m.def("quant_fp8", &quant_fp8, "per-token 1x128 e4m3 quantization");

@@ -35,8 +35,9 @@ constexpr uint32_t kSpinLimit = 1u << 26;  // ~seconds of polling before giving 
 // Flags written by other GPUs over NVLink: release stores / acquire loads at
 // system scope.  Waits are bounded by wall time (the global timer) and give up
 // at once when the error flag is already set, so one lost peer costs one
-// timeout, not one per wait.
-constexpr uint64_t kPeerWaitNs = 5ull * 1000 * 1000 * 1000;  // 5 s
+// timeout, not one per wait.  The limit is a run-time setting of the kernels
+// that wait (tp.cu keeps it per device); this is its start value.
+constexpr uint64_t kPeerWaitDefaultNs = 5ull * 1000 * 1000 * 1000;  // 5 s
 
 __device__ __forceinline__ uint64_t global_timer_ns() {
   uint64_t t;
@@ -58,14 +59,14 @@ __device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
   asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
 
-// Wait until *flag >= target (wrap-safe).  Returns false on timeout.
-__device__ __forceinline__ bool wait_flag_geq(const uint32_t* flag, uint32_t target, int* err) {
+// Wait until *flag >= target (wrap-safe), at most limit_ns.  Returns false on timeout.
+__device__ __forceinline__ bool wait_flag_geq(const uint32_t* flag, uint32_t target, int* err, uint64_t limit_ns) {
   if (err != nullptr && *reinterpret_cast<volatile int*>(err) != 0) return false;
   const uint64_t t0 = global_timer_ns();
   uint32_t polls = 0;
   while (static_cast<int32_t>(ld_acquire_sys(flag) - target) < 0) {
     if ((++polls & 255u) == 0) {
-      if (global_timer_ns() - t0 > kPeerWaitNs) {
+      if (global_timer_ns() - t0 > limit_ns) {
         set_error(err, kErrPeerTimeout);
         return false;
       }

@@ -18,7 +18,7 @@ void launch_kv_copy_pages(void* kv, const int* plan, int n, int layers, int num_
                           int* err, cudaStream_t st);
 void launch_kv_move_slots(void* kv, const int* src, const int* dst, int n, int layers, int num_pages, int Hkv, int ps,
                           int hd, int* err, cudaStream_t st);
-void launch_topk(const float* logits, int B, int V, int k, const int64_t* keys, float inv_temp, float* out_lp,
+cudaError_t launch_topk(const float* logits, int B, int V, int k, const int64_t* keys, float inv_temp, float* out_lp,
                  int64_t* out_id, float* part, int chunks, cudaStream_t st);
 int topk_record_floats();
 void launch_gather_logprobs(const float* logits, int R, int V, const int* rows, const int* toks, int n, float* lse,

@@ -290,11 +290,12 @@ __global__ void gather_lp_kernel(const float* __restrict__ logits, int V, int R,
   out[i] = logits[static_cast<int64_t>(r) * V + t] - lse[r];
 }
 
-void launch_topk(const float* logits, int B, int V, int k, const int64_t* keys, float inv_temp, float* out_lp,
+cudaError_t launch_topk(const float* logits, int B, int V, int k, const int64_t* keys, float inv_temp, float* out_lp,
                  int64_t* out_id, float* part, int chunks, cudaStream_t st) {
   const int chunk = (V + chunks - 1) / chunks;
-  launch_k(topk_chunk_kernel, dim3(chunks, B), dim3(kChunkThreads), 0, st, logits, V, k, chunk, keys, inv_temp, part);
-  launch_k(topk_merge_kernel, dim3(B), dim3(32), 0, st, static_cast<const float*>(part), chunks, k, V, out_lp, out_id);
+  const cudaError_t e = launch_k(topk_chunk_kernel, dim3(chunks, B), dim3(kChunkThreads), 0, st, logits, V, k, chunk, keys, inv_temp, part);
+  if (e != cudaSuccess) return e;
+  return launch_k(topk_merge_kernel, dim3(B), dim3(32), 0, st, static_cast<const float*>(part), chunks, k, V, out_lp, out_id);
 }
 
 int topk_record_floats() { return 2 + 3 * kMaxK; }

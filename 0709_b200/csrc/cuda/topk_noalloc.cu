@@ -63,7 +63,13 @@ extern "C" int atlas_topk_logprobs_noalloc(const float* logits, int rows, int vo
     return ATLAS_NOALLOC_EINVAL;
   }
   const int rec_floats = atlas::topk_record_floats();
-  if (rec_floats > kRecordFloatsMax) return ATLAS_NOALLOC_ECUDA;
+  if (rec_floats > kRecordFloatsMax) {
+    std::fprintf(stderr,
+                 "atlas_topk_logprobs_noalloc: the kernel's chunk record (%d floats) is larger than the fixed "
+                 "scratch's record slot (%d floats); the library was built inconsistently\n",
+                 rec_floats, kRecordFloatsMax);
+    return ATLAS_NOALLOC_ECUDA;
+  }
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return ATLAS_NOALLOC_ECUDA;
   float* scratch = nullptr;
@@ -85,8 +91,12 @@ extern "C" int atlas_topk_logprobs_noalloc(const float* logits, int rows, int vo
                  rows, chunks, records, kMaxRecords);
     return ATLAS_NOALLOC_ETOOLARGE;
   }
-  atlas::launch_topk(logits, rows, vocab, k, keys, inv_temperature, out_logprobs, out_ids, scratch,
-                     static_cast<int>(chunks), stream);
-  if (cudaGetLastError() != cudaSuccess) return ATLAS_NOALLOC_ECUDA;
+  // The launches' own return codes: an error left earlier by the caller stays the caller's to read.
+  const cudaError_t e = atlas::launch_topk(logits, rows, vocab, k, keys, inv_temperature, out_logprobs, out_ids,
+                                           scratch, static_cast<int>(chunks), stream);
+  if (e != cudaSuccess) {
+    std::fprintf(stderr, "atlas_topk_logprobs_noalloc: launch failed: %s\n", cudaGetErrorString(e));
+    return ATLAS_NOALLOC_ECUDA;
+  }
   return ATLAS_NOALLOC_OK;
 }

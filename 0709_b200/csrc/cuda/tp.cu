@@ -12,9 +12,10 @@
 //  tp_wait: the same wait alone (the root rank before it reads the gathered
 //    vocabulary-parallel logits).
 //
-// All waits are bounded (wait_flag_geq): on timeout the kernel records
-// kErrPeerTimeout and carries on with whatever is in the buffers; the host
-// reads the error flag.
+// All waits are bounded by g_peer_wait_ns (wall time, per device, set from the
+// host with set_peer_wait_ns): on timeout the kernel records kErrPeerTimeout
+// and carries on with whatever is in the buffers; the host reads the error
+// flag with the next result it copies back and stops before using them.
 
 #include "common.cuh"
 #include "launch.h"
@@ -23,10 +24,14 @@
 
 namespace atlas {
 
+// Wall-time limit of every cross-GPU wait in this file's kernels, in ns.  Read
+// at run time, so graphs captured earlier follow a later set_peer_wait_ns.
+static __device__ uint64_t g_peer_wait_ns = kPeerWaitDefaultNs;
+
 __device__ __forceinline__ void wait_all_ranks(const uint32_t* flags, const uint32_t* seq, int nsrc, int* err) {
   if (flags != nullptr && static_cast<int>(threadIdx.x) < nsrc) {
     const uint32_t target = *reinterpret_cast<const volatile uint32_t*>(seq);
-    wait_flag_geq(flags + threadIdx.x, target, err);
+    wait_flag_geq(flags + threadIdx.x, target, err, g_peer_wait_ns);
   }
   __syncthreads();
 }
@@ -45,6 +50,7 @@ constexpr int kReduceVec = 4;      // float4 per thread kept in registers (H <= 
 __device__ __forceinline__ float4 take_slot(float* ptr, int* err) {
   float4 v;
   const uint64_t t0 = global_timer_ns();
+  const uint64_t limit = g_peer_wait_ns;
   uint32_t polls = 0;
   while (true) {
     asm volatile("ld.volatile.global.v4.f32 {%0, %1, %2, %3}, [%4];"
@@ -55,7 +61,7 @@ __device__ __forceinline__ float4 take_slot(float* ptr, int* err) {
         __float_as_uint(v.z) != kPeerSentinel && __float_as_uint(v.w) != kPeerSentinel)
       break;
     if ((++polls & 63u) == 0) {
-      if (*reinterpret_cast<volatile int*>(err) != 0 || global_timer_ns() - t0 > kPeerWaitNs) {
+      if (*reinterpret_cast<volatile int*>(err) != 0 || global_timer_ns() - t0 > limit) {
         set_error(err, kErrPeerTimeout);
         break;
       }
@@ -177,5 +183,9 @@ void launch_tp_reduce_rmsnorm(const float* recv, int64_t slot_stride, const uint
 void launch_tp_wait(const uint32_t* flags, const uint32_t* seq, int nsrc, int* err, cudaStream_t st) {
   launch_k(tp_wait_kernel, dim3(1), dim3(32), 0, st, flags, seq, nsrc, err);
 }
+
+cudaError_t set_peer_wait_ns(uint64_t ns) { return cudaMemcpyToSymbol(g_peer_wait_ns, &ns, sizeof(ns)); }
+
+cudaError_t get_peer_wait_ns(uint64_t* ns) { return cudaMemcpyFromSymbol(ns, g_peer_wait_ns, sizeof(*ns)); }
 
 }  // namespace atlas

@@ -16,4 +16,8 @@ void launch_tp_reduce_rmsnorm(const float* recv, int64_t slot_stride, const uint
                               bool bf16, int* err, cudaStream_t st);
 void launch_tp_wait(const uint32_t* flags, const uint32_t* seq, int nsrc, int* err, cudaStream_t st);
 
+// Wall-time limit (ns) of the cross-GPU waits of the kernels above, on the current device.
+cudaError_t set_peer_wait_ns(uint64_t ns);
+cudaError_t get_peer_wait_ns(uint64_t* ns);
+
 }  // namespace atlas

@@ -31,6 +31,7 @@ root" (once per forward):
 
 from __future__ import annotations
 
+import os
 from dataclasses import dataclass
 
 import torch
@@ -58,6 +59,9 @@ class TPGroup:
     vocab: int
     group: object = None
     max_rows: int = 64
+    # Wall-time limit of every cross-GPU wait in the fused kernels; a peer that
+    # misses it makes the kernel record kErrPeerTimeout and return.
+    peer_wait_ms: float | None = None
 
     def __post_init__(self) -> None:
         if self.mode not in MODES:
@@ -80,6 +84,10 @@ class TPGroup:
 
             self.ext = _native.cuda()
             self.err = device_error_flag(self.device)
+            wait_ms = self.peer_wait_ms if self.peer_wait_ms is not None else float(
+                os.environ.get("ATLAS_PEER_WAIT_MS", "5000"))
+            self.ext.set_peer_wait_ns(int(wait_ms * 1e6), self.device.index if self.device.index is not None
+                                      else torch.cuda.current_device())
         if self.mode == "fused":
             self._setup_symmetric()
 
