@@ -8,7 +8,7 @@ Layout:
 - ``ops``      native extensions (C++ page pool, sm_100a kernels) and PyTorch op semantics;
 - ``runtime``  route store, frontier/builders, drafter and target runtimes, engine;
 - ``serving``  async/serial coordinators, RPC (HTTP + in-process), CLIs, sessions;
-- ``parallel`` tensor parallelism, fused collectives, peer handoff;
+- ``parallel`` tensor parallelism and its fused peer-memory collectives;
 - ``utils``    timeline, interventions, timing and clocks.
 """
 

@@ -44,8 +44,12 @@ def build_parser() -> argparse.ArgumentParser:
     p.add_argument("--max-new-tokens-capacity", type=int, default=4096,
                    help="Generated tokens to provision KV for beyond --prefix-len.")
     p.add_argument("--workspace-mb", type=int, default=128, help="Accepted for compatibility; unused.")
-    p.add_argument("--flashinfer-backend", default="auto", help="Accepted for compatibility; unused.")
-    p.add_argument("--use-packed-custom-mask", action="store_true", help="Accepted for compatibility; unused.")
+    p.add_argument("--flashinfer-backend", default="auto", choices=["auto"],
+                   help="No-op, kept so reference command lines run: attention is this package's own kernel, "
+                        "so there is no FlashInfer backend to choose (only 'auto' is accepted).")
+    p.add_argument("--use-packed-custom-mask", action="store_true",
+                   help="No-op, kept so reference command lines run: the tree mask is always the kernel's own "
+                        "packed ancestor bitmask.")
     p.add_argument("--trust-remote-code", action="store_true", help="Accepted for compatibility; unused.")
     p.add_argument("--path-score-weights", default=None,
                    help="Comma-separated per-token weights, e.g. 0.45,0.30,0.17,0.08 (normalized).")
