@@ -15,6 +15,7 @@
 #include <unordered_map>
 
 #include "attention.h"
+#include "peer_ring.h"
 #include "gemm.h"
 #include "gemm_fp8.h"
 #include "kernels.h"
@@ -524,6 +525,29 @@ int64_t peer_wait_ns(int64_t device) {
   return static_cast<int64_t>(ns);
 }
 
+// ------------------------------------------------------- peer rings
+// ring_push: src (device or pinned host address) holds header + payload.
+void ring_push(int64_t src, int64_t bytes, int64_t peer_ring, int64_t seq, int64_t device) {
+  const c10::cuda::CUDAGuard guard(static_cast<c10::DeviceIndex>(device));
+  const cudaError_t e = atlas::launch_ring_push(reinterpret_cast<const void*>(src), bytes,
+                                                reinterpret_cast<void*>(peer_ring), static_cast<uint32_t>(seq),
+                                                at::cuda::getCurrentCUDAStream());
+  TORCH_CHECK(e == cudaSuccess, "ring_push: ", cudaGetErrorString(e));
+}
+
+// ring_pop: dst (device or pinned host address) receives header + payload;
+// nbytes_out (int32 device tensor) the payload length or -1; err the ring's flag.
+void ring_pop(int64_t ring, int64_t seq, int64_t dst, int64_t dst_bytes, torch::Tensor nbytes_out, torch::Tensor err,
+              int64_t limit_ns) {
+  const c10::cuda::CUDAGuard guard(err.device());
+  TORCH_CHECK(err.scalar_type() == torch::kInt32 && nbytes_out.scalar_type() == torch::kInt32, "int32 flags");
+  const cudaError_t e = atlas::launch_ring_pop(reinterpret_cast<const void*>(ring), static_cast<uint32_t>(seq),
+                                               reinterpret_cast<void*>(dst), dst_bytes, nbytes_out.data_ptr<int>(),
+                                               err.data_ptr<int>(), static_cast<uint64_t>(limit_ns),
+                                               at::cuda::getCurrentCUDAStream());
+  TORCH_CHECK(e == cudaSuccess, "ring_pop: ", cudaGetErrorString(e));
+}
+
 // CUDA IPC: a plain cudaMalloc region (not the caching allocator, whose blocks
 // share one IPC handle per segment) that peers map into their address space.
 int64_t ipc_malloc(int64_t bytes, int64_t device) {
@@ -730,6 +754,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm_peer", &gemm_peer, "tcgen05 GEMM with the fp32 tile stored into peer buffers, then a release flag");
   m.def("tp_reduce_rmsnorm", &tp_reduce_rmsnorm, "wait for peers, h += sum of partials, x = rmsnorm(h)");
   m.def("tp_wait", &tp_wait);
+  m.def("ring_push", &ring_push, "copy a message into a peer GPU's ring and publish its sequence number");
+  m.def("ring_pop", &ring_pop, "bounded wait for a ring's next message, then copy it out");
   m.def("set_peer_wait_ns", &set_peer_wait_ns, "wall-time limit (ns) of cross-GPU waits on a device");
   m.def("peer_wait_ns", &peer_wait_ns);
   m.def("gemm_fp8", &gemm_fp8, "block-scaled fp8 tcgen05 GEMM; returns [bn, splits, kb_per_split]");

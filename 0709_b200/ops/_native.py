@@ -75,6 +75,7 @@ CUDA_SOURCES = [
     "sampling.cu",
     "topk_noalloc.cu",
     "tp.cu",
+    "peer_ring.cu",
     "gemm_fp8.cu",
 ]
 

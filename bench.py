@@ -75,6 +75,10 @@ def parse(argv=None) -> argparse.Namespace:
     p.add_argument("--impl", choices=["atlas", "reference"], default="atlas")
     p.add_argument("--parallelism", choices=["tp", "dp"], default="tp",
                    help="tp: target sharded over all GPUs (strong scaling); dp: one session per GPU")
+    p.add_argument("--placement", choices=["colocated", "split"], default="colocated",
+                   help="split: drafter on rank 0's GPU, target on rank 1's GPU (2 ranks; config 2's placement)")
+    p.add_argument("--handoff", choices=["peer", "nccl"], default="peer",
+                   help="split placement: peer-memory message rings (kernels) or NCCL send/recv")
     p.add_argument("--comm", choices=["fused", "nccl", "torch"], default="fused",
                    help="TP collectives of the headline (torch: gloo collectives, CPU ranks)")
     p.add_argument("--device", choices=["cuda", "cpu"], default="cuda",
@@ -209,17 +213,7 @@ def build_session(args, device, te):
     max_ctx, pages = context_sizes(args)
     wd = llama.random_weights(llama.get_config(args.drafter), seed=args.seed + 1, dtype=dtype, device=device)
     de = engine.LlamaEngine(wd, num_pages=pages, page_size=args.page_size, max_positions=max_ctx + 64)
-    weights = [float(x) for x in args.path_score_weights.split(",")] if args.path_score_weights else None
-    tv = target_mod.TargetVerifier(
-        te,
-        k=args.k,
-        d=args.d,
-        score_weights=weights,
-        fallback_threshold=args.fallback_threshold,
-        first_token_threshold=args.first_token_threshold,
-        fallback_ar_tokens=args.fallback_ar_tokens,
-        model_name=f"random-init {args.target}",
-    )
+    tv = make_verifier(args, te)
     # The target is on the critical path of every round (verify, then fallback AR);
     # the drafter's forest only fills the wait, so the target stream gets priority.
     if device.type == "cuda":
@@ -388,6 +382,8 @@ def main() -> int:
             dist.init_process_group("nccl", timeout=timedelta(seconds=180), device_id=device)
         else:
             dist.init_process_group("gloo", timeout=timedelta(seconds=180))
+    if args.placement == "split":
+        return split_main(args, device, world, rank, local, counters)
     tp = args.parallelism == "tp" and world > 1
     te = build_target_engine(args, device, world, tp)
     marker = te if tp else LocalMarks(world, device)
@@ -408,8 +404,25 @@ def main() -> int:
         dist.destroy_process_group()
         return 0
 
+    gen, de, tv = build_session(args, device, te)
+
+    def check_errors() -> None:
+        de.ops.check()
+        te.ops.check()
+        if tp:
+            te.tp.check()
+
+    def set_thresholds(fallback, first) -> None:
+        tv.fallback_threshold, tv.first_token_threshold = fallback, first
+
+    def to_nccl() -> None:
+        te.set_comm_mode("nccl")
+        tv.warm_graphs()
+
     try:
-        line = run_root(args, device, te, marker, clocks, world, rank, tp, counters)
+        line = run_root(args, device, gen, marker, counters, rank, check_errors=check_errors,
+                        set_thresholds=set_thresholds,
+                        to_nccl=to_nccl if tp and args.comm == "fused" else None)
     finally:
         if tp:
             te.stop_workers()
@@ -440,18 +453,108 @@ def main() -> int:
     return 0
 
 
-def run_root(args, device, te, marker, clocks, world, rank, tp, counters) -> dict:
-    import torch
+def make_verifier(args, te):
+    weights = [float(x) for x in args.path_score_weights.split(",")] if args.path_score_weights else None
+    return _pkg("runtime.target").TargetVerifier(
+        te, k=args.k, d=args.d, score_weights=weights, fallback_threshold=args.fallback_threshold,
+        first_token_threshold=args.first_token_threshold, fallback_ar_tokens=args.fallback_ar_tokens,
+        model_name=f"random-init {args.target}")
 
-    gen, de, tv = build_session(args, device, te)
+
+def split_main(args, device, world, rank, local, counters) -> int:
+    """Config 2's placement: the drafter and coordinator on rank 0, the target server on rank 1.
+
+    Requests and responses travel through ``serving.peer_transport`` (peer-memory
+    rings, or NCCL send/recv as the baseline).  The timing marks travel the same
+    way: the target records its events when the mark request arrives.
+    """
+    import torch.distributed as dist
+
+    if world != 2:
+        raise SystemExit("--placement split runs on exactly 2 ranks")
+    transport = _pkg("serving.peer_transport")
+    kind = args.handoff if device.type == "cuda" else "nccl"  # gloo point-to-point on CPU ranks
+    channel = transport.make_channel(kind, rank=rank, peer=1 - rank, device=device)
+    marker = LocalMarks(1, device)
+    clocks = RegionClocks(physical_gpu(local) if device.type == "cuda" else None)
+    marker.mark_hook = clocks
+    if rank == 1:
+        te = build_target_engine(args, device, 1, False)
+        tv = make_verifier(args, te)
+        tv.warm_graphs()
+
+        def mark(req):
+            sync(device)
+            marker.mark(str(req["tag"]))
+            return {"ok": True}
+
+        def set_thresholds(req):
+            tv.fallback_threshold, tv.first_token_threshold = req["fallback"], req["first"]
+            return {"ok": True}
+
+        def report(_req):
+            sync(device)
+            te.ops.check()
+            return {"ok": True, "report": rank_report(marker, clocks, REGIONS), "channel": dict(channel.stats)}
+
+        transport.serve_target_channel(_pkg("serving.rpc").TargetServerApp(tv), channel,
+                                       extra={"mark": mark, "set_thresholds": set_thresholds, "report": report})
+        channel.close()
+        dist.destroy_process_group()
+        return 0
+
+    llama = _pkg("models.llama")
+    max_ctx, pages = context_sizes(args)
+    wd = llama.random_weights(llama.get_config(args.drafter), seed=args.seed + 1, dtype=dtype_of(args.dtype),
+                              device=device)
+    de = _pkg("runtime.engine").LlamaEngine(wd, num_pages=pages, page_size=args.page_size,
+                                            max_positions=max_ctx + 64)
+    dr = _pkg("runtime.drafter").DrafterRuntime(de)
+    dr.warm_graphs(args.k, args.fallback_ar_tokens)
+    client = transport.ChannelTargetClient(channel)
+    edge = _pkg("serving.edge")
+    gen = edge.PagedDistributedAtlasGenerator(
+        config=edge.DistributedAtlasConfig(k=args.k, d=args.d, max_new_tokens=args.max_new_tokens,
+                                           fallback_ar_tokens=args.fallback_ar_tokens, generation_seed=args.seed,
+                                           forest_gate=args.forest_gate),
+        drafter=dr, target_client=client)
+
+    class SplitMarks:
+        """Marks on both GPUs: the target records its event when the mark request arrives."""
+
+        def mark(self, tag: str, *, barrier: bool = False) -> None:
+            sync(device)
+            client.call("mark", {"tag": tag})
+            marker.mark(tag)
+
+    try:
+        line = run_root(args, device, gen, SplitMarks(), counters, rank, check_errors=de.ops.check,
+                        set_thresholds=lambda fb, first: client.call("set_thresholds",
+                                                                     {"fallback": fb, "first": first}))
+        remote = client.call("report")
+    finally:
+        client.stop_server()
+    sync(device)
+    reports = [rank_report(marker, clocks, REGIONS), remote["report"]]
+    line["handoff_channel"] = {"kind": kind, "client": dict(channel.stats), "server": remote["channel"],
+                               "client_wait_ms_per_call": round(1e3 * client.wait_s / max(1, client.calls), 3)}
+    channel.close()
+    dist.destroy_process_group()
+    finish_line(line, reports, args, world, False)
+    line["_tokens_all"] = float(line.pop("_tokens_rank"))
+    emit(line, args, world)
+    return 0
+
+
+def run_root(args, device, gen, marker, counters, rank, *, check_errors, set_thresholds, to_nccl=None) -> dict:
+    """The measured passes on the rank that drives the generator.
+
+    ``check_errors()`` raises on a device error flag, ``set_thresholds(fallback,
+    first_token)`` sets the target's thresholds, ``to_nccl()`` (tensor-parallel
+    runs) switches the target's collectives to NCCL.
+    """
     drv = Driver(gen, make_prompts(args, rank))
     line: dict = {}
-
-    def check_errors() -> None:
-        de.ops.check()
-        te.ops.check()
-        if tp:
-            te.tp.check()
 
     # ---- headline: config thresholds, K requests
     for _ in range(args.warmup):
@@ -497,8 +600,7 @@ def run_root(args, device, te, marker, clocks, world, rank, tp, counters) -> dic
 
     # ---- select path: thresholds off, every round commits a drafted route
     if args.select_steps > 0:
-        tv.fallback_threshold = None
-        tv.first_token_threshold = None
+        set_thresholds(None, None)
         gen.fallback_ema = 0.0
         drv.step()
         r1 = len(drv.rounds)
@@ -510,13 +612,11 @@ def run_root(args, device, te, marker, clocks, world, rank, tp, counters) -> dic
         sync(device)
         check_errors()
         line["select"] = {**drv.summary(r1), "tokens": sel_tokens, "requests": args.select_steps}
-        tv.fallback_threshold = args.fallback_threshold
-        tv.first_token_threshold = args.first_token_threshold
+        set_thresholds(args.fallback_threshold, args.first_token_threshold)
 
     # ---- NCCL baseline: the same requests with library collectives
-    if tp and args.nccl_steps > 0 and args.comm == "fused":
-        te.set_comm_mode("nccl")
-        tv.warm_graphs()
+    if to_nccl is not None and args.nccl_steps > 0:
+        to_nccl()
         gen.fallback_ema = 0.0
         drv.step()
         r2 = len(drv.rounds)
@@ -557,7 +657,17 @@ def emit(line: dict, args, world: int) -> None:
     ms = main["ms_max_over_ranks"]
     tokens = line["_tokens_all"]
     value = tokens / (ms / 1000.0)
-    tp = args.parallelism == "tp" and world > 1
+    tp = args.parallelism == "tp" and world > 1 and args.placement == "colocated"
+    if args.placement == "split":
+        parallelism = (f"split placement: drafter on GPU0, target on GPU1 ({line['handoff_channel']['kind']} "
+                       "handoff through ring messages)" if line['handoff_channel']['kind'] == "peer" else
+                       "split placement: drafter on GPU0, target on GPU1 (NCCL send/recv handoff)")
+    elif tp:
+        parallelism = f"tp{world} (target sharded over {world} GPUs, {args.comm} collectives; drafter on rank 0)"
+    elif args.parallelism == "tp":
+        parallelism = "tp1 (single GPU)"
+    else:
+        parallelism = f"dp{world} (one drafter+target session per GPU)"
     out = {
         "metric": METRIC,
         "value": round(value, 3),
@@ -575,9 +685,7 @@ def emit(line: dict, args, world: int) -> None:
             "model": f"{args.drafter} drafter + {args.target} target (random init)",
             "global_batch": 1 if args.parallelism == "tp" else world,
             "seq_len": f"prompt U[{args.min_prompt},{args.max_prompt}] + {args.max_new_tokens} new",
-            "parallelism": (f"tp{world} (target sharded over {world} GPUs, {args.comm} collectives; drafter on rank 0)"
-                            if tp else ("tp1 (single GPU)" if args.parallelism == "tp"
-                                        else f"dp{world} (one drafter+target session per GPU)")),
+            "parallelism": parallelism,
             "k": args.k,
             "d": args.d,
             "page_size": args.page_size,
@@ -602,6 +710,7 @@ def emit(line: dict, args, world: int) -> None:
         "clocks": _clock_summary(main["clocks_per_rank"]),
         "e2e": line["e2e"],
         "gpu_launches": int(main["launches_all_ranks"]),
+        **({"handoff_channel": line["handoff_channel"]} if "handoff_channel" in line else {}),
         "timing": "CUDA events per rank between barrier-aligned marks; max over ranks",
     }
     sel = line.get("select")

@@ -49,3 +49,18 @@ def test_bench_single_process():
                        capture_output=True, text=True, timeout=600)
     assert r.returncode == 0, r.stderr[-4000:]
     _check(last_json(r.stdout), 1)
+
+
+def test_bench_split_placement_two_gloo_ranks():
+    """Config 2's placement: drafter + coordinator on rank 0, target server on rank 1 (gloo send/recv here)."""
+    cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes", "1", "--nproc-per-node", "2",
+           "--master-addr", "127.0.0.1", "--master-port", str(free_port()), "bench.py", "--gpus", "2",
+           "--placement", "split", *ARGS]
+    r = subprocess.run(cmd, cwd=REPO, env=dict(os.environ, OMP_NUM_THREADS="1"), capture_output=True, text=True,
+                       timeout=600)
+    assert r.returncode == 0, r.stderr[-4000:]
+    d = last_json(r.stdout)
+    assert d["config"]["parallelism"].startswith("split placement")
+    assert d["config"]["tokens_timed"] == 32 and d["select_path"]["fallback_rate"] == 0.0
+    ch = d["handoff_channel"]
+    assert ch["client"]["messages_sent"] == ch["server"]["messages_received"] + 1  # the stop message
