@@ -41,6 +41,135 @@ constexpr float kRescaleThreshold = 8.0f;  // log2 units: P stays <= 256 between
 constexpr int kThreadsTC = 192;            // warps 0-3 softmax, 4 TMA, 5 MMA
 }  // namespace
 
+// Element offset of key x of row m (kv head h) in the cache, or -1 when x is not visible to the row.
+__device__ __forceinline__ int64_t resolve_key(const AttnParams& p, int m, int h, int x, int full, int rlen,
+                                               int shared_len, int n_shared_pages, int mask_base) {
+  if (x >= rlen) return -1;
+  bool vis = x < full;
+  if (!vis) {
+    const int b = x - mask_base;
+    if (b >= 0 && b < 64 * p.mask_words) {
+      const uint64_t w = static_cast<uint64_t>(p.row_mask[static_cast<int64_t>(m) * p.mask_words + (b >> 6)]);
+      vis = (w >> (b & 63)) & 1ull;
+    }
+  }
+  if (!vis) return -1;
+  const int ps = p.page_size;
+  const int j = x / ps;
+  const bool in_shared = j < n_shared_pages || x < shared_len;
+  const int page = in_shared ? p.prefix_pages[j]
+                             : p.tail_pages[static_cast<int64_t>(m) * p.tail_stride + (j - n_shared_pages)];
+  if (page < 0 || page >= p.num_pages) {
+    set_error(p.err, kErrBadIndex);
+    return -1;
+  }
+  return ((static_cast<int64_t>(p.layer) * p.num_pages + page) * 2 * p.Hkv + h) * (static_cast<int64_t>(ps) * kHd) +
+         (x % ps) * kHd;
+}
+
+// One warp folds row m's keys beyond the shared range -- route-private tail pages
+// (drafter) or ancestor-masked nodes (tree verify) -- into its running (mx, l, o),
+// keys in position order; lane t holds dimensions 4t..4t+3.
+template <typename T>
+__device__ __forceinline__ void row_tail(const AttnParams& p, int m, int h, int64_t pair, int lane, float& mx,
+                                         float& l, float* o) {
+  const int shared_len = p.dparams[0];
+  const int n_shared_pages = p.dparams[1];
+  const int mask_base = p.dparams[2];
+  const int full = p.row_full[m];
+  const int rlen = p.row_len[m];
+  const int start = min(full, shared_len);
+  if (start >= rlen) return;
+  const float sl2 = p.scale * kLog2e;
+  const int64_t kv_head = static_cast<int64_t>(p.page_size) * kHd;
+  const T* qp = static_cast<const T*>(p.q) + pair * kHd + lane * 4;
+  const float q0 = to_f32(qp[0]), q1 = to_f32(qp[1]), q2 = to_f32(qp[2]), q3 = to_f32(qp[3]);
+  for (int t0 = start; t0 < rlen; t0 += 32) {
+    const int64_t base = resolve_key(p, m, h, t0 + lane, full, rlen, shared_len, n_shared_pages, mask_base);
+    const int cnt = min(32, rlen - t0);
+    for (int j0 = 0; j0 < cnt; j0 += 8) {
+      int64_t bj[8];
+      float2 kh[8], vh[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        bj[u] = (j0 + u < cnt) ? __shfl_sync(0xffffffffu, base, j0 + u) : -1;
+        if (bj[u] >= 0) {
+          const T* kp = static_cast<const T*>(p.kv) + bj[u] + lane * 4;
+          kh[u] = *reinterpret_cast<const float2*>(kp);
+          vh[u] = *reinterpret_cast<const float2*>(kp + static_cast<int64_t>(p.Hkv) * kv_head);
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        if (bj[u] < 0) continue;  // warp-uniform
+        const T* ke = reinterpret_cast<const T*>(&kh[u]);
+        const T* ve = reinterpret_cast<const T*>(&vh[u]);
+        float sc = q0 * to_f32(ke[0]) + q1 * to_f32(ke[1]) + q2 * to_f32(ke[2]) + q3 * to_f32(ke[3]);
+        sc = warp_sum(sc) * sl2;
+        const float nm = fmaxf(mx, sc);
+        const float a = exp2f(mx - nm), w = exp2f(sc - nm);
+        o[0] = o[0] * a + w * to_f32(ve[0]);
+        o[1] = o[1] * a + w * to_f32(ve[1]);
+        o[2] = o[2] * a + w * to_f32(ve[2]);
+        o[3] = o[3] * a + w * to_f32(ve[3]);
+        l = l * a + w;
+        mx = nm;
+      }
+    }
+  }
+}
+
+// Fused-merge epilogue: the p.splits CTAs of one (kv head, row tile) are one cluster,
+// each has staged its partial (max, sum) per row in ml_s and its O rows in o_s.  CTA r
+// of the cluster owns an equal share of the tile's valid rows; one warp per row reads
+// the partials of every split over distributed shared memory in split order
+// (deterministic), adds the row's tail keys and writes the normalized output.
+template <typename T>
+__device__ void merge_rows_and_tails(const AttnParams& p, const float* o_s, const float2* ml_s, int h, int warp,
+                                     int lane) {
+  const int G = p.Hq / p.Hkv;
+  const int C = p.splits;
+  const int tile0 = static_cast<int>(blockIdx.z) * 128;
+  const int rows_valid = min(128, p.M * G - tile0);
+  const int per = (rows_valid + C - 1) / C;
+  const int r0 = static_cast<int>(cluster_ctarank()) * per;
+  const int r1 = min(rows_valid, r0 + per);
+  for (int row = r0 + warp; row < r1; row += kThreadsTC / 32) {
+    const int grow = tile0 + row;
+    const int m = grow / G;
+    const int hq = h * G + grow % G;
+    const int64_t pair = static_cast<int64_t>(m) * p.Hq + hq;
+    float2 ml = make_float2(-INFINITY, 0.f);
+    if (lane < C) ml = ld_dsmem_f2(ml_s + row, static_cast<uint32_t>(lane));
+    if (!(ml.y > 0.f)) ml.x = -INFINITY;
+    float mx = warp_max(ml.x);
+    float l = 0.f;
+    float o[4] = {0.f, 0.f, 0.f, 0.f};
+    if (mx > -INFINITY) {
+      const float w = ml.x > -INFINITY ? exp2f(ml.x - mx) : 0.f;
+      l = warp_sum(w * ml.y);
+      const float* src = o_s + row * kHd + ((lane ^ (row & 31)) * 4);
+      for (int s = 0; s < C; ++s) {
+        const float ws = __shfl_sync(0xffffffffu, w, s);
+        if (ws > 0.f) {  // warp-uniform
+          const float4 v = ld_dsmem_f4(src, static_cast<uint32_t>(s));
+          o[0] += ws * v.x;
+          o[1] += ws * v.y;
+          o[2] += ws * v.z;
+          o[3] += ws * v.w;
+        }
+      }
+    }
+    row_tail<T>(p, m, h, pair, lane, mx, l, o);
+    const float inv = l > 0.f ? 1.f / l : 0.f;
+    T* op = static_cast<T*>(p.out) + pair * kHd + lane * 4;
+    op[0] = from_f32<T>(o[0] * inv);
+    op[1] = from_f32<T>(o[1] * inv);
+    op[2] = from_f32<T>(o[2] * inv);
+    op[3] = from_f32<T>(o[3] * inv);
+  }
+}
+
 // Warp-specialized flash attention over the shared key range.
 //   warp 4  TMA producer: K/V pages of each 64-key chunk into a 4-stage ring
 //           (non-causal: the first stages are issued before the PDL wait --
@@ -299,7 +428,20 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
 #pragma unroll
       for (int i = 0; i < kHd; ++i) acc[i] = 0.f;
     }
-    if (m < p.M) {
+    if (p.fused_merge) {
+      // Stage this split's (max, sum) and unnormalized O rows for the cluster merge: O over the
+      // drained K/V ring (every TMA load landed and every MMA finished before `fin`), 16-byte
+      // chunks XOR-swizzled by row so the 128 row threads do not share banks.
+      float* o_s = reinterpret_cast<float*>(kv_s);
+      float2* ml_s = reinterpret_cast<float2*>(p_s);
+      ml_s[rho] = make_float2(l_run > 0.f ? m_run : -INFINITY, l_run);
+      if (l_run > 0.f) {
+#pragma unroll
+        for (int c4 = 0; c4 < kHd / 4; ++c4)
+          *reinterpret_cast<float4*>(o_s + rho * kHd + ((c4 ^ (rho & 31)) * 4)) =
+              make_float4(acc[c4 * 4], acc[c4 * 4 + 1], acc[c4 * 4 + 2], acc[c4 * 4 + 3]);
+      }
+    } else if (m < p.M) {
       const int64_t rowi = static_cast<int64_t>(m) * p.Hq + hq;
       if (p.direct_out) {
         const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
@@ -327,6 +469,12 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
   tc_fence_before();
   __syncthreads();
   if (warp == 0) tmem_dealloc(tmem, 256);
+  if (p.fused_merge) {
+    cluster_sync();  // every split of the cluster has staged its partials
+    merge_rows_and_tails<T>(p, reinterpret_cast<const float*>(kv_s), reinterpret_cast<const float2*>(p_s), h, warp,
+                            tid & 31);
+    cluster_sync();  // the other CTAs are done reading this CTA's shared memory
+  }
 }
 
 // One warp per (row, q head): merge split partials, then the row's tail keys.
@@ -362,27 +510,8 @@ __global__ void __launch_bounds__(128) attn_combine_tail(AttnParams p) {
   const int full = p.row_full[m];
   const int rlen = p.row_len[m];
   const int start = min(full, shared_len);
-  // Element offset of key x of this row in the cache, or -1 if x is not visible.
   auto resolve = [&](int x) -> int64_t {
-    if (x >= rlen) return -1;
-    bool vis = x < full;
-    if (!vis) {
-      const int b = x - mask_base;
-      if (b >= 0 && b < 64 * p.mask_words) {
-        const uint64_t w = static_cast<uint64_t>(p.row_mask[static_cast<int64_t>(m) * p.mask_words + (b >> 6)]);
-        vis = (w >> (b & 63)) & 1ull;
-      }
-    }
-    if (!vis) return -1;
-    const int j = x / ps;
-    const bool in_shared = j < n_shared_pages || x < shared_len;
-    const int page = in_shared ? p.prefix_pages[j]
-                               : p.tail_pages[static_cast<int64_t>(m) * p.tail_stride + (j - n_shared_pages)];
-    if (page < 0 || page >= p.num_pages) {
-      set_error(p.err, kErrBadIndex);
-      return -1;
-    }
-    return ((static_cast<int64_t>(p.layer) * p.num_pages + page) * 2 * p.Hkv + h) * kv_head + (x % ps) * kHd;
+    return resolve_key(p, m, h, x, full, rlen, shared_len, n_shared_pages, mask_base);
   };
   const int64_t base_first = start < rlen ? resolve(start + lane) : -1;
 
@@ -474,14 +603,40 @@ __global__ void __launch_bounds__(128) attn_combine_tail(AttnParams p) {
 }
 
 template <typename T>
+static void configure_tc() {
+  static bool configured = false;
+  if (!configured) {
+    cudaFuncSetAttribute(attn_shared_tc<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
+    cudaFuncSetAttribute(attn_shared_tc<T>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+    configured = true;
+  }
+}
+
+template <typename T>
 static void launch_typed(const CUtensorMap& kvmap, const AttnParams& p, bool run_tc, bool run_combine, int row_tiles,
                          cudaStream_t st) {
+  if (p.fused_merge) {
+    // Splits of one head = one cluster; the merge and the tails run in the same kernel.
+    configure_tc<T>();
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(p.Hkv, p.splits, row_tiles);
+    cfg.blockDim = dim3(kThreadsTC);
+    cfg.dynamicSmemBytes = kSmemBytes;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = pdl_enabled() ? 1 : 0;
+    attr[1].id = cudaLaunchAttributeClusterDimension;
+    attr[1].val.clusterDim.x = 1;
+    attr[1].val.clusterDim.y = p.splits;
+    attr[1].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 2;
+    cudaLaunchKernelEx(&cfg, attn_shared_tc<T>, kvmap, p);
+    return;
+  }
   if (run_tc) {
-    static bool configured = false;
-    if (!configured) {
-      cudaFuncSetAttribute(attn_shared_tc<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
-      configured = true;
-    }
+    configure_tc<T>();
     dim3 grid(p.Hkv, p.splits, row_tiles);
     launch_k(attn_shared_tc<T>, grid, dim3(kThreadsTC), kSmemBytes, st, kvmap, p);
   }
@@ -489,6 +644,34 @@ static void launch_typed(const CUtensorMap& kvmap, const AttnParams& p, bool run
     const int64_t pairs = static_cast<int64_t>(p.M) * p.Hq;
     launch_k(attn_combine_tail<T>, dim3(static_cast<unsigned>((pairs + 3) / 4)), dim3(128), 0, st, p);
   }
+}
+
+template <typename T>
+static int max_cluster_typed() {
+  configure_tc<T>();
+  for (int c : {16, 8}) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(1, c, 1);
+    cfg.blockDim = dim3(kThreadsTC);
+    cfg.dynamicSmemBytes = kSmemBytes;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 1;
+    attr[0].val.clusterDim.y = c;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    int n = 0;
+    if (cudaOccupancyMaxActiveClusters(&n, attn_shared_tc<T>, &cfg) == cudaSuccess && n >= 1) return c;
+    cudaGetLastError();  // a refused size leaves a sticky error of this query only
+  }
+  return 8;
+}
+
+int attention_max_cluster(bool bf16) {
+  static const int v16 = max_cluster_typed<__half>();
+  static const int vbf = max_cluster_typed<__nv_bfloat16>();
+  return bf16 ? vbf : v16;
 }
 
 void launch_attention(const CUtensorMap& kvmap, const AttnParams& p, bool run_tc, bool run_combine, int row_tiles,

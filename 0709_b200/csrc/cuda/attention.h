@@ -23,8 +23,13 @@ struct AttnParams {
   int M, Hq, Hkv, page_size, num_pages, layer;
   int mask_words, tail_stride, splits, direct_out, bf16;
   int min_pages_per_split;  // a split covers at least this many pages (surplus splits exit at once)
+  int fused_merge;          // 1: the splits of a head form one cluster and merge + tail in the same kernel
   float scale;
 };
+
+// Largest cluster (splits of one head) the fused-merge path may launch with on this device: 16 when the
+// device can hold a 16-CTA cluster of the tensor-core kernel, else 8.
+int attention_max_cluster(bool bf16);
 
 void launch_attention(const CUtensorMap& kvmap, const AttnParams& p, bool run_tc, bool run_combine, int row_tiles,
                       cudaStream_t st);

@@ -604,7 +604,7 @@ torch::Tensor wrap_ptr(int64_t ptr, std::vector<int64_t> sizes, torch::ScalarTyp
 void attention(torch::Tensor q, torch::Tensor kv, int64_t layer, torch::Tensor out, torch::Tensor dparams,
                torch::Tensor prefix_pages, torch::Tensor row_full, torch::Tensor row_len, torch::Tensor row_mask,
                torch::Tensor tail_pages, torch::Tensor part_o, torch::Tensor part_ml, torch::Tensor err,
-               int64_t splits, bool run_tc, bool run_combine, bool direct_out, double scale) {
+               int64_t splits, bool run_tc, bool run_combine, bool direct_out, double scale, bool fused_merge) {
   check_cuda(q, "q");
   TORCH_CHECK(q.dim() == 3 && q.size(2) == 128 && q.is_contiguous(), "q must be contiguous [M, Hq, 128]");
   TORCH_CHECK(kv.scalar_type() == q.scalar_type(), "q and kv dtype mismatch");
@@ -616,7 +616,11 @@ void attention(torch::Tensor q, torch::Tensor kv, int64_t layer, torch::Tensor o
   TORCH_CHECK(Hq % Hkv == 0, "Hq must be a multiple of Hkv");
   const int64_t G = Hq / Hkv;
   TORCH_CHECK(128 % G == 0, "GQA group must divide 128");
-  if (!direct_out && run_tc) {
+  if (fused_merge) {
+    TORCH_CHECK(run_tc && run_combine && !direct_out, "the fused merge runs both stages and writes the output");
+    TORCH_CHECK(splits >= 1 && splits <= atlas::attention_max_cluster(q.scalar_type() == torch::kBFloat16),
+                "fused-merge splits must fit one cluster");
+  } else if (!direct_out && run_tc) {
     TORCH_CHECK(part_o.numel() >= splits * M * Hq * 128 && part_ml.numel() >= splits * M * Hq * 2,
                 "attention split workspace too small");
   }
@@ -655,6 +659,7 @@ void attention(torch::Tensor q, torch::Tensor kv, int64_t layer, torch::Tensor o
     return v != nullptr ? std::max(1, std::atoi(v)) : 4;
   }();
   p.min_pages_per_split = min_pages;
+  p.fused_merge = fused_merge ? 1 : 0;
   p.scale = static_cast<float>(scale);
   const int row_tiles = static_cast<int>((M * G + 127) / 128);
   atlas::launch_attention(kvmap, p, run_tc, run_combine, row_tiles, at::cuda::getCurrentCUDAStream());
@@ -740,6 +745,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "sm_100a kernels: tcgen05/TMA GEMM and paged attention, fused norm/rope/append, KV copies, top-k";
   m.def("gemm", &gemm, "tcgen05 GEMM out = epi(x @ w^T); returns [bn, splits, kb_per_split]");
   m.def("attention", &attention, "paged attention (tensor-core shared range + per-row tail/combine)");
+  m.def("attention_max_cluster", [](bool bf16) { return atlas::attention_max_cluster(bf16); },
+        "largest split cluster of the fused-merge attention on the current device");
   m.def("embed", &embed);
   m.def("rmsnorm", &rmsnorm);
   m.def("rope_append", &rope_append);

@@ -190,6 +190,27 @@ __device__ __forceinline__ float ld_dsmem_f32(const float* local, uint32_t rank)
   return v;
 }
 
+// The same address in the shared memory of CTA `rank` of this cluster.
+__device__ __forceinline__ uint32_t dsmem_addr(const void* local, uint32_t rank) {
+  uint32_t remote;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(smem_u32(local)), "r"(rank));
+  return remote;
+}
+__device__ __forceinline__ float2 ld_dsmem_f2(const void* local, uint32_t rank) {
+  float2 v;
+  asm volatile("ld.shared::cluster.v2.f32 {%0, %1}, [%2];" : "=f"(v.x), "=f"(v.y) : "r"(dsmem_addr(local, rank))
+               : "memory");
+  return v;
+}
+__device__ __forceinline__ float4 ld_dsmem_f4(const void* local, uint32_t rank) {
+  float4 v;
+  asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];"
+               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+               : "r"(dsmem_addr(local, rank))
+               : "memory");
+  return v;
+}
+
 // ----------------------------------------------------------------- fences
 __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");

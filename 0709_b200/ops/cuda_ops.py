@@ -11,6 +11,7 @@ a GPU machine, construction raises -- there is no silent fallback.
 from __future__ import annotations
 
 import math
+import os
 
 import torch
 
@@ -55,6 +56,9 @@ class CudaOps:
         self.part_ml = torch.empty(0, dtype=torch.float32, device=dev)
         self.num_sms = torch.cuda.get_device_properties(dev).multi_processor_count
         self.last_gemm_config: list[int] | None = None
+        # Split merge inside the attention kernel (thread-block clusters); 0 keeps the two-kernel path.
+        self.fused_merge = os.environ.get("ATLAS_ATTN_FUSED_MERGE", "1") != "0"
+        self._max_cluster: dict[bool, int] = {}
 
     # ----------------------------------------------------------- errors
     def check(self) -> None:
@@ -230,15 +234,32 @@ class CudaOps:
         run_tc = desc.shared_len > 0 and stages[0]
         sp = splits or getattr(desc, "_splits", None) or self.attention_splits(m, hq, kv.shape[3], desc.shared_len,
                                                                                 kv.shape[4])
+        if run_tc and stages[1] and self.fused_merge:
+            # One launch: the splits of a head form one cluster and merge (plus the rows' tail keys)
+            # over distributed shared memory; no split workspace.
+            c = min(int(sp), self.max_cluster(q.dtype))
+            self.ext.attention(
+                q.contiguous(), kv, layer, out, self._dparams(desc), desc.prefix_pages, desc.row_full, desc.row_len,
+                desc.row_mask, desc.tail_pages, self.part_o, self.part_ml, self.err, c, True, True, False,
+                float(scale), True,
+            )
+            counters.launches(1)
+            return out
         if run_tc:
             self._ensure_parts(sp, m, hq)
         self.ext.attention(
             q.contiguous(), kv, layer, out, self._dparams(desc), desc.prefix_pages, desc.row_full, desc.row_len,
             desc.row_mask, desc.tail_pages, self.part_o, self.part_ml, self.err, sp, run_tc, stages[1], False,
-            float(scale),
+            float(scale), False,
         )
         counters.launches(int(run_tc) + int(stages[1]))
         return out
+
+    def max_cluster(self, dtype: torch.dtype) -> int:
+        key = dtype == torch.bfloat16
+        if key not in self._max_cluster:
+            self._max_cluster[key] = int(self.ext.attention_max_cluster(key))
+        return self._max_cluster[key]
 
     def attention_causal(self, q, kv_layer, desc: AttnDesc, causal_start: int, scale: float | None = None):
         kv, layer = self._layer_index(kv_layer)
@@ -254,6 +275,7 @@ class CudaOps:
         self.ext.attention(
             q.contiguous(), kv, layer, out, dp, desc.prefix_pages, desc.row_full, desc.row_len,
             desc.row_mask, desc.tail_pages, self.part_o, self.part_ml, self.err, 1, True, False, True, float(scale),
+            False,
         )
         counters.launches(1)
         return out

@@ -135,9 +135,18 @@ def _drafter_desc(prefix_pages, shared_len, tails, lens, ps):
     )
 
 
+@pytest.fixture(params=[True, False], ids=["fused_merge", "two_kernels"])
+def merge_path(request, ops):
+    """Run an attention test with the splits merged inside the kernel (clusters) and with the separate merge kernel."""
+    old = ops.fused_merge
+    ops.fused_merge = request.param
+    yield request.param
+    ops.fused_merge = old
+
+
 @pytest.mark.parametrize("dtype", DT)
 @pytest.mark.parametrize("shared_len", [0, 5, 37, 300, 999])
-def test_attention_drafter_rows(ops, dtype, shared_len):
+def test_attention_drafter_rows(ops, merge_path, dtype, shared_len):
     """Rows share the prefix pages; each row has private tail pages after it."""
     torch_ops = mod("ops.torch_ops")
     engine_mod = mod("runtime.engine")
@@ -159,8 +168,8 @@ def test_attention_drafter_rows(ops, dtype, shared_len):
 
 
 @pytest.mark.parametrize("dtype", DT)
-@pytest.mark.parametrize("prefix,nodes", [(64, 7), (1000, 12), (4096, 48), (33, 70)])
-def test_attention_tree_mask(ops, dtype, prefix, nodes):
+@pytest.mark.parametrize("prefix,nodes", [(64, 7), (1000, 12), (4096, 48), (33, 70), (2100, 13)])
+def test_attention_tree_mask(ops, merge_path, dtype, prefix, nodes):
     torch_ops = mod("ops.torch_ops")
     attn_desc = mod("ops.attn_desc")
     ps, hkv, hq = 16, 8, 32
@@ -186,6 +195,38 @@ def test_attention_tree_mask(ops, dtype, prefix, nodes):
     torch.cuda.synchronize()
     ops.check()
     assert rel_err(out, ref) < 1e-2
+
+
+@pytest.mark.parametrize("splits", [1, 2, 3, 5, 8, 16])
+def test_attention_fused_merge_any_cluster_size(ops, splits):
+    """The in-kernel merge for every cluster size up to the largest the device allows, against fp32."""
+    if splits > ops.max_cluster(torch.float16):
+        pytest.skip(f"this device allows clusters of at most {ops.max_cluster(torch.float16)} CTAs")
+    torch_ops = mod("ops.torch_ops")
+    attn_desc = mod("ops.attn_desc")
+    ps, hkv, hq, prefix, nodes = 16, 8, 32, 3000, 12
+    npages = (prefix + nodes + ps - 1) // ps
+    kv, g = _paged_setup(torch.float16, pages=npages + 4, hkv=hkv, layers=1)
+    ops.engine = type("E", (), {"kv": kv})()
+    pages = torch.randperm(npages + 4, generator=torch.Generator().manual_seed(3))[:npages].to(torch.int32).cuda()
+    masks = torch.tensor([[(1 << (i + 1)) - 1] for i in range(nodes)], dtype=torch.int64)
+    lens = torch.full((nodes,), prefix + nodes, dtype=torch.int32, device="cuda")
+    full = torch.full((nodes,), prefix, dtype=torch.int32, device="cuda")
+    desc = attn_desc.single_sequence_desc(pages, lens, shared_len=prefix, mask_base=prefix, masks=masks.cuda(),
+                                          full=full)
+    q = torch.randn(nodes, hq, 128, device="cuda", generator=g).to(torch.float16)
+    old = ops.fused_merge
+    ops.fused_merge = True
+    try:
+        out = ops.attention(q, kv[0], desc, splits=splits)
+        again = ops.attention(q, kv[0], desc, splits=splits)
+    finally:
+        ops.fused_merge = old
+    ref = torch_ops.attention(q.float(), kv[0].float(), desc)
+    torch.cuda.synchronize()
+    ops.check()
+    assert rel_err(out, ref) < 1e-2
+    assert torch.equal(out, again)  # split order is fixed: the merge is deterministic
 
 
 @pytest.mark.parametrize("dtype", DT)
