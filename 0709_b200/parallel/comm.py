@@ -125,11 +125,14 @@ class TPGroup:
         dist.barrier(group=self.group)
 
     def close(self) -> None:
-        if self.mode == "fused" and self.base:
+        """Unmap the peers' buffers, wait until every peer has unmapped ours, then free ours (all ranks call it)."""
+        if self.base:
             torch.cuda.synchronize(self.device)
             for ptr in self._opened:
                 self.ext.ipc_close(ptr, self.dev_index)
             self._opened = []
+            if self.world > 1:
+                dist.barrier(group=self.group)
             self.ext.ipc_free(self.base, self.dev_index)
             self.base = 0
 
