@@ -228,7 +228,7 @@ class AtlasCleanGenerator:
         out = []
         for r in routes:
             if r.materialized_tokens[: len(pre)] != pre:
-                raise RuntimeError("cannot promote a route outside the selected stage-1 branch")
+                raise RuntimeError("only routes under the selected stage-1 route can be promoted")
             out.append(self.store.register(CleanRoute(r.route_id, r.route_id, None, r.materialized_tokens[len(pre):],
                                                       r.pending_token_id, r.cumulative_logprob, r.stage2_depth, 0)))
         return out

@@ -273,7 +273,7 @@ class DrafterRuntime:
         """
         suffix = tuple(int(t) for t in token_ids)
         if not suffix:
-            raise ValueError("known prefix extension cannot be empty")
+            raise ValueError("nothing to append to the drafter prefix")
         if self.route_pool.num_routes:
             raise RuntimeError("drop speculative routes before extending the prefix")
         start = int(self.route_pool.prefix_len)

@@ -41,7 +41,7 @@ class DrafterSamplingConfig:
     def validate(self) -> None:
         t = float(self.temperature)
         if not math.isfinite(t) or t <= 0.0:
-            raise ValueError("drafter sampling temperature must be finite and positive")
+            raise ValueError(f"drafter sampling temperature {self.temperature} is not a positive finite number")
 
     def to_dict(self) -> dict[str, object]:
         return {
@@ -92,7 +92,7 @@ class DrafterSamplingContext:
 def _pack_tokens(tokens: Sequence[int]) -> bytes:
     for t in tokens:
         if t < 0 or t > KEY_MASK:
-            raise ValueError(f"token id is outside the supported int63 range: {t}")
+            raise ValueError(f"token id {t} does not fit the 63-bit sampling key")
     return struct.pack(f"<{len(tokens)}Q", *tokens)
 
 
@@ -144,10 +144,10 @@ def batch_parent_token_candidates(
         raise ValueError("k must be positive")
     rows = logits.unsqueeze(0) if logits.ndim == 1 else logits
     if rows.ndim != 2:
-        raise ValueError(f"expected 1D or 2D logits, got shape {tuple(logits.shape)}")
+        raise ValueError(f"logits must be [vocab] or [rows, vocab], not {tuple(logits.shape)}")
     batch, vocab = int(rows.shape[0]), int(rows.shape[1])
     if len(relative_parent_paths) != batch:
-        raise ValueError("relative_parent_paths must contain one semantic path per logits row")
+        raise ValueError(f"{len(relative_parent_paths)} parent paths for {batch} rows of logits")
     kk = min(int(k), vocab)
     do_sample = sampling is not None and sampling.config.do_sample
     keys = None
@@ -181,7 +181,7 @@ def single_parent_token_candidates(
 ) -> tuple[torch.Tensor, torch.Tensor]:
     rows = logits.unsqueeze(0) if logits.ndim == 1 else logits
     if int(rows.shape[0]) != 1:
-        raise ValueError("single-parent candidate selection expects exactly one logits row")
+        raise ValueError("single_parent_token_candidates takes one row of logits")
     vals, ids = batch_parent_token_candidates(
         rows, k=k, sampling=sampling, relative_parent_paths=(tuple(relative_parent_path),)
     )

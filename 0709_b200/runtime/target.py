@@ -46,10 +46,10 @@ def validate_score_weights(weights: Sequence[float] | None) -> tuple[float, ...]
     if not vals:
         return None
     if any(v < 0.0 for v in vals):
-        raise ValueError("score weights must be non-negative")
+        raise ValueError("every path score weight must be non-negative")
     total = sum(vals)
     if total <= 0.0:
-        raise ValueError("at least one score weight must be positive")
+        raise ValueError("the path score weights sum to zero; at least one must be positive")
     return tuple(v / total for v in vals)
 
 
@@ -80,7 +80,7 @@ class TargetVerifier:
         self.k = int(k)
         self.d = int(d)
         if self.k <= 0 or self.d <= 0:
-            raise ValueError("k and d must be positive")
+            raise ValueError(f"the target verifies k routes of depth d, both at least 1 (got k={k}, d={d})")
         self.host = _native.host()
         # The engine's last page is the trash page for padded graph rows.
         self.page_pool = page_pool if page_pool is not None else self.host.PagePool(engine.num_pages - 1, engine.page_size)
@@ -95,19 +95,20 @@ class TargetVerifier:
         self.first_token_threshold = None if first_token_threshold is None else float(first_token_threshold)
         self.fallback_ar_tokens = int(fallback_ar_tokens)
         if self.fallback_ar_tokens <= 0:
-            raise ValueError("fallback_ar_tokens must be positive")
+            raise ValueError("the fallback AR budget (fallback_ar_tokens) must be positive")
         self.profile_fallback_ar = bool(profile_fallback_ar)
         policy = str(route_selection_policy).strip().lower()
         if policy not in {"target_best", "target_sample", "first_route"}:
-            raise ValueError("route_selection_policy must be one of: target_best, target_sample, first_route")
+            raise ValueError(f"unknown route_selection_policy {route_selection_policy!r} "
+                             "(choose target_best, target_sample or first_route)")
         self.route_selection_policy = policy
         temp = float(route_sampling_temperature)
         if not math.isfinite(temp) or temp <= 0.0:
-            raise ValueError("route_sampling_temperature must be finite and positive")
+            raise ValueError(f"route_sampling_temperature {route_sampling_temperature} is not a positive finite number")
         self.route_sampling_temperature = temp
         if policy == "first_route" and (self.fallback_threshold is not None or self.first_token_threshold is not None):
             raise ValueError(
-                "first_route is a strict diagnostic policy and requires fallback thresholds to be disabled"
+                "the first_route policy always commits route 0, so it cannot be combined with fallback thresholds"
             )
         self.model_name = model_name
         self.prefill_chunk_size = int(prefill_chunk_size)
@@ -135,7 +136,7 @@ class TargetVerifier:
     def prefill(self, prompt_token_ids: Sequence[int]) -> PrefixState:
         toks = tuple(int(t) for t in prompt_token_ids)
         if not toks:
-            raise ValueError("target prefill requires a non-empty prompt")
+            raise ValueError("cannot prefill the target with an empty prompt")
         self.seq.clear()
         self.mirror.host = []
         slots, _ = self.seq.append_prefix(len(toks))
@@ -177,7 +178,7 @@ class TargetVerifier:
             self.prefill([int(t) for t in prefix])
         elif prefix != self.prefix_token_ids:
             raise RuntimeError(
-                "target committed prefix mismatch; incremental verify cannot silently rebuild KV: "
+                "the request's committed prefix differs from the one whose KV the target holds (it never re-prefills silently): "
                 f"request_len={len(prefix)}, target_len={len(self.prefix_token_ids)}"
             )
         paths, depth = self._validate_routes(routes)
@@ -282,27 +283,27 @@ class TargetVerifier:
 
     def _validate_routes(self, routes: Sequence[VerifyRoutePayload]) -> tuple[list[tuple[int, ...]], int]:
         if not routes:
-            raise ValueError("verify requires at least one route")
+            raise ValueError("a verify request carried no routes")
         if len(routes) != self.k:
-            raise ValueError(f"verify route count does not match configured k: routes={len(routes)}, k={self.k}")
+            raise ValueError(f"this target verifies k={self.k} routes per request, got {len(routes)}")
         ids = [int(r.route_id) for r in routes]
         if len(set(ids)) != len(ids):
-            raise ValueError("verify route ids must be unique")
+            raise ValueError("two routes of the request share a route_id")
         paths = [tuple(int(t) for t in r.token_ids) for r in routes]
         for r, p in zip(routes, paths):
             if r.draft_token_logprobs and len(r.draft_token_logprobs) != len(p):
                 raise ValueError(
-                    "draft_token_logprobs must be empty or match route depth: "
+                    "a route's draft_token_logprobs must be omitted or hold one value per token: "
                     f"route_id={int(r.route_id)}, values={len(r.draft_token_logprobs)}, depth={len(p)}"
                 )
         lengths = {len(p) for p in paths}
         if len(lengths) != 1:
-            raise ValueError(f"all verify routes must have the same depth, got {sorted(lengths)}")
+            raise ValueError(f"the routes of one request must be equally long; lengths {sorted(lengths)}")
         depth = next(iter(lengths))
         if depth <= 0:
-            raise ValueError("verify routes must contain at least one token")
+            raise ValueError("a verify route needs at least one token")
         if depth != self.d:
-            raise ValueError(f"verify route depth does not match configured d: depth={depth}, d={self.d}")
+            raise ValueError(f"this target verifies routes of depth d={self.d}, got depth {depth}")
         return paths, depth
 
     # ------------------------------------------------------- tree forward
@@ -487,7 +488,7 @@ class TargetVerifier:
             return None
         if len(self.score_weights) != int(depth):
             raise ValueError(
-                f"score weights must match verify route depth: weights={len(self.score_weights)}, depth={depth}"
+                f"{len(self.score_weights)} path score weights for routes of depth {depth}"
             )
         return self.score_weights
 
@@ -539,7 +540,7 @@ class TargetVerifier:
 
     def _select_route_with_metadata(self, scores, *, route_sampling_seed=None, route_sampling_round=None):
         if not scores:
-            raise ValueError("cannot select from an empty route score list")
+            raise ValueError("no route scores to choose from")
         if self.route_selection_policy == "first_route":
             return scores[0], self._sampling_disabled()
         if self.route_selection_policy == "target_sample":
@@ -555,11 +556,11 @@ class TargetVerifier:
         """
         if seed is None or rnd is None:
             raise ValueError(
-                "target_sample requires explicit route_sampling_seed and route_sampling_round on every verify request"
+                "the target_sample policy needs route_sampling_seed and route_sampling_round in every verify request"
             )
         rnd = int(rnd)
         if rnd < 0:
-            raise ValueError("route_sampling_round must be non-negative")
+            raise ValueError("route_sampling_round is a round index and must be non-negative")
         seed = int(seed)
         ordered = sorted(
             scores,
@@ -568,7 +569,7 @@ class TargetVerifier:
         temp = self.route_sampling_temperature
         logits = [s.effective_selection_score / temp for s in ordered]
         if any(math.isnan(v) for v in logits):
-            raise ValueError("cannot sample a route from NaN target scores")
+            raise ValueError("a target route score is NaN; no sampling distribution exists")
         pos_inf = [math.isinf(v) and v > 0 for v in logits]
         if any(pos_inf):
             cnt = sum(pos_inf)
@@ -612,7 +613,7 @@ class TargetVerifier:
 
     def _route_intervention_metadata(self, scores, selected) -> dict[str, object]:
         if not scores:
-            raise ValueError("route intervention metadata requires non-empty scores")
+            raise ValueError("intervention metadata needs at least one route score")
         route0 = scores[0]
         order = sorted(enumerate(scores), key=lambda p: (-float(p[1].draft_path_logprob), int(p[0])))
         ranks = {int(s.route_id): i for i, (_, s) in enumerate(order, start=1)}
@@ -674,10 +675,10 @@ class TargetVerifier:
     @staticmethod
     def _truncate_selected_path(*, token_ids, node_ids, max_tokens, eos_token_id):
         if len(token_ids) != len(node_ids) or not token_ids:
-            raise ValueError("selected path tokens and node ids must have equal non-zero length")
+            raise ValueError("a committed path needs as many node ids as tokens, and at least one")
         limit = len(token_ids) if max_tokens is None else min(len(token_ids), int(max_tokens))
         if limit <= 0:
-            raise ValueError("selected_path_max_tokens must be positive")
+            raise ValueError("selected_path_max_tokens must be positive when given")
         toks = [int(t) for t in token_ids[:limit]]
         if eos_token_id is not None:
             for i, t in enumerate(toks):
@@ -701,7 +702,7 @@ class TargetVerifier:
     @torch.inference_mode()
     def _commit_selected_path(self, token_ids, node_ids, logits: torch.Tensor) -> None:
         if len(token_ids) != len(node_ids) or not node_ids:
-            raise ValueError("selected path tokens and node ids must have equal non-zero length")
+            raise ValueError("a committed path needs as many node ids as tokens, and at least one")
         p = len(self.prefix_token_ids)
         moves = [(p + int(n), p + j) for j, n in enumerate(node_ids) if int(n) != j]
         if moves:
@@ -727,7 +728,7 @@ class TargetVerifier:
         every step is enqueued and before the host waits for the tokens."""
         self._flush_pending()
         if self._prefix_logits is None:
-            raise RuntimeError("target fallback AR requires initialized prefix KV")
+            raise RuntimeError("fallback AR needs a prefilled target (no prefix logits yet)")
         steps = int(max_tokens)
         if steps <= 0:
             return []

@@ -33,7 +33,7 @@ def build_parser() -> argparse.ArgumentParser:
 def parse_ids(raw: str) -> list[int]:
     ids = [int(x.strip()) for x in raw.split(",") if x.strip()]
     if not ids:
-        raise ValueError("prompt-token-ids cannot be empty")
+        raise ValueError("--prompt-token-ids parsed to an empty list")
     return ids
 
 

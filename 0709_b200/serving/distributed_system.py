@@ -101,7 +101,7 @@ def make_target_client(args, ctx: int):
 def main(argv=None) -> int:
     args = build_parser().parse_args(argv)
     if args.warmup_runs < 0:
-        raise SystemExit("--warmup-runs must be non-negative")
+        raise SystemExit("--warmup-runs is a count and cannot be negative")
     tok = load_tokenizer(args.tokenizer)
     prompt = parse_token_ids(args.prompt_token_ids, tokenizer=tok, prompt=args.prompt, prefix_len=args.prefix_len,
                              repeat_token_id=args.repeat_token_id)

@@ -70,18 +70,18 @@ class DistributedAtlasConfig:
 
     def validate(self) -> None:
         if self.k <= 0:
-            raise ValueError("k must be positive")
+            raise ValueError(f"tree width k={self.k}: need at least one route")
         if self.d <= 0:
-            raise ValueError("d must be positive")
+            raise ValueError(f"tree depth d={self.d}: need at least one drafted token per route")
         if self.max_new_tokens <= 0:
-            raise ValueError("max_new_tokens must be positive")
+            raise ValueError(f"max_new_tokens={self.max_new_tokens}: nothing to generate")
         if self.fallback_ar_tokens <= 0:
-            raise ValueError("fallback_ar_tokens must be positive")
+            raise ValueError(f"fallback_ar_tokens={self.fallback_ar_tokens}: a fallback must commit at least one token")
         t = float(self.drafter_temperature)
         if not math.isfinite(t) or t <= 0.0:
-            raise ValueError("drafter_temperature must be finite and positive")
+            raise ValueError(f"drafter_temperature {self.drafter_temperature} is not a positive finite number")
         if self.fixed_forest_depth is not None and not 0 <= int(self.fixed_forest_depth) <= int(self.d):
-            raise ValueError("fixed_forest_depth must be between 0 and d")
+            raise ValueError(f"fixed_forest_depth {self.fixed_forest_depth} is outside 0..d={self.d}")
         if self.forest_gate not in ("overlap", "adaptive"):
             raise ValueError("forest_gate must be 'overlap' or 'adaptive'")
         if not 0.0 < float(self.forest_gate_threshold) <= 1.0:
@@ -216,7 +216,7 @@ class PagedDistributedAtlasGenerator:
     # ------------------------------------------------------------ helpers
     def _now(self) -> float:
         if self._t0 is None:
-            raise RuntimeError("edge timeline clock has not been initialized")
+            raise RuntimeError("the round timeline clock starts with a session; start() one first")
         return time.perf_counter() - self._t0
 
     def _timed(self, name: str, fn, *args):
@@ -285,7 +285,7 @@ class PagedDistributedAtlasGenerator:
         for r in stage1.completed_routes:
             if int(r.route_id) == int(route_id):
                 return r
-        raise KeyError(f"selected route_id={route_id} is not in the completed stage1 routes")
+        raise KeyError(f"the target selected route {route_id}, which is not one of this round's stage-1 routes")
 
     def _verify_call(self, committed, routes, remaining, round_index, fallback_event=None, decision_event=None):
         kw = {}
@@ -337,7 +337,7 @@ class PagedDistributedAtlasGenerator:
     def _fallback_extend_handoff(self, store: KVTreeStore, tokens: Sequence[int]):
         suffix = [int(t) for t in tokens]
         if not suffix:
-            raise ValueError("fallback handoff requires at least one Target token")
+            raise ValueError("a fallback round returned no target tokens to extend the drafter with")
         dropped = self.drafter.drop_speculative()
         store.committed_token_ids.extend(suffix)
         self.drafter.append_known_tokens_as_prefix(suffix)
@@ -368,11 +368,11 @@ class PagedDistributedAtlasGenerator:
         clock = self._now if self._t0 is not None else time.perf_counter
         if forest_depth >= cfg.d:
             if forest_completed is None or forest_last_logits is None:
-                raise RuntimeError("completed forest is missing its decoded routes or logits")
+                raise RuntimeError("the forest reached depth d but its last routes or logits were not kept")
             idx = [i for i, r in enumerate(forest_completed) if int(r.stage1_root_id) == root]
             if len(idx) != cfg.k:
                 raise RuntimeError(
-                    "completed forest does not contain k routes for the selected stage-1 root: "
+                    "the finished forest should hold k routes under the selected root: "
                     f"expected={cfg.k}, got={len(idx)}"
                 )
             s0 = clock()
@@ -393,7 +393,7 @@ class PagedDistributedAtlasGenerator:
         retained = select_routes_by_stage1_root(forest_frontier, root)
         if len(retained) != cfg.k:
             raise RuntimeError(
-                "partial forest does not contain k active routes for the selected stage-1 root: "
+                "the unfinished forest should hold k frontier routes under the selected root: "
                 f"expected={cfg.k}, got={len(retained)}"
             )
         s0 = clock()
@@ -442,10 +442,10 @@ class PagedDistributedAtlasGenerator:
     def _validate_drafter_prefix_state(self, store: KVTreeStore, committed, routes) -> None:
         exp = [int(t) for t in committed]
         if list(self.drafter.prefix_token_ids) != exp or list(store.committed_token_ids) != exp:
-            raise RuntimeError("Drafter logical committed prefix diverged from the coordinator")
+            raise RuntimeError("the drafter's committed tokens no longer match the coordinator's")
         if int(self.drafter.route_pool.prefix_len) != len(exp):
             raise RuntimeError(
-                f"Drafter physical prefix length diverged from the coordinator: "
+                f"the drafter's page pool holds a different committed length than the coordinator: "
                 f"slots={int(self.drafter.route_pool.prefix_len)}, tokens={len(exp)}"
             )
         for r in routes:
@@ -592,7 +592,7 @@ class AtlasSession:
             reason = None if resp.get("fallback_reason") is None else str(resp.get("fallback_reason"))
             if len(fb_tokens) > remaining:
                 raise RuntimeError(
-                    "target fallback returned more tokens than the remaining budget: "
+                    "the target's fallback overran the token budget: "
                     f"returned={len(fb_tokens)}, remaining={remaining}"
                 )
             now = list(fb_tokens)
@@ -615,7 +615,7 @@ class AtlasSession:
             stop = not now or g._should_stop(now, generated)
             if not stop:
                 if now != full:
-                    raise RuntimeError("cannot reuse stage-2 KV after a partial stage-1 commit")
+                    raise RuntimeError("the commit was truncated, so the forest built on the full route cannot be promoted")
                 h = g._handoff_after_verify(
                     store=store,
                     selected_stage1_route=sel,
@@ -630,7 +630,7 @@ class AtlasSession:
                 reused, reused_depth, remaining_depth = h.reused_stage2_routes, h.reused_stage2_depth, h.remaining_tree_depth
                 phys = h.physical_stats
         else:
-            raise RuntimeError(f"unknown target verify decision: {decision!r}")
+            raise RuntimeError(f"the target answered with decision {decision!r}, expected select or fallback_ar")
         if cfg.validate_state_alignment:
             g._validate_target_prefix_lengths(tmeta, p_round, len(committed))
             if not stop:

@@ -40,11 +40,11 @@ def parse_token_ids(raw: str | None, *, tokenizer, prompt: str, prefix_len: int 
                     repeat_token_id: int | None = None) -> list[int]:
     if repeat_token_id is not None:
         if prefix_len is None or prefix_len <= 0:
-            raise ValueError("--repeat-token-id requires a positive --prefix-len")
+            raise ValueError("--repeat-token-id builds a prompt of --prefix-len tokens, so give a positive --prefix-len")
         return [int(repeat_token_id)] * int(prefix_len)
     toks = [int(p.strip()) for p in raw.split(",") if p.strip()] if raw else encode(tokenizer, prompt)
     if not toks:
-        raise ValueError("prompt token list is empty")
+        raise ValueError("the prompt has no tokens")
     if prefix_len is None:
         return toks
     return (toks * ((int(prefix_len) + len(toks) - 1) // len(toks)))[: int(prefix_len)]

@@ -69,7 +69,7 @@ def target_verify_result_to_dict(result: TargetVerifyResult) -> dict[str, object
 
 def selected_route_id_from_response(response: Mapping[str, object]) -> int:
     if str(response.get("decision", "select")) != "select":
-        raise ValueError(f"target response did not select a route: {response.get('decision')}")
+        raise ValueError(f"no route was selected (decision {response.get('decision')!r})")
     return int(response["selected_route_id"])
 
 
@@ -84,11 +84,11 @@ def _resolve_prefix(backend, request: Mapping[str, Any]) -> list[int]:
     n = request.get("prefix_len")
     tail = request.get("prefix_tail_token_ids", [])
     if n is None or not isinstance(tail, list):
-        raise ValueError("verify requires prefix_token_ids: list[int] (or prefix_len + prefix_tail_token_ids)")
+        raise ValueError("a verify request names its committed prefix: prefix_token_ids, or prefix_len with prefix_tail_token_ids")
     have = list(backend.prefix_token_ids)
     if int(n) != len(have) or (tail and have[-len(tail):] != [int(t) for t in tail]):
         raise RuntimeError(
-            "target committed prefix mismatch; incremental verify cannot silently rebuild KV: "
+            "the request's committed prefix differs from the one whose KV the target holds (it never re-prefills silently): "
             f"request_len={int(n)}, target_len={len(have)}"
         )
     return have
@@ -107,7 +107,7 @@ class TargetServerApp:
     def prefill(self, request: Mapping[str, Any]) -> dict[str, object]:
         toks = request.get("prompt_token_ids")
         if not isinstance(toks, list):
-            raise ValueError("prefill requires prompt_token_ids: list[int]")
+            raise ValueError("a prefill request carries prompt_token_ids as a list of ints")
         with self.lock:
             st = self.backend.prefill([int(t) for t in toks])
         return {"ok": True, "prompt_len": int(st.committed_length), "metadata": dict(st.metadata)}
@@ -115,7 +115,7 @@ class TargetServerApp:
     def verify(self, request: Mapping[str, Any]) -> dict[str, object]:
         routes = request.get("routes")
         if not isinstance(routes, list):
-            raise ValueError("verify requires routes: list[object]")
+            raise ValueError("a verify request carries routes as a list of objects")
         payloads = [verify_payload_from_mapping(dict(r)) for r in routes]
         with self.lock:
             prefix = _resolve_prefix(self.backend, request)

@@ -87,10 +87,10 @@ class SerialAtlasGenerator(PagedDistributedAtlasGenerator):
                 fb = [int(x) for x in resp.get("fallback_token_ids", [])]
                 reason = None if resp.get("fallback_reason") is None else str(resp.get("fallback_reason"))
                 if not fb:
-                    raise RuntimeError("serial Target fallback returned no tokens")
+                    raise RuntimeError("a fallback round returned no target tokens")
                 if len(fb) > remaining:
                     raise RuntimeError(
-                        f"serial Target fallback returned more tokens than the remaining budget: "
+                        f"the target's fallback overran the token budget: "
                         f"returned={len(fb)}, remaining={remaining}"
                     )
                 now = list(fb)
@@ -101,10 +101,10 @@ class SerialAtlasGenerator(PagedDistributedAtlasGenerator):
                 full = list(store.materialized_token_path(sel)[: cfg.d])
                 now = self._truncate_commit(full, generated)
                 if not now:
-                    raise RuntimeError("serial Target selected an empty route commit")
+                    raise RuntimeError("the target selected a route but nothing was left to commit")
                 mode = "serial_tree_only_persistent_kv"
             else:
-                raise RuntimeError(f"unknown target verify decision: {decision!r}")
+                raise RuntimeError(f"the target answered with decision {decision!r}, expected select or fallback_ar")
             generated.extend(now)
             committed.extend(now)
             stop = self._should_stop(now, generated)

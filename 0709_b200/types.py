@@ -200,7 +200,7 @@ class TargetVerifyResult:
     @property
     def selected_score(self) -> TargetRouteScore:
         if self.selected_route_id is None:
-            raise KeyError("fallback result does not have a selected route")
+            raise KeyError("a fallback_ar result commits target tokens, not a route")
         for score in self.scores:
             if score.route_id == self.selected_route_id:
                 return score
@@ -215,7 +215,7 @@ def verify_payload_from_mapping(item: Mapping[str, Any]) -> VerifyRoutePayload:
     elif isinstance(raw, (list, tuple)):
         draft_token_logprobs = tuple(float(v) for v in raw)
     else:
-        raise ValueError("draft_token_logprobs must be a list of numbers when provided")
+        raise ValueError("draft_token_logprobs, when present, is a list of numbers")
     return VerifyRoutePayload(
         route_id=int(item["route_id"]),
         token_ids=tuple(int(t) for t in item["token_ids"]),

@@ -261,7 +261,7 @@ def paired_target_quality(target_best_rows: Sequence[Mapping[str, Any]],
     best = {int(r["index"]): r for r in target_best_rows}
     first = {int(r["index"]): r for r in first_route_rows}
     if len(best) != len(target_best_rows) or len(first) != len(first_route_rows):
-        raise ValueError("prediction inputs contain duplicate sample indices")
+        raise ValueError("a sample index appears twice in the predictions (duplicate)")
     if set(best) != set(first):
         raise ValueError(f"paired sample indices differ: missing_target_best={sorted(set(first) - set(best))[:10]}, "
                          f"missing_first_route={sorted(set(best) - set(first))[:10]}")
