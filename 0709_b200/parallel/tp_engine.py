@@ -270,9 +270,7 @@ class TPLlamaEngine(LlamaEngine):
             raise ValueError(f"comm mode must be one of {MODES}")
         if mode == "fused" and not self.tp.base:
             raise ValueError("fused collectives need the peer buffers mapped at start-up (build in fused mode)")
-        if self.device.type == "cuda":
-            torch.cuda.synchronize(self.device)
-        self._graphs.clear()
+        self.drop_graphs()
         self.tp.mode = mode
 
     def _w_mirror_new(self, mid: int, capacity: int) -> None:

@@ -209,6 +209,14 @@ class LlamaEngine:
         launches = counters.snapshot()["launches"] - before
         return CapturedForward(graphs, out, launches, keep)
 
+    def drop_graphs(self) -> None:
+        """Release every captured graph.  Their private memory pool goes with them, so later
+        captures start a new pool (a released pool cannot be captured into again)."""
+        self._graphs.clear()
+        if self.device.type == "cuda":
+            torch.cuda.synchronize(self.device)
+            self._graph_pool = torch.cuda.graph_pool_handle()
+
     def _capture_one(self, fn):
         g = torch.cuda.CUDAGraph()
         g.capture_begin(self._graph_pool, capture_error_mode="thread_local")

@@ -9,7 +9,12 @@ decoder commits when the speculation cannot change them:
     no tree forward);
 (b) ``k = 1`` with the first-route policy and no fallback: the committed
     tokens are the drafter's greedy tokens -- compared with the drafter's paged
-    AR baseline (every token committed at once);
+    AR baseline (every token committed at once).  Here the two paths read the
+    same keys through different kernels: AR commits every token, so its keys
+    sit in the shared prefix (tensor-core pass, fp16 probabilities), while a
+    speculative route keeps up to 2d private keys in its tail pages (fp32
+    tail pass).  The sequences must be identical, or diverge only where the
+    drafter's fp32 logits of the two candidates lie within a numerical tie;
 (c) persistent target KV: after 16 rounds that each commit a selected route
     by compacting its nodes' KV in place, the prefix logits match a fresh
     prefill of the same tokens (tolerance) with the same top-1, as in the
@@ -112,8 +117,23 @@ def test_k1_first_route_equals_drafter_paged_greedy(weights, drafter_ref, gate, 
     for seed, want in drafter_ref.items():
         res = gen.generate(_prompt(seed))
         assert all(r.decision == "select" for r in res.rounds)
-        assert res.generated_token_ids == want
+        _same_or_tie(dw, _prompt(seed), res.generated_token_ids, want)
     gen.drafter.engine.ops.check()
+
+
+TIE = 0.05  # fp32 logit gap below which fp16 rounding of two kernels may pick either token
+
+
+def _same_or_tie(w, prompt, got, want) -> None:
+    """``got == want``, or the first difference is a near-tie under the fp32 oracle."""
+    assert len(got) == len(want)
+    diff = next((i for i, (a, b) in enumerate(zip(got, want)) if a != b), None)
+    if diff is None:
+        return
+    llama = mod("models.llama")
+    logits = llama.reference_forward(w, torch.tensor(prompt + want[:diff], device="cuda"))[-1].float()
+    gap = float((logits[want[diff]] - logits[got[diff]]).abs())
+    assert gap < TIE, f"diverged at {diff}: {got[diff]} vs {want[diff]}, fp32 logit gap {gap:.4f}"
 
 
 def test_persistent_target_kv_matches_fresh_prefill(weights):
