@@ -56,8 +56,11 @@ class CudaOps:
         self.part_ml = torch.empty(0, dtype=torch.float32, device=dev)
         self.num_sms = torch.cuda.get_device_properties(dev).multi_processor_count
         self.last_gemm_config: list[int] | None = None
-        # Split merge inside the attention kernel (thread-block clusters); 0 keeps the two-kernel path.
-        self.fused_merge = os.environ.get("ATLAS_ATTN_FUSED_MERGE", "1") != "0"
+        # Split merge inside the attention kernel (thread-block clusters, ATLAS_ATTN_FUSED_MERGE=1) or the
+        # separate merge kernel (default, faster in the serving round as measured); cluster size capped
+        # by ATLAS_ATTN_MAX_CLUSTER.
+        self.fused_merge = os.environ.get("ATLAS_ATTN_FUSED_MERGE", "0") == "1"
+        self.cluster_cap = int(os.environ.get("ATLAS_ATTN_MAX_CLUSTER", "16"))
         self._max_cluster: dict[bool, int] = {}
 
     # ----------------------------------------------------------- errors
@@ -259,7 +262,7 @@ class CudaOps:
         key = dtype == torch.bfloat16
         if key not in self._max_cluster:
             self._max_cluster[key] = int(self.ext.attention_max_cluster(key))
-        return self._max_cluster[key]
+        return max(1, min(self._max_cluster[key], self.cluster_cap))
 
     def attention_causal(self, q, kv_layer, desc: AttnDesc, causal_start: int, scale: float | None = None):
         kv, layer = self._layer_index(kv_layer)

@@ -135,7 +135,8 @@ def run_root(args, eng, cfg, device, dtype, pages, ctx) -> dict[str, object]:
         torch.cuda.synchronize(device)
         res["tree_verify_ms"] = (time.perf_counter() - t0) * 1e3 / args.timing_iters
 
-    dcfg = get_config(args.drafter)
+    # The drafter proposes target tokens and extends with the target's fallback tokens: one vocabulary.
+    dcfg = get_config(args.drafter, vocab_size=cfg.vocab_size)
     dw = random_weights(dcfg, seed=args.seed, dtype=dtype, device=device)
     gens = []
     for tv in (TargetVerifier(eng, **kw), TargetVerifier(ref, **kw)):

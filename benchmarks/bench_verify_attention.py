@@ -46,6 +46,10 @@ def main() -> int:
     ap.add_argument("--prefixes", default="1024,4096,16384")
     ap.add_argument("--iters", type=int, default=20)
     ap.add_argument("--flashinfer", action="store_true")
+    ap.add_argument("--merge", default="two",
+                    help="comma list of split-merge paths: two (separate merge kernel), fused8, fused16 "
+                         "(merge inside the kernel, clusters of at most 8 / 16 CTAs)")
+    ap.add_argument("--rows", default="tree", help="tree (the deduplicated round), or a row count (decode rows)")
     ap.add_argument("--json-out", default=None)
     args = ap.parse_args()
     sys.path.insert(0, os.path.join(ROOT, "benchmarks"))
@@ -60,6 +64,9 @@ def main() -> int:
     routes = round_routes(3, 4, g)
     tokens, parents, depths, node_paths, masks = host.build_tree(torch.tensor(routes, dtype=torch.int64))
     n = int(tokens.numel())
+    if args.rows != "tree":  # decode rows: each row sees the prefix and itself
+        n = int(args.rows)
+        masks = torch.tensor([[1 << i] for i in range(n)], dtype=torch.int64)
     rows = []
     for P in (int(x) for x in args.prefixes.split(",")):
         npages = (P + n + ps - 1) // ps + 1
@@ -72,10 +79,16 @@ def main() -> int:
         q = torch.randn(n, hq, hd, device="cuda").half()
         ops.reserve_attention_workspace(64, hq, hkv, P + 64, ps)
         splits = ops.attention_splits(n, hq, hkv, P, ps)
-        us = timeit(lambda: ops.attention(q, kv[0], desc, splits=splits), args.iters)
         nbytes = 2 * (P + n) * hkv * hd * 2
-        row = {"prefix": P, "raw_nodes": len(routes) * 4, "dedup_nodes": n, "splits": splits, "us": round(us, 2),
-               "GB/s": round(nbytes / us / 1e3, 1), f"hbm_frac_of_{src}": round(nbytes / us / 1e3 / hbm, 3)}
+        row = {"prefix": P, "raw_nodes": len(routes) * 4, "dedup_nodes": n, "rows": n, "splits": splits}
+        for mode in args.merge.split(","):
+            ops.fused_merge = mode.startswith("fused")
+            ops.cluster_cap = int(mode[5:]) if ops.fused_merge else ops.cluster_cap
+            us = timeit(lambda: ops.attention(q, kv[0], desc, splits=splits), args.iters)
+            tag = "" if mode == "two" else f"_{mode}"
+            row.update({f"us{tag}": round(us, 2), f"GB/s{tag}": round(nbytes / us / 1e3, 1),
+                        f"hbm_frac_of_{src}{tag}": round(nbytes / us / 1e3 / hbm, 3)})
+        ops.fused_merge = False
         if args.flashinfer:
             row.update(flashinfer_case(kv, q, P, n, masks, ps, args.iters, timeit, nbytes, hbm, src))
         rows.append(row)
