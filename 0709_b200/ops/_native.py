@@ -70,6 +70,7 @@ CUDA_SOURCES = [
     "bindings.cpp",
     "gemm_tcgen05.cu",
     "attention.cu",
+    "attention_decode.cu",
     "elementwise.cu",
     "kvcache.cu",
     "sampling.cu",
