@@ -10,15 +10,13 @@
 //
 // Grid (kv heads, splits), 128 threads.  Split s covers keys [s*K, s*K + K)
 // with K = ceil(shared_len / splits), processed in chunks of kChunk keys:
-//   pass 1  thread t loads the K and V rows of key t of the chunk (all 32
-//           16-byte loads of a thread in flight at once), stages V in shared
-//           memory (16-byte chunks XOR-swizzled by key), and scores K against
-//           every row (Q rows staged in shared memory as fp32, read as
-//           broadcasts); the chunk's row maxima meet through warp shuffles and
-//           a shared-memory step, and the probabilities p = 2^(s - m) go to
-//           shared memory;
+//   pass 1  thread t scores key t of the chunk (t < kChunk) against every row
+//           (Q rows staged in shared memory as fp32, read as broadcasts), one
+//           K row per thread; the chunk's row maxima and sums meet through
+//           warp shuffles and a shared-memory step, and the probabilities
+//           p = 2^(s - m) go to shared memory;
 //   pass 2  warp w owns rows w, w + 4, ...; lane l owns dimensions 4l..4l+3
-//           and accumulates sum_j p[r][j] * V[j] from shared memory.
+//           and accumulates sum_j p[r][j] * V[j] with coalesced V loads.
 // Running (max, sum, O) are rescaled when a later chunk raises a row's max.
 // Before the programmatic-launch wait the split's K/V rows are prefetched to
 // L2 (they are committed prefix keys, not outputs of the preceding kernel).
@@ -38,8 +36,6 @@ constexpr float kLog2eD = 1.4426950408889634f;
 
 template <typename T>
 __global__ void __launch_bounds__(kDecThreads) attn_decode_split(AttnParams p) {
-  extern __shared__ __align__(16) uint8_t dsm[];
-  uint4* v_s = reinterpret_cast<uint4*>(dsm);            // [kChunk keys][16 chunks of 8 elements], swizzled
   __shared__ float q_s[kDecodeMaxRows][kHdD];           // 8 KB
   __shared__ float p_s[kDecodeMaxRows][kChunk];          // 8 KB: scores, then probabilities
   __shared__ int64_t off_s[kChunk];                      // element offset of each key's K row (-1: none)
@@ -116,27 +112,14 @@ __global__ void __launch_bounds__(kDecThreads) attn_decode_split(AttnParams p) {
       }
     }
     off_s[tid] = off;
-    uint4 kraw[kHdD / 8], vraw[kHdD / 8];
-    if (off >= 0) {
-      const uint4* kp4 = reinterpret_cast<const uint4*>(kv + off);
-      const uint4* vp4 = reinterpret_cast<const uint4*>(kv + off + v_step);
-#pragma unroll
-      for (int c = 0; c < kHdD / 8; ++c) kraw[c] = kp4[c];
-#pragma unroll
-      for (int c = 0; c < kHdD / 8; ++c) vraw[c] = vp4[c];
-    } else {
-#pragma unroll
-      for (int c = 0; c < kHdD / 8; ++c) kraw[c] = vraw[c] = make_uint4(0, 0, 0, 0);
-    }
-#pragma unroll
-    for (int c = 0; c < kHdD / 8; ++c) v_s[tid * (kHdD / 8) + (c ^ (tid & 15))] = vraw[c];
     float sc[kDecodeMaxRows];
 #pragma unroll
     for (int r = 0; r < kDecodeMaxRows; ++r) sc[r] = 0.f;
     if (off >= 0) {
-#pragma unroll
+      const uint4* kp4 = reinterpret_cast<const uint4*>(kv + off);
+#pragma unroll 4
       for (int c = 0; c < kHdD / 8; ++c) {
-        const uint4 raw = kraw[c];
+        const uint4 raw = kp4[c];
         const T* e = reinterpret_cast<const T*>(&raw);
         float kf[8];
 #pragma unroll
@@ -194,11 +177,10 @@ __global__ void __launch_bounds__(kDecThreads) attn_decode_split(AttnParams p) {
         acc[i][3] *= a;
       }
     }
-#pragma unroll 4
     for (int j = 0; j < n; ++j) {
-      // Dimensions 4l..4l+3 are half of 16-byte chunk l / 2 of key j's row (zeros for a missing key).
-      const uint4* vrow = v_s + j * (kHdD / 8) + ((lane >> 1) ^ (j & 15));
-      const float2 raw = reinterpret_cast<const float2*>(vrow)[lane & 1];
+      const int64_t o = off_s[j];
+      if (o < 0) continue;  // block-uniform
+      const float2 raw = *reinterpret_cast<const float2*>(kv + o + v_step + lane * 4);
       const T* e = reinterpret_cast<const T*>(&raw);
       const float v0 = to_f32(e[0]), v1 = to_f32(e[1]), v2 = to_f32(e[2]), v3 = to_f32(e[3]);
 #pragma unroll
@@ -234,18 +216,11 @@ __global__ void __launch_bounds__(kDecThreads) attn_decode_split(AttnParams p) {
   }
 }
 
-template <typename T>
-static cudaError_t launch_decode_typed(const AttnParams& p, cudaStream_t st) {
-  constexpr int kDyn = kChunk * kHdD * static_cast<int>(sizeof(T));  // staged V rows of one chunk
-  static const cudaError_t configured =
-      cudaFuncSetAttribute(attn_decode_split<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, kDyn);
-  if (configured != cudaSuccess) return configured;
-  return launch_k(attn_decode_split<T>, dim3(p.Hkv, p.splits), dim3(kDecThreads), kDyn, st, p);
-}
-
 cudaError_t launch_attention_decode(const AttnParams& p, cudaStream_t st) {
   if (p.M * (p.Hq / p.Hkv) > kDecodeMaxRows) return cudaErrorInvalidValue;
-  return p.bf16 ? launch_decode_typed<__nv_bfloat16>(p, st) : launch_decode_typed<__half>(p, st);
+  const dim3 grid(p.Hkv, p.splits);
+  if (p.bf16) return launch_k(attn_decode_split<__nv_bfloat16>, grid, dim3(kDecThreads), 0, st, p);
+  return launch_k(attn_decode_split<__half>, grid, dim3(kDecThreads), 0, st, p);
 }
 
 }  // namespace atlas
