@@ -635,9 +635,7 @@ static void launch_typed(const CUtensorMap& kvmap, const AttnParams& p, bool run
     cudaLaunchKernelEx(&cfg, attn_shared_tc<T>, kvmap, p);
     return;
   }
-  if (run_tc && p.small_rows) {
-    launch_attention_decode(p, st);
-  } else if (run_tc) {
+  if (run_tc) {
     configure_tc<T>();
     dim3 grid(p.Hkv, p.splits, row_tiles);
     launch_k(attn_shared_tc<T>, grid, dim3(kThreadsTC), kSmemBytes, st, kvmap, p);

@@ -24,7 +24,6 @@ struct AttnParams {
   int mask_words, tail_stride, splits, direct_out, bf16;
   int min_pages_per_split;  // a split covers at least this many pages (surplus splits exit at once)
   int fused_merge;          // 1: the splits of a head form one cluster and merge + tail in the same kernel
-  int small_rows;           // 1: the split pass runs on CUDA cores (few query rows), then the merge kernel
   float scale;
 };
 
@@ -34,10 +33,5 @@ int attention_max_cluster(bool bf16);
 
 void launch_attention(const CUtensorMap& kvmap, const AttnParams& p, bool run_tc, bool run_combine, int row_tiles,
                       cudaStream_t st);
-
-// Split pass for few query rows on CUDA cores (attention_decode.cu): the same partials as the
-// tensor-core split kernel, for M * (Hq / Hkv) <= kDecodeMaxRows.
-constexpr int kDecodeMaxRows = 16;
-cudaError_t launch_attention_decode(const AttnParams& p, cudaStream_t st);
 
 }  // namespace atlas

@@ -604,8 +604,7 @@ torch::Tensor wrap_ptr(int64_t ptr, std::vector<int64_t> sizes, torch::ScalarTyp
 void attention(torch::Tensor q, torch::Tensor kv, int64_t layer, torch::Tensor out, torch::Tensor dparams,
                torch::Tensor prefix_pages, torch::Tensor row_full, torch::Tensor row_len, torch::Tensor row_mask,
                torch::Tensor tail_pages, torch::Tensor part_o, torch::Tensor part_ml, torch::Tensor err,
-               int64_t splits, bool run_tc, bool run_combine, bool direct_out, double scale, bool fused_merge,
-               bool small_rows) {
+               int64_t splits, bool run_tc, bool run_combine, bool direct_out, double scale, bool fused_merge) {
   check_cuda(q, "q");
   TORCH_CHECK(q.dim() == 3 && q.size(2) == 128 && q.is_contiguous(), "q must be contiguous [M, Hq, 128]");
   TORCH_CHECK(kv.scalar_type() == q.scalar_type(), "q and kv dtype mismatch");
@@ -661,11 +660,6 @@ void attention(torch::Tensor q, torch::Tensor kv, int64_t layer, torch::Tensor o
   }();
   p.min_pages_per_split = min_pages;
   p.fused_merge = fused_merge ? 1 : 0;
-  p.small_rows = small_rows ? 1 : 0;
-  if (small_rows) {
-    TORCH_CHECK(!fused_merge && !direct_out && M * G <= atlas::kDecodeMaxRows,
-                "the small-row split pass takes at most 16 query rows per kv head and writes split partials");
-  }
   p.scale = static_cast<float>(scale);
   const int row_tiles = static_cast<int>((M * G + 127) / 128);
   atlas::launch_attention(kvmap, p, run_tc, run_combine, row_tiles, at::cuda::getCurrentCUDAStream());

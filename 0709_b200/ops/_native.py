@@ -70,7 +70,6 @@ CUDA_SOURCES = [
     "bindings.cpp",
     "gemm_tcgen05.cu",
     "attention.cu",
-    "attention_decode.cu",
     "elementwise.cu",
     "kvcache.cu",
     "sampling.cu",

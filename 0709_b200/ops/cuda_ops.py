@@ -61,8 +61,6 @@ class CudaOps:
         # by ATLAS_ATTN_MAX_CLUSTER.
         self.fused_merge = os.environ.get("ATLAS_ATTN_FUSED_MERGE", "0") == "1"
         self.cluster_cap = int(os.environ.get("ATLAS_ATTN_MAX_CLUSTER", "16"))
-        # CUDA-core split pass for at most SMALL_ROWS_MAX query rows per kv head (ATLAS_ATTN_SMALL_ROWS=0: off).
-        self.small_rows = os.environ.get("ATLAS_ATTN_SMALL_ROWS", "1") != "0"
         self._max_cluster: dict[bool, int] = {}
 
     # ----------------------------------------------------------- errors
@@ -246,18 +244,16 @@ class CudaOps:
             self.ext.attention(
                 q.contiguous(), kv, layer, out, self._dparams(desc), desc.prefix_pages, desc.row_full, desc.row_len,
                 desc.row_mask, desc.tail_pages, self.part_o, self.part_ml, self.err, c, True, True, False,
-                float(scale), True, False,
+                float(scale), True,
             )
             counters.launches(1)
             return out
         if run_tc:
             self._ensure_parts(sp, m, hq)
-        # Few query rows per kv head (decode): the split pass runs on CUDA cores.
-        small = run_tc and self.small_rows and m * (hq // kv.shape[3]) <= SMALL_ROWS_MAX
         self.ext.attention(
             q.contiguous(), kv, layer, out, self._dparams(desc), desc.prefix_pages, desc.row_full, desc.row_len,
             desc.row_mask, desc.tail_pages, self.part_o, self.part_ml, self.err, sp, run_tc, stages[1], False,
-            float(scale), False, small,
+            float(scale), False,
         )
         counters.launches(int(run_tc) + int(stages[1]))
         return out
@@ -282,7 +278,7 @@ class CudaOps:
         self.ext.attention(
             q.contiguous(), kv, layer, out, dp, desc.prefix_pages, desc.row_full, desc.row_len,
             desc.row_mask, desc.tail_pages, self.part_o, self.part_ml, self.err, 1, True, False, True, float(scale),
-            False, False,
+            False,
         )
         counters.launches(1)
         return out
@@ -315,8 +311,6 @@ class CudaOps:
         counters.launches(2)
         return out
 
-
-SMALL_ROWS_MAX = 16  # kDecodeMaxRows of csrc/cuda/attention.h
 
 _SHARED: dict[int, CudaOps] = {}
 

@@ -197,38 +197,6 @@ def test_attention_tree_mask(ops, merge_path, dtype, prefix, nodes):
     assert rel_err(out, ref) < 1e-2
 
 
-@pytest.mark.parametrize("dtype", DT)
-@pytest.mark.parametrize("rows", [1, 2, 4])
-@pytest.mark.parametrize("shared_len,splits", [(5, 0), (37, 0), (1000, 0), (3000, 2), (3000, 18)])
-def test_attention_small_rows(ops, dtype, rows, shared_len, splits):
-    """CUDA-core split pass for decode rows (<= 16 query rows per kv head): route tails after the prefix."""
-    torch_ops = mod("ops.torch_ops")
-    ps, hkv, hq = 16, 8, 32
-    npages = shared_len // ps + 1 + 2 * rows
-    kv, g = _paged_setup(dtype, pages=npages + 8, hkv=hkv, layers=1)
-    ops.engine = type("E", (), {"kv": kv})()
-    perm = torch.randperm(npages + 8, generator=torch.Generator().manual_seed(shared_len)).to(torch.int32)
-    n_pf = shared_len // ps
-    prefix_pages = perm[: n_pf + 1].cuda()
-    tails = perm[n_pf + 1: n_pf + 1 + 2 * rows].reshape(rows, 2).cuda()
-    lens = torch.tensor([shared_len + 1 + (i % 3) for i in range(rows)], dtype=torch.int32, device="cuda")
-    desc = _drafter_desc(prefix_pages, shared_len, tails, lens, ps)
-    q = torch.randn(rows, hq, 128, device="cuda", generator=g).to(dtype)
-    ref = torch_ops.attention(q.float(), kv[0].float(), desc)
-    old = ops.small_rows
-    try:
-        ops.small_rows = True
-        out = ops.attention(q, kv[0], desc, splits=splits or None)
-        ops.small_rows = False
-        tc = ops.attention(q, kv[0], desc, splits=splits or None)
-    finally:
-        ops.small_rows = old
-    torch.cuda.synchronize()
-    ops.check()
-    assert rel_err(out, ref) < 1e-2
-    assert rel_err(out, tc) < 1e-2
-
-
 @pytest.mark.parametrize("splits", [1, 2, 3, 5, 8, 16])
 def test_attention_fused_merge_any_cluster_size(ops, splits):
     """The in-kernel merge for every cluster size up to the largest the device allows, against fp32."""
