@@ -55,7 +55,7 @@ def main() -> int:
     ops.check()
     us = timeit(lambda: ops.gemm_fp8(xq, sa, w, out, ops.ext.EPI_STORE), args.iters)
     hbm, _, src = peaks()
-    nbytes = w.nbytes() + xq.numel() + out.numel() * 2
+    nbytes = w.nbytes + xq.numel() + out.numel() * 2
     print(json.dumps({"shape": args.shape, "n_out": n_out, "k": k, "rows": args.rows, "us": round(us, 2),
                       "GB/s": round(nbytes / us / 1e3, 1), f"hbm_frac_of_{src}": round(nbytes / us / 1e3 / hbm, 3),
                       "max_rel_err_vs_fp32_dequant": err, "config": ops.last_gemm_config}), flush=True)
