@@ -24,6 +24,7 @@ from __future__ import annotations
 import os
 import pickle
 import struct
+import threading
 import time
 from typing import Any, Sequence
 
@@ -190,17 +191,24 @@ class ChannelTargetClient:
 
     supports_early_decision = False
 
-    def __init__(self, channel, *, tail: int = 8) -> None:
+    def __init__(self, channel, *, tail: int = 8, session_id: str | None = None, lock=None) -> None:
+        """``session_id`` addresses one session of a multi-session server; clients of one channel
+        in several threads share ``lock`` (one request in flight per channel)."""
         self.ch = channel
         self.tail = int(tail)
+        self.session_id = session_id
+        self.lock = lock if lock is not None else threading.Lock()
         self.calls = 0
         self.wait_s = 0.0
 
     def _call(self, name: str, request: dict[str, Any]) -> dict[str, Any]:
-        t0 = time.perf_counter()
-        self.ch.send((name, request))
-        out = self.ch.recv()
-        self.wait_s += time.perf_counter() - t0
+        if self.session_id is not None:
+            request = {**request, "session_id": self.session_id}
+        with self.lock:
+            t0 = time.perf_counter()
+            self.ch.send((name, request))
+            out = self.ch.recv()
+            self.wait_s += time.perf_counter() - t0
         self.calls += 1
         if not out.get("ok"):
             raise RuntimeError(f"target {name} failed: {out.get('error', out)}")
@@ -230,8 +238,9 @@ class ChannelTargetClient:
         return self._call(name, dict(request or {}))
 
     def stop_server(self) -> None:
-        self.ch.send((STOP, {}))
-        self.ch.recv()
+        with self.lock:
+            self.ch.send((STOP, {}))
+            self.ch.recv()
 
 
 def serve_target_channel(app, channel, *, extra: dict | None = None) -> int:

@@ -57,6 +57,8 @@ def parse():
     p.add_argument("--rounds", type=int, default=16, help="timed rounds per session")
     p.add_argument("--warmup", type=int, default=3, help="untimed rounds per session")
     p.add_argument("--seed", type=int, default=0)
+    p.add_argument("--transport", choices=["shm", "peer"], default="shm",
+                   help="drafter <-> target transport of a GPU pair: shared-memory mailbox or peer-memory rings")
     p.add_argument("--json-out", default=None)
     return p.parse_args()
 
@@ -163,6 +165,10 @@ def main() -> int:
         dist.init_process_group("gloo", timeout=timedelta(seconds=1800))
     pairs = max(1, world // 2)
     pair = rank // 2 if world > 1 else 0
+    transport = pkg("serving.peer_transport")
+    use_peer = args.transport == "peer" and world > 1
+    # One process group per drafter/target pair (every rank creates all of them, in order).
+    pair_group = [dist.new_group([2 * q, 2 * q + 1]) for q in range(pairs)][pair] if use_peer else None
     sids = [f"s{i}" for i in range(args.sessions) if i % pairs == pair]
     shm = "/dev/shm" if os.path.isdir("/dev/shm") else "/tmp"
     base = os.path.join(shm, f"atlas_sess_{os.environ.get('MASTER_PORT', os.getpid())}_{pair}")
@@ -187,19 +193,30 @@ def main() -> int:
         for sid in sids:
             app._app(sid)
         dist.barrier()
-        ch = sessions_mod.ShmChannel(base, server=True)
-        sessions_mod.serve_target_shm(app, ch)
+        if use_peer:
+            ch = transport.PeerChannel(rank=rank, peer=rank - 1, device=dev, group=pair_group)
+            transport.serve_target_channel(app, ch)
+            ch.close()
+        else:
+            ch = sessions_mod.ShmChannel(base, server=True)
+            sessions_mod.serve_target_shm(app, ch)
         torch.cuda.synchronize(dev)
         te.ops.check()
         results = [None] * world
         dist.all_gather_object(results, None)
     else:
         dist.barrier()
-        ch = sessions_mod.ShmChannel(base, server=False)
         lock = threading.Lock()
-        clients = [sessions_mod.ShmTargetClient(ch, session_id=s, lock=lock) for s in sids]
+        if use_peer:
+            ch = transport.PeerChannel(rank=rank, peer=rank + 1, device=dev, group=pair_group)
+            clients = [transport.ChannelTargetClient(ch, session_id=s, lock=lock) for s in sids]
+        else:
+            ch = sessions_mod.ShmChannel(base, server=False)
+            clients = [sessions_mod.ShmTargetClient(ch, session_id=s, lock=lock) for s in sids]
         result = run_sessions(args, dev, sids, clients, rank)
         clients[0].stop_server()
+        if use_peer:
+            ch.close()
         results = [None] * world
         dist.all_gather_object(results, result)
     if world > 1:
@@ -220,6 +237,7 @@ def main() -> int:
                                  "mean": round(1e3 * sum(lat) / len(lat), 3)},
             "prompts_started": sum(r["prompts"] for r in rs), "wall_s": round(wall, 3),
             "layout": "one GPU (both sides)" if world == 1 else f"{pairs} drafter/target GPU pairs",
+            "transport": "shared-memory mailbox" if not use_peer else "peer-memory rings",
             "thresholds": {"fallback": args.fallback_threshold, "first_token": args.first_token_threshold},
         }
         print(json.dumps(line), flush=True)
