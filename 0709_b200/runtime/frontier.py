@@ -94,17 +94,17 @@ def propose_children(
     paths = [tuple(history(p)) for p in parents] if keyed else [()] * len(parents)
     lp, ids = batch_parent_token_candidates(rows, k=k, sampling=sampling, relative_parent_paths=paths)
     ids_h, lp_h = read_back([ids, lp.float()], status, where="drafter top-k")
+    id_rows, lp_rows = ids_h.tolist(), lp_h.astype(np.float64).tolist()
     out: list[PendingCandidate] = []
-    for row, parent in enumerate(parents):
+    for parent, row_ids, row_lps in zip(parents, id_rows, lp_rows):
         if parent is None:
             pid, root, base = 0, 0, 0.0
         else:
-            pid, root, base = int(parent.route_id), int(parent.stage1_root_id), float(parent.cumulative_logprob)
+            pid, root, base = parent.route_id, parent.stage1_root_id, parent.cumulative_logprob
         if root_of is not None:
-            root = int(root_of(parent))
-        for rank, (tok, tlp) in enumerate(zip(ids_h[row].tolist(), lp_h[row].astype(np.float64).tolist())):
-            out.append(PendingCandidate(parent_route_id=pid, stage1_root_id=root, pending_token_id=int(tok),
-                                        cumulative_logprob=base + tlp, rank_in_parent=rank, parent_logprob=base))
+            root = root_of(parent)
+        for rank, (tok, tlp) in enumerate(zip(row_ids, row_lps)):
+            out.append(PendingCandidate(pid, root, tok, base + tlp, rank, base))
     return out, int(ids.numel() + lp.numel()) + (1 if status is not None else 0)
 
 

@@ -11,7 +11,7 @@ from __future__ import annotations
 
 from dataclasses import dataclass, field
 from enum import Enum
-from typing import Any, Mapping, Sequence
+from typing import Any, Mapping, NamedTuple, Sequence
 
 import torch
 
@@ -75,8 +75,10 @@ class RouteState:
         return int(self.stage1_depth) + int(self.stage2_depth)
 
 
-@dataclass(frozen=True)
-class PendingCandidate:
+class PendingCandidate(NamedTuple):
+    """One proposed child of a frontier route (immutable; a tuple so that a depth's few dozen
+    candidates are cheap to build on the host between two drafter forwards)."""
+
     parent_route_id: int
     stage1_root_id: int
     pending_token_id: int
