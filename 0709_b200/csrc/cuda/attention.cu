@@ -67,25 +67,21 @@ __device__ __forceinline__ int64_t resolve_key(const AttnParams& p, int m, int h
          (x % ps) * kHd;
 }
 
-// One warp folds row m's keys beyond the shared range -- route-private tail pages
-// (drafter) or ancestor-masked nodes (tree verify) -- into its running (mx, l, o),
-// keys in position order; lane t holds dimensions 4t..4t+3.
+// One warp folds keys [start, rlen) of row m (kv head h) into its running
+// (mx, l, o), keys in position order; lane t holds dimensions 4t..4t+3 and
+// q[0..3] are the row's query values at those dimensions.  `first` is the
+// cache offset of key start + lane when the caller resolved it already (so
+// the address chain runs before the PDL wait), or -2 to resolve it here.
 template <typename T>
-__device__ __forceinline__ void row_tail(const AttnParams& p, int m, int h, int64_t pair, int lane, float& mx,
-                                         float& l, float* o) {
-  const int shared_len = p.dparams[0];
-  const int n_shared_pages = p.dparams[1];
-  const int mask_base = p.dparams[2];
-  const int full = p.row_full[m];
-  const int rlen = p.row_len[m];
-  const int start = min(full, shared_len);
-  if (start >= rlen) return;
+__device__ __forceinline__ void fold_tail_keys(const AttnParams& p, int m, int h, int lane, const float* q, int start,
+                                               int rlen, int full, int shared_len, int n_shared_pages, int mask_base,
+                                               int64_t first, float& mx, float& l, float* o) {
   const float sl2 = p.scale * kLog2e;
   const int64_t kv_head = static_cast<int64_t>(p.page_size) * kHd;
-  const T* qp = static_cast<const T*>(p.q) + pair * kHd + lane * 4;
-  const float q0 = to_f32(qp[0]), q1 = to_f32(qp[1]), q2 = to_f32(qp[2]), q3 = to_f32(qp[3]);
   for (int t0 = start; t0 < rlen; t0 += 32) {
-    const int64_t base = resolve_key(p, m, h, t0 + lane, full, rlen, shared_len, n_shared_pages, mask_base);
+    const int64_t base = (t0 == start && first != -2)
+                             ? first
+                             : resolve_key(p, m, h, t0 + lane, full, rlen, shared_len, n_shared_pages, mask_base);
     const int cnt = min(32, rlen - t0);
     for (int j0 = 0; j0 < cnt; j0 += 8) {
       int64_t bj[8];
@@ -93,10 +89,10 @@ __device__ __forceinline__ void row_tail(const AttnParams& p, int m, int h, int6
 #pragma unroll
       for (int u = 0; u < 8; ++u) {
         bj[u] = (j0 + u < cnt) ? __shfl_sync(0xffffffffu, base, j0 + u) : -1;
-        if (bj[u] >= 0) {
+        if (bj[u] >= 0) {  // L2 loads: the merge kernel issues them before its PDL wait
           const T* kp = static_cast<const T*>(p.kv) + bj[u] + lane * 4;
-          kh[u] = *reinterpret_cast<const float2*>(kp);
-          vh[u] = *reinterpret_cast<const float2*>(kp + static_cast<int64_t>(p.Hkv) * kv_head);
+          kh[u] = __ldcg(reinterpret_cast<const float2*>(kp));
+          vh[u] = __ldcg(reinterpret_cast<const float2*>(kp + static_cast<int64_t>(p.Hkv) * kv_head));
         }
       }
 #pragma unroll
@@ -104,7 +100,7 @@ __device__ __forceinline__ void row_tail(const AttnParams& p, int m, int h, int6
         if (bj[u] < 0) continue;  // warp-uniform
         const T* ke = reinterpret_cast<const T*>(&kh[u]);
         const T* ve = reinterpret_cast<const T*>(&vh[u]);
-        float sc = q0 * to_f32(ke[0]) + q1 * to_f32(ke[1]) + q2 * to_f32(ke[2]) + q3 * to_f32(ke[3]);
+        float sc = q[0] * to_f32(ke[0]) + q[1] * to_f32(ke[1]) + q[2] * to_f32(ke[2]) + q[3] * to_f32(ke[3]);
         sc = warp_sum(sc) * sl2;
         const float nm = fmaxf(mx, sc);
         const float a = exp2f(mx - nm), w = exp2f(sc - nm);
@@ -117,6 +113,21 @@ __device__ __forceinline__ void row_tail(const AttnParams& p, int m, int h, int6
       }
     }
   }
+}
+
+// One warp folds row m's keys beyond the shared range -- route-private tail pages
+// (drafter) or ancestor-masked nodes (tree verify) -- into its running (mx, l, o).
+template <typename T>
+__device__ __forceinline__ void row_tail(const AttnParams& p, int m, int h, int64_t pair, int lane, float& mx,
+                                         float& l, float* o) {
+  const int shared_len = p.dparams[0];
+  const int full = p.row_full[m];
+  const int rlen = p.row_len[m];
+  const int start = min(full, shared_len);
+  if (start >= rlen) return;
+  const T* qp = static_cast<const T*>(p.q) + pair * kHd + lane * 4;
+  const float q[4] = {to_f32(qp[0]), to_f32(qp[1]), to_f32(qp[2]), to_f32(qp[3])};
+  fold_tail_keys<T>(p, m, h, lane, q, start, rlen, full, shared_len, p.dparams[1], p.dparams[2], -2, mx, l, o);
 }
 
 // Fused-merge epilogue: the p.splits CTAs of one (kv head, row tile) are one cluster,
@@ -224,7 +235,6 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  pdl_trigger();
 
   // Key range of this split (shared_len and the page table are graph inputs
   // written before the chain started, so they are safe to read before the wait).
@@ -294,6 +304,9 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
   } else {
     if (warp < 4) {
       pdl_wait();
+      // The successor (the merge/tail kernel) may start now: it reads the queries and the
+      // tail keys before its own wait, which the kernel this wait covered has written.
+      pdl_trigger();
       const bool valid = m < p.M;
       if (valid) a_lim = min(p.row_full[m], shared_len);
       const T* qrow = static_cast<const T*>(p.q) + (static_cast<int64_t>(m) * p.Hq + hq) * kHd;
@@ -477,16 +490,17 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
   }
 }
 
-// One warp per (row, q head): merge split partials, then the row's tail keys.
-// Latency-bound, so the kernel is arranged as few dependent round trips as
-// possible: the row's metadata and the first 32 tail keys' KV addresses are
-// resolved before the PDL wait (they come from graph inputs, not from the
-// kernels before this one); after it the split records, the query, all
-// non-empty partial O rows (16 splits per batch) and then up to 8 tail keys'
-// K/V per batch are loaded with every load of a batch in flight at once.
-// The arithmetic (split order, then keys in position order) is unchanged.
+// One warp per (row, q head): the row's tail keys and the merge of the split partials.
+// Latency-bound, so the dependent round trips after the PDL wait are cut to one: the
+// tensor-core kernel triggers this launch only after its own wait returned (the kernel
+// that wrote the queries and the tail keys is complete), so the whole tail -- key
+// addresses, K/V loads and the online softmax over those keys -- runs before this
+// kernel's wait, overlapping the split pass.  After the wait the split records and the
+// split partials are loaded together and merged in split order, then folded with the
+// tail's partial (a fixed order, independent of timing).
 template <typename T>
 __global__ void __launch_bounds__(128) attn_combine_tail(AttnParams p) {
+  constexpr int kBatch = 24;  // split partials loaded in the first round trip
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const int64_t pair = static_cast<int64_t>(blockIdx.x) * 4 + warp;
@@ -498,108 +512,89 @@ __global__ void __launch_bounds__(128) attn_combine_tail(AttnParams p) {
   const int hq = static_cast<int>(pair % p.Hq);
   const int G = p.Hq / p.Hkv;
   const int h = hq / G;
-  const int ps = p.page_size;
-  const float sl2 = p.scale * kLog2e;
   const int64_t stride_split = static_cast<int64_t>(p.M) * p.Hq;
-  const int64_t kv_head = static_cast<int64_t>(ps) * kHd;
 
-  // ---- before the wait: graph inputs only (metadata, masks, page tables)
+  // ---- before the wait: the tail keys [start, rlen) of this row
   const int shared_len = p.dparams[0];
-  const int n_shared_pages = p.dparams[1];
-  const int mask_base = p.dparams[2];
   const int full = p.row_full[m];
   const int rlen = p.row_len[m];
   const int start = min(full, shared_len);
-  auto resolve = [&](int x) -> int64_t {
-    return resolve_key(p, m, h, x, full, rlen, shared_len, n_shared_pages, mask_base);
-  };
-  const int64_t base_first = start < rlen ? resolve(start + lane) : -1;
+  float mt = -INFINITY, lt = 0.f;
+  float ot[4] = {0.f, 0.f, 0.f, 0.f};
+  if (start < rlen) {
+    const uint2 qraw = __ldcg(reinterpret_cast<const uint2*>(static_cast<const T*>(p.q) + pair * kHd + lane * 4));
+    const T* qe = reinterpret_cast<const T*>(&qraw);
+    const float q[4] = {to_f32(qe[0]), to_f32(qe[1]), to_f32(qe[2]), to_f32(qe[3])};
+    fold_tail_keys<T>(p, m, h, lane, q, start, rlen, full, shared_len, p.dparams[1], p.dparams[2], -2, mt, lt, ot);
+  }
 
   pdl_wait();
   pdl_trigger();
 
-  // ---- split records and the query (one round trip)
+  // ---- split records and partials in one round trip (lane s holds records s and s + 32; splits <= 64)
+  const int S = p.splits;
   float2 ml0 = make_float2(-INFINITY, 0.f), ml1 = make_float2(-INFINITY, 0.f);
-  if (lane < p.splits) ml0 = p.part_ml[lane * stride_split + pair];
-  if (lane + 32 < p.splits) ml1 = p.part_ml[(lane + 32) * stride_split + pair];
-  const T* qp = static_cast<const T*>(p.q) + pair * kHd + lane * 4;
-  const float q0 = to_f32(qp[0]), q1 = to_f32(qp[1]), q2 = to_f32(qp[2]), q3 = to_f32(qp[3]);
+  if (lane < S) ml0 = __ldcg(p.part_ml + lane * stride_split + pair);
+  if (lane + 32 < S) ml1 = __ldcg(p.part_ml + (lane + 32) * stride_split + pair);
+  const float* po = p.part_o + pair * kHd + lane * 4;
+  float4 ov[kBatch];
+#pragma unroll
+  for (int j = 0; j < kBatch; ++j)
+    ov[j] = j < S ? __ldcg(reinterpret_cast<const float4*>(po + j * stride_split * kHd)) : make_float4(0.f, 0.f, 0.f, 0.f);
 
-  // ---- merge the splits (lane s holds split s and s + 32; splits <= 64)
   float mx = -INFINITY, l = 0.f;
   float o[4] = {0.f, 0.f, 0.f, 0.f};
-  if (p.splits > 0) {
-    if (!(ml0.y > 0.f)) ml0.x = -INFINITY;
-    if (!(ml1.y > 0.f)) ml1.x = -INFINITY;
-    mx = warp_max(fmaxf(ml0.x, ml1.x));
-    if (mx > -INFINITY) {
-      const float w0 = ml0.x > -INFINITY ? exp2f(ml0.x - mx) : 0.f;
-      const float w1 = ml1.x > -INFINITY ? exp2f(ml1.x - mx) : 0.f;
-      l = warp_sum(w0 * ml0.y + w1 * ml1.y);
-      const float* po = p.part_o + pair * kHd + lane * 4;
-      for (int s0 = 0; s0 < p.splits; s0 += 16) {
-        float4 ov[16];
-        float wv[16];
+  if (!(ml0.y > 0.f)) ml0.x = -INFINITY;  // a split that saw no key of this row left no O
+  if (!(ml1.y > 0.f)) ml1.x = -INFINITY;
+  mx = warp_max(fmaxf(ml0.x, ml1.x));
+  if (mx > -INFINITY) {
+    const float w0 = ml0.x > -INFINITY ? exp2f(ml0.x - mx) : 0.f;
+    const float w1 = ml1.x > -INFINITY ? exp2f(ml1.x - mx) : 0.f;
+    l = warp_sum(w0 * ml0.y + w1 * ml1.y);
+    auto weight = [&](int sidx) {
+      return sidx < 32 ? __shfl_sync(0xffffffffu, w0, sidx & 31) : __shfl_sync(0xffffffffu, w1, sidx & 31);
+    };
 #pragma unroll
-        for (int j = 0; j < 16; ++j) {
-          const int sidx = s0 + j;
-          const float wsrc = sidx < 32 ? __shfl_sync(0xffffffffu, w0, sidx & 31)
-                                       : __shfl_sync(0xffffffffu, w1, sidx & 31);
-          wv[j] = sidx < p.splits ? wsrc : 0.f;
-          ov[j] = wv[j] > 0.f ? *reinterpret_cast<const float4*>(po + static_cast<int64_t>(sidx) * stride_split * kHd)
-                              : make_float4(0.f, 0.f, 0.f, 0.f);
-        }
+    for (int j = 0; j < kBatch; ++j) {
+      const float w = j < S ? weight(j) : 0.f;
+      if (w > 0.f) {  // warp-uniform; unwritten partials are never read into the sum
+        o[0] += w * ov[j].x;
+        o[1] += w * ov[j].y;
+        o[2] += w * ov[j].z;
+        o[3] += w * ov[j].w;
+      }
+    }
+    for (int s0 = kBatch; s0 < S; s0 += 16) {
+      float4 v[16];
+      float wv[16];
 #pragma unroll
-        for (int j = 0; j < 16; ++j) {
-          o[0] += wv[j] * ov[j].x;
-          o[1] += wv[j] * ov[j].y;
-          o[2] += wv[j] * ov[j].z;
-          o[3] += wv[j] * ov[j].w;
-        }
+      for (int j = 0; j < 16; ++j) {
+        const int sidx = s0 + j;
+        wv[j] = sidx < S ? weight(sidx) : 0.f;
+        v[j] = wv[j] > 0.f ? __ldcg(reinterpret_cast<const float4*>(po + sidx * stride_split * kHd))
+                           : make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+#pragma unroll
+      for (int j = 0; j < 16; ++j) {
+        o[0] += wv[j] * v[j].x;
+        o[1] += wv[j] * v[j].y;
+        o[2] += wv[j] * v[j].z;
+        o[3] += wv[j] * v[j].w;
       }
     }
   }
 
-  // ---- tail keys [start, rlen): lane t resolves key t0 + t; K/V of 8 keys per batch
-  for (int t0 = start; t0 < rlen; t0 += 32) {
-    const int64_t base = t0 == start ? base_first : resolve(t0 + lane);
-    const int cnt = min(32, rlen - t0);
-    for (int j0 = 0; j0 < cnt; j0 += 8) {
-      int64_t bj[8];
-      float2 kh[8], vh[8];
-#pragma unroll
-      for (int u = 0; u < 8; ++u) {
-        bj[u] = (j0 + u < cnt) ? __shfl_sync(0xffffffffu, base, j0 + u) : -1;
-        if (bj[u] >= 0) {
-          const T* kp = static_cast<const T*>(p.kv) + bj[u] + lane * 4;
-          kh[u] = *reinterpret_cast<const float2*>(kp);
-          vh[u] = *reinterpret_cast<const float2*>(kp + static_cast<int64_t>(p.Hkv) * kv_head);
-        }
-      }
-#pragma unroll
-      for (int u = 0; u < 8; ++u) {
-        if (bj[u] < 0) continue;  // warp-uniform
-        const T* ke = reinterpret_cast<const T*>(&kh[u]);
-        const T* ve = reinterpret_cast<const T*>(&vh[u]);
-        float sc = q0 * to_f32(ke[0]) + q1 * to_f32(ke[1]) + q2 * to_f32(ke[2]) + q3 * to_f32(ke[3]);
-        sc = warp_sum(sc) * sl2;
-        const float nm = fmaxf(mx, sc);
-        const float a = exp2f(mx - nm), w = exp2f(sc - nm);
-        o[0] = o[0] * a + w * to_f32(ve[0]);
-        o[1] = o[1] * a + w * to_f32(ve[1]);
-        o[2] = o[2] * a + w * to_f32(ve[2]);
-        o[3] = o[3] * a + w * to_f32(ve[3]);
-        l = l * a + w;
-        mx = nm;
-      }
-    }
-  }
+  // ---- fold in the tail's partial
+  const float M = fmaxf(mx, mt);
+  const float a = mx > -INFINITY ? exp2f(mx - M) : 0.f;
+  const float b = mt > -INFINITY ? exp2f(mt - M) : 0.f;
+  l = l * a + lt * b;
   const float inv = l > 0.f ? 1.f / l : 0.f;
   T* op = static_cast<T*>(p.out) + pair * kHd + lane * 4;
-  op[0] = from_f32<T>(o[0] * inv);
-  op[1] = from_f32<T>(o[1] * inv);
-  op[2] = from_f32<T>(o[2] * inv);
-  op[3] = from_f32<T>(o[3] * inv);
+  op[0] = from_f32<T>((o[0] * a + ot[0] * b) * inv);
+  op[1] = from_f32<T>((o[1] * a + ot[1] * b) * inv);
+  op[2] = from_f32<T>((o[2] * a + ot[2] * b) * inv);
+  op[3] = from_f32<T>((o[3] * a + ot[3] * b) * inv);
 }
 
 template <typename T>

@@ -601,6 +601,17 @@ torch::Tensor wrap_ptr(int64_t ptr, std::vector<int64_t> sizes, torch::ScalarTyp
 }
 
 // ----------------------------------------------------------- attention
+// The grid is sized for the longest context a graph may see; on a short one
+// the surplus splits find no pages and exit instead of each paying the CTA's
+// fixed cost for a single chunk (ATLAS_ATTN_MIN_PAGES overrides, default 4).
+static int attn_min_pages() {
+  static const int min_pages = [] {
+    const char* v = std::getenv("ATLAS_ATTN_MIN_PAGES");
+    return v != nullptr ? std::max(1, std::atoi(v)) : 4;
+  }();
+  return min_pages;
+}
+
 void attention(torch::Tensor q, torch::Tensor kv, int64_t layer, torch::Tensor out, torch::Tensor dparams,
                torch::Tensor prefix_pages, torch::Tensor row_full, torch::Tensor row_len, torch::Tensor row_mask,
                torch::Tensor tail_pages, torch::Tensor part_o, torch::Tensor part_ml, torch::Tensor err,
@@ -651,14 +662,7 @@ void attention(torch::Tensor q, torch::Tensor kv, int64_t layer, torch::Tensor o
   p.splits = run_tc ? static_cast<int>(splits) : 0;
   p.direct_out = direct_out ? 1 : 0;
   p.bf16 = q.scalar_type() == torch::kBFloat16;
-  // The grid is sized for the longest context a graph may see; on a short one
-  // the surplus splits find no pages and exit instead of each paying the CTA's
-  // fixed cost for a single chunk (ATLAS_ATTN_MIN_PAGES overrides, default 4).
-  static const int min_pages = [] {
-    const char* v = std::getenv("ATLAS_ATTN_MIN_PAGES");
-    return v != nullptr ? std::max(1, std::atoi(v)) : 4;
-  }();
-  p.min_pages_per_split = min_pages;
+  p.min_pages_per_split = attn_min_pages();
   p.fused_merge = fused_merge ? 1 : 0;
   p.scale = static_cast<float>(scale);
   const int row_tiles = static_cast<int>((M * G + 127) / 128);

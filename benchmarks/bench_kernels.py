@@ -174,7 +174,7 @@ def main() -> int:
 
         llama = pkg("models.llama")
         engine_mod = pkg("runtime.engine")
-        for name, rows in (("llama-8b", 12), ("llama-8b", 1), ("llama-1b", 9), ("llama-1b", 3)):
+        for name, rows in (("llama-8b", 12), ("llama-8b", 1), ("llama-1b", 9), ("llama-1b", 4), ("llama-1b", 3)):
             cfg = llama.get_config(name)
             w = llama.random_weights(cfg, seed=1, dtype=dt, device="cuda")
             eng = engine_mod.LlamaEngine(w, num_pages=512, page_size=16, max_positions=8192)

@@ -38,6 +38,8 @@ def main() -> int:
     ap.add_argument("--replays", type=int, default=3)
     ap.add_argument("--json-out", default=None)
     ap.add_argument("--fp8", action="store_true", help="block-scaled fp8 weights (Fp8LlamaEngine)")
+    ap.add_argument("--window", type=int, nargs=2, default=None, metavar=("FIRST", "COUNT"),
+                    help="also list kernels FIRST..FIRST+COUNT-1 of the last forward with start/end offsets (us)")
     args = ap.parse_args()
     llama = importlib.import_module("0709_b200.models.llama")
     engine_mod = importlib.import_module("0709_b200.runtime.engine")
@@ -87,6 +89,11 @@ def main() -> int:
            "kernel_sum_us": round(busy, 1), "gap_sum_us": round(gaps, 1), "overlap_us": round(overlap, 1),
            "per_kernel": {k: {"n": len(v), "avg_us": round(sum(v) / len(v), 2), "sum_us": round(sum(v), 1)}
                           for k, v in sorted(kinds.items(), key=lambda kv: -sum(kv[1]))}}
+    if args.window:
+        a, n = args.window
+        w0 = last[a].time_range.start
+        out["window"] = [[re.sub(r"\(.*", "", e.name)[:60], round(e.time_range.start - w0, 2),
+                          round(e.time_range.end - w0, 2)] for e in last[a: a + n]]
     print(json.dumps(out, indent=1))
     if args.json_out:
         with open(args.json_out, "w") as f:

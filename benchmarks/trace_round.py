@@ -4,7 +4,7 @@
     python benchmarks/trace_round.py --rounds 6 [bench.py flags]
 
 Builds the drafter + target of ``bench.py`` (same flags and defaults), warms
-up, then profiles a few rounds.  For each round it reports the host wall time,
+up, then profiles a few rounds of one request (rounds only: no prefill).  For each round it reports the host wall time,
 the time at least one kernel was running on the GPU (union over streams), the
 idle remainder, and the largest idle gaps with the kernels on either side --
 the places where host work (selection, scoring, thread handoffs, syncs)
@@ -100,10 +100,21 @@ def main() -> int:
     args = bench.parse()
     device = torch.device("cuda", 0)
     torch.cuda.set_device(device)
-    gen, _, _ = bench.build(args, device)
-    drv = bench.Driver(gen, bench.make_prompts(args, 0))
+    te = bench.build_target_engine(args, device, 1, False)
+    gen, _, _ = bench.build_session(args, device, te)
+    prompts = iter(bench.make_prompts(args, 0) * 1000)
+    session = gen.start(next(prompts))
+
+    def one_round():
+        nonlocal session
+        if session.finished:
+            session = gen.start(next(prompts))  # prefill outside the profiled round
+        session.step()
+
     for _ in range(own.trace_warmup):
-        drv.step()
+        one_round()
+    if session.finished:
+        session = gen.start(next(prompts))
     torch.cuda.synchronize()
     walls = []
     # Round boundaries: torch's tiny spin kernel on the default stream between
@@ -114,7 +125,9 @@ def main() -> int:
             torch.cuda._sleep(100)
             torch.cuda.synchronize()
             t0 = time.perf_counter()
-            drv.step()
+            if session.finished:
+                break
+            session.step()
             torch.cuda.synchronize()
             walls.append(time.perf_counter() - t0)
         torch.cuda._sleep(100)
