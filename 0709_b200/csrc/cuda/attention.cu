@@ -41,6 +41,35 @@ constexpr float kRescaleThreshold = 8.0f;  // log2 units: P stays <= 256 between
 constexpr int kThreadsTC = 192;            // warps 0-3 softmax, 4 TMA, 5 MMA
 }  // namespace
 
+// 2^x for x <= 0 (softmax weights): the PTX approximate base-2 exponential, subnormal results flushed.
+__device__ __forceinline__ float exp2_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// Two fp32 values as one packed pair of T (a in the low half).
+template <typename T>
+__device__ __forceinline__ uint32_t pack_pair(float a, float b);
+template <>
+__device__ __forceinline__ uint32_t pack_pair<__half>(float a, float b) {
+  const __half2 h = __floats2half2_rn(a, b);
+  return *reinterpret_cast<const uint32_t*>(&h);
+}
+template <>
+__device__ __forceinline__ uint32_t pack_pair<__nv_bfloat16>(float a, float b) {
+  const __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+  return *reinterpret_cast<const uint32_t*>(&h);
+}
+
+// Profiling stamp k of this CTA (SM clock), when a phase buffer is set.
+__device__ __forceinline__ void phase_stamp(const AttnParams& p, int k) {
+  if (p.phases != nullptr) {
+    const int64_t cta = (static_cast<int64_t>(blockIdx.z) * gridDim.y + blockIdx.y) * gridDim.x + blockIdx.x;
+    p.phases[cta * kAttnPhases + k] = clock64();
+  }
+}
+
 // Element offset of key x of row m (kv head h) in the cache, or -1 when x is not visible to the row.
 __device__ __forceinline__ int64_t resolve_key(const AttnParams& p, int m, int h, int x, int full, int rlen,
                                                int shared_len, int n_shared_pages, int mask_base) {
@@ -215,6 +244,34 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
   const int G = p.Hq / p.Hkv;
   const int ps = p.page_size;
   const bool causal = p.direct_out != 0;
+  // Stamps (thread 0 = row 0 unless noted): 0 entry, 1 set up, 2 after the PDL wait, 3 Q staged,
+  // 4/6 S(0)/S(1) ready, 5/7 P(0)/P(1) published, 8 O final, 9 partials stored, 10 exit;
+  // 11 MMA thread past its first full stage, 12 MMA thread done; 13/14 producer's first / last
+  // load issued; 15 global timer (ns) at entry.
+  if (tid == 0 && p.phases != nullptr) {
+    phase_stamp(p, 0);
+    const int64_t cta = (static_cast<int64_t>(blockIdx.z) * gridDim.y + blockIdx.y) * gridDim.x + blockIdx.x;
+    p.phases[cta * kAttnPhases + 15] = global_timer_ns();
+  }
+
+  // Key range of this split, its first page ids and the row limits: graph inputs written
+  // before the chain started, so they are safe to read before the wait, and read first so
+  // that their latency overlaps the set-up.  The Q tile needs the previous kernel's output.
+  const int shared_len = p.dparams[0];
+  const int np_total = (shared_len + ps - 1) / ps;
+  const int pps = max((np_total + p.splits - 1) / max(p.splits, 1), causal ? 1 : p.min_pages_per_split);
+  const int pb = split * pps;
+  const int cp = kChunkKeys / ps;  // pages per chunk
+  const int rho = tid;
+  const int grow = blockIdx.z * 128 + rho;
+  const int m = grow / G;
+  const int hq = h * G + (grow % G);
+  const int pe0 = min(np_total, pb + pps);
+  const int nch_loaded = pe0 > pb ? (pe0 - pb + cp - 1) / cp : 0;
+  int first_page = -1;  // producer lane i: page pb + i
+  if (warp == 4 && pb + (tid & 31) < pe0) first_page = p.prefix_pages[pb + (tid & 31)];
+  int row_full_m = 0;
+  if (warp < 4 && m < p.M) row_full_m = p.row_full[m];
 
   if (tid == 0) {
     for (int s = 0; s < kStages; ++s) {
@@ -235,22 +292,8 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  if (tid == 0) phase_stamp(p, 1);
 
-  // Key range of this split (shared_len and the page table are graph inputs
-  // written before the chain started, so they are safe to read before the wait).
-  const int shared_len = p.dparams[0];
-  const int np_total = (shared_len + ps - 1) / ps;
-  const int pps = max((np_total + p.splits - 1) / max(p.splits, 1), causal ? 1 : p.min_pages_per_split);
-  const int pb = split * pps;
-  const int cp = kChunkKeys / ps;  // pages per chunk
-
-  // Row limits and the Q tile need the previous kernel's output.
-  const int rho = tid;
-  const int grow = blockIdx.z * 128 + rho;
-  const int m = grow / G;
-  const int hq = h * G + (grow % G);
-  const int pe0 = min(np_total, pb + pps);
-  const int nch_loaded = pe0 > pb ? (pe0 - pb + cp - 1) / cp : 0;
   int a_lim = 0;
   int nchunks = 0, pe = pb;
   if (warp == 4) {
@@ -270,7 +313,8 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
         staged_base = p0;
         for (int i = lane; i < kPageIds; i += 32) {
           const int pi = p0 + i;
-          int page = pi < pe0 ? p.prefix_pages[pi] : -1;
+          int page = -1;
+          if (pi < pe0) page = (p0 == pb && i == lane) ? first_page : p.prefix_pages[pi];
           if (pi < pe0 && (page < 0 || page >= p.num_pages)) {
             set_error(p.err, kErrBadIndex);
             page = 0;
@@ -298,17 +342,20 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
             }
           }
         }
+        if (c == 0) phase_stamp(p, 13);
       }
       ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
     }
+    if (lane == 0) phase_stamp(p, 14);
   } else {
     if (warp < 4) {
       pdl_wait();
       // The successor (the merge/tail kernel) may start now: it reads the queries and the
       // tail keys before its own wait, which the kernel this wait covered has written.
       pdl_trigger();
+      if (tid == 0) phase_stamp(p, 2);
       const bool valid = m < p.M;
-      if (valid) a_lim = min(p.row_full[m], shared_len);
+      if (valid) a_lim = min(row_full_m, shared_len);
       const T* qrow = static_cast<const T*>(p.q) + (static_cast<int64_t>(m) * p.Hq + hq) * kHd;
 #pragma unroll
       for (int c = 0; c < 16; ++c) {
@@ -317,9 +364,11 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
         *reinterpret_cast<uint4*>(q_s + (c >> 3) * (128 * 128) + sw128_offset(rho, c & 7)) = v;
       }
       fence_proxy_async_smem();
-      atomicMax(&s_int[0], a_lim);
+      const int warp_lim = __reduce_max_sync(0xffffffffu, a_lim);
+      if ((tid & 31) == 0) atomicMax(&s_int[0], warp_lim);
     }
     asm volatile("bar.sync 1, 160;" ::: "memory");  // warps 0-3 and 5
+    if (tid == 0) phase_stamp(p, 3);
     const int tile_max = s_int[0];
     pe = min(pe0, (tile_max + ps - 1) / ps);
     nchunks = pe > pb ? (pe - pb + cp - 1) / cp : 0;
@@ -337,6 +386,7 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
           const int s = c % kStages;
           ok = mbar_wait(&full[s], (c / kStages) & 1, p.err);
           if (!ok) break;
+          if (c == 0) phase_stamp(p, 11);
           tc_fence_after();
           const uint32_t st = smem_u32(kv_s + s * kStageBytes);
           const uint32_t tS = tmem + (c & 1) * 64;
@@ -370,6 +420,7 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
         if (ok) mbar_arrive(&empty[c % kStages]);
       }
       umma_commit(fin);
+      phase_stamp(p, 12);
     }
   } else if (warp < 4) {
     const uint32_t lane_base = static_cast<uint32_t>(warp * 32) << 16;
@@ -380,17 +431,25 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
     bool ok = true;
     for (int c = 0; c < nchunks; ++c) {
       ok = mbar_wait(&s_full[c & 1], (c >> 1) & 1, p.err) && ok;
+      if (tid == 0 && c < 2) phase_stamp(p, 4 + 2 * c);
       tc_fence_after();
       float sv[kChunkKeys];
       tmem_ld32(tmem + (c & 1) * 64 + lane_base, sv);
       tmem_ld32(tmem + (c & 1) * 64 + lane_base + 32, sv + 32);
       const int x0 = (pb + c * cp) * ps;
-      float cmax = -INFINITY;
+      if (x0 + kChunkKeys > lim) {  // the row sees this chunk only in part (or not at all)
 #pragma unroll
-      for (int j = 0; j < kChunkKeys; ++j) {
-        sv[j] = (x0 + j < lim) ? sv[j] * sl2 : -INFINITY;
-        cmax = fmaxf(cmax, sv[j]);
+        for (int j = 0; j < kChunkKeys; ++j)
+          if (x0 + j >= lim) sv[j] = -INFINITY;
       }
+      // Row maximum (a tree; the scale is positive, so it is applied after the max) in log2 units.
+      float mx8[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i)
+        mx8[i] = fmaxf(fmaxf(fmaxf(sv[i], sv[i + 8]), fmaxf(sv[i + 16], sv[i + 24])),
+                       fmaxf(fmaxf(sv[i + 32], sv[i + 40]), fmaxf(sv[i + 48], sv[i + 56])));
+      const float cmax = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
+                               fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7]))) * sl2;
       const bool grow_max = cmax > m_run + kRescaleThreshold || (m_run == -INFINITY && cmax > -INFINITY);
       float alpha = 1.f;
       if (grow_max) {
@@ -414,24 +473,30 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
       // P buffer c%2 is free once PV(c-2) completed.
       if (c >= 2) ok = mbar_wait(&pv_done[c & 1], ((c - 2) >> 1) & 1, p.err) && ok;
       uint8_t* pbuf = p_s + (c & 1) * kPBytes;
-      float psum = 0.f;
+      // P = 2^(s * scale * log2(e) - m): one FMA and one ex2 per key.  A row that has seen
+      // no key yet has m = -inf and every s = -inf, so P = 0.
+      const float neg_m = m_run == -INFINITY ? 0.f : -m_run;
+      float psum4[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
       for (int cc = 0; cc < 8; ++cc) {
-        T pk[8];
+        uint32_t w[4];
 #pragma unroll
-        for (int e = 0; e < 8; ++e) {
-          const float pv = (m_run == -INFINITY) ? 0.f : exp2f(sv[cc * 8 + e] - m_run);
-          psum += pv;
-          pk[e] = from_f32<T>(pv);
+        for (int e = 0; e < 4; ++e) {
+          const float p0 = exp2_approx(fmaf(sv[cc * 8 + 2 * e], sl2, neg_m));
+          const float p1 = exp2_approx(fmaf(sv[cc * 8 + 2 * e + 1], sl2, neg_m));
+          psum4[e] += p0 + p1;
+          w[e] = pack_pair<T>(p0, p1);
         }
-        *reinterpret_cast<uint4*>(pbuf + sw128_offset(rho, cc)) = *reinterpret_cast<uint4*>(pk);
+        *reinterpret_cast<uint4*>(pbuf + sw128_offset(rho, cc)) = make_uint4(w[0], w[1], w[2], w[3]);
       }
-      l_run += psum;
+      l_run += (psum4[0] + psum4[1]) + (psum4[2] + psum4[3]);
       fence_proxy_async_smem();
       tc_fence_before();
       mbar_arrive(&p_full[c & 1]);
+      if (tid == 0 && c < 2) phase_stamp(p, 5 + 2 * c);
     }
     ok = mbar_wait(fin, 0, p.err) && ok;
+    if (tid == 0) phase_stamp(p, 8);
     tc_fence_after();
     float acc[kHd];
     if (nchunks > 0) {
@@ -479,8 +544,10 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
       }
     }
   }
+  if (tid == 0) phase_stamp(p, 9);
   tc_fence_before();
   __syncthreads();
+  if (tid == 0) phase_stamp(p, 10);
   if (warp == 0) tmem_dealloc(tmem, 256);
   if (p.fused_merge) {
     cluster_sync();  // every split of the cluster has staged its partials
@@ -669,8 +736,14 @@ int attention_max_cluster(bool bf16) {
   return bf16 ? vbf : v16;
 }
 
-void launch_attention(const CUtensorMap& kvmap, const AttnParams& p, bool run_tc, bool run_combine, int row_tiles,
+static unsigned long long* g_phase_buffer = nullptr;
+
+void set_attention_phase_buffer(unsigned long long* buf) { g_phase_buffer = buf; }
+
+void launch_attention(const CUtensorMap& kvmap, const AttnParams& p_in, bool run_tc, bool run_combine, int row_tiles,
                       cudaStream_t st) {
+  AttnParams p = p_in;
+  p.phases = g_phase_buffer;
   if (p.bf16)
     launch_typed<__nv_bfloat16>(kvmap, p, run_tc, run_combine, row_tiles, st);
   else

@@ -25,7 +25,15 @@ struct AttnParams {
   int min_pages_per_split;  // a split covers at least this many pages (surplus splits exit at once)
   int fused_merge;          // 1: the splits of a head form one cluster and merge + tail in the same kernel
   float scale;
+  // Profiling only (null otherwise): per CTA of the tensor-core kernel, kAttnPhases SM-clock
+  // stamps of its pipeline steps (see attn_shared_tc) and the global timer at entry.
+  unsigned long long* phases;
 };
+
+constexpr int kAttnPhases = 16;
+
+// Phase buffer for the next launches of the tensor-core attention kernel (nullptr: off).
+void set_attention_phase_buffer(unsigned long long* buf);
 
 // Largest cluster (splits of one head) the fused-merge path may launch with on this device: 16 when the
 // device can hold a 16-CTA cluster of the tensor-core kernel, else 8.

@@ -749,6 +749,13 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "sm_100a kernels: tcgen05/TMA GEMM and paged attention, fused norm/rope/append, KV copies, top-k";
   m.def("gemm", &gemm, "tcgen05 GEMM out = epi(x @ w^T); returns [bn, splits, kb_per_split]");
   m.def("attention", &attention, "paged attention (tensor-core shared range + per-row tail/combine)");
+  m.def("set_attention_phase_buffer", [](torch::Tensor buf) {
+    TORCH_CHECK(!buf.defined() || buf.numel() == 0 || (buf.is_cuda() && buf.scalar_type() == torch::kInt64),
+                "phase buffer must be a CUDA int64 tensor (or empty to switch off)");
+    atlas::set_attention_phase_buffer(buf.defined() && buf.numel() ? reinterpret_cast<unsigned long long*>(
+                                                                          buf.data_ptr<int64_t>())
+                                                                    : nullptr);
+  }, "profiling: SM-clock stamps of the tensor-core attention kernel's steps into buf (empty: off)");
   m.def("attention_max_cluster", [](bool bf16) { return atlas::attention_max_cluster(bf16); },
         "largest split cluster of the fused-merge attention on the current device");
   m.def("embed", &embed);
