@@ -393,7 +393,9 @@ class StaticBatch:
         pin = dev.type == "cuda"
         self.dev = torch.zeros(o, dtype=torch.int32, device=dev)
         self.hosts = [torch.zeros(o, dtype=torch.int32, pin_memory=pin) for _ in range(2)]
-        self.events = [None, None]
+        # One reusable event per host buffer: its last copy must finish before the buffer is refilled.
+        self.events = [torch.cuda.Event() for _ in range(2)] if pin else [None, None]
+        self._copy_pending = [False, False]
         self.turn = 0
         self.lock = threading.Lock()
         v = self.dev
@@ -434,9 +436,8 @@ class StaticBatch:
         with self.lock:
             i = self.turn
             self.turn ^= 1
-            ev = self.events[i]
-            if ev is not None:
-                ev.synchronize()
+            if self._copy_pending[i]:
+                self.events[i].synchronize()
             hv = self._host_views[i]
             m = self.M
             r0 = m - n if pad_front else 0
@@ -461,9 +462,8 @@ class StaticBatch:
             if dev_tokens:
                 self.tokens[rs].copy_(tokens.reshape(-1).to(torch.int32))
             if self.dev.is_cuda:
-                ev = torch.cuda.Event()
-                ev.record()
-                self.events[i] = ev
+                self.events[i].record(torch.cuda.current_stream(self.dev.device))
+                self._copy_pending[i] = True
         counters.h2d(self.words * 4)
         return n
 

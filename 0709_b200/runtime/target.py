@@ -345,6 +345,12 @@ class TargetVerifier:
         n = int(tokens.numel())
         p = len(self.prefix_token_ids)
         scratch = self.seq.reserve_scratch(p + n)
+        # Path log-probs: token t of route r is scored by the prefix row (t == 0) or by its
+        # parent node's row; the gather's indices go to the device before the forward.
+        r_, d_ = node_paths.shape
+        rows = torch.full((r_, d_), -1, dtype=torch.long)
+        rows[:, 1:] = node_paths[:, :-1].long()
+        gidx = self._stage_gather(rows, torch.tensor([list(x) for x in paths], dtype=torch.long), prefix_row=True)
         self._sync()
         logits = self.engine.run_rows(
             row_bucket(n),
@@ -361,13 +367,7 @@ class TargetVerifier:
             row_len=np.full(n, p + n),
             row_mask=masks.numpy(),
         )
-        # Path log-probs: token t of route r is scored by the prefix row (t == 0)
-        # or by its parent node's row; one gather, one host transfer.
-        r_, d_ = node_paths.shape
-        rows = torch.full((r_, d_), -1, dtype=torch.long)
-        rows[:, 1:] = node_paths[:, :-1].long()
-        toks = torch.tensor([list(x) for x in paths], dtype=torch.long)
-        lp = self.gather_logprobs(logits, rows, toks)
+        lp = self.gather_logprobs(logits, gidx)
         return {
             "logits": logits,
             "node_count": n,
@@ -395,6 +395,9 @@ class TargetVerifier:
         base = p - 1  # the lead token's position
         scratch = self.seq.reserve_scratch(p + n - 1)
         slots = torch.cat((self.seq.slots_for_positions(base, 1), scratch))
+        # Token t of a route is scored by its parent's row: the lead row for t == 0.
+        gidx = self._stage_gather(node_paths[:, :-1].long(), torch.tensor([list(x) for x in paths], dtype=torch.long),
+                                  prefix_row=False)
         self._sync()
         logits = self.engine.run_rows(
             row_bucket(n),
@@ -411,9 +414,7 @@ class TargetVerifier:
             row_len=np.full(n, base + n),
             row_mask=masks.numpy(),
         )
-        # Token t of a route is scored by its parent's row: the lead row for t == 0.
-        toks = torch.tensor([list(x) for x in paths], dtype=torch.long)
-        lp = self.gather_logprobs(logits, node_paths[:, :-1].long(), toks, prefix_row=False)
+        lp = self.gather_logprobs(logits, gidx)
         self._prefix_logits = logits[0].detach().clone()
         self._pending_token = None
         real = node_paths[:, 1:] - 1  # node i >= 1 of this trie is node i - 1 of the routes' trie
@@ -448,26 +449,31 @@ class TargetVerifier:
         self._prefix_logits = logits[0].detach().clone()
         self._pending_token = None
 
-    def gather_logprobs(self, logits: torch.Tensor, rows: torch.Tensor, toks: torch.Tensor, *,
-                        prefix_row: bool = True) -> list[list[float]]:
-        """Log-probs of ``toks`` under the rows ``rows`` of ``logits``; with ``prefix_row``
+    def _stage_gather(self, rows: torch.Tensor, toks: torch.Tensor, *, prefix_row: bool) -> dict:
+        """Indices of a path log-prob gather (host tensors ``rows``, ``toks`` of one shape), sent
+        to the device now -- pinned and asynchronous, ahead of the forward whose logits they
+        index -- so that the gather itself waits for nothing on the host.  With ``prefix_row``
         the prefix logits are row -1."""
-        dev = logits.device
-        if prefix_row:
+        r = (rows + 1 if prefix_row else rows).reshape(-1)
+        return {"rows": ids_to_device(r, self.device), "toks": ids_to_device(toks.reshape(-1), self.device),
+                "shape": tuple(rows.shape), "prefix_row": prefix_row}
+
+    def gather_logprobs(self, logits: torch.Tensor, g: dict) -> list[list[float]]:
+        """Log-probs of the staged tokens under the staged rows of ``logits`` (see ``_stage_gather``)."""
+        if g["prefix_row"]:
             assert self._prefix_logits is not None
             allrows = torch.cat((self._prefix_logits.reshape(1, -1).float(), logits.float()), dim=0)
-            r = (rows + 1).reshape(-1)
         else:
             allrows = logits.float()
-            r = rows.reshape(-1)
-        t = toks.reshape(-1)
+        r, t = g["rows"], g["toks"]
         if allrows.is_cuda:
             from ..ops.cuda_ops import shared_ops
 
-            vals = shared_ops(dev).gather_logprobs(allrows, r, t).reshape(rows.shape)
+            vals = shared_ops(allrows.device).gather_logprobs(allrows, r, t).reshape(g["shape"])
         else:
+            r, t = r.long(), t.long()
             lse = torch.logsumexp(allrows, dim=-1)
-            vals = (allrows[r, t] - lse[r]).reshape(rows.shape).float()
+            vals = (allrows[r, t] - lse[r]).reshape(g["shape"]).float()
         # The one transfer of the verify also brings back the device error flag.
         (host,) = read_back([vals], self.status_flag(), where="target tree verify")
         return host.astype(np.float64).tolist()

@@ -229,7 +229,16 @@ class PagedDistributedAtlasGenerator:
         return DrafterSamplingConfig(bool(c.drafter_do_sample), int(c.generation_seed), float(c.drafter_temperature))
 
     def _sampling(self, committed: Sequence[int]) -> DrafterSamplingContext:
-        return DrafterSamplingContext(self._sampling_config(), tuple(committed))
+        cfg = self._sampling_config()
+        if not cfg.do_sample:
+            # Greedy drafting never reads the prefix (it only keys sampling noise): one
+            # shared context per configuration instead of a copy of the prefix per call.
+            cached = getattr(self, "_greedy_context", None)
+            if cached is None or cached.config != cfg:
+                cached = DrafterSamplingContext(cfg, ())
+                self._greedy_context = cached
+            return cached
+        return DrafterSamplingContext(cfg, tuple(committed))
 
     def _should_build_forest_step(self, *, verify_done: bool, forest_depth: int) -> bool:
         if forest_depth >= self.config.d:
