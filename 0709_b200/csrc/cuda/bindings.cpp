@@ -669,6 +669,17 @@ void attention(torch::Tensor q, torch::Tensor kv, int64_t layer, torch::Tensor o
   atlas::launch_attention(kvmap, p, run_tc, run_combine, row_tiles, at::cuda::getCurrentCUDAStream());
 }
 
+// Device -> pinned host copy on the current stream, with no allocator bookkeeping: safe to
+// capture into a CUDA graph (the graph then copies into the same host buffer on every replay).
+void copy_to_host_async(torch::Tensor host, torch::Tensor src) {
+  TORCH_CHECK(src.is_cuda() && src.is_contiguous(), "source must be a contiguous CUDA tensor");
+  TORCH_CHECK(!host.is_cuda() && host.is_pinned() && host.is_contiguous(), "destination must be pinned host memory");
+  TORCH_CHECK(host.nbytes() >= src.nbytes(), "destination smaller than the source");
+  const c10::cuda::CUDAGuard guard(src.device());
+  C10_CUDA_CHECK(cudaMemcpyAsync(host.data_ptr(), src.data_ptr(), src.nbytes(), cudaMemcpyDeviceToHost,
+                                 at::cuda::getCurrentCUDAStream()));
+}
+
 // --------------------------------------------------------- elementwise
 void embed(torch::Tensor tok, torch::Tensor table, torch::Tensor out, torch::Tensor err) {
   TORCH_CHECK(tok.scalar_type() == torch::kInt32 && out.scalar_type() == torch::kFloat32, "embed dtypes");
@@ -763,6 +774,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("rope_append", &rope_append);
   m.def("kv_copy_pages", &kv_copy_pages);
   m.def("kv_move_slots", &kv_move_slots);
+  m.def("copy_to_host_async", &copy_to_host_async, "device -> pinned host copy on the current stream (capturable)");
   m.def("topk", &topk);
   m.def("gather_logprobs", &gather_logprobs);
   m.def("gemm_fused", &gemm_fused, "GEMM with folded RMSNorm (residual-norm / rope / scaled epilogues)");

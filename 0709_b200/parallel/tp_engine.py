@@ -148,7 +148,7 @@ class TPLlamaEngine(LlamaEngine):
         if self.device.type != "cuda" or not self.use_graphs:
             logits = self.forward(sb.tokens, sb.positions, sb.slots, desc)
             return None if logits is None else logits[sb.real_slice(n)].clone()
-        key = (sb.key, prefix_pages.data_ptr())
+        key = (sb.key, prefix_pages.data_ptr(), None)  # same key as ``warm_graph`` (no graph top-k)
         graph = self._graphs.get(key)
         if graph is None:
             graph = self._capture(sb, desc)

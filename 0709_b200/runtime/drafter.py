@@ -34,6 +34,10 @@ from .engine import LlamaEngine, row_bucket
 from .store import KVTreeStore
 
 
+# Largest k the in-graph top-k kernel takes.
+GRAPH_TOPK_MAX = 8
+
+
 class PrefixPageMirror:
     """Device copy of a pool's prefix page list, updated incrementally."""
 
@@ -174,10 +178,19 @@ class DrafterRuntime:
                     f"route {rid} physical length {rp.route_len(rid)} != logical length {r.kv_view.length}"
                 )
 
+    @property
+    def supports_graph_topk(self) -> bool:
+        """Whether ``decode_frontier_one_token(..., topk=k)`` selects candidates inside the forward's graph."""
+        f = getattr(self.engine, "graph_topk_available", None)
+        return bool(f is not None and f())
+
     @torch.inference_mode()
     def decode_frontier_one_token(
-        self, active_routes: Sequence[RouteState], attention_backend: Any = None
+        self, active_routes: Sequence[RouteState], attention_backend: Any = None, topk: int | None = None
     ) -> FrontierDecodeOutput:
+        """One token for every route.  With ``topk`` (greedy drafting, CUDA graphs) the forward's
+        graph also selects each row's top-``topk`` children and copies them to the host, so no
+        launch follows the forward before the host reads them (``FrontierDecodeOutput.candidates``)."""
         if self.route_store is None:
             raise RuntimeError("bind_store() must be called before decoding")
         t0 = time.perf_counter()
@@ -190,8 +203,7 @@ class DrafterRuntime:
         tails, lens = self.route_pool.row_tables(rids, self.max_tail_pages)
         lens_np = lens.numpy()
         plen = int(self.route_pool.prefix_len)
-        logits = self.engine.run_rows(
-            row_bucket(len(rids)),
+        fields = dict(
             tail_stride=self.max_tail_pages,
             mask_words=1,
             prefix_pages=self.mirror.dev,
@@ -205,6 +217,11 @@ class DrafterRuntime:
             row_len=lens_np,
             tail_pages=tails.numpy(),
         )
+        readout = None
+        if topk is not None and topk <= GRAPH_TOPK_MAX and self.supports_graph_topk:
+            logits, readout = self.engine.run_rows_topk(row_bucket(len(rids)), int(topk), **fields)
+        else:
+            logits = self.engine.run_rows(row_bucket(len(rids)), **fields)
         node_ids = tuple(self.route_store.reserve_node_ids(len(active_routes)))
         c = self.counters
         c["decode_steps"] += 1
@@ -215,6 +232,7 @@ class DrafterRuntime:
             next_token_logits=logits,
             new_node_ids=node_ids,
             new_node_ids_cpu=node_ids,
+            candidates=readout,
             model_ms=(time.perf_counter() - t0) * 1000.0,
             metadata={
                 "backend": "b200_native_paged_decode",
@@ -314,9 +332,13 @@ class DrafterRuntime:
         return logits
 
     def warm_graphs(self, k: int, extend_tokens: int = 4) -> None:
-        """Capture the decode buckets (k and k^2 routes) and the EXTEND bucket up front."""
+        """Capture the decode buckets (k and k^2 routes, with and without the in-graph top-k)
+        and the EXTEND bucket up front."""
+        topks = [None, k] if self.supports_graph_topk and k <= GRAPH_TOPK_MAX else [None]
         for b in sorted({row_bucket(1), row_bucket(k), row_bucket(k * k)}):
-            self.engine.warm_graph(b, tail_stride=self.max_tail_pages, mask_words=1, prefix_pages=self.mirror.dev)
+            for t in topks:
+                self.engine.warm_graph(b, tail_stride=self.max_tail_pages, mask_words=1, prefix_pages=self.mirror.dev,
+                                       topk=t)
         self.engine.warm_graph(row_bucket(extend_tokens), tail_stride=1, mask_words=1, prefix_pages=self.mirror.dev)
 
     # ---------------------------------------------------------- validation

@@ -137,29 +137,49 @@ class LlamaEngine:
         with self._run_lock:  # sessions in several threads may share this engine's static inputs
             return self._run_rows_locked(rows, tail_stride, mask_words, prefix_pages, fields)
 
-    def _run_rows_locked(self, rows, tail_stride, mask_words, prefix_pages, fields):
+    def _run_rows_locked(self, rows, tail_stride, mask_words, prefix_pages, fields, topk=None):
         sb = self.static_batch(rows, tail_stride, mask_words)
         n = sb.load(**fields)
         if self.device.type != "cuda" or not self.use_graphs:
             logits = self.forward(sb.tokens, sb.positions, sb.slots, sb.desc(prefix_pages))
             return logits[sb.real_slice(n)].clone()
-        key = (sb.key, prefix_pages.data_ptr())
+        key = (sb.key, prefix_pages.data_ptr(), topk)
         graph = self._graphs.get(key)
         if graph is None:  # a replay reads the static inputs directly; only a capture needs the descriptor
-            graph = self._capture(sb, sb.desc(prefix_pages))
+            graph = self._capture(sb, sb.desc(prefix_pages), topk)
             self._graphs[key] = graph
         for g in graph.graphs:
             g.replay()
+        if graph.cand is not None:
+            graph.cand.done.record()
         if graph.launches:
             from ..utils import counters
 
             counters.launches(graph.launches)
         self.stats.calls += 1
         self.stats.rows += n
-        return graph.out[sb.real_slice(n)].clone()
+        logits = graph.out[sb.real_slice(n)].clone()
+        if topk:
+            return logits, CandidateReadout(graph.cand, sb.real_slice(n), self.ops.err)
+        return logits
+
+    def graph_topk_available(self) -> bool:
+        """Whether ``run_rows_topk`` reads its candidates out of the captured graph."""
+        return self.device.type == "cuda" and self.use_graphs and hasattr(self.ops, "topk_logprobs")
 
     @torch.inference_mode()
-    def warm_graph(self, rows: int, *, tail_stride: int = 1, mask_words: int = 1, prefix_pages: torch.Tensor) -> None:
+    def run_rows_topk(self, rows: int, k: int, *, tail_stride: int = 1, mask_words: int = 1,
+                      prefix_pages: torch.Tensor, **fields):
+        """``run_rows`` whose graph also selects each row's top-``k`` (greedy) candidates and copies
+        them to the host; returns (logits, ``CandidateReadout``).  CUDA graphs only."""
+        if not self.graph_topk_available():
+            raise RuntimeError("run_rows_topk needs a CUDA engine with graphs")
+        with self._run_lock:
+            return self._run_rows_locked(rows, tail_stride, mask_words, prefix_pages, fields, topk=int(k))
+
+    @torch.inference_mode()
+    def warm_graph(self, rows: int, *, tail_stride: int = 1, mask_words: int = 1, prefix_pages: torch.Tensor,
+                   topk: int | None = None) -> None:
         """Capture the graph of one row bucket now (call before concurrent serving starts).
 
         Padding-only rows: every row writes the trash slot and attends to
@@ -168,15 +188,15 @@ class LlamaEngine:
         if self.device.type != "cuda" or not self.use_graphs:
             return
         sb = self.static_batch(rows, tail_stride, mask_words)
-        key = (sb.key, prefix_pages.data_ptr())
+        key = (sb.key, prefix_pages.data_ptr(), topk)
         if key in self._graphs:
             return
         sb.load(tokens=[], positions=[], slots=[], shared_len=1, n_shared_pages=1, mask_base=1, row_full=[],
                 row_len=[])
-        self._graphs[key] = self._capture(sb, sb.desc(prefix_pages))
+        self._graphs[key] = self._capture(sb, sb.desc(prefix_pages), topk)
         torch.cuda.synchronize(self.device)
 
-    def _capture(self, sb: "StaticBatch", desc: AttnDesc):
+    def _capture(self, sb: "StaticBatch", desc: AttnDesc, topk: int | None = None):
         from ..utils import counters
 
         stream = torch.cuda.Stream(device=self.device)
@@ -188,6 +208,21 @@ class LlamaEngine:
         before = counters.snapshot()["launches"]
         split = self._graph_split()
         keep = ()
+        cand: list = []
+        if topk:
+            # Filled by the graph on every replay (allocated before capture: pinned, fixed address).
+            host = torch.zeros(sb.M * topk * 2 + 1, dtype=torch.int32, pin_memory=True)
+
+            def tail(logits):
+                lp, ids = self.ops.topk_logprobs(logits, topk)
+                pack = torch.cat((ids.to(torch.int32).reshape(-1), lp.reshape(-1).view(torch.int32),
+                                  self.ops.err.reshape(-1)[:1]))
+                self.ops.ext.copy_to_host_async(host, pack)
+                cand.append(CandidateBuffers(topk, sb.M, host, torch.cuda.Event()))
+                return logits
+        else:
+            def tail(logits):
+                return logits
         # Capture on the side stream without the device-wide synchronize that
         # ``torch.cuda.graph`` performs first: another serving thread may be
         # capturing or running at the same time (thread-local capture mode).
@@ -199,15 +234,15 @@ class LlamaEngine:
                 g1 = self._capture_one(lambda: self._fused_layers(
                     self.ops.embed_norm(sb.tokens, self.w.embed), sb.positions, sb.slots, desc, None, 0, split))
                 keep = g1[1]
-                g2 = self._capture_one(lambda: self._fused_end(
-                    self._fused_layers(keep, sb.positions, sb.slots, desc, None, split, self.cfg.num_layers), None))
+                g2 = self._capture_one(lambda: tail(self._fused_end(
+                    self._fused_layers(keep, sb.positions, sb.slots, desc, None, split, self.cfg.num_layers), None)))
                 graphs, out = [g1[0], g2[0]], g2[1]
             else:
-                g, out = self._capture_one(lambda: self.forward(sb.tokens, sb.positions, sb.slots, desc))
+                g, out = self._capture_one(lambda: tail(self.forward(sb.tokens, sb.positions, sb.slots, desc)))
                 graphs = [g]
         torch.cuda.current_stream(self.device).wait_stream(stream)
         launches = counters.snapshot()["launches"] - before
-        return CapturedForward(graphs, out, launches, keep)
+        return CapturedForward(graphs, out, launches, keep, cand[0] if cand else None)
 
     def drop_graphs(self) -> None:
         """Release every captured graph.  Their private memory pool goes with them, so later
@@ -355,12 +390,53 @@ class LlamaEngine:
 
 class CapturedForward(NamedTuple):
     """CUDA graphs of one forward (replayed in order), its static output, the kernel
-    launches they contain, and the tensors carried from one graph to the next."""
+    launches they contain, the tensors carried from one graph to the next, and (when
+    captured with a top-k) the candidate read-out buffers."""
 
     graphs: list
     out: torch.Tensor | None
     launches: int
     keep: tuple
+    cand: "CandidateBuffers | None" = None
+
+
+@dataclass
+class CandidateBuffers:
+    """Top-``k`` candidates of every row of a captured forward.  The graph itself runs
+    the top-k kernel on its logits, packs [ids (int32) | log-probs (fp32 bits) | the
+    device error flag] and copies the pack into ``host`` (pinned), so a replay needs no
+    further launch before the host reads it; ``done`` is recorded after each replay."""
+
+    k: int
+    rows: int
+    host: torch.Tensor
+    done: torch.cuda.Event
+
+
+class CandidateReadout:
+    """The candidates of one replay (rows ``real`` of the bucket), read once after ``done``."""
+
+    def __init__(self, buf: CandidateBuffers, real: slice, status: torch.Tensor) -> None:
+        self.buf, self.real, self.status = buf, real, status
+        self.words = buf.rows * buf.k * 2 + 1
+
+    def get(self) -> tuple[np.ndarray, np.ndarray]:
+        """(ids int64 [n, k], log-probs float32 [n, k]); raises ``KernelError`` on a device error."""
+        from ..utils import counters
+        from ..utils.transfer import KernelError
+
+        b = self.buf
+        b.done.synchronize()
+        h = b.host.numpy()
+        code = int(h[self.words - 1])
+        if code:
+            self.status.zero_()
+            raise KernelError(code, "drafter top-k")
+        rk = b.rows * b.k
+        ids = h[:rk].reshape(b.rows, b.k)[self.real].astype(np.int64)
+        lps = h[rk: 2 * rk].view(np.float32).reshape(b.rows, b.k)[self.real].copy()
+        counters.d2h(self.words * 4)
+        return ids, lps
 
 
 class StaticBatch:

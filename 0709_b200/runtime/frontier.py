@@ -8,7 +8,10 @@ A depth is four moves:
 2. ``propose``: the fused top-k kernel turns each route's logits into ``k``
    candidate children (greedy, or keyed Gumbel-top-k sampling), and a single
    device-to-host copy brings back their ids and log-probs together with the
-   device's kernel error flag -- the host's only wait of the depth;
+   device's kernel error flag -- the host's only wait of the depth.  For greedy
+   drafting on a CUDA-graph backend the top-k and that copy are part of the
+   forward's graph (``decode_frontier_one_token(..., topk=k)``), so nothing is
+   launched between the forward and the host's read;
 3. ``rank``: the selection policy picks the next frontier on the host (a
    stage-1 tree keeps the best ``k`` overall, a stage-2 forest the best ``k``
    per stage-1 root; at most k^3 candidates);
@@ -75,6 +78,7 @@ def propose_children(
     history: Callable[[RouteState | None], Sequence[int]] | None = None,
     status: torch.Tensor | None = None,
     root_of: Callable[[RouteState | None], int] | None = None,
+    readout: Any = None,
 ) -> tuple[list[PendingCandidate], int]:
     """``k`` candidate children for each parent (one row of ``logits`` each).
 
@@ -91,9 +95,18 @@ def propose_children(
     keyed = sampling is not None and sampling.config.do_sample
     if keyed and history is None:
         raise ValueError("keyed sampling needs each parent's token history")
-    paths = [tuple(history(p)) for p in parents] if keyed else [()] * len(parents)
-    lp, ids = batch_parent_token_candidates(rows, k=k, sampling=sampling, relative_parent_paths=paths)
-    ids_h, lp_h = read_back([ids, lp.float()], status, where="drafter top-k")
+    if readout is not None and not keyed:
+        # Selected inside the forward's graph (greedy): only the host read remains.
+        ids_h, lp_h = readout.get()
+        if ids_h.shape[1] < k:
+            raise ValueError(f"the graph selected {ids_h.shape[1]} children per row, {k} requested")
+        ids_h, lp_h = ids_h[:, :k], lp_h[:, :k]
+        words = int(readout.words)
+    else:
+        paths = [tuple(history(p)) for p in parents] if keyed else [()] * len(parents)
+        lp, ids = batch_parent_token_candidates(rows, k=k, sampling=sampling, relative_parent_paths=paths)
+        ids_h, lp_h = read_back([ids, lp.float()], status, where="drafter top-k")
+        words = int(ids.numel() + lp.numel()) + (1 if status is not None else 0)
     id_rows, lp_rows = ids_h.tolist(), lp_h.astype(np.float64).tolist()
     out: list[PendingCandidate] = []
     for parent, row_ids, row_lps in zip(parents, id_rows, lp_rows):
@@ -105,7 +118,7 @@ def propose_children(
             root = root_of(parent)
         for rank, (tok, tlp) in enumerate(zip(row_ids, row_lps)):
             out.append(PendingCandidate(pid, root, tok, base + tlp, rank, base))
-    return out, int(ids.numel() + lp.numel()) + (1 if status is not None else 0)
+    return out, words
 
 
 def backend_status(backend) -> torch.Tensor | None:
@@ -137,10 +150,15 @@ def advance_frontier_one_token(
     if not active_routes:
         raise ValueError("a frontier step needs at least one active route")
     routes = list(active_routes)
-    out = model_backend.decode_frontier_one_token(routes, attention_backend=attention_backend)
+    keyed = sampling is not None and sampling.config.do_sample
+    if not keyed and getattr(model_backend, "supports_graph_topk", False):
+        out = model_backend.decode_frontier_one_token(routes, attention_backend=attention_backend, topk=k)
+    else:
+        out = model_backend.decode_frontier_one_token(routes, attention_backend=attention_backend)
     node_ids = _decoded_node_ids(out, len(routes))
     cands, words = propose_children(routes, out.next_token_logits, k=k, sampling=sampling,
-                                    history=route_store.pending_token_path, status=backend_status(model_backend))
+                                    history=route_store.pending_token_path, status=backend_status(model_backend),
+                                    readout=getattr(out, "candidates", None))
     picks = selection_policy.select(cands, k=k, active_routes=routes)
     grown = route_store.grow(routes, node_ids, selection_policy.phase)
     nxt = route_store.spawn(picks, grown)

@@ -122,6 +122,9 @@ class FrontierDecodeOutput:
     model_ms: float = 0.0
     kv_append_ms: float = 0.0
     metadata: Mapping[str, Any] = field(default_factory=dict)
+    # Greedy top-k children of every row selected inside the forward's graph (an object with
+    # ``get() -> (ids [n, k], log-probs [n, k])`` and ``words``), or None.
+    candidates: Any = None
 
 
 @dataclass(frozen=True)
