@@ -27,7 +27,6 @@ import torch
 
 from ..ops import _native
 from ..ops.attn_desc import AttnDesc
-from ..utils import counters
 from ..utils.transfer import ids_to_device
 from ..types import DraftPrefixState, FrontierDecodeOutput, PrefixKVView, RouteState
 from .engine import LlamaEngine, row_bucket
@@ -197,9 +196,7 @@ class DrafterRuntime:
         self._ensure_views(active_routes)
         rids = [int(r.route_id) for r in active_routes]
         slots, copies = self.route_pool.prepare_append(rids)
-        self.engine.copy_pages(copies)
-        if copies.numel():
-            counters.h2d(copies.numel() * 4)
+        cow = copies.numpy() if copies.numel() else None  # copied inside the forward's input copy
         tails, lens = self.route_pool.row_tables(rids, self.max_tail_pages)
         lens_np = lens.numpy()
         plen = int(self.route_pool.prefix_len)
@@ -216,6 +213,7 @@ class DrafterRuntime:
             row_full=lens_np,
             row_len=lens_np,
             tail_pages=tails.numpy(),
+            cow=cow,
         )
         readout = None
         if topk is not None and topk <= GRAPH_TOPK_MAX and self.supports_graph_topk:

@@ -133,13 +133,24 @@ class LlamaEngine:
 
         ``fields`` are host arrays (see ``StaticBatch.load``); returns fp32 logits
         [real rows, V] (a fresh tensor).  On CPU the eager forward runs instead.
+        ``cow`` (optional, [n, 3] host array of (src page, dst page, tokens)) are
+        copy-on-write page copies done first; they reach the device inside the
+        static batch's copy.
         """
         with self._run_lock:  # sessions in several threads may share this engine's static inputs
             return self._run_rows_locked(rows, tail_stride, mask_words, prefix_pages, fields)
 
     def _run_rows_locked(self, rows, tail_stride, mask_words, prefix_pages, fields, topk=None):
         sb = self.static_batch(rows, tail_stride, mask_words)
+        cow = fields.pop("cow", None)
+        if cow is not None and len(cow):
+            if fields.get("aux") is not None:
+                raise ValueError("copy-on-write page copies and auxiliary words share one region")
+            fields["aux"] = np.asarray(cow, dtype=np.int32).reshape(-1)
         n = sb.load(**fields)
+        if cow is not None and len(cow):
+            # Tail-page copies (src page, dst page, tokens) before the forward appends to the copies.
+            self.ops.kv_copy_pages(self.kv, sb.aux[: 3 * len(cow)].view(len(cow), 3))
         if self.device.type != "cuda" or not self.use_graphs:
             logits = self.forward(sb.tokens, sb.positions, sb.slots, sb.desc(prefix_pages))
             return logits[sb.real_slice(n)].clone()
@@ -464,6 +475,10 @@ class StaticBatch:
         o += o % 2
         self.offs["row_mask"] = (o, 2 * m * w)
         o += 2 * m * w
+        # Free-form words that ride along in the same copy: a caller's small index arrays
+        # (path log-prob gather indices, copy-on-write page copies) with no copy of their own.
+        self.offs["aux"] = (o, max(128, 8 * m))
+        o += self.offs["aux"][1]
         self.words = o
         dev = engine.device
         pin = dev.type == "cuda"
@@ -485,6 +500,8 @@ class StaticBatch:
         self.tail_pages = v[a: a + m * t].view(m, t)
         a = self.offs["row_mask"][0]
         self.row_mask = v[a: a + 2 * m * w].view(torch.int64).view(m, w)
+        a, size = self.offs["aux"]
+        self.aux = v[a: a + size]
         self.pad_front = False
         # numpy views of each pinned host buffer, made once (load runs for every forward)
         self._host_views = []
@@ -502,7 +519,7 @@ class StaticBatch:
         return slice(self.M - n, self.M) if self.pad_front else slice(0, n)
 
     def load(self, *, tokens, positions, slots, shared_len, n_shared_pages, mask_base, row_full, row_len,
-             tail_pages=None, row_mask=None, pad_front: bool = False) -> int:
+             tail_pages=None, row_mask=None, pad_front: bool = False, aux=None) -> int:
         from ..utils import counters
 
         n = len(tokens)
@@ -534,6 +551,11 @@ class StaticBatch:
             mk[:] = -1
             if row_mask is not None:
                 mk[rs, : np.asarray(row_mask).shape[1]] = row_mask
+            if aux is not None:
+                av = np.asarray(aux).reshape(-1)
+                if av.size > hv["aux"].size:
+                    raise ValueError(f"{av.size} auxiliary words exceed the bucket's {hv['aux'].size}")
+                hv["aux"][: av.size] = av
             self.dev.copy_(self.hosts[i], non_blocking=True)
             if dev_tokens:
                 self.tokens[rs].copy_(tokens.reshape(-1).to(torch.int32))

@@ -355,6 +355,7 @@ class TargetVerifier:
         logits = self.engine.run_rows(
             row_bucket(n),
             tail_stride=1,
+            aux=gidx["aux"],
             mask_words=int(masks.shape[1]),
             prefix_pages=self.mirror.dev,
             tokens=tokens.numpy(),
@@ -367,7 +368,7 @@ class TargetVerifier:
             row_len=np.full(n, p + n),
             row_mask=masks.numpy(),
         )
-        lp = self.gather_logprobs(logits, gidx)
+        lp = self.gather_logprobs(logits, gidx, self.engine.static_batch(row_bucket(n), 1, int(masks.shape[1])))
         return {
             "logits": logits,
             "node_count": n,
@@ -402,6 +403,7 @@ class TargetVerifier:
         logits = self.engine.run_rows(
             row_bucket(n),
             tail_stride=1,
+            aux=gidx["aux"],
             mask_words=int(masks.shape[1]),
             prefix_pages=self.mirror.dev,
             tokens=tokens.numpy(),
@@ -414,7 +416,7 @@ class TargetVerifier:
             row_len=np.full(n, base + n),
             row_mask=masks.numpy(),
         )
-        lp = self.gather_logprobs(logits, gidx)
+        lp = self.gather_logprobs(logits, gidx, self.engine.static_batch(row_bucket(n), 1, int(masks.shape[1])))
         self._prefix_logits = logits[0].detach().clone()
         self._pending_token = None
         real = node_paths[:, 1:] - 1  # node i >= 1 of this trie is node i - 1 of the routes' trie
@@ -449,23 +451,27 @@ class TargetVerifier:
         self._prefix_logits = logits[0].detach().clone()
         self._pending_token = None
 
-    def _stage_gather(self, rows: torch.Tensor, toks: torch.Tensor, *, prefix_row: bool) -> dict:
-        """Indices of a path log-prob gather (host tensors ``rows``, ``toks`` of one shape), sent
-        to the device now -- pinned and asynchronous, ahead of the forward whose logits they
-        index -- so that the gather itself waits for nothing on the host.  With ``prefix_row``
-        the prefix logits are row -1."""
-        r = (rows + 1 if prefix_row else rows).reshape(-1)
-        return {"rows": ids_to_device(r, self.device), "toks": ids_to_device(toks.reshape(-1), self.device),
-                "shape": tuple(rows.shape), "prefix_row": prefix_row}
+    @staticmethod
+    def _stage_gather(rows: torch.Tensor, toks: torch.Tensor, *, prefix_row: bool) -> dict:
+        """Indices of a path log-prob gather (host tensors ``rows``, ``toks`` of one shape).  They
+        travel in the forward's own input copy (the static batch's auxiliary words), so the
+        gather after the forward waits for nothing on the host.  With ``prefix_row`` the prefix
+        logits are row -1."""
+        r = (rows + 1 if prefix_row else rows).reshape(-1).numpy()
+        t = toks.reshape(-1).numpy()
+        return {"aux": np.concatenate((r, t)).astype(np.int32), "n": int(r.size), "shape": tuple(rows.shape),
+                "prefix_row": prefix_row}
 
-    def gather_logprobs(self, logits: torch.Tensor, g: dict) -> list[list[float]]:
-        """Log-probs of the staged tokens under the staged rows of ``logits`` (see ``_stage_gather``)."""
+    def gather_logprobs(self, logits: torch.Tensor, g: dict, sb) -> list[list[float]]:
+        """Log-probs of the staged tokens under the staged rows of ``logits`` (see ``_stage_gather``);
+        ``sb`` is the static batch whose forward carried the indices."""
         if g["prefix_row"]:
             assert self._prefix_logits is not None
             allrows = torch.cat((self._prefix_logits.reshape(1, -1).float(), logits.float()), dim=0)
         else:
             allrows = logits.float()
-        r, t = g["rows"], g["toks"]
+        n = g["n"]
+        r, t = sb.aux[:n], sb.aux[n: 2 * n]
         if allrows.is_cuda:
             from ..ops.cuda_ops import shared_ops
 
