@@ -41,7 +41,8 @@ def initialize_stage1_routes(
 ) -> list[RouteState]:
     """``k`` stage-1 routes seeded from the committed prefix's next-token logits (one pending token each)."""
     cands, _ = propose_children([None], draft_prefix_state.next_token_logits, k=k, sampling=sampling,
-                                history=lambda _p: (), status=backend_status(model_backend))
+                                history=lambda _p: (), status=backend_status(model_backend),
+                                readout=getattr(draft_prefix_state, "candidates", None))
     prefix = draft_prefix_state.prefix_kv_view
     return [route_store.new_route(root=None, parent=None, token=c.pending_token_id,
                                   token_logprob=c.cumulative_logprob, prefix=prefix) for c in cands]

@@ -93,6 +93,8 @@ class DrafterRuntime:
         self.route_store: KVTreeStore | None = None
         self.prefix_token_ids: tuple[int, ...] = ()
         self.prefix_next_token_logits: torch.Tensor | None = None
+        self._prefix_candidates = None  # graph-selected children of the prefix (after an extend)
+        self._graph_k: int | None = None  # the session's k (set by warm_graphs): extends select it in-graph
         self.counters = {
             "decode_steps": 0,
             "decode_rows": 0,
@@ -127,6 +129,7 @@ class DrafterRuntime:
         self.route_pool.clear()
         self.prefix_token_ids = ()
         self.prefix_next_token_logits = None
+        self._prefix_candidates = None
         self.mirror.host = []
 
     @torch.inference_mode()
@@ -147,6 +150,7 @@ class DrafterRuntime:
         )
         self.prefix_token_ids = toks
         self.prefix_next_token_logits = logits.unsqueeze(0)
+        self._prefix_candidates = None
         if self.route_store is not None:
             self.route_store.committed_token_ids = list(toks)
         return self.prefix_state()
@@ -157,6 +161,7 @@ class DrafterRuntime:
             token_tuple=tuple(self.prefix_token_ids),
             prefix_kv_view=PrefixKVView(committed_length=len(self.prefix_token_ids)),
             next_token_logits=self.prefix_next_token_logits,
+            candidates=self._prefix_candidates,
             committed_length=len(self.prefix_token_ids),
         )
 
@@ -262,6 +267,7 @@ class DrafterRuntime:
         # Logical: the same commit on the node arena, survivors rebased onto the new prefix.
         tokens, promoted = store.advance_prefix(committed_route, retained_routes)
         self.prefix_token_ids = (*self.prefix_token_ids, *tokens)
+        self._prefix_candidates = None
         if self.route_pool.prefix_len != len(self.prefix_token_ids):
             raise RuntimeError(f"drafter pages hold {self.route_pool.prefix_len} committed tokens, the route "
                                f"store {len(self.prefix_token_ids)}")
@@ -297,10 +303,10 @@ class DrafterRuntime:
         slots, copies = self.route_pool.append_prefix(n)
         self.engine.copy_pages(copies)
         self._sync_prefix()
+        self._prefix_candidates = None
         if n <= 64:
             masks = np.array([(1 << (r + 1)) - 1 if r < 63 else -1 for r in range(n)], dtype=np.int64)[:, None]
-            logits = self.engine.run_rows(
-                row_bucket(n),
+            fields = dict(
                 tail_stride=1,
                 mask_words=1,
                 prefix_pages=self.mirror.dev,
@@ -314,7 +320,14 @@ class DrafterRuntime:
                 row_len=np.full(n, start + n),
                 row_mask=masks,
                 pad_front=True,
-            )[-1]
+            )
+            k = self._graph_k
+            if k is not None and k <= GRAPH_TOPK_MAX and self.supports_graph_topk:
+                rows, readout = self.engine.run_rows_topk(row_bucket(n), k, **fields)
+                logits = rows[-1]
+                self._prefix_candidates = readout.last_row()  # the padded bucket ends with the real rows
+            else:
+                logits = self.engine.run_rows(row_bucket(n), **fields)[-1]
         else:
             logits = self.engine.prefill_sequence(
                 ids_to_device(suffix, self.device),
@@ -333,11 +346,14 @@ class DrafterRuntime:
         """Capture the decode buckets (k and k^2 routes, with and without the in-graph top-k)
         and the EXTEND bucket up front."""
         topks = [None, k] if self.supports_graph_topk and k <= GRAPH_TOPK_MAX else [None]
+        self._graph_k = k if len(topks) > 1 else None
         for b in sorted({row_bucket(1), row_bucket(k), row_bucket(k * k)}):
             for t in topks:
                 self.engine.warm_graph(b, tail_stride=self.max_tail_pages, mask_words=1, prefix_pages=self.mirror.dev,
                                        topk=t)
-        self.engine.warm_graph(row_bucket(extend_tokens), tail_stride=1, mask_words=1, prefix_pages=self.mirror.dev)
+        for t in topks:
+            self.engine.warm_graph(row_bucket(extend_tokens), tail_stride=1, mask_words=1, prefix_pages=self.mirror.dev,
+                                   topk=t)
 
     # ---------------------------------------------------------- validation
     def validate_route_physical_state(self, route: RouteState) -> None:

@@ -431,6 +431,10 @@ class CandidateReadout:
         self.buf, self.real, self.status = buf, real, status
         self.words = buf.rows * buf.k * 2 + 1
 
+    def last_row(self) -> "CandidateReadout":
+        """The same replay's read-out restricted to the bucket's last row."""
+        return CandidateReadout(self.buf, slice(self.buf.rows - 1, self.buf.rows), self.status)
+
     def get(self) -> tuple[np.ndarray, np.ndarray]:
         """(ids int64 [n, k], log-probs float32 [n, k]); raises ``KernelError`` on a device error."""
         from ..utils import counters

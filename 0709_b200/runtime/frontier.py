@@ -95,11 +95,9 @@ def propose_children(
     keyed = sampling is not None and sampling.config.do_sample
     if keyed and history is None:
         raise ValueError("keyed sampling needs each parent's token history")
-    if readout is not None and not keyed:
+    if readout is not None and not keyed and readout.buf.k >= k:
         # Selected inside the forward's graph (greedy): only the host read remains.
         ids_h, lp_h = readout.get()
-        if ids_h.shape[1] < k:
-            raise ValueError(f"the graph selected {ids_h.shape[1]} children per row, {k} requested")
         ids_h, lp_h = ids_h[:, :k], lp_h[:, :k]
         words = int(readout.words)
     else:

@@ -105,6 +105,9 @@ class DraftPrefixState:
     prefix_kv_view: PrefixKVView
     next_token_logits: torch.Tensor
     committed_length: int
+    # Greedy top-k children of the prefix selected inside the extend forward's graph (see
+    # ``FrontierDecodeOutput.candidates``), or None.
+    candidates: Any = None
 
     @property
     def token_ids(self) -> torch.Tensor:

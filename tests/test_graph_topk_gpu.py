@@ -60,3 +60,23 @@ def test_graph_topk_reports_device_error(engine):
     with pytest.raises(transfer.KernelError):
         readout.get()
     assert int(engine.ops.err.item()) == 0  # cleared when raised
+
+
+def test_extend_selects_prefix_children_in_graph():
+    """After an extend, the prefix's children come from the extend graph and equal top-k of its logits."""
+    llama = mod("models.llama")
+    transfer = mod("utils.transfer")
+    w = llama.random_weights(llama.get_config("small-drafter"), seed=4, dtype=torch.float16,
+                             device=torch.device("cuda", 0))
+    eng = mod("runtime.engine").LlamaEngine(w, num_pages=256, page_size=16, max_positions=4096)
+    dr = mod("runtime.drafter").DrafterRuntime(eng)
+    dr.warm_graphs(3, 4)
+    dr.prefill(list(range(100, 400)))
+    assert dr.prefix_state().candidates is None  # a prefill selects nothing in-graph
+    dr.append_known_tokens_as_prefix([5, 6, 7, 8])
+    st = dr.prefix_state()
+    ids, lps = st.candidates.get()
+    lp_ref, id_ref = eng.ops.topk_logprobs(st.next_token_logits, 3)
+    id_h, lp_h = transfer.read_back([id_ref, lp_ref], eng.ops.err)
+    np.testing.assert_array_equal(ids, id_h)
+    np.testing.assert_allclose(lps, lp_h, rtol=0, atol=1e-6)
