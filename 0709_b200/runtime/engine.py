@@ -159,10 +159,13 @@ class LlamaEngine:
         if graph is None:  # a replay reads the static inputs directly; only a capture needs the descriptor
             graph = self._capture(sb, sb.desc(prefix_pages), topk)
             self._graphs[key] = graph
+        if graph.cand is not None and graph.cand.pending is not None:
+            graph.cand.pending.materialize()  # keep the previous replay's pack before it is overwritten
         for g in graph.graphs:
             g.replay()
         if graph.cand is not None:
             graph.cand.done.record()
+            graph.cand.pending = _Replay(graph.cand, self.ops.err)
         if graph.launches:
             from ..utils import counters
 
@@ -171,7 +174,7 @@ class LlamaEngine:
         self.stats.rows += n
         logits = graph.out[sb.real_slice(n)].clone()
         if topk:
-            return logits, CandidateReadout(graph.cand, sb.real_slice(n), self.ops.err)
+            return logits, CandidateReadout(graph.cand.pending, sb.real_slice(n))
         return logits
 
     def graph_topk_available(self) -> bool:
@@ -416,42 +419,66 @@ class CandidateBuffers:
     """Top-``k`` candidates of every row of a captured forward.  The graph itself runs
     the top-k kernel on its logits, packs [ids (int32) | log-probs (fp32 bits) | the
     device error flag] and copies the pack into ``host`` (pinned), so a replay needs no
-    further launch before the host reads it; ``done`` is recorded after each replay."""
+    further launch before the host reads it; ``done`` is recorded after each replay and
+    ``pending`` is the last replay's read-out state."""
 
     k: int
     rows: int
     host: torch.Tensor
     done: torch.cuda.Event
+    pending: "_Replay | None" = None
+
+
+class _Replay:
+    """One replay's pack in a graph's pinned buffer, copied out once: by its reader, or -- when
+    another thread replays the same graph first (sessions sharing an engine) -- by that replay
+    before it overwrites the buffer."""
+
+    def __init__(self, buf: CandidateBuffers, status: torch.Tensor) -> None:
+        self.buf, self.status = buf, status
+        self.lock = threading.Lock()
+        self.data: tuple[int, np.ndarray, np.ndarray] | None = None
+        self.cleared = False
+
+    def materialize(self) -> tuple[int, np.ndarray, np.ndarray]:
+        with self.lock:
+            if self.data is None:
+                b = self.buf
+                b.done.synchronize()
+                h = b.host.numpy()
+                rk = b.rows * b.k
+                self.data = (int(h[2 * rk]), h[:rk].reshape(b.rows, b.k).astype(np.int64),
+                             h[rk: 2 * rk].view(np.float32).reshape(b.rows, b.k).copy())
+            return self.data
 
 
 class CandidateReadout:
-    """The candidates of one replay (rows ``real`` of the bucket), read once after ``done``."""
+    """The candidates of one replay (rows ``real`` of the bucket)."""
 
-    def __init__(self, buf: CandidateBuffers, real: slice, status: torch.Tensor) -> None:
-        self.buf, self.real, self.status = buf, real, status
-        self.words = buf.rows * buf.k * 2 + 1
+    def __init__(self, replay: _Replay, real: slice) -> None:
+        self.replay, self.real = replay, real
+        self.buf = replay.buf
+        self.words = self.buf.rows * self.buf.k * 2 + 1
 
     def last_row(self) -> "CandidateReadout":
         """The same replay's read-out restricted to the bucket's last row."""
-        return CandidateReadout(self.buf, slice(self.buf.rows - 1, self.buf.rows), self.status)
+        return CandidateReadout(self.replay, slice(self.buf.rows - 1, self.buf.rows))
 
     def get(self) -> tuple[np.ndarray, np.ndarray]:
-        """(ids int64 [n, k], log-probs float32 [n, k]); raises ``KernelError`` on a device error."""
+        """(ids int64 [n, k], log-probs float32 [n, k]); raises ``KernelError`` on a device error
+        (the device flag is cleared once)."""
         from ..utils import counters
         from ..utils.transfer import KernelError
 
-        b = self.buf
-        b.done.synchronize()
-        h = b.host.numpy()
-        code = int(h[self.words - 1])
+        code, ids, lps = self.replay.materialize()
         if code:
-            self.status.zero_()
+            with self.replay.lock:
+                if not self.replay.cleared:
+                    self.replay.status.zero_()
+                    self.replay.cleared = True
             raise KernelError(code, "drafter top-k")
-        rk = b.rows * b.k
-        ids = h[:rk].reshape(b.rows, b.k)[self.real].astype(np.int64)
-        lps = h[rk: 2 * rk].view(np.float32).reshape(b.rows, b.k)[self.real].copy()
         counters.d2h(self.words * 4)
-        return ids, lps
+        return ids[self.real], lps[self.real]
 
 
 class StaticBatch:
