@@ -34,8 +34,7 @@ constexpr int kQBytes = 2 * 128 * 128;                     // 2 halves x 128 row
 constexpr int kKVHalfBytes = kChunkKeys * 128;             // 64 keys x 128 B
 constexpr int kStageBytes = 4 * kKVHalfBytes;              // K (2 halves) + V (2 halves)
 constexpr int kPBytes = 128 * 128;                         // 128 rows x 64 keys x 2 B (one buffer)
-constexpr int kPageIds = 1024;  // page ids of a split staged in shared memory per refill
-constexpr int kSmemBytes = kQBytes + kStages * kStageBytes + 2 * kPBytes + 1024 + 512 + kPageIds * 4;
+constexpr int kSmemBytes = kQBytes + kStages * kStageBytes + 2 * kPBytes + 1024 + 512;
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kRescaleThreshold = 8.0f;  // log2 units: P stays <= 256 between rescales
 constexpr int kThreadsTC = 192;            // warps 0-3 softmax, 4 TMA, 5 MMA
@@ -214,14 +213,15 @@ __device__ void merge_rows_and_tails(const AttnParams& p, const float* o_s, cons
 //   warp 4  TMA producer: K/V pages of each 64-key chunk into a 4-stage ring
 //           (non-causal: the first stages are issued before the PDL wait --
 //           they read only committed prefix KV);
-//   warp 5  MMA issuer: S(c) = Q K(c)^T into TMEM buffer c%2, then, once the
-//           softmax warps publish P(c-1), O += P(c-1) V(c-1) into TMEM;
+//   warp 5  MMA issuer: loads the Q tile by TMA right after the PDL wait, then
+//           S(c) = Q K(c)^T into TMEM buffer c%2 and, once the softmax warps
+//           publish P(c-1), O += P(c-1) V(c-1) into TMEM;
 //   warps 0-3  one thread per query row: online softmax with lazy rescaling
 //           (O in TMEM is rescaled only when a row's max grows by more than
 //           2^8), P written to a double-buffered shared tile.
 template <typename T>
 __global__ void __launch_bounds__(kThreadsTC, 1)
-    attn_shared_tc(const __grid_constant__ CUtensorMap kvmap, AttnParams p) {
+    attn_shared_tc(const __grid_constant__ CUtensorMap kvmap, const __grid_constant__ CUtensorMap qmap, AttnParams p) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* q_s = smem;
@@ -233,9 +233,8 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
   uint64_t* p_full = s_full + 2;       // [2], 128 arrivals
   uint64_t* pv_done = p_full + 2;      // [2]
   uint64_t* fin = pv_done + 2;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(fin + 1);
-  int* s_int = reinterpret_cast<int*>(tmem_slot + 1);  // [0] tile max A
-  int* page_ids = reinterpret_cast<int*>(reinterpret_cast<uint8_t*>(full) + 256);  // after barriers/slots
+  uint64_t* q_full = fin + 1;  // the Q tile (TMA)
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(q_full + 1);
 
   const int tid = threadIdx.x;
   const int warp = tid >> 5;
@@ -272,6 +271,15 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
   if (warp == 4 && pb + (tid & 31) < pe0) first_page = p.prefix_pages[pb + (tid & 31)];
   int row_full_m = 0;
   if (warp < 4 && m < p.M) row_full_m = p.row_full[m];
+  // Largest shared-range limit over the tile's tokens (every warp computes the same value, so
+  // no warp waits for another to learn how many chunks the tile needs).
+  const int tok_per_tile = 128 / G;
+  const int m_lo = static_cast<int>(blockIdx.z) * tok_per_tile;
+  int tile_max = 0;
+  for (int j = tid & 31; j < tok_per_tile; j += 32) {
+    const int mm = m_lo + j;
+    if (mm < p.M) tile_max = max(tile_max, min(p.row_full[mm], shared_len));
+  }
 
   if (tid == 0) {
     for (int s = 0; s < kStages; ++s) {
@@ -284,45 +292,48 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
       mbar_init(&pv_done[b], 1);
     }
     mbar_init(fin, 1);
+    mbar_init(q_full, 1);
     fence_barrier_init();
-    s_int[0] = 0;
     tma_prefetch_desc(&kvmap);
+    tma_prefetch_desc(&qmap);
   }
   if (warp == 0) tmem_alloc(tmem_slot, 256);
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
   if (tid == 0) phase_stamp(p, 1);
+  tile_max = __reduce_max_sync(0xffffffffu, tile_max);
+  const int pe = min(pe0, (tile_max + ps - 1) / ps);
+  const int nchunks = pe > pb ? (pe - pb + cp - 1) / cp : 0;
+  // The Q tile (tokens m_lo.., this head's G query heads, two 64-dimension halves) by TMA:
+  // rows land 128B-swizzled like the K/V stages, rows past the last token are zero-filled.
+  // Issued once the previous kernel (which wrote Q) is complete; only by a CTA that loads keys.
+  auto load_q = [&]() {
+    mbar_arrive_expect_tx(q_full, static_cast<uint32_t>(kQBytes));
+    tma_load_3d(q_s, &qmap, q_full, 0, h * G, m_lo);
+    tma_load_3d(q_s + kQBytes / 2, &qmap, q_full, 64, h * G, m_lo);
+  };
 
   int a_lim = 0;
-  int nchunks = 0, pe = pb;
   if (warp == 4) {
-    // Producer warp: stage the split's page ids in shared memory (all lanes,
-    // in parallel), then lane 0 streams the chunks.  It never joins a block
-    // barrier before the end (the MMA warp frees its ring stages).
+    // Producer warp: lane i holds page id pb + i (read before the set-up; the next 32 are read
+    // when a split has more), lane 0 streams the chunks.  Pages past the split's end repeat a
+    // valid page: finite data that the softmax masks to P = 0.  It never joins a block barrier
+    // before the end (the MMA warp frees its ring stages).
     const int lane = tid & 31;
     if (causal) pdl_wait();  // causal prefill reads keys the previous kernel wrote
     bool ok = true;
-    int staged_base = -1;
+    int pid = first_page, pid_base = pb;
     for (int c = 0; c < nch_loaded && ok; ++c) {
       const int p0 = pb + c * cp;
       const int npg = min(cp, pe0 - p0);
-      if (staged_base < 0 || p0 + cp > staged_base + kPageIds) {
-        // Refill: pages [p0, p0 + kPageIds) of this split.
-        __syncwarp();
-        staged_base = p0;
-        for (int i = lane; i < kPageIds; i += 32) {
-          const int pi = p0 + i;
-          int page = -1;
-          if (pi < pe0) page = (p0 == pb && i == lane) ? first_page : p.prefix_pages[pi];
-          if (pi < pe0 && (page < 0 || page >= p.num_pages)) {
-            set_error(p.err, kErrBadIndex);
-            page = 0;
-          }
-          page_ids[i] = page;
-        }
-        __syncwarp();
+      if (p0 + cp > pid_base + 32) {
+        pid_base = p0;
+        pid = p0 + lane < pe0 ? p.prefix_pages[p0 + lane] : -1;
       }
+      int pg[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) pg[i] = __shfl_sync(0xffffffffu, pid, (p0 - pid_base + (i < npg ? i : 0)) & 31);
       if (lane == 0) {
         const int s = c % kStages;
         if (c >= kStages) ok = mbar_wait(&empty[s], ((c / kStages) - 1) & 1, p.err);
@@ -330,9 +341,11 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
           uint8_t* st = kv_s + s * kStageBytes;
           mbar_arrive_expect_tx(&full[s], static_cast<uint32_t>(cp * ps * 128 * 4));
           for (int i = 0; i < cp; ++i) {
-            // Pages past the split's end repeat a valid page: finite data that the
-            // softmax masks to P = 0.
-            const int page = page_ids[p0 - staged_base + (i < npg ? i : 0)];
+            int page = pg[i];
+            if (page < 0 || page >= p.num_pages) {
+              set_error(p.err, kErrBadIndex);
+              page = 0;
+            }
             const int zc = p.layer * p.num_pages + page;
             const int roff = i * ps * 128;
 #pragma unroll
@@ -354,24 +367,8 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
       // tail keys before its own wait, which the kernel this wait covered has written.
       pdl_trigger();
       if (tid == 0) phase_stamp(p, 2);
-      const bool valid = m < p.M;
-      if (valid) a_lim = min(row_full_m, shared_len);
-      const T* qrow = static_cast<const T*>(p.q) + (static_cast<int64_t>(m) * p.Hq + hq) * kHd;
-#pragma unroll
-      for (int c = 0; c < 16; ++c) {
-        uint4 v = make_uint4(0, 0, 0, 0);
-        if (valid) v = *reinterpret_cast<const uint4*>(qrow + c * 8);
-        *reinterpret_cast<uint4*>(q_s + (c >> 3) * (128 * 128) + sw128_offset(rho, c & 7)) = v;
-      }
-      fence_proxy_async_smem();
-      const int warp_lim = __reduce_max_sync(0xffffffffu, a_lim);
-      if ((tid & 31) == 0) atomicMax(&s_int[0], warp_lim);
+      if (m < p.M) a_lim = min(row_full_m, shared_len);
     }
-    asm volatile("bar.sync 1, 160;" ::: "memory");  // warps 0-3 and 5
-    if (tid == 0) phase_stamp(p, 3);
-    const int tile_max = s_int[0];
-    pe = min(pe0, (tile_max + ps - 1) / ps);
-    nchunks = pe > pb ? (pe - pb + cp - 1) / cp : 0;
   }
 
   if (warp == 5) {
@@ -380,7 +377,15 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
       const uint32_t idesc_s = umma_idesc_f16(128, kChunkKeys, is_bf16, false, false);
       const uint32_t idesc_o = umma_idesc_f16(128, kHd, is_bf16, false, true);
       const uint32_t tO = tmem + 128;
+      // The Q tile: loaded (once the kernel that wrote Q is complete) by every CTA that loads
+      // keys, and waited for even when this tile needs none of them, so no copy into shared
+      // memory outlives the CTA.
       bool ok = true;
+      if (nch_loaded > 0) {
+        pdl_wait();
+        load_q();
+        ok = mbar_wait(q_full, 0, p.err);
+      }
       for (int c = 0; c <= nchunks && ok; ++c) {
         if (c < nchunks) {
           const int s = c % kStages;
@@ -675,8 +680,8 @@ static void configure_tc() {
 }
 
 template <typename T>
-static void launch_typed(const CUtensorMap& kvmap, const AttnParams& p, bool run_tc, bool run_combine, int row_tiles,
-                         cudaStream_t st) {
+static void launch_typed(const CUtensorMap& kvmap, const CUtensorMap& qmap, const AttnParams& p, bool run_tc,
+                         bool run_combine, int row_tiles, cudaStream_t st) {
   if (p.fused_merge) {
     // Splits of one head = one cluster; the merge and the tails run in the same kernel.
     configure_tc<T>();
@@ -694,13 +699,13 @@ static void launch_typed(const CUtensorMap& kvmap, const AttnParams& p, bool run
     attr[1].val.clusterDim.z = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 2;
-    cudaLaunchKernelEx(&cfg, attn_shared_tc<T>, kvmap, p);
+    cudaLaunchKernelEx(&cfg, attn_shared_tc<T>, kvmap, qmap, p);
     return;
   }
   if (run_tc) {
     configure_tc<T>();
     dim3 grid(p.Hkv, p.splits, row_tiles);
-    launch_k(attn_shared_tc<T>, grid, dim3(kThreadsTC), kSmemBytes, st, kvmap, p);
+    launch_k(attn_shared_tc<T>, grid, dim3(kThreadsTC), kSmemBytes, st, kvmap, qmap, p);
   }
   if (run_combine) {
     const int64_t pairs = static_cast<int64_t>(p.M) * p.Hq;
@@ -740,14 +745,14 @@ static unsigned long long* g_phase_buffer = nullptr;
 
 void set_attention_phase_buffer(unsigned long long* buf) { g_phase_buffer = buf; }
 
-void launch_attention(const CUtensorMap& kvmap, const AttnParams& p_in, bool run_tc, bool run_combine, int row_tiles,
-                      cudaStream_t st) {
+void launch_attention(const CUtensorMap& kvmap, const CUtensorMap& qmap, const AttnParams& p_in, bool run_tc,
+                      bool run_combine, int row_tiles, cudaStream_t st) {
   AttnParams p = p_in;
   p.phases = g_phase_buffer;
   if (p.bf16)
-    launch_typed<__nv_bfloat16>(kvmap, p, run_tc, run_combine, row_tiles, st);
+    launch_typed<__nv_bfloat16>(kvmap, qmap, p, run_tc, run_combine, row_tiles, st);
   else
-    launch_typed<__half>(kvmap, p, run_tc, run_combine, row_tiles, st);
+    launch_typed<__half>(kvmap, qmap, p, run_tc, run_combine, row_tiles, st);
 }
 
 }  // namespace atlas

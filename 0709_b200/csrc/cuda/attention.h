@@ -30,7 +30,7 @@ struct AttnParams {
   unsigned long long* phases;
 };
 
-constexpr int kAttnPhases = 16;
+constexpr int kAttnPhases = 20;
 
 // Phase buffer for the next launches of the tensor-core attention kernel (nullptr: off).
 void set_attention_phase_buffer(unsigned long long* buf);
@@ -39,7 +39,9 @@ void set_attention_phase_buffer(unsigned long long* buf);
 // device can hold a 16-CTA cluster of the tensor-core kernel, else 8.
 int attention_max_cluster(bool bf16);
 
-void launch_attention(const CUtensorMap& kvmap, const AttnParams& p, bool run_tc, bool run_combine, int row_tiles,
-                      cudaStream_t st);
+// kvmap: the cache (see map_kv); qmap: q [M, Hq, 128] as a 3-D map (128, Hq, M) with box
+// (64, Hq / Hkv, 128 / (Hq / Hkv)) and 128B swizzle, one box per 64-dimension half of a tile.
+void launch_attention(const CUtensorMap& kvmap, const CUtensorMap& qmap, const AttnParams& p, bool run_tc,
+                      bool run_combine, int row_tiles, cudaStream_t st);
 
 }  // namespace atlas

@@ -130,6 +130,26 @@ CUtensorMap map_kv(const torch::Tensor& kv) {
   return m;
 }
 
+// q [M, Hq, 128] as (128, Hq, M): one box = 64 dimensions x the G query heads of a kv head x the
+// 128 / G tokens of a row tile (128 rows of 128 B, 128B-swizzled like the K/V stages).  Not
+// cached: a graph captures the map once; an eager call encodes its own (host only, ~1 us).
+CUtensorMap map_q(const torch::Tensor& q, int64_t G) {
+  TORCH_CHECK(q.dim() == 3 && q.is_contiguous() && q.size(2) == 128, "q must be contiguous [M, Hq, 128]");
+  TORCH_CHECK(reinterpret_cast<uintptr_t>(q.data_ptr()) % 16 == 0, "q must be 16-byte aligned");
+  const int64_t M = q.size(0), Hq = q.size(1);
+  const int64_t es_b = q.element_size();
+  CUtensorMap m;
+  cuuint64_t dims[3] = {128, static_cast<cuuint64_t>(Hq), static_cast<cuuint64_t>(M)};
+  cuuint64_t strides[2] = {static_cast<cuuint64_t>(128 * es_b), static_cast<cuuint64_t>(Hq * 128 * es_b)};
+  cuuint32_t box[3] = {64, static_cast<cuuint32_t>(G), static_cast<cuuint32_t>(128 / G)};
+  cuuint32_t es[3] = {1, 1, 1};
+  CUresult r = encode_fn()(&m, tma_dtype(q.scalar_type()), 3, q.data_ptr(), dims, strides, box, es,
+                           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                           CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  TORCH_CHECK(r == CUDA_SUCCESS, "cuTensorMapEncodeTiled (q) failed: ", static_cast<int>(r));
+  return m;
+}
+
 int pick_bn(int64_t n) {
   if (n <= 16) return 16;
   if (n <= 32) return 32;
@@ -636,8 +656,11 @@ void attention(torch::Tensor q, torch::Tensor kv, int64_t layer, torch::Tensor o
                 "attention split workspace too small");
   }
   const c10::cuda::CUDAGuard guard(q.device());
-  CUtensorMap kvmap{};
-  if (run_tc) kvmap = map_kv(kv);
+  CUtensorMap kvmap{}, qmap{};
+  if (run_tc) {
+    kvmap = map_kv(kv);
+    qmap = map_q(q, G);
+  }
   AttnParams p{};
   p.q = q.data_ptr();
   p.kv = kv.data_ptr();
@@ -666,7 +689,7 @@ void attention(torch::Tensor q, torch::Tensor kv, int64_t layer, torch::Tensor o
   p.fused_merge = fused_merge ? 1 : 0;
   p.scale = static_cast<float>(scale);
   const int row_tiles = static_cast<int>((M * G + 127) / 128);
-  atlas::launch_attention(kvmap, p, run_tc, run_combine, row_tiles, at::cuda::getCurrentCUDAStream());
+  atlas::launch_attention(kvmap, qmap, p, run_tc, run_combine, row_tiles, at::cuda::getCurrentCUDAStream());
 }
 
 // Device -> pinned host copy on the current stream, with no allocator bookkeeping: safe to

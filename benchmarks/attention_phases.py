@@ -28,7 +28,8 @@ sys.path.insert(0, ROOT)
 
 NAMES = {0: "entry", 1: "set_up", 2: "pdl_wait_done", 3: "q_staged", 4: "s0_ready", 5: "p0_published",
          6: "s1_ready", 7: "p1_published", 8: "o_final", 9: "partials_stored", 10: "exit",
-         11: "mma_first_stage", 12: "mma_done", 13: "producer_first_load", 14: "producer_last_load"}
+         11: "mma_first_stage", 12: "mma_done", 13: "producer_first_load", 14: "producer_last_load",
+         16: "q_stored", 17: "q_fenced", 18: "q_reduced", 19: "q_atomic"}
 
 
 def main() -> int:
@@ -43,7 +44,7 @@ def main() -> int:
     ext = importlib.import_module("0709_b200.ops._native").cuda()
     cfg = llama.get_config(args.model)
     npages = (args.prefix + args.rows) // 16 + 4
-    buf = torch.zeros(8192 * 16, dtype=torch.int64, device="cuda")
+    buf = torch.zeros(8192 * 20, dtype=torch.int64, device="cuda")
     ext.set_attention_phase_buffer(buf)
     try:
         w = llama.random_weights(cfg, seed=1, dtype=torch.float16, device="cuda")
@@ -62,11 +63,11 @@ def main() -> int:
         torch.cuda.synchronize()
     finally:
         ext.set_attention_phase_buffer(torch.empty(0, dtype=torch.int64, device="cuda"))
-    st = buf.view(-1, 16).cpu().numpy().astype(np.int64)
+    st = buf.view(-1, 20).cpu().numpy().astype(np.int64)
     ctas = st[(st[:, 0] != 0) & (st[:, 8] != 0)]
     with_keys = ctas[ctas[:, 11] != 0] if (ctas[:, 11] != 0).any() else ctas
     base = with_keys[:, 2:3]
-    rel = {NAMES[k]: with_keys[:, k] - base[:, 0] for k in NAMES if k != 15 and (with_keys[:, k] != 0).any()}
+    rel = {NAMES[k]: with_keys[:, k] - base[:, 0] for k in NAMES if (with_keys[:, k] != 0).any()}
     to_us = 1.0 / args.mhz
     out = {
         "model": args.model, "rows": args.rows, "prefix": args.prefix, "ctas_stamped": int(len(ctas)),
