@@ -703,6 +703,19 @@ void copy_to_host_async(torch::Tensor host, torch::Tensor src) {
                                  at::cuda::getCurrentCUDAStream()));
 }
 
+// Pinned host -> device copy on the current stream, then `event` (a cudaEvent_t handle, 0 for
+// none) recorded after it: one call for the static batch's per-forward input copy and the
+// event that guards the reuse of its host buffer.
+void upload_async(torch::Tensor dev, torch::Tensor host, int64_t event) {
+  TORCH_CHECK(dev.is_cuda() && dev.is_contiguous(), "destination must be a contiguous CUDA tensor");
+  TORCH_CHECK(!host.is_cuda() && host.is_pinned() && host.is_contiguous(), "source must be pinned host memory");
+  TORCH_CHECK(dev.nbytes() >= host.nbytes(), "destination smaller than the source");
+  const c10::cuda::CUDAGuard guard(dev.device());
+  cudaStream_t st = at::cuda::getCurrentCUDAStream();
+  C10_CUDA_CHECK(cudaMemcpyAsync(dev.data_ptr(), host.data_ptr(), host.nbytes(), cudaMemcpyHostToDevice, st));
+  if (event != 0) C10_CUDA_CHECK(cudaEventRecord(reinterpret_cast<cudaEvent_t>(event), st));
+}
+
 // --------------------------------------------------------- elementwise
 void embed(torch::Tensor tok, torch::Tensor table, torch::Tensor out, torch::Tensor err) {
   TORCH_CHECK(tok.scalar_type() == torch::kInt32 && out.scalar_type() == torch::kFloat32, "embed dtypes");
@@ -797,6 +810,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("rope_append", &rope_append);
   m.def("kv_copy_pages", &kv_copy_pages);
   m.def("kv_move_slots", &kv_move_slots);
+  m.def("upload_async", &upload_async, "pinned host -> device copy on the current stream, then an event record");
   m.def("copy_to_host_async", &copy_to_host_async, "device -> pinned host copy on the current stream (capturable)");
   m.def("topk", &topk);
   m.def("gather_logprobs", &gather_logprobs);

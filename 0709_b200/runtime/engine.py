@@ -518,6 +518,13 @@ class StaticBatch:
         # One reusable event per host buffer: its last copy must finish before the buffer is refilled.
         self.events = [torch.cuda.Event() for _ in range(2)] if pin else [None, None]
         self._copy_pending = [False, False]
+        self._upload = None
+        self._event_handles = [0, 0]
+        if pin and hasattr(engine.ops, "ext") and hasattr(engine.ops.ext, "upload_async"):
+            for ev in self.events:
+                ev.record()  # creates the CUDA event, so its handle exists
+            self._event_handles = [int(getattr(ev, "cuda_event", 0) or 0) for ev in self.events]
+            self._upload = engine.ops.ext.upload_async
         self.turn = 0
         self.lock = threading.Lock()
         v = self.dev
@@ -587,12 +594,17 @@ class StaticBatch:
                 if av.size > hv["aux"].size:
                     raise ValueError(f"{av.size} auxiliary words exceed the bucket's {hv['aux'].size}")
                 hv["aux"][: av.size] = av
-            self.dev.copy_(self.hosts[i], non_blocking=True)
+            if self._upload is not None and self._event_handles[i]:
+                # One native call: the copy and the event that guards this host buffer's reuse.
+                self._upload(self.dev, self.hosts[i], self._event_handles[i])
+                self._copy_pending[i] = True
+            else:
+                self.dev.copy_(self.hosts[i], non_blocking=True)
+                if self.dev.is_cuda:
+                    self.events[i].record(torch.cuda.current_stream(self.dev.device))
+                    self._copy_pending[i] = True
             if dev_tokens:
                 self.tokens[rs].copy_(tokens.reshape(-1).to(torch.int32))
-            if self.dev.is_cuda:
-                self.events[i].record(torch.cuda.current_stream(self.dev.device))
-                self._copy_pending[i] = True
         counters.h2d(self.words * 4)
         return n
 
