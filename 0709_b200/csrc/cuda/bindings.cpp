@@ -755,6 +755,18 @@ void kv_copy_pages(torch::Tensor kv, torch::Tensor plan, torch::Tensor err) {
                               at::cuda::getCurrentCUDAStream());
 }
 
+// plan int32 [max_n, 3] and count int32 [1] on the device (read when the kernel runs).
+void kv_copy_pages_counted(torch::Tensor kv, torch::Tensor plan, torch::Tensor count, torch::Tensor err) {
+  TORCH_CHECK(plan.scalar_type() == torch::kInt32 && plan.dim() == 2 && plan.size(1) == 3, "plan must be int32 [n,3]");
+  TORCH_CHECK(count.scalar_type() == torch::kInt32 && count.numel() >= 1 && count.is_cuda(), "count must be int32");
+  const c10::cuda::CUDAGuard guard(kv.device());
+  atlas::launch_kv_copy_pages_counted(kv.data_ptr(), plan.data_ptr<int>(), count.data_ptr<int>(),
+                                      static_cast<int>(plan.size(0)), static_cast<int>(kv.size(0)),
+                                      static_cast<int>(kv.size(1)), static_cast<int>(kv.size(3)),
+                                      static_cast<int>(kv.size(4)), static_cast<int>(kv.size(5)), err.data_ptr<int>(),
+                                      at::cuda::getCurrentCUDAStream());
+}
+
 void kv_move_slots(torch::Tensor kv, torch::Tensor src, torch::Tensor dst, torch::Tensor err) {
   TORCH_CHECK(src.numel() == dst.numel() && src.numel() <= 64, "at most 64 slot moves per launch");
   const c10::cuda::CUDAGuard guard(kv.device());
@@ -809,6 +821,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("rmsnorm", &rmsnorm);
   m.def("rope_append", &rope_append);
   m.def("kv_copy_pages", &kv_copy_pages);
+  m.def("kv_copy_pages_counted", &kv_copy_pages_counted,
+        "copy-on-write pages whose plan and count are read on the device (capturable once for any count)");
   m.def("kv_move_slots", &kv_move_slots);
   m.def("upload_async", &upload_async, "pinned host -> device copy on the current stream, then an event record");
   m.def("copy_to_host_async", &copy_to_host_async, "device -> pinned host copy on the current stream (capturable)");

@@ -14,6 +14,8 @@ void launch_rmsnorm(const float* x, const void* w, void* out, int M, int H, floa
 void launch_rope_append(const void* qkv, const float* table, const int* pos, const int* slots, void* kv_layer,
                         void* qout, int M, int Hq, int Hkv, int hd, int ps, int num_pages, int max_pos, bool bf16,
                         int* err, cudaStream_t st);
+void launch_kv_copy_pages_counted(void* kv, const int* plan, const int* count, int max_n, int layers, int num_pages,
+                                  int Hkv, int ps, int hd, int* err, cudaStream_t st);
 void launch_kv_copy_pages(void* kv, const int* plan, int n, int layers, int num_pages, int Hkv, int ps, int hd,
                           int* err, cudaStream_t st);
 void launch_kv_move_slots(void* kv, const int* src, const int* dst, int n, int layers, int num_pages, int Hkv, int ps,

@@ -288,6 +288,11 @@ class CudaOps:
         self.ext.kv_copy_pages(kv, copies.to(self.device, torch.int32).contiguous(), self.err)
         counters.launches(1)
 
+    def kv_copy_pages_counted(self, kv: torch.Tensor, plan: torch.Tensor, count: torch.Tensor) -> None:
+        """Copy-on-write of ``count[0]`` rows of ``plan`` [max, 3] (both read on the device)."""
+        self.ext.kv_copy_pages_counted(kv, plan, count, self.err)
+        counters.launches(1)
+
     def kv_move_slots(self, kv: torch.Tensor, src: torch.Tensor, dst: torch.Tensor) -> None:
         self.ext.kv_move_slots(kv, src.to(self.device, torch.int32), dst.to(self.device, torch.int32), self.err)
         counters.launches(1)

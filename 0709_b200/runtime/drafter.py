@@ -104,6 +104,10 @@ class DrafterRuntime:
             "extend_calls": 0,
             "extend_tokens": 0,
         }
+        # Decode forwards copy tail pages on write: let the engine's graphs do it from the plan that
+        # rides in the static batch (one launch fewer between the host's inputs and the forward).
+        if hasattr(engine, "cow_in_graph"):
+            engine.cow_in_graph = True
 
     # ---------------------------------------------------------------- store
     def bind_store(self, store: KVTreeStore) -> None:

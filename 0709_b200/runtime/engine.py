@@ -94,6 +94,9 @@ class LlamaEngine:
         self.graph_head_layers = int(os.environ.get("ATLAS_GRAPH_HEAD_LAYERS", "2"))
         # Scratch page for padded rows' KV writes (never part of any sequence).
         self.trash_slot = (self.num_pages - 1) * self.page_size
+        # Graphs captured from now on start with the copy-on-write copy of the plan that rides in
+        # the static batch (set by the drafter, whose decode forwards copy tail pages).
+        self.cow_in_graph = False
 
     # ------------------------------------------------------------------
     def _fold_norms(self):
@@ -143,19 +146,26 @@ class LlamaEngine:
     def _run_rows_locked(self, rows, tail_stride, mask_words, prefix_pages, fields, topk=None):
         sb = self.static_batch(rows, tail_stride, mask_words)
         cow = fields.pop("cow", None)
-        if cow is not None and len(cow):
+        ncow = len(cow) if cow is not None else 0
+        if ncow:
             if fields.get("aux") is not None:
                 raise ValueError("copy-on-write page copies and auxiliary words share one region")
+            if ncow > sb.M:
+                raise ValueError(f"{ncow} copy-on-write pages for a bucket of {sb.M} rows")
             fields["aux"] = np.asarray(cow, dtype=np.int32).reshape(-1)
-        n = sb.load(**fields)
-        if cow is not None and len(cow):
+        graphed = self.device.type == "cuda" and self.use_graphs
+        key = (sb.key, prefix_pages.data_ptr(), topk)
+        graph = self._graphs.get(key) if graphed else None
+        # A captured graph that starts with the copy-on-write node copies the plan itself (count in
+        # the static batch); otherwise (eager, or the call that captures) it is copied here first.
+        in_graph = graph is not None and graph.cow
+        n = sb.load(**fields, cow_count=ncow if in_graph else 0)
+        if ncow and not in_graph:
             # Tail-page copies (src page, dst page, tokens) before the forward appends to the copies.
-            self.ops.kv_copy_pages(self.kv, sb.aux[: 3 * len(cow)].view(len(cow), 3))
-        if self.device.type != "cuda" or not self.use_graphs:
+            self.ops.kv_copy_pages(self.kv, sb.aux[: 3 * ncow].view(ncow, 3))
+        if not graphed:
             logits = self.forward(sb.tokens, sb.positions, sb.slots, sb.desc(prefix_pages))
             return logits[sb.real_slice(n)].clone()
-        key = (sb.key, prefix_pages.data_ptr(), topk)
-        graph = self._graphs.get(key)
         if graph is None:  # a replay reads the static inputs directly; only a capture needs the descriptor
             graph = self._capture(sb, sb.desc(prefix_pages), topk)
             self._graphs[key] = graph
@@ -223,6 +233,17 @@ class LlamaEngine:
         split = self._graph_split()
         keep = ()
         cand: list = []
+        cow = bool(self.cow_in_graph and hasattr(self.ops, "kv_copy_pages_counted"))
+
+        def head(fn):
+            if not cow:
+                return fn
+            plan = sb.aux[: 3 * sb.M].view(sb.M, 3)
+
+            def run():
+                self.ops.kv_copy_pages_counted(self.kv, plan, sb.dparams[3:4])
+                return fn()
+            return run
         if topk:
             # Filled by the graph on every replay (allocated before capture: pinned, fixed address).
             host = torch.zeros(sb.M * topk * 2 + 1, dtype=torch.int32, pin_memory=True)
@@ -245,18 +266,18 @@ class LlamaEngine:
                 # Head: embedding + layers [0, split).  The residual stream and
                 # its norm statistics carry over to the tail graph; they stay
                 # referenced so no other capture reuses their memory.
-                g1 = self._capture_one(lambda: self._fused_layers(
-                    self.ops.embed_norm(sb.tokens, self.w.embed), sb.positions, sb.slots, desc, None, 0, split))
+                g1 = self._capture_one(head(lambda: self._fused_layers(
+                    self.ops.embed_norm(sb.tokens, self.w.embed), sb.positions, sb.slots, desc, None, 0, split)))
                 keep = g1[1]
                 g2 = self._capture_one(lambda: tail(self._fused_end(
                     self._fused_layers(keep, sb.positions, sb.slots, desc, None, split, self.cfg.num_layers), None)))
                 graphs, out = [g1[0], g2[0]], g2[1]
             else:
-                g, out = self._capture_one(lambda: tail(self.forward(sb.tokens, sb.positions, sb.slots, desc)))
+                g, out = self._capture_one(head(lambda: tail(self.forward(sb.tokens, sb.positions, sb.slots, desc))))
                 graphs = [g]
         torch.cuda.current_stream(self.device).wait_stream(stream)
         launches = counters.snapshot()["launches"] - before
-        return CapturedForward(graphs, out, launches, keep, cand[0] if cand else None)
+        return CapturedForward(graphs, out, launches, keep, cand[0] if cand else None, cow)
 
     def drop_graphs(self) -> None:
         """Release every captured graph.  Their private memory pool goes with them, so later
@@ -412,6 +433,7 @@ class CapturedForward(NamedTuple):
     launches: int
     keep: tuple
     cand: "CandidateBuffers | None" = None
+    cow: bool = False  # the first graph copies the static batch's copy-on-write plan itself
 
 
 @dataclass
@@ -557,7 +579,7 @@ class StaticBatch:
         return slice(self.M - n, self.M) if self.pad_front else slice(0, n)
 
     def load(self, *, tokens, positions, slots, shared_len, n_shared_pages, mask_base, row_full, row_len,
-             tail_pages=None, row_mask=None, pad_front: bool = False, aux=None) -> int:
+             tail_pages=None, row_mask=None, pad_front: bool = False, aux=None, cow_count: int = 0) -> int:
         from ..utils import counters
 
         n = len(tokens)
@@ -573,7 +595,7 @@ class StaticBatch:
             m = self.M
             r0 = m - n if pad_front else 0
             rs = slice(r0, r0 + n)
-            hv["head"][:] = (int(shared_len), int(n_shared_pages), int(mask_base), 0)
+            hv["head"][:] = (int(shared_len), int(n_shared_pages), int(mask_base), int(cow_count))
             dev_tokens = isinstance(tokens, torch.Tensor) and tokens.device.type != "cpu"
             for name, vals in (("tokens", 0 if dev_tokens else tokens), ("positions", positions), ("slots", slots),
                                ("row_full", row_full), ("row_len", row_len)):

@@ -80,3 +80,25 @@ def test_extend_selects_prefix_children_in_graph():
     id_h, lp_h = transfer.read_back([id_ref, lp_ref], eng.ops.err)
     np.testing.assert_array_equal(ids, id_h)
     np.testing.assert_allclose(lps, lp_h, rtol=0, atol=1e-6)
+
+
+def test_copy_on_write_inside_the_graph():
+    """A drafter engine's graphs copy the tail pages named in the static batch before the forward."""
+    llama = mod("models.llama")
+    w = llama.random_weights(llama.get_config("small-drafter"), seed=5, dtype=torch.float16,
+                             device=torch.device("cuda", 0))
+    eng = mod("runtime.engine").LlamaEngine(w, num_pages=256, page_size=16, max_positions=4096)
+    eng.cow_in_graph = True
+    pages = torch.arange(64, dtype=torch.int32, device="cuda")
+    kv = eng.kv
+    g = torch.Generator(device="cuda").manual_seed(1)
+    for call in range(3):  # the first call captures (and copies eagerly), the others replay
+        kv[:, 40].copy_(torch.randn(kv[:, 40].shape, generator=g, device="cuda").half())
+        kv[:, 41].zero_()
+        eng.run_rows(1, prefix_pages=pages, tokens=[3], positions=[300], slots=[41 * 16 + 9], shared_len=300,
+                     n_shared_pages=19, mask_base=300, row_full=[301], row_len=[301], cow=np.array([[40, 41, 9]]))
+        torch.cuda.synchronize()
+        assert torch.equal(kv[:, 41, :, :, :9], kv[:, 40, :, :, :9]), f"call {call}"
+    key = next(k for k in eng._graphs)
+    assert eng._graphs[key].cow
+    eng.ops.check()
