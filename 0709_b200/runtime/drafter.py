@@ -26,7 +26,6 @@ import numpy as np
 import torch
 
 from ..ops import _native
-from ..ops.attn_desc import AttnDesc
 from ..utils.transfer import ids_to_device
 from ..types import DraftPrefixState, FrontierDecodeOutput, PrefixKVView, RouteState
 from .engine import LlamaEngine, row_bucket

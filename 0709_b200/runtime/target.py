@@ -28,8 +28,6 @@ import numpy as np
 import torch
 
 from ..ops import _native
-from ..ops.attn_desc import AttnDesc, single_sequence_desc
-from ..utils import counters
 from ..utils.transfer import KernelError, ids_to_device, read_back
 from ..utils.nvtx import nvtx_range
 from ..types import PrefixState, TargetRouteScore, TargetVerifyResult, VerifyRoutePayload
