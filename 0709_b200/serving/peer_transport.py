@@ -5,10 +5,13 @@ the target on another, one process per GPU.  ``PeerChannel`` moves each
 request and response through a ring in the RECEIVER's GPU memory, mapped into
 the sender by CUDA IPC (``csrc/cuda/peer_ring.cu``): the sender's kernel stores
 the message over NVLink and publishes a sequence number with a system-scope
-release; the receiver's kernel waits with bounded acquire polls and reports a
-timeout in the ring's own error flag instead of hanging.  Between polls the
-receiving host checks that the peer process is alive, so a lost peer ends in
-``PeerLost`` after ``timeout_s``, not in a hang.
+release.  The receiving host watches that flag with 4-byte copies (the copy
+engine: no SM is held while it waits, so a GPU serving other sessions keeps all
+of its SMs) and then launches the receive kernel, which re-checks the flag with
+bounded acquire polls, copies the message out and reports a timeout in the
+ring's own error flag instead of hanging.  Between checks the host also makes
+sure that the peer process is alive, so a lost peer ends in ``PeerLost`` after
+``timeout_s``, not in a hang.
 
 ``NcclChannel`` is the library baseline: the same messages as uint8 tensors
 through ``torch.distributed`` point-to-point ``send``/``recv``.
@@ -52,7 +55,7 @@ class PeerChannel:
     """
 
     def __init__(self, *, rank: int, peer: int, device: torch.device, capacity: int = 4 << 20, group=None,
-                 timeout_s: float = 600.0, poll_ms: float = 200.0) -> None:
+                 timeout_s: float = 600.0, poll_ms: float = 200.0, idle_sleep_us: float = 20.0) -> None:
         from ..ops import _native
 
         self.ext = _native.cuda()
@@ -78,6 +81,12 @@ class PeerChannel:
         self.recv_dev = torch.empty(cap, dtype=torch.uint8, device=self.device)
         self.recv_host = torch.empty(cap, dtype=torch.uint8).pin_memory()
         self.status = torch.zeros(2, dtype=torch.int32, device=self.device)  # payload bytes, error
+        # The receive ring's sequence flag, read by a 4-byte copy (the copy engine, no SM) while a
+        # message is awaited; the bounded pop kernel is launched only once it has arrived, so a
+        # waiting receiver holds no SM of a GPU that serves other sessions meanwhile.
+        self.flag_dev = self.ext.wrap_ptr(self.ring, [1], torch.int32, self.dev_index)
+        self.flag_host = torch.zeros(1, dtype=torch.int32).pin_memory()
+        self.idle_sleep_s = float(idle_sleep_us) * 1e-6
         self.group = group
         self.sent = 0
         self.received = 0
@@ -104,10 +113,27 @@ class PeerChannel:
         self.stats["bytes_sent"] += len(data)
 
     # --------------------------------------------------------------- receive
+    def _arrived(self, seq: int) -> bool:
+        """Whether the ring's flag shows message ``seq`` (a hint; the pop kernel re-checks it)."""
+        with torch.cuda.stream(self.stream):
+            self.flag_host.copy_(self.flag_dev, non_blocking=True)
+        self.stream.synchronize()
+        return ((int(self.flag_host[0]) & 0xFFFFFFFF) - seq) & 0xFFFFFFFF < 0x80000000
+
     def recv(self, timeout_s: float | None = None) -> Any:
         limit = self.timeout_s if timeout_s is None else float(timeout_s)
         seq = (self.received + 1) & 0xFFFFFFFF
         t0 = time.monotonic()
+        polls = 0
+        while not self._arrived(seq):
+            polls += 1
+            if polls % 256 == 0:
+                if not _pid_alive(self.peer_pid):
+                    raise PeerLost(f"peer process {self.peer_pid} (rank {self.peer}) is gone")
+                if time.monotonic() - t0 > limit:
+                    raise PeerLost(f"no message from rank {self.peer} within {limit:.0f} s")
+            time.sleep(self.idle_sleep_s)
+        self.stats["idle_polls"] += polls
         while True:
             with torch.cuda.stream(self.stream):
                 self.ext.ring_pop(self.ring, seq, self.recv_dev.data_ptr(), self.recv_dev.numel(),
