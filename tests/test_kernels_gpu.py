@@ -413,3 +413,31 @@ def test_long_context_prefill_and_verify(prefill_chunk):
         assert rel_err(tv.prefix_logits, lo[0]) < 3e-2
         assert rel_err(out["logits"][nodes[path]], lo[1:]) < 3e-2
     eng.ops.check()
+
+
+@pytest.mark.parametrize("hq,hkv", [(64, 8), (8, 8), (16, 8)])
+@pytest.mark.parametrize("m", [1, 5, 40])
+def test_attention_gqa_groups(ops, hq, hkv, m):
+    """GQA groups other than 4 (70B: 8 query heads per kv head; MHA: 1; 2) against fp32, with
+    rows past one 128-row tile when the group is large."""
+    torch_ops = mod("ops.torch_ops")
+    attn_desc = mod("ops.attn_desc")
+    ps, prefix = 16, 700
+    npages = (prefix + m + ps - 1) // ps
+    kv, g = _paged_setup(torch.bfloat16, pages=npages + 2, hkv=hkv, layers=1)
+    ops.engine = type("E", (), {"kv": kv})()
+    pages = torch.randperm(npages + 2, generator=torch.Generator().manual_seed(7))[:npages].to(torch.int32).cuda()
+    words = (m + 63) // 64
+    masks = torch.zeros(m, words, dtype=torch.int64)
+    for i in range(m):  # a chain: node i sees nodes 0..i
+        for a in range(i + 1):
+            masks[i, a // 64] |= (1 << (a % 64)) if a % 64 < 63 else -(1 << 63)
+    lens = torch.full((m,), prefix + m, dtype=torch.int32, device="cuda")
+    full = torch.full((m,), prefix, dtype=torch.int32, device="cuda")
+    desc = attn_desc.single_sequence_desc(pages, lens, shared_len=prefix, mask_base=prefix, masks=masks.cuda(), full=full)
+    q = torch.randn(m, hq, 128, device="cuda", generator=g).to(torch.bfloat16)
+    out = ops.attention(q, kv[0], desc)
+    ref = torch_ops.attention(q.float(), kv[0].float(), desc)
+    torch.cuda.synchronize()
+    ops.check()
+    assert rel_err(out, ref) < 1e-2
