@@ -16,7 +16,7 @@ import os
 import threading
 from pathlib import Path
 
-import torch
+import torch  # noqa: F401  (libtorch is loaded before the extension modules that link to it)
 
 _PKG = Path(__file__).resolve().parent.parent
 _CSRC = _PKG / "csrc"
