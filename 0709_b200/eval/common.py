@@ -1,4 +1,8 @@
-"""Shared pieces of the evaluation drivers: JSONL I/O with resume, generator construction."""
+"""Shared pieces of the evaluation drivers: JSONL I/O with resume, generator construction.
+
+Counterparts in the reference's GSM8K driver: JSONL rows and resume
+(scripts/gsm8k_eval.py:62-89), the AR / ATLAS / serial generator factories (:186-315).
+"""
 
 from __future__ import annotations
 

@@ -2,7 +2,7 @@
 
 Weights are quantized per 128x128 block (one fp32 scale per block, amax/448)
 and activations per token per 128 columns (1x128), the DeepSeek-V3 style
-block scaling the BASELINE 70B configuration names.  The projection weights
+block scaling used for the single-GPU 70B target.  The projection weights
 (QKV, O, gate/up, down) are fp8; embedding, norms and the LM head stay in the
 activation dtype.  Quantization happens once at load (here, from seeded
 random bf16 weights), so ``random_weights_fp8`` and ``quantize_weights``

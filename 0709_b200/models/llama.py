@@ -11,6 +11,12 @@ Weights are stored in the layouts the sm_100a kernels consume:
 
 ``reference_forward`` is the fp32 oracle used by the numerics tests: plain
 PyTorch, contiguous K/V, an explicit boolean visibility mask.
+
+The reference runs the same architecture as Hugging Face Llama modules plus a manual
+forward around FlashInfer (src/atlas_0709/flashinfer_full_verify.py:259-335 rotary
+embedding, :1066-1122 AR decode, :1183-1231 masked tree verify) and checks it against
+transformers' own logits (:1263-1346); here the checkpoint layout is converted once at load
+(``models/loader.py``) and the oracle plays the role of that check.
 """
 
 from __future__ import annotations
@@ -86,7 +92,7 @@ class LlamaConfig:
 
 
 PRESETS: dict[str, LlamaConfig] = {
-    # BASELINE config 1 (CPU plumbing): tiny drafter and target.
+    # CPU plumbing configuration: tiny drafter and target.
     "tiny-drafter": LlamaConfig("tiny-drafter", 2, 256, 4, 2, 64, 512, 1024, rope_theta=10000.0, rope_scaling=None),
     "tiny-target": LlamaConfig("tiny-target", 4, 256, 4, 2, 64, 512, 1024, rope_theta=10000.0, rope_scaling=None),
     # Small head_dim-128 models for GPU tests (the CUDA attention kernel needs head_dim 128).

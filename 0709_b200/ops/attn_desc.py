@@ -15,6 +15,12 @@ through ``prefix_pages`` -- the kernels process that range once for all rows
 - target tree verify: ``shared_len = row_full = mask_base`` = prefix, ``row_len`` =
   prefix + nodes, ``row_mask`` = ancestor masks;
 - target AR / single sequence: ``row_full = row_len`` = position + 1.
+
+This one descriptor replaces two reference structures: FlashInfer's paged-KV metadata
+(``kv_indptr / kv_page_indices / kv_last_page_len``, built per batch from token-slot paths in
+src/atlas_0709/flashinfer_paged/paged_metadata.py:32-120) and the verify tree's dense
+``[N, prefix + N]`` custom mask (src/atlas_0709/flashinfer_full_verify.py:704-741).  The mask
+here covers the node region only, one bit per key.
 """
 
 from __future__ import annotations

@@ -6,6 +6,10 @@ thread-block cluster and needs no workspace; ``ws``/``counters`` are unused
 placeholders kept for the binding signature).  The error flag is set by kernels instead of trapping (bad index, bounded wait that
 timed out).  ``check()`` reads the flag.  If the extension cannot be loaded on
 a GPU machine, construction raises -- there is no silent fallback.
+
+The reference reaches the same operations through SGLang, FlashInfer, cuBLAS and torch
+(drafter: src/atlas_0709/flashinfer_paged/frontier.py:128-307 and sglang_runtime.py:708-798,
+1031-1092; target: src/atlas_0709/target_runtime.py:144-321, 767-851, 873-920).
 """
 
 from __future__ import annotations

@@ -3,6 +3,11 @@
 These run the CPU configuration (fp32 tiny models) and serve as the
 per-kernel numerics reference for the CUDA kernels.  KV cache layout for all
 paths: ``[layers, pages, 2 (k, v), kv_heads, page_size, head_dim]``.
+
+Reference counterparts of the op semantics: the manual Llama layer around FlashInfer
+(src/atlas_0709/flashinfer_full_verify.py:1183-1231), its suffix KV write (:1027-1044),
+``topk_logprobs`` (src/atlas_0709/flashinfer_paged/utils.py:11-25) and the tail-page
+copy-on-write of the route pool (src/atlas_0709/flashinfer_paged/sglang_runtime.py:708-798).
 """
 
 from __future__ import annotations

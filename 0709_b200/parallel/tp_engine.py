@@ -18,7 +18,7 @@ mailbox, and the workers repeat it on their shards in the same order, so the
 device-side collectives pair up.  Workers run ``serve()`` until the root
 posts stop.
 
-The reference has no tensor parallelism; this is the BASELINE 70B
+The reference has no tensor parallelism; this is the 70B-target
 configuration's TP=2/4/8 target.
 """
 

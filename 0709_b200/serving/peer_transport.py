@@ -1,6 +1,6 @@
 """Drafter <-> target transport between two GPUs: message rings in peer memory (NCCL p2p as baseline).
 
-Placement of BASELINE config 2: the drafter (and the coordinator) on one GPU,
+Split placement of the 1B + 8B configuration: the drafter (and the coordinator) on one GPU,
 the target on another, one process per GPU.  ``PeerChannel`` moves each
 request and response through a ring in the RECEIVER's GPU memory, mapped into
 the sender by CUDA IPC (``csrc/cuda/peer_ring.cu``): the sender's kernel stores

@@ -14,7 +14,7 @@ direction, bounded waits and peer-liveness checks; see
 
 The reference serves one session per target server (a global lock around
 one backend, src/atlas_0709/rpc.py:66-128); this module is this framework's
-data-parallel serving layer.
+data-parallel serving layer (several sessions per target engine, sessions spread over GPU pairs).
 """
 
 from __future__ import annotations

@@ -3,6 +3,11 @@
 The runtimes call ``h2d``/``d2h`` where a round's inputs go to the device and
 its results come back; ``CudaOps`` counts every launch of this package's
 kernels.  Benchmarks read deltas around their timed region.
+
+The reference keeps per-route-pool counters of the same kind (attention metadata builds,
+copy-on-write pages, host transfer batches and elements:
+src/atlas_0709/flashinfer_paged/sglang_runtime.py:110-126, 1094-1117); the drafter's
+``hot_path_counters()`` reports those names, these counters add the byte totals.
 """
 
 from __future__ import annotations

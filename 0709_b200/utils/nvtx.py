@@ -1,6 +1,8 @@
 """Optional NVTX ranges (``ATLAS_NVTX=1``) around serving phases, for Nsight timelines.
 
-Zero cost when disabled: the context manager does nothing.
+Zero cost when disabled: the context manager does nothing.  The reference has no NVTX
+ranges; its timing is host ``perf_counter`` spans (src/atlas_0709/edge_timeline.py:11-126),
+which ``utils/timeline.py`` keeps.
 """
 
 from __future__ import annotations

@@ -65,7 +65,10 @@ def read_back(parts: Sequence[torch.Tensor], status: torch.Tensor | None = None,
     write instead of trapping), copied with a single wait, and unpacked as numpy
     arrays of each part's shape (int64 parts come back as int64).  A nonzero flag
     is cleared and raised as ``KernelError`` before the caller can act on the
-    values, so no token computed after a device fault is committed.
+    values, so no token computed after a device fault is committed.  The reference
+    packs a depth's candidates the same way, float64 bits in int64 words
+    (src/atlas_0709/flashinfer_paged/frontier.py:192-307,
+    src/atlas_0709/flashinfer_paged/utils.py:135-151), without a status word.
     """
     words = [_as_words(p) for p in parts]
     if status is not None:

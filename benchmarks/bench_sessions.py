@@ -1,5 +1,5 @@
 #!/usr/bin/env python
-"""Multi-session serving benchmark.
+"""Multi-session serving benchmark (several sessions per target, sessions over GPU pairs).
 
     torchrun --nproc-per-node N benchmarks/bench_sessions.py --sessions 8      (N even: GPU pairs)
     python benchmarks/bench_sessions.py --sessions 2                            (one GPU)

@@ -1,5 +1,5 @@
 #!/usr/bin/env python
-"""70B-class target benchmark (BASELINE config 4): tensor-parallel or fp8 target + colocated 1B drafter.
+"""70B-class target benchmark: tensor-parallel or fp8 target + colocated 1B drafter.
 
     torchrun --nproc-per-node N benchmarks/bench_tp.py --target llama-70b --mode fused|nccl [--fp8]
 

@@ -1,5 +1,5 @@
 #!/usr/bin/env python
-"""Verify-attention microbenchmark: ancestor-masked paged tree attention.
+"""Verify-attention microbenchmark (the reference's masked-verify configuration): ancestor-masked paged tree attention.
 
     python benchmarks/bench_verify_attention.py [--prefixes 1024,4096,16384] [--flashinfer]
 

@@ -1,4 +1,4 @@
-"""End-to-end CPU plumbing (BASELINE config 1): tiny random-init Llama drafter and target.
+"""End-to-end CPU plumbing: tiny random-init Llama drafter and target.
 
 Checks against the fp32 oracle:
 - fallback on every round (threshold above any log-prob) == target greedy AR;
