@@ -1,6 +1,9 @@
 // Row-wise kernels around the GEMMs: embedding gather into the fp32 residual
 // stream, RMSNorm (fp32 stream -> activation dtype), and the fused
 // rotary-embedding + paged KV append that follows the QKV projection.
+// Reference counterparts: HF RMSNorm modules and torch rotary embedding
+// (src/atlas_0709/flashinfer_full_verify.py:259-335) followed by a separate
+// suffix KV write (:1027-1044).
 
 #include "common.cuh"
 #include "kernels.h"

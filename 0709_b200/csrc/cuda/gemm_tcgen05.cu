@@ -22,6 +22,10 @@
 // every TP rank's receive buffer over NVLink (P2P stores through CUDA IPC
 // mappings) and the grid's last CTA raises a sequence flag on each rank, so
 // the row-parallel GEMM and the all-reduce's data movement are one kernel.
+// Reference counterpart: the Llama projections run as Hugging Face nn.Linear
+// modules (cuBLAS through torch) inside the manual forward of
+// src/atlas_0709/flashinfer_full_verify.py:1183-1231 (target) and inside
+// SGLang's model runner (drafter); the reference has no tensor parallelism.
 
 #include <cuda.h>
 
