@@ -16,7 +16,9 @@ device time of the whole operation, which includes the per-depth host
 synchronisation the frontier needs; host wall time is reported beside it.
 
 Parity: reference benchmarks/bench_atlas_0709_isolated_components.py:1042-1233
-(paired ABBA protocol, synthetic verify paths with shared leading tokens).
+(paired ABBA protocol, synthetic verify paths with shared leading tokens); like it, an
+odd iteration count is rejected and the per-block ratios are summarized by their geometric
+mean (:1034, :1132-1153).
 """
 
 from __future__ import annotations
@@ -24,6 +26,7 @@ from __future__ import annotations
 import argparse
 import importlib
 import json
+import math
 import os
 import statistics
 import sys
@@ -58,6 +61,28 @@ class PerRouteTop1Selection:
         return [c for c in candidates if c.rank_in_parent == 0]
 
 
+def abba_order(i: int) -> tuple[str, str]:
+    """Arm order of iteration ``i``: A B, then B A, so each block of two iterations is A B B A."""
+    return ("a", "b") if i % 2 == 0 else ("b", "a")
+
+
+def check_pairs(n: int) -> int:
+    """Iteration counts must fill whole ABBA blocks (an odd count leaves one arm's drift unmatched)."""
+    if int(n) < 2 or int(n) % 2:
+        raise ValueError(f"--pairs must be a positive even number (whole A B B A blocks), got {n}")
+    return int(n)
+
+
+def block_ratios(a_ms, b_ms) -> dict[str, float]:
+    """B/A per ABBA block (sums over the block's two iterations of each arm) and their
+    geometric mean, minimum and maximum."""
+    if len(a_ms) != len(b_ms) or len(a_ms) % 2:
+        raise ValueError("block_ratios needs two equally long lists of whole ABBA blocks")
+    ratios = [(b_ms[j] + b_ms[j + 1]) / (a_ms[j] + a_ms[j + 1]) for j in range(0, len(a_ms), 2)]
+    return {"geometric_mean": round(math.exp(statistics.fmean(math.log(r) for r in ratios)), 4),
+            "min": round(min(ratios), 4), "max": round(max(ratios), 4), "blocks": len(ratios)}
+
+
 def timed(fn):
     torch.cuda.synchronize()
     a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -76,11 +101,12 @@ def main() -> int:
     ap.add_argument("--prefix", type=int, default=8192)
     ap.add_argument("--width", dest="k", type=int, default=3)
     ap.add_argument("--depth", dest="d", type=int, default=4)
-    ap.add_argument("--pairs", type=int, default=6)
+    ap.add_argument("--pairs", type=int, default=6, help="timed iterations per arm (even: whole ABBA blocks)")
     ap.add_argument("--dtype", default="float16")
     ap.add_argument("--skip-target", action="store_true")
     ap.add_argument("--json-out", default=None)
     args = ap.parse_args()
+    check_pairs(args.pairs)
     llama, engine_mod = pkg("models.llama"), pkg("runtime.engine")
     drafter_mod, store_mod, builders = pkg("runtime.drafter"), pkg("runtime.store"), pkg("runtime.builders")
     frontier = pkg("runtime.frontier")
@@ -130,14 +156,20 @@ def main() -> int:
                      ("batch_ar_k2", lambda: batch_ar(k * k))):  # warm-up
         run(name, fn)
     results: dict[str, list[tuple[float, float]]] = {n: [] for n in ("tree", "batch_ar_k", "forest", "batch_ar_k2")}
+    # Arm A is the matched batch AR, arm B the tree (forest); the order alternates A B / B A.
+    arms = {"a": ("batch_ar_k", lambda: batch_ar(k)), "b": ("tree", tree)}
+    arms2 = {"a": ("batch_ar_k2", lambda: batch_ar(k * k)), "b": ("forest", forest_after_tree)}
+    orders = []
     for i in range(args.pairs):
-        order = [("batch_ar_k", lambda: batch_ar(k)), ("tree", tree)]
-        order2 = [("batch_ar_k2", lambda: batch_ar(k * k)), ("forest", forest_after_tree)]
-        if i % 2:
-            order.reverse()
-            order2.reverse()
-        for name, fn in order + order2:
+        order = abba_order(i)
+        orders.append("".join(order).upper())
+        for name, fn in [arms[x] for x in order] + [arms2[x] for x in order]:
             results[name].append(run(name, fn))
+    out["orders"] = orders
+    out["tree_over_batch_ar_blocks"] = block_ratios([v[0] for v in results["batch_ar_k"]],
+                                                    [v[0] for v in results["tree"]])
+    out["forest_over_batch_ar_blocks"] = block_ratios([v[0] for v in results["batch_ar_k2"]],
+                                                      [v[0] for v in results["forest"]])
     for name, vals in results.items():
         out[f"{name}_ms"] = round(statistics.mean(v[0] for v in vals), 3)
         out[f"{name}_host_ms"] = round(statistics.mean(v[1] for v in vals), 3)

@@ -75,3 +75,20 @@ def test_round_trace_accounting():
                                                          (10.0, "Memcpy HtoD", "(round end)")}
     assert r1["gpu_busy_us"] == 30.0 and r1["gpu_idle_us"] == 70.0
     assert out["mean_gpu_idle_us"] == 55.0
+
+
+def test_abba_protocol_helpers():
+    import pytest
+
+    bench = _load("bench_isolated_components")
+    assert [bench.abba_order(i) for i in range(4)] == [("a", "b"), ("b", "a"), ("a", "b"), ("b", "a")]
+    for bad in (0, 1, 3, 7):
+        with pytest.raises(ValueError):
+            bench.check_pairs(bad)
+    assert bench.check_pairs(6) == 6
+    # Block ratios: (b0 + b1) / (a0 + a1) per block; geometric mean of 2 and 0.5 is 1.
+    r = bench.block_ratios([1.0, 1.0, 2.0, 2.0], [2.0, 2.0, 1.0, 1.0])
+    assert r["blocks"] == 2 and r["min"] == 0.5 and r["max"] == 2.0
+    assert abs(r["geometric_mean"] - 1.0) < 1e-9
+    with pytest.raises(ValueError):
+        bench.block_ratios([1.0, 2.0, 3.0], [1.0, 2.0, 3.0])
