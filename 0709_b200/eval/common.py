@@ -53,9 +53,53 @@ def optional_float(v: str) -> float | None:
     return x
 
 
+def non_negative_float(v: str) -> float:
+    x = float(v)
+    if not math.isfinite(x) or x < 0.0:
+        raise ValueError("value must be finite and non-negative")
+    return x
+
+
+def exponential_path_weights(depth: int, alpha: float) -> tuple[float, ...]:
+    """Path-score weights ``w[i] = exp(-alpha * i)`` over the ``depth`` route tokens, normalized
+    to sum to one (the reference's ``--path-weight-alpha``, scripts/gsm8k_eval.py:49-56)."""
+    if depth <= 0:
+        raise ValueError("depth must be positive")
+    raw = [math.exp(-float(alpha) * i) for i in range(int(depth))]
+    total = sum(raw)
+    return tuple(x / total for x in raw)
+
+
+# Settings of the reference's SGLang/FlashInfer runtimes (memory fraction, scheduler limits,
+# NCCL port, FlashInfer workspace) with no counterpart here: accepted so that reference command
+# lines run, and ignored.
+_INERT_FLAGS = (("--mem-fraction-static", float), ("--max-running-requests", int), ("--max-total-tokens", int),
+                ("--nccl-port", int), ("--target-workspace-mb", int))
+
+
+def add_runtime_compat_flags(p) -> None:
+    for flag, typ in _INERT_FLAGS:
+        p.add_argument(flag, type=typ, default=None,
+                       help="No-op, kept so reference command lines run (a setting of the reference's "
+                            "SGLang/FlashInfer runtime with no counterpart here).")
+    p.add_argument("--use-packed-custom-mask", action="store_true",
+                   help="No-op: the tree mask is always the attention kernel's packed ancestor bitmask.")
+    p.add_argument("--trust-remote-code", action="store_true", help="No-op: checkpoints are read as safetensors.")
+    p.add_argument("--gpu-id", type=int, default=None, help="CUDA device index (same as --device cuda:N)")
+    p.add_argument("--prefill-chunk-size", type=int, default=8192, help="tokens per prefill forward (both models)")
+    p.add_argument("--target-timeout", type=float, default=600.0, help="seconds per remote target call")
+    p.add_argument("--warmup-runs", type=int, default=1,
+                   help="untimed generations of the first pending prompt before the recorded ones")
+
+
 def add_generation_flags(p) -> None:
     p.add_argument("--backend", choices=["ar", "atlas", "atlas_serial"], required=True)
     p.add_argument("--model", required=True, help="AR model, or the ATLAS drafter (preset or checkpoint dir)")
+    add_atlas_flags(p)
+
+
+def add_atlas_flags(p) -> None:
+    """Model, tree, target-policy and drafter-sampling flags shared by every driver."""
     p.add_argument("--target-model", default=None, help="in-process target (preset or checkpoint dir)")
     p.add_argument("--target-url", default=None, help="remote target server (HTTP)")
     p.add_argument("--tokenizer", default=None, help="tokenizer.json or its directory (bytes if absent)")
@@ -73,9 +117,21 @@ def add_generation_flags(p) -> None:
     p.add_argument("--route-selection-policy", choices=["target_best", "target_sample", "first_route"],
                    default="target_best")
     p.add_argument("--generation-seed", type=int, default=0)
+    p.add_argument("--path-weight-alpha", type=non_negative_float, default=None,
+                   help="normalized exponential weights exp(-alpha * i); overrides --path-score-weights")
+    p.add_argument("--route-sampling-temperature", type=float, default=1.0,
+                   help="target route temperature of the target_sample policy (in-process target)")
+    p.add_argument("--drafter-do-sample", action="store_true",
+                   help="semantic-prefix keyed drafter sampling instead of greedy top-k")
+    p.add_argument("--drafter-temperature", type=float, default=1.0, help="proposal temperature with sampling")
+    p.add_argument("--fixed-forest-depth", type=int, default=None,
+                   help="build exactly this many forest depths per round (async backend; replay runs)")
+    p.add_argument("--validate-state-alignment", action="store_true",
+                   help="check the drafter, target and coordinator prefixes after every handoff")
     p.add_argument("--seed", type=int, default=0, help="seed of random-init presets")
     p.add_argument("--device", default=None)
     p.add_argument("--resume", action="store_true")
+    add_runtime_compat_flags(p)
 
 
 def make_generate(args):
@@ -84,7 +140,13 @@ def make_generate(args):
     from ..runtime.drafter import DrafterRuntime
     from ..runtime.engine import LlamaEngine
 
-    dev = torch.device(args.device or ("cuda" if torch.cuda.is_available() else "cpu"))
+    if args.device:
+        dev = torch.device(args.device)
+    elif getattr(args, "gpu_id", None) is not None:
+        dev = torch.device("cuda", int(args.gpu_id))
+    else:
+        dev = torch.device("cuda" if torch.cuda.is_available() else "cpu")
+    chunk = int(getattr(args, "prefill_chunk_size", 8192) or 8192)
     ctx = int(args.context_length) + int(args.max_new_tokens) + 8 * args.k * args.d + 64
     pages = 2 * math.ceil(ctx / args.page_size) + 64
 
@@ -92,7 +154,7 @@ def make_generate(args):
         return LlamaEngine(resolve_model(spec, dtype=args.dtype, device=dev, seed=seed), num_pages=pages,
                            page_size=args.page_size, max_positions=ctx + 64)
 
-    drafter = DrafterRuntime(engine(args.model, args.seed))
+    drafter = DrafterRuntime(engine(args.model, args.seed), prefill_chunk_size=chunk)
     if args.backend == "ar":
         from ..serving.ar import PagedGreedyARGenerator
 
@@ -109,16 +171,21 @@ def make_generate(args):
     from ..runtime.target import TargetVerifier
 
     if args.target_url:
-        client = RemoteTargetClient(args.target_url)
+        client = RemoteTargetClient(args.target_url, timeout=float(getattr(args, "target_timeout", 600.0)))
     else:
         if not args.target_model:
             raise SystemExit("ATLAS backends need --target-model or --target-url")
-        weights = [float(x) for x in args.path_score_weights.split(",")] if args.path_score_weights else None
+        if getattr(args, "path_weight_alpha", None) is not None:
+            weights = list(exponential_path_weights(args.d, args.path_weight_alpha))
+        else:
+            weights = [float(x) for x in args.path_score_weights.split(",")] if args.path_score_weights else None
         tv = TargetVerifier(engine(args.target_model, args.seed + 1), k=args.k, d=args.d, score_weights=weights,
                             fallback_threshold=args.fallback_threshold,
                             first_token_threshold=args.first_token_threshold,
                             fallback_ar_tokens=args.fallback_ar_tokens,
-                            route_selection_policy=args.route_selection_policy, model_name=str(args.target_model))
+                            route_selection_policy=args.route_selection_policy,
+                            route_sampling_temperature=float(getattr(args, "route_sampling_temperature", 1.0)),
+                            model_name=str(args.target_model), prefill_chunk_size=chunk)
         if dev.type == "cuda":
             tv.warm_graphs()
         client = InProcessTargetClient(tv)
@@ -128,7 +195,11 @@ def make_generate(args):
     cfg = DistributedAtlasConfig(k=args.k, d=args.d, max_new_tokens=args.max_new_tokens,
                                  eos_token_id=args.eos_token_id, fallback_ar_tokens=args.fallback_ar_tokens,
                                  generation_seed=args.generation_seed,
-                                 fixed_forest_depth=None)
+                                 drafter_do_sample=bool(getattr(args, "drafter_do_sample", False)),
+                                 drafter_temperature=float(getattr(args, "drafter_temperature", 1.0)),
+                                 fixed_forest_depth=(None if args.backend == "atlas_serial"
+                                                     else getattr(args, "fixed_forest_depth", None)),
+                                 validate_state_alignment=bool(getattr(args, "validate_state_alignment", False)))
     gen = cls(config=cfg, drafter=drafter, target_client=client)
 
     def run(ids):
@@ -136,6 +207,13 @@ def make_generate(args):
         return r.generated_token_ids, dict(r.metadata), list(r.rounds)
 
     return run
+
+
+def warm_up(generate, ids, runs: int) -> None:
+    """Untimed generations before the recorded ones (graph capture, allocator, clocks).  Every
+    ``generate`` call starts from its own prefill of both models, so nothing carries over."""
+    for _ in range(max(0, int(runs))):
+        generate(ids)
 
 
 def timed(fn, *a):

@@ -9,9 +9,11 @@ prompt's token hash so paired runs can be aligned; ``summary.json`` holds
 accuracy, throughput and the aggregated intervention statistics.
 
 Prompts: zero-shot with an answer-format instruction, or few-shot from
-``--fewshot-file`` (JSONL of question/answer pairs).  There is no network
+``--fewshot-file`` (JSONL of question/answer pairs; ``--protocol llama-8shot``
+insists on eight), optionally after ``--system-prompt``.  There is no network
 here, so the dataset must be a local file.  Parity: reference
-scripts/gsm8k_eval.py (backends, resume, interventions, summary).
+scripts/gsm8k_eval.py (backends, resume, interventions, summary; its flags,
+:318-422, are accepted -- the SGLang memory and scheduler settings as no-ops).
 """
 
 from __future__ import annotations
@@ -24,7 +26,7 @@ from pathlib import Path
 from ..serving.prompts import decode, encode, load_tokenizer
 from ..utils.interventions import aggregate_prediction_interventions, summarize_generation_interventions
 from .common import add_generation_flags, append_jsonl, done_indices, make_generate, read_jsonl, rows_summary, \
-    timed, token_ids_sha256
+    timed, token_ids_sha256, warm_up
 
 GOLD_RE = re.compile(r"####\s*([^\n\r]+)")
 FINAL_RE = re.compile(r"final answer is\s*\$?\s*(-?[\d,]*\.?\d+)", re.IGNORECASE)
@@ -58,8 +60,8 @@ def extract(text: str, *, strict: bool = False) -> str | None:
     return normalize(nums[-1]) if nums else None
 
 
-def build_prompt(question: str, fewshot: list[dict]) -> str:
-    parts = [INSTRUCTION, ""]
+def build_prompt(question: str, fewshot: list[dict], system_prompt: str = "") -> str:
+    parts = ([system_prompt, ""] if system_prompt else []) + [INSTRUCTION, ""]
     for ex in fewshot:
         parts += [f"Question: {ex['question']}", f"Answer: {ex['answer']}", ""]
     parts += [f"Question: {question}", "Answer:"]
@@ -76,6 +78,10 @@ def build_parser() -> argparse.ArgumentParser:
     p.add_argument("--end", type=int, default=None)
     p.add_argument("--max-examples", type=int, default=None)
     p.add_argument("--strict-marker", action="store_true", help="require 'The final answer is'")
+    p.add_argument("--protocol", choices=["auto", "llama-8shot", "zero-shot"], default="auto",
+                   help="llama-8shot: the eight chain-of-thought exemplars of --fewshot-file; zero-shot: none; "
+                        "auto: few-shot exactly when --fewshot-file is given")
+    p.add_argument("--system-prompt", default="", help="text placed before the instruction")
     return p
 
 
@@ -87,16 +93,21 @@ def main(argv=None) -> int:
     rows = read_jsonl(args.data_file)[args.start:args.end]
     if args.max_examples is not None:
         rows = rows[: args.max_examples]
-    fewshot = read_jsonl(args.fewshot_file) if args.fewshot_file else []
+    fewshot = read_jsonl(args.fewshot_file) if args.fewshot_file and args.protocol != "zero-shot" else []
+    if args.protocol == "llama-8shot" and len(fewshot) != 8:
+        raise SystemExit("--protocol llama-8shot needs the eight exemplars as JSONL in --fewshot-file "
+                         f"(got {len(fewshot)}); there is no network here to fetch them")
     tok = load_tokenizer(args.tokenizer)
     done = done_indices(pred_path) if args.resume else set()
     if not args.resume and pred_path.exists():
         pred_path.unlink()
     generate = make_generate(args)
-    for i, row in enumerate(rows, start=args.start):
-        if i in done:
-            continue
-        ids = encode(tok, build_prompt(str(row["question"]), fewshot))
+    pending = [(i, row) for i, row in enumerate(rows, start=args.start) if i not in done]
+    if pending:
+        warm_up(generate, encode(tok, build_prompt(str(pending[0][1]["question"]), fewshot, args.system_prompt)),
+                args.warmup_runs)
+    for i, row in pending:
+        ids = encode(tok, build_prompt(str(row["question"]), fewshot, args.system_prompt))
         (gen_ids, meta, rounds), secs = timed(generate, ids)
         text = decode(tok, gen_ids) or ""
         pred, gold = extract(text, strict=args.strict_marker), gold_answer(row)

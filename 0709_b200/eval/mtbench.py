@@ -2,6 +2,7 @@
 
     python -m 0709_b200.eval.mtbench generate --backend atlas --questions q.jsonl --output-dir out ...
     python -m 0709_b200.eval.mtbench judge --answers out/answers.jsonl --judge-url https://.../v1/chat/completions
+    python -m 0709_b200.eval.mtbench --drafter-model ... --target-url ... --questions-file q.jsonl --output-dir out
 
 ``generate`` reads local question records (``question_id``, ``category``,
 ``turns``: list of user turns), runs each conversation turn by turn (the
@@ -14,8 +15,13 @@ to an OpenAI-compatible chat-completions endpoint (API key from
 and writes judgments plus a per-category average.  This machine has no
 network, so ``judge`` only runs where the endpoint is reachable.
 
-Parity: reference scripts/mtbench_deepseek_eval.py (generate_answers,
-rounds_detail, judge client).
+The third form is the reference's one command (generate, then judge; ``--skip-*`` and
+``--resume-*`` per phase; ``--ar-generations`` grades AR answers in the same run).  The judge
+retries HTTP 429 / 5xx and connection errors, can grade each answer ``--judge-repeats`` times,
+and sends the DeepSeek ``thinking`` / ``reasoning_effort`` fields when they are given.
+
+Parity: reference scripts/mtbench_deepseek_eval.py (generate_answers :314-542,
+rounds_detail :164-207, judge client :545-662, flags :1299-1383).
 """
 
 from __future__ import annotations
@@ -25,12 +31,16 @@ import json
 import os
 import re
 import statistics
+import sys
+import time
+import urllib.error
 import urllib.request
+from dataclasses import dataclass
 from pathlib import Path
 
 from ..serving.prompts import decode, encode, load_tokenizer
 from ..utils.interventions import summarize_generation_interventions
-from .common import add_generation_flags, append_jsonl, make_generate, read_jsonl, timed
+from .common import add_atlas_flags, add_generation_flags, append_jsonl, make_generate, read_jsonl, timed, warm_up
 
 RATING_RE = re.compile(r"\[\[(\d+(?:\.\d+)?)\]\]")
 JUDGE_PROMPT = (
@@ -53,9 +63,16 @@ def compact_rounds(rounds) -> list[dict]:
     return out
 
 
+def select_questions(qs: list[dict], args) -> list[dict]:
+    """``--question-start`` / ``--question-end`` slice, then at most ``--max-questions``."""
+    qs = qs[int(getattr(args, "question_start", 0) or 0): getattr(args, "question_end", None)]
+    n = getattr(args, "max_questions", None)
+    return qs[: int(n)] if n is not None else qs
+
+
 def cmd_generate(args) -> int:
     tok = load_tokenizer(args.tokenizer)
-    qs = read_jsonl(args.questions)
+    qs = select_questions(read_jsonl(args.questions), args)
     out = Path(args.output_dir)
     out.mkdir(parents=True, exist_ok=True)
     path = out / "answers.jsonl"
@@ -63,12 +80,15 @@ def cmd_generate(args) -> int:
     if not args.resume and path.exists():
         path.unlink()
     generate = make_generate(args)
-    for q in qs:
-        if q["question_id"] in done:
-            continue
-        history: list[int] = []
+    system = f"System: {args.system_prompt}\n" if getattr(args, "system_prompt", "") else ""
+    pending = [q for q in qs if q["question_id"] not in done]
+    if pending:
+        warm_up(generate, encode(tok, f"{system}User: {pending[0]['turns'][0]}\nAssistant:"), args.warmup_runs)
+    for q in pending:
+        history: list[int] = encode(tok, system) if system else []
         turns = []
-        for t, user in enumerate(q["turns"]):
+        user_turns = q["turns"][:1] if getattr(args, "turn_mode", "conversation") == "first" else q["turns"]
+        for t, user in enumerate(user_turns):
             ids = history + encode(tok, f"User: {user}\nAssistant:")
             (gen, meta, rounds), secs = timed(generate, ids)
             text = decode(tok, gen) or ""
@@ -85,59 +105,234 @@ def cmd_generate(args) -> int:
     return 0
 
 
-def judge_one(url: str, model: str, key: str | None, question: str, answer: str, timeout: float) -> tuple[float | None, str]:
-    body = {"model": model, "temperature": 0.0,
-            "messages": [{"role": "user", "content": JUDGE_PROMPT.format(question=question, answer=answer)}]}
-    req = urllib.request.Request(url, data=json.dumps(body).encode(), method="POST",
-                                 headers={"content-type": "application/json",
-                                          **({"authorization": f"Bearer {key}"} if key else {})})
-    with urllib.request.urlopen(req, timeout=timeout) as r:
-        content = json.loads(r.read().decode())["choices"][0]["message"]["content"]
-    m = RATING_RE.search(content)
-    return (float(m.group(1)) if m else None), content
+@dataclass(frozen=True)
+class JudgeSettings:
+    """One chat-completions endpoint and how to call it.  ``thinking`` / ``reasoning_effort`` are
+    DeepSeek request fields (sent only when set); HTTP 429 / 5xx and connection errors are
+    retried ``retries`` times with exponentially growing delays."""
+
+    url: str
+    model: str
+    key: str | None = None
+    timeout: float = 120.0
+    retries: int = 0
+    retry_delay: float = 2.0
+    max_tokens: int | None = None
+    thinking: str | None = None
+    reasoning_effort: str | None = None
+
+
+def chat_completions_url(base: str) -> str:
+    base = base.rstrip("/")
+    return base if base.endswith("/chat/completions") else f"{base}/chat/completions"
+
+
+def parse_rating(content: str) -> float | None:
+    """``[[r]]`` as the grading prompt asks, else the ``score`` of a JSON object answer."""
+    m = RATING_RE.search(content or "")
+    if m:
+        return float(m.group(1))
+    text = (content or "").strip().strip("`")
+    text = text[4:] if text.startswith("json") else text
+    try:
+        obj = json.loads(text)
+    except ValueError:
+        return None
+    score = obj.get("score") if isinstance(obj, dict) else None
+    return float(score) if isinstance(score, (int, float)) and not isinstance(score, bool) else None
+
+
+def judge_one(s: JudgeSettings, question: str, answer: str) -> tuple[float | None, str]:
+    body: dict = {"model": s.model, "temperature": 0.0, "stream": False,
+                  "messages": [{"role": "user", "content": JUDGE_PROMPT.format(question=question, answer=answer)}]}
+    if s.max_tokens:
+        body["max_tokens"] = int(s.max_tokens)
+    if s.thinking:
+        body["thinking"] = {"type": s.thinking}
+        if s.thinking == "enabled" and s.reasoning_effort:
+            body["reasoning_effort"] = s.reasoning_effort
+    data = json.dumps(body, ensure_ascii=False).encode("utf-8")
+    headers = {"content-type": "application/json; charset=utf-8", **({"authorization": f"Bearer {s.key}"} if s.key else {})}
+    last: Exception | None = None
+    for attempt in range(int(s.retries) + 1):
+        try:
+            req = urllib.request.Request(s.url, data=data, method="POST", headers=headers)
+            with urllib.request.urlopen(req, timeout=s.timeout) as r:
+                content = json.loads(r.read().decode("utf-8"))["choices"][0]["message"]["content"]
+            if not content:
+                raise ValueError("empty judge content")
+            return parse_rating(content), content
+        except urllib.error.HTTPError as exc:
+            last = exc
+            if exc.code != 429 and not 500 <= exc.code < 600:
+                raise
+        except (urllib.error.URLError, TimeoutError, KeyError, IndexError, ValueError) as exc:
+            last = exc
+        if attempt < int(s.retries):
+            time.sleep(float(s.retry_delay) * 2 ** attempt)
+    raise RuntimeError(f"judge failed after {int(s.retries) + 1} attempts: {last!r}")
+
+
+def _answer_sets(args) -> list[tuple[str, list[dict]]]:
+    """(label, answer records) of every answer file to grade: ``--answers`` and, with
+    ``--ar-generations``, the AR answers (records of ``generate --backend ar``; ``--ar-run-id``
+    keeps the records whose ``run_id`` matches).  Each answer is graded on its own, so the
+    judge never sees which system wrote it."""
+    sets = [("answers", read_jsonl(args.answers))]
+    extra = getattr(args, "ar_generations", None)
+    if extra:
+        recs = read_jsonl(extra)
+        run = getattr(args, "ar_run_id", None)
+        if run is not None:
+            recs = [r for r in recs if str(r.get("run_id")) == str(run)]
+            if not recs:
+                raise SystemExit(f"--ar-run-id {run}: no record of {extra} carries that run_id")
+        groups: dict[str, list[dict]] = {}
+        for r in recs:
+            groups.setdefault(f"ar:{r.get('model', 'unknown')}", []).append(r)
+        sets += sorted(groups.items())
+    return sets
 
 
 def cmd_judge(args) -> int:
-    answers = read_jsonl(args.answers)
     qs = {q["question_id"]: q for q in read_jsonl(args.questions)}
-    key = os.environ.get(args.api_key_env) if args.api_key_env else None
+    settings = JudgeSettings(
+        url=args.judge_url or chat_completions_url(args.judge_base_url), model=args.judge_model,
+        key=os.environ.get(args.api_key_env) if args.api_key_env else None, timeout=args.timeout,
+        retries=args.judge_retries, retry_delay=args.judge_retry_delay, max_tokens=args.judge_max_tokens,
+        thinking=args.judge_thinking, reasoning_effort=args.judge_reasoning_effort)
     out = Path(args.output or (Path(args.answers).parent / "judgments.jsonl"))
-    scores: dict[str, list[float]] = {}
+    done: set[tuple] = set()
+    if out.exists():
+        if getattr(args, "resume", False):
+            done = {(str(r.get("source", "answers")), r["question_id"], r["turn"], r.get("repeat", 0))
+                    for r in read_jsonl(out) if r.get("rating") is not None}
+        else:
+            out.unlink()
+    scores: dict[str, dict[str, list[float]]] = {}
     failures = 0
-    for a in answers:
-        q = qs[a["question_id"]]
-        for t in a["turns"]:
-            try:
-                rating, raw = judge_one(args.judge_url, args.judge_model, key, q["turns"][t["turn"]], t["answer"],
-                                        args.timeout)
-            except Exception as exc:  # noqa: BLE001 - recorded, the run continues
-                rating, raw = None, f"error: {exc!r}"
-                failures += 1
-            append_jsonl(out, {"question_id": a["question_id"], "turn": t["turn"], "rating": rating, "judgment": raw})
-            if rating is not None:
-                scores.setdefault(str(a.get("category")), []).append(rating)
-    allv = [v for vs in scores.values() for v in vs]
-    print(json.dumps({"mean": statistics.fmean(allv) if allv else None, "judged": len(allv), "failures": failures,
-                      "by_category": {c: statistics.fmean(v) for c, v in sorted(scores.items())}}))
+    for label, answers in _answer_sets(args):
+        for a in answers:
+            q = qs[a["question_id"]]
+            for t in a["turns"]:
+                for rep in range(max(1, int(args.judge_repeats))):
+                    key = (label, a["question_id"], t["turn"], rep)
+                    if key in done:
+                        continue
+                    try:
+                        rating, raw = judge_one(settings, q["turns"][t["turn"]], t["answer"])
+                    except Exception as exc:  # noqa: BLE001 - recorded, the run continues
+                        rating, raw = None, f"error: {exc!r}"
+                        failures += 1
+                    append_jsonl(out, {"source": label, "question_id": a["question_id"], "turn": t["turn"],
+                                       "repeat": rep, "rating": rating, "judgment": raw})
+    for r in read_jsonl(out) if out.exists() else []:
+        if r.get("rating") is not None:
+            cat = str(qs.get(r["question_id"], {}).get("category"))
+            scores.setdefault(str(r.get("source", "answers")), {}).setdefault(cat, []).append(float(r["rating"]))
+    summary = {}
+    for label, cats in scores.items():
+        allv = [v for vs in cats.values() for v in vs]
+        summary[label] = {"mean": statistics.fmean(allv), "judged": len(allv),
+                          "by_category": {c: statistics.fmean(v) for c, v in sorted(cats.items())}}
+    main_set = summary.get("answers", {})
+    print(json.dumps({"mean": main_set.get("mean"), "judged": main_set.get("judged", 0), "failures": failures,
+                      "by_category": main_set.get("by_category", {}), "sources": summary}))
     return 0
 
 
+def add_judge_flags(j, *, flat: bool) -> None:
+    if not flat:
+        j.add_argument("--judge-url", default=None, help="full chat-completions URL (or --judge-base-url)")
+        j.add_argument("--api-key-env", default="JUDGE_API_KEY")
+        j.add_argument("--timeout", type=float, default=120.0)
+        j.add_argument("--output", default=None)
+        j.add_argument("--resume", action="store_true", help="keep judgments already made (with a rating)")
+        j.add_argument("--ar-generations", default=None, help="AR answers to grade in the same run")
+        j.add_argument("--ar-run-id", default=None)
+    j.add_argument("--judge-base-url", default="https://api.deepseek.com")
+    j.add_argument("--judge-model", default="deepseek-chat")
+    j.add_argument("--judge-thinking", choices=["enabled", "disabled"], default=None)
+    j.add_argument("--judge-reasoning-effort", choices=["high", "max"], default=None)
+    j.add_argument("--judge-max-tokens", type=int, default=None)
+    j.add_argument("--judge-retries", type=int, default=0)
+    j.add_argument("--judge-retry-delay", type=float, default=2.0)
+    j.add_argument("--judge-repeats", type=int, default=1)
+
+
+def flat_parser() -> argparse.ArgumentParser:
+    """The reference's one-command form (scripts/mtbench_deepseek_eval.py:1299-1383): generate,
+    then judge, each skippable and resumable."""
+    p = argparse.ArgumentParser(description="MT-Bench generation + judging in one command")
+    p.add_argument("--drafter-model", required=True, help="ATLAS drafter (preset or checkpoint dir)")
+    add_atlas_flags(p)
+    p.add_argument("--execution-mode", choices=["async", "serial"], default="async")
+    p.add_argument("--questions-file", required=True, help="local MT-Bench question JSONL")
+    p.add_argument("--questions-url", default=None, help="not fetched: there is no network here")
+    p.add_argument("--download-timeout", type=float, default=60.0, help="No-op (nothing is downloaded).")
+    p.add_argument("--output-dir", required=True)
+    add_question_flags(p)
+    p.add_argument("--skip-generate", action="store_true")
+    p.add_argument("--resume-generate", action="store_true")
+    p.add_argument("--skip-judge", action="store_true")
+    p.add_argument("--resume-judge", action="store_true")
+    p.add_argument("--ar-generations", default=None)
+    p.add_argument("--ar-run-id", default=None)
+    p.add_argument("--deepseek-api-key-env", default="DEEPSEEK_API_KEY")
+    p.add_argument("--judge-timeout", type=float, default=180.0)
+    add_judge_flags(p, flat=True)
+    # The reference's defaults for this form: longer answers and context, a patient judge.
+    p.set_defaults(max_new_tokens=1024, context_length=16384, judge_max_tokens=4096, judge_retries=4)
+    return p
+
+
+def add_question_flags(p) -> None:
+    p.add_argument("--question-start", type=int, default=0)
+    p.add_argument("--question-end", type=int, default=None)
+    p.add_argument("--max-questions", type=int, default=None)
+    p.add_argument("--turn-mode", choices=["first", "conversation"], default="conversation")
+    p.add_argument("--system-prompt", default="")
+
+
+def run_flat(argv) -> int:
+    a = flat_parser().parse_args(argv)
+    if not Path(a.questions_file).exists():
+        raise SystemExit(f"{a.questions_file}: not found (questions are not downloaded; there is no network here)")
+    out = Path(a.output_dir)
+    if not a.skip_generate:
+        g = argparse.Namespace(**vars(a))
+        g.backend = "atlas_serial" if a.execution_mode == "serial" else "atlas"
+        g.model, g.questions, g.resume = a.drafter_model, a.questions_file, a.resume_generate
+        rc = cmd_generate(g)
+        if rc:
+            return rc
+    if a.skip_judge:
+        return 0
+    j = argparse.Namespace(**vars(a))
+    j.answers, j.questions, j.output = str(out / "answers.jsonl"), a.questions_file, None
+    j.judge_url, j.api_key_env, j.timeout, j.resume = None, a.deepseek_api_key_env, a.judge_timeout, a.resume_judge
+    return cmd_judge(j)
+
+
 def main(argv=None) -> int:
-    p = argparse.ArgumentParser(description="MT-Bench generation and judging")
+    argv = list(sys.argv[1:] if argv is None else argv)
+    if not argv or argv[0] not in ("generate", "judge", "-h", "--help"):
+        return run_flat(argv)
+    p = argparse.ArgumentParser(description="MT-Bench generation and judging (or the reference's one-command "
+                                            "form: --drafter-model ... --questions-file ... --output-dir ...)")
     sub = p.add_subparsers(dest="cmd", required=True)
     g = sub.add_parser("generate")
     add_generation_flags(g)
     g.add_argument("--questions", required=True)
     g.add_argument("--output-dir", required=True)
+    add_question_flags(g)
     j = sub.add_parser("judge")
     j.add_argument("--answers", required=True)
     j.add_argument("--questions", required=True)
-    j.add_argument("--judge-url", required=True)
-    j.add_argument("--judge-model", default="deepseek-chat")
-    j.add_argument("--api-key-env", default="JUDGE_API_KEY")
-    j.add_argument("--timeout", type=float, default=120.0)
-    j.add_argument("--output", default=None)
+    add_judge_flags(j, flat=False)
     args = p.parse_args(argv)
+    if args.cmd == "judge" and not (args.judge_url or args.judge_base_url):
+        p.error("judge needs --judge-url or --judge-base-url")
     return cmd_generate(args) if args.cmd == "generate" else cmd_judge(args)
 
 

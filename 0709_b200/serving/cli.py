@@ -21,6 +21,10 @@ def build_parser() -> argparse.ArgumentParser:
     p.add_argument("--max-new-tokens", type=int, default=32)
     p.add_argument("--eos-token-id", type=int, default=None)
     p.add_argument("--prompt-token-ids", default="1,2,3,4")
+    p.add_argument("--prompt", default=None,
+                   help="prompt text (model backends): encoded with --tokenizer, or as UTF-8 bytes without one")
+    p.add_argument("--tokenizer", default=None, help="tokenizer.json or its directory")
+    p.add_argument("--trust-remote-code", action="store_true", help="No-op: checkpoints are read as safetensors.")
     p.add_argument("--drafter-model", default="tiny-drafter")
     p.add_argument("--target-model", default="tiny-target")
     p.add_argument("--dtype", choices=["float16", "bfloat16", "float32"], default="float32")
@@ -68,11 +72,25 @@ def result_to_jsonable(res) -> dict[str, object]:
     }
 
 
+def prompt_ids(args) -> list[int]:
+    if args.prompt is None:
+        return parse_ids(args.prompt_token_ids)
+    if args.backend == "mock":
+        raise SystemExit("--prompt needs a model backend (recompute/hf); the mock backends take --prompt-token-ids")
+    from .prompts import encode, load_tokenizer
+
+    ids = encode(load_tokenizer(args.tokenizer), args.prompt)
+    if not ids:
+        raise SystemExit("--prompt encoded to no tokens")
+    return ids
+
+
 def main(argv=None) -> int:
     args = build_parser().parse_args(argv)
+    ids = prompt_ids(args)
     drafter, target = make_backends(args)
     cfg = AtlasCleanConfig(k=args.k, d=args.d, max_new_tokens=args.max_new_tokens, eos_token_id=args.eos_token_id)
-    res = AtlasCleanGenerator(config=cfg, drafter=drafter, target=target).generate(parse_ids(args.prompt_token_ids))
+    res = AtlasCleanGenerator(config=cfg, drafter=drafter, target=target).generate(ids)
     print(json.dumps({
         "config": {"k": cfg.k, "d": cfg.d, "max_new_tokens": cfg.max_new_tokens, "eos_token_id": cfg.eos_token_id,
                    "tree_decode": f"ordinary_batch_{cfg.k}", "forest_decode": f"ordinary_batch_{cfg.k * cfg.k}",

@@ -65,6 +65,18 @@ def test_clean_cli_mock(capsys):
     assert out["config"]["forest_decode"] == "ordinary_batch_4"
 
 
+def test_clean_cli_prompt_text(capsys):
+    import pytest
+
+    cli = mod("serving.cli")
+    assert cli.main(["--backend", "recompute", "--max-new-tokens", "3", "--k", "2", "--d", "2", "--prompt", "hi!",
+                     "--trust-remote-code"]) == 0
+    out = json.loads(capsys.readouterr().out)
+    assert out["result"]["prompt_token_ids"] == list(b"hi!") and len(out["result"]["generated_token_ids"]) == 3
+    with pytest.raises(SystemExit):
+        cli.main(["--backend", "mock", "--prompt", "hi"])
+
+
 def test_clean_cli_recompute_matches_paged_greedy_contract(capsys):
     # k=1: the clean controller's single route is drafter greedy; with the
     # recompute backends the committed tokens are the target's choice among one

@@ -73,3 +73,108 @@ def test_mtbench_generate_and_judge_against_local_endpoint(tmp_path):
         srv.shutdown()
     j = [json.loads(l) for l in (out / "judgments.jsonl").read_text().splitlines()]
     assert [x["rating"] for x in j] == [7.0, 7.0]
+
+
+class _Judge:
+    """A local chat-completions endpoint: answers ``[[7]]``, first failing ``fail_first`` calls with 503."""
+
+    def __init__(self, fail_first: int = 0) -> None:
+        self.bodies: list[dict] = []
+        self.fail_first = fail_first
+        owner = self
+
+        class H(BaseHTTPRequestHandler):
+            def do_POST(self):  # noqa: N802
+                owner.bodies.append(json.loads(self.rfile.read(int(self.headers["content-length"]))))
+                if owner.fail_first > 0:
+                    owner.fail_first -= 1
+                    self.send_response(503)
+                    self.send_header("content-length", "0")
+                    self.end_headers()
+                    return
+                body = json.dumps({"choices": [{"message": {"content": "ok. Rating: [[7]]"}}]}).encode()
+                self.send_response(200)
+                self.send_header("content-type", "application/json")
+                self.send_header("content-length", str(len(body)))
+                self.end_headers()
+                self.wfile.write(body)
+
+            def log_message(self, *a):
+                pass
+
+        self.srv = HTTPServer(("127.0.0.1", 0), H)
+        self.base = f"http://127.0.0.1:{self.srv.server_address[1]}/v1"
+        threading.Thread(target=self.srv.serve_forever, daemon=True).start()
+
+    def close(self) -> None:
+        self.srv.shutdown()
+
+
+def test_generation_flag_helpers():
+    c = mod("eval.common")
+    w = c.exponential_path_weights(4, 0.5)
+    assert abs(sum(w) - 1.0) < 1e-12 and all(a > b for a, b in zip(w, w[1:]))
+    assert c.exponential_path_weights(3, 0.0) == (1 / 3, 1 / 3, 1 / 3)
+    mt = mod("eval.mtbench")
+    assert mt.chat_completions_url("https://x/v1/") == "https://x/v1/chat/completions"
+    assert mt.chat_completions_url("https://x/v1/chat/completions") == "https://x/v1/chat/completions"
+    assert mt.parse_rating("Rating: [[8.5]]") == 8.5
+    assert mt.parse_rating('```json\n{"score": 6, "reason": "r"}\n```') == 6.0
+    assert mt.parse_rating("no score") is None
+
+
+def test_gsm8k_reference_flags(tmp_path):
+    import pytest
+
+    g = mod("eval.gsm8k")
+    data = tmp_path / "test.jsonl"
+    data.write_text(json.dumps({"question": "What is 1+1?", "answer": "x\n#### 2"}) + "\n")
+    out = tmp_path / "out"
+    ref_flags = ["--path-weight-alpha", "0.3", "--fixed-forest-depth", "1", "--validate-state-alignment",
+                 "--drafter-do-sample", "--drafter-temperature", "0.8", "--mem-fraction-static", "0.75",
+                 "--max-running-requests", "32", "--nccl-port", "29500", "--warmup-runs", "0",
+                 "--system-prompt", "Be brief.", "--protocol", "zero-shot", "--use-packed-custom-mask"]
+    assert g.main(_flags(tmp_path, "atlas") + ["--data-file", str(data), "--output-dir", str(out)] + ref_flags) == 0
+    assert json.loads((out / "summary.json").read_text())["samples"] == 1
+    with pytest.raises(SystemExit):
+        g.main(_flags(tmp_path, "atlas") + ["--data-file", str(data), "--output-dir", str(out),
+                                              "--protocol", "llama-8shot"])
+
+
+def test_mtbench_reference_one_command_form(tmp_path, monkeypatch):
+    mt = mod("eval.mtbench")
+    q = tmp_path / "q.jsonl"
+    q.write_text("\n".join(json.dumps({"question_id": i, "category": "c", "turns": ["hi", "more?"]})
+                           for i in range(3)) + "\n")
+    out = tmp_path / "mt"
+    judge = _Judge(fail_first=1)
+    monkeypatch.setenv("TEST_JUDGE_KEY", "k")
+    flags = ["--drafter-model", "tiny-drafter", "--target-model", "tiny-target", "--dtype", "float32",
+             "--page-size", "4", "--max-new-tokens", "4", "--k", "2", "--d", "2", "--path-score-weights", "",
+             "--device", "cpu", "--context-length", "256", "--questions-file", str(q), "--output-dir", str(out),
+             "--max-questions", "2", "--turn-mode", "first", "--execution-mode", "serial", "--warmup-runs", "0",
+             "--judge-base-url", judge.base, "--deepseek-api-key-env", "TEST_JUDGE_KEY", "--judge-retry-delay", "0",
+             "--judge-thinking", "enabled", "--judge-reasoning-effort", "high", "--judge-repeats", "2"]
+    try:
+        assert mt.main(flags) == 0
+        answers = [json.loads(l) for l in (out / "answers.jsonl").read_text().splitlines()]
+        assert [a["question_id"] for a in answers] == [0, 1] and all(len(a["turns"]) == 1 for a in answers)
+        assert answers[0]["backend"] == "atlas_serial"
+        js = [json.loads(l) for l in (out / "judgments.jsonl").read_text().splitlines()]
+        assert len(js) == 4 and {x["rating"] for x in js} == {7.0} and {x["repeat"] for x in js} == {0, 1}
+        # One 503 retried; the DeepSeek fields and the token limit ride in every request.
+        assert len(judge.bodies) == 5
+        assert judge.bodies[-1]["thinking"] == {"type": "enabled"} and judge.bodies[-1]["reasoning_effort"] == "high"
+        assert judge.bodies[-1]["max_tokens"] == 4096
+        # Resume: nothing generated or judged again; AR answers are graded beside them.
+        ar = tmp_path / "ar.jsonl"
+        ar.write_text(json.dumps({"question_id": 0, "model": "ar_1b", "run_id": "r1",
+                                  "turns": [{"turn": 0, "answer": "x"}]}) + "\n")
+        n = len(judge.bodies)
+        assert mt.main(flags + ["--skip-generate", "--resume-judge", "--ar-generations", str(ar),
+                                "--ar-run-id", "r1"]) == 0
+        assert len(judge.bodies) == n + 2
+        js = [json.loads(l) for l in (out / "judgments.jsonl").read_text().splitlines()]
+        assert sorted({x["source"] for x in js}) == ["answers", "ar:ar_1b"]
+    finally:
+        judge.close()
