@@ -92,3 +92,16 @@ def test_abba_protocol_helpers():
     assert abs(r["geometric_mean"] - 1.0) < 1e-9
     with pytest.raises(ValueError):
         bench.block_ratios([1.0, 2.0, 3.0], [1.0, 2.0, 3.0])
+
+
+def test_full_verify_benchmark_aligns_on_cpu(capsys):
+    bench = _load("bench_full_verify")
+    assert bench.main(["--model", "tiny-target", "--device", "cpu", "--dtype", "float32", "--prefix-len", "32",
+                       "--page-size", "4", "--k", "3", "--d", "3", "--warmup", "0", "--iters", "1",
+                       "--alignment-atol", "1e-4", "--alignment-rtol", "1e-4", "--fail-on-logit-mismatch",
+                       "--use-packed-custom-mask", "--flashinfer-backend", "auto"]) == 0
+    out = json.loads(capsys.readouterr().out.strip().splitlines()[-1])
+    assert out["logits_aligned"] and out["masked_verify"]["nodes"] == 7 and out["linear_verify"]["nodes"] == 9
+    assert out["logit_alignment"]["masked_tree"]["top1_match_rate"] == 1.0
+    assert bench.prefix_tokens(bench.build_parser().parse_args(
+        ["--model", "m", "--prefix-len", "5", "--prompt-token-ids", "1,2"])) == [1, 2, 1, 2, 1]
