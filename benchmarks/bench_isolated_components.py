@@ -2,6 +2,8 @@
 """Isolated component benchmark: tree / forest vs matched batch AR, target AR1 and tree verify.
 
     python benchmarks/bench_isolated_components.py --prefix 8192 --pairs 6
+    python benchmarks/bench_isolated_components.py --drafter-model llama-1b --target-model llama-8b \
+        --prefix-len 8192 --k 3 --d 4 --iters 6 --warmup 1 --pair-order-seed 0   # the reference's flags
 
 Drafter side (decode-ready, d depths each):
 * ``tree``: k stage-1 routes, global top-k per depth;
@@ -83,7 +85,14 @@ def block_ratios(a_ms, b_ms) -> dict[str, float]:
             "min": round(min(ratios), 4), "max": round(max(ratios), 4), "blocks": len(ratios)}
 
 
-def timed(fn):
+def timed(fn, cuda: bool = True):
+    """(device ms, host ms) of ``fn``: CUDA events on the current stream with a synchronize on
+    both sides (wall time twice on CPU)."""
+    if not cuda:
+        t0 = time.perf_counter()
+        fn()
+        ms = (time.perf_counter() - t0) * 1e3
+        return ms, ms
     torch.cuda.synchronize()
     a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     t0 = time.perf_counter()
@@ -94,35 +103,76 @@ def timed(fn):
     return a.elapsed_time(b), (time.perf_counter() - t0) * 1e3
 
 
-def main() -> int:
-    ap = argparse.ArgumentParser()
-    ap.add_argument("--drafter", default="llama-1b")
-    ap.add_argument("--target", default="llama-8b")
-    ap.add_argument("--prefix", type=int, default=8192)
-    ap.add_argument("--width", dest="k", type=int, default=3)
-    ap.add_argument("--depth", dest="d", type=int, default=4)
-    ap.add_argument("--pairs", type=int, default=6, help="timed iterations per arm (even: whole ABBA blocks)")
+# Settings of the reference's SGLang runtime with no counterpart here (accepted, ignored).
+_INERT = (("--mem-fraction-static", float), ("--max-running-requests", int), ("--max-total-tokens", int),
+          ("--nccl-port", int), ("--prefill-chunk-size", int), ("--workspace-mb", int))
+
+
+def build_parser() -> argparse.ArgumentParser:
+    ap = argparse.ArgumentParser(description="Tree / forest vs matched batch AR (paired ABBA), target AR1, AR2, "
+                                             "linear and masked verify.  The reference's flag names are accepted.")
+    ap.add_argument("--drafter", "--drafter-model", dest="drafter", default="llama-1b")
+    ap.add_argument("--target", "--target-model", dest="target", default="llama-8b")
+    ap.add_argument("--prefix", "--prefix-len", dest="prefix", type=int, default=8192)
+    ap.add_argument("--width", "--k", dest="k", type=int, default=3)
+    ap.add_argument("--depth", "--d", dest="d", type=int, default=4)
+    ap.add_argument("--pairs", "--iters", dest="pairs", type=int, default=6,
+                    help="timed iterations per arm (even: whole A B B A blocks)")
+    ap.add_argument("--warmup", type=int, default=1, help="untimed iterations of every arm before the timed ones")
+    ap.add_argument("--pair-order-seed", type=int, default=0, help="odd: the first block runs B A A B")
+    ap.add_argument("--page-size", type=int, default=16)
+    ap.add_argument("--context-length", type=int, default=None, help="engine positions (default prefix + 1024)")
+    ap.add_argument("--repeat-token-id", type=int, default=None,
+                    help="prefix = this token repeated (default: seeded random ids)")
+    ap.add_argument("--shared-path-tokens", type=int, default=2,
+                    help="leading tokens the synthetic verify routes share")
+    ap.add_argument("--skip-tree", action="store_true")
+    ap.add_argument("--skip-forest", action="store_true")
+    ap.add_argument("--skip-native-batch-ar", action="store_true")
+    ap.add_argument("--skip-verify", "--skip-target", dest="skip_target", action="store_true")
     ap.add_argument("--dtype", default="float16")
-    ap.add_argument("--skip-target", action="store_true")
+    ap.add_argument("--device", default="cuda")
+    ap.add_argument("--gpu-id", type=int, default=None, help="CUDA device index")
+    for flag, typ in _INERT:
+        ap.add_argument(flag, type=typ, default=None, help="No-op (a setting of the reference's SGLang runtime).")
+    for flag in ("--legacy-token-attention-metadata", "--skip-page-layout-validation", "--trust-remote-code"):
+        ap.add_argument(flag, action="store_true", help="No-op (the reference's SGLang page-table switches).")
     ap.add_argument("--json-out", default=None)
-    args = ap.parse_args()
+    return ap
+
+
+def main(argv=None) -> int:
+    args = build_parser().parse_args(argv)
     check_pairs(args.pairs)
     llama, engine_mod = pkg("models.llama"), pkg("runtime.engine")
     drafter_mod, store_mod, builders = pkg("runtime.drafter"), pkg("runtime.store"), pkg("runtime.builders")
     frontier = pkg("runtime.frontier")
     dt = getattr(torch, args.dtype)
-    dev = torch.device("cuda")
-    k, d, P = args.k, args.d, args.prefix
+    dev = torch.device(args.device if args.gpu_id is None else f"cuda:{args.gpu_id}")
+    if dev.type == "cuda":
+        torch.cuda.set_device(dev)
+    cuda = dev.type == "cuda"
+    k, d, P, ps = args.k, args.d, args.prefix, int(args.page_size)
+    dcfg, tcfg = llama.get_config(args.drafter), llama.get_config(args.target)
+    vocab = min(dcfg.vocab_size, tcfg.vocab_size)
     g = torch.Generator().manual_seed(0)
-    prompt = torch.randint(0, 128256, (P,), generator=g).tolist()
-    pages = 2 * (P // 16) + 512
-    out: dict[str, object] = {"prefix": P, "k": k, "d": d, "pairs": args.pairs, "dtype": args.dtype,
+    if args.repeat_token_id is not None:
+        prompt = [int(args.repeat_token_id) % vocab] * P
+    else:
+        prompt = torch.randint(0, vocab, (P,), generator=g).tolist()
+    ctx = int(args.context_length or P + 1024)
+    if ctx < P + 2 * k * k * d + 64:
+        raise SystemExit(f"--context-length {ctx} leaves no room for {k * k} routes of depth {d} after {P} tokens")
+    pages = 2 * (ctx // ps) + 512
+    run_tree, run_forest, run_ar = not args.skip_tree, not args.skip_forest, not args.skip_native_batch_ar
+    out: dict[str, object] = {"prefix": P, "k": k, "d": d, "pairs": args.pairs, "warmup": args.warmup,
+                              "pair_order_seed": args.pair_order_seed, "dtype": args.dtype, "device": str(dev),
                               "reference_h800_ms": REFERENCE_H800_MS}
 
-    dw = llama.random_weights(llama.get_config(args.drafter), seed=1, dtype=dt, device=dev)
-    dr = drafter_mod.DrafterRuntime(engine_mod.LlamaEngine(dw, num_pages=pages, page_size=16,
-                                                           max_positions=P + 256))
-    dr.warm_graphs(k, 4)
+    dw = llama.random_weights(dcfg, seed=1, dtype=dt, device=dev)
+    dr = drafter_mod.DrafterRuntime(engine_mod.LlamaEngine(dw, num_pages=pages, page_size=ps, max_positions=ctx))
+    if cuda:
+        dr.warm_graphs(k, 4)
     store = store_mod.KVTreeStore()
     dr.bind_store(store)
     dr.prefill(prompt)
@@ -148,89 +198,91 @@ def main() -> int:
     def run(name, fn):
         if name == "forest":
             fn = fn()
-        dev_ms, host_ms = timed(fn)
+        dev_ms, host_ms = timed(fn, cuda)
         dr.drop_speculative()
         return dev_ms, host_ms
 
-    for name, fn in (("tree", tree), ("batch_ar_k", lambda: batch_ar(k)), ("forest", forest_after_tree),
-                     ("batch_ar_k2", lambda: batch_ar(k * k))):  # warm-up
-        run(name, fn)
-    results: dict[str, list[tuple[float, float]]] = {n: [] for n in ("tree", "batch_ar_k", "forest", "batch_ar_k2")}
-    # Arm A is the matched batch AR, arm B the tree (forest); the order alternates A B / B A.
-    arms = {"a": ("batch_ar_k", lambda: batch_ar(k)), "b": ("tree", tree)}
-    arms2 = {"a": ("batch_ar_k2", lambda: batch_ar(k * k)), "b": ("forest", forest_after_tree)}
+    # Arm A is the matched batch AR, arm B the tree (forest); each block of two iterations is
+    # A B B A (B A A B with an odd --pair-order-seed).
+    pairs = [({"a": ("batch_ar_k", lambda: batch_ar(k)), "b": ("tree", tree)}, run_ar, run_tree),
+             ({"a": ("batch_ar_k2", lambda: batch_ar(k * k)), "b": ("forest", forest_after_tree)}, run_ar,
+              run_forest)]
+    enabled = {"a": None, "b": None}
+    results: dict[str, list[tuple[float, float]]] = {}
     orders = []
-    for i in range(args.pairs):
-        order = abba_order(i)
-        orders.append("".join(order).upper())
-        for name, fn in [arms[x] for x in order] + [arms2[x] for x in order]:
-            results[name].append(run(name, fn))
+    for i in range(-int(args.warmup), args.pairs):
+        order = abba_order(i + int(args.pair_order_seed))
+        if i >= 0:
+            orders.append("".join(order).upper())
+        for arms, a_on, b_on in pairs:
+            enabled["a"], enabled["b"] = a_on, b_on
+            for x in order:
+                if not enabled[x]:
+                    continue
+                name, fn = arms[x]
+                r = run(name, fn)
+                if i >= 0:
+                    results.setdefault(name, []).append(r)
     out["orders"] = orders
-    out["tree_over_batch_ar_blocks"] = block_ratios([v[0] for v in results["batch_ar_k"]],
-                                                    [v[0] for v in results["tree"]])
-    out["forest_over_batch_ar_blocks"] = block_ratios([v[0] for v in results["batch_ar_k2"]],
-                                                      [v[0] for v in results["forest"]])
     for name, vals in results.items():
         out[f"{name}_ms"] = round(statistics.mean(v[0] for v in vals), 3)
         out[f"{name}_host_ms"] = round(statistics.mean(v[1] for v in vals), 3)
-    out["tree_over_batch_ar"] = round(out["tree_ms"] / out["batch_ar_k_ms"], 4)
-    out["forest_over_batch_ar"] = round(out["forest_ms"] / out["batch_ar_k2_ms"], 4)
+    for b_name, a_name, key in (("tree", "batch_ar_k", "tree_over_batch_ar"),
+                                ("forest", "batch_ar_k2", "forest_over_batch_ar")):
+        if b_name in results and a_name in results:
+            out[key] = round(out[f"{b_name}_ms"] / out[f"{a_name}_ms"], 4)
+            out[f"{key}_blocks"] = block_ratios([v[0] for v in results[a_name]], [v[0] for v in results[b_name]])
     dr.engine.ops.check()
     del dr, dw
-    torch.cuda.empty_cache()
+    if cuda:
+        torch.cuda.empty_cache()
 
     if not args.skip_target:
         target_mod = pkg("runtime.target")
         types = pkg("types")
-        tw = llama.random_weights(llama.get_config(args.target), seed=2, dtype=dt, device=dev)
-        te = engine_mod.LlamaEngine(tw, num_pages=pages, page_size=16, max_positions=P + 1024)
+        tw = llama.random_weights(tcfg, seed=2, dtype=dt, device=dev)
+        te = engine_mod.LlamaEngine(tw, num_pages=pages, page_size=ps, max_positions=ctx)
         tv = target_mod.TargetVerifier(te, k=k, d=d)
-        tv.warm_graphs()
+        if cuda:
+            tv.warm_graphs()
         tv.prefill(prompt)
+        shared_n = max(0, min(int(args.shared_path_tokens), d))
 
         def synthetic_routes():
-            shared = torch.randint(0, 128256, (2,), generator=g).tolist()
+            shared = torch.randint(0, vocab, (shared_n,), generator=g).tolist()
             return [types.VerifyRoutePayload(route_id=r, token_ids=tuple(
-                shared + torch.randint(0, 128256, (d - 2,), generator=g).tolist()), draft_logprob=-1.0,
+                shared + torch.randint(0, vocab, (d - shared_n,), generator=g).tolist()), draft_logprob=-1.0,
                 draft_token_logprobs=tuple([-0.25] * d)) for r in range(k)]
 
-        ver, ar = [], []
-        for i in range(args.pairs + 2):
-            routes = synthetic_routes()
-            ver.append(timed(lambda: tv.verify_payloads(prefix_token_ids=tv.prefix_token_ids, routes=routes)))
+        def one_row(n):
             p = len(tv.prefix_token_ids)
-            slots = tv.seq.reserve_scratch(p + 1).numpy()
+            slots = tv.seq.reserve_scratch(p + n).numpy()
             tv._sync()
-            tok = torch.zeros(1, dtype=torch.int32, device=dev)
-            ar.append(timed(lambda: te.run_rows(1, prefix_pages=tv.mirror.dev, tokens=tok, positions=[p],
-                                                slots=slots[:1], shared_len=p, n_shared_pages=len(tv.mirror.host),
-                                                mask_base=p, row_full=[p + 1], row_len=[p + 1])))
-        ver, ar = ver[2:], ar[2:]
-        # Two dependent one-token forwards (the second token fed on the device) and the
-        # linear (non-deduplicated) verify of the same kind of routes, without commit.
-        ar2, lin, tree_fwd = [], [], []
-        for i in range(args.pairs + 2):
-            p = len(tv.prefix_token_ids)
-            slots = tv.seq.reserve_scratch(p + 2).numpy()
-            tv._sync()
-            tok = torch.zeros(2, dtype=torch.int32, device=dev)
+            tok = torch.zeros(n, dtype=torch.int32, device=dev)
 
-            def two():
-                for j in range(2):
+            def fwd():
+                for j in range(n):
                     te.run_rows(1, prefix_pages=tv.mirror.dev, tokens=tok[j:j + 1], positions=[p + j],
                                 slots=slots[j:j + 1], shared_len=p + j, n_shared_pages=len(tv.mirror.host),
                                 mask_base=p + j, row_full=[p + j + 1], row_len=[p + j + 1])
+            return fwd
 
-            ar2.append(timed(two))
+        warm = max(1, int(args.warmup))
+        ver, ar, ar2, lin, tree_fwd = [], [], [], [], []
+        for i in range(args.pairs + warm):
+            routes = synthetic_routes()
+            ver.append(timed(lambda: tv.verify_payloads(prefix_token_ids=tv.prefix_token_ids, routes=routes), cuda))
+            ar.append(timed(one_row(1), cuda))
+            # Two dependent one-token forwards and the linear (non-deduplicated) verify of the same
+            # kind of routes, without commit.
+            ar2.append(timed(one_row(2), cuda))
             paths = [list(r.token_ids) for r in synthetic_routes()]
-            lin.append(timed(lambda: tv.run_tree(paths, deduplicate=False)))
-            tree_fwd.append(timed(lambda: tv.run_tree(paths)))
-        out["target_ar2_ms"] = round(statistics.mean(v[0] for v in ar2[2:]), 3)
-        out["target_linear_verify_ms"] = round(statistics.mean(v[0] for v in lin[2:]), 3)
-        out["target_tree_forward_ms"] = round(statistics.mean(v[0] for v in tree_fwd[2:]), 3)
-        out["target_verify_ms"] = round(statistics.mean(v[0] for v in ver), 3)
-        out["target_verify_host_ms"] = round(statistics.mean(v[1] for v in ver), 3)
-        out["target_ar1_ms"] = round(statistics.mean(v[0] for v in ar), 3)
+            lin.append(timed(lambda: tv.run_tree(paths, deduplicate=False), cuda))
+            tree_fwd.append(timed(lambda: tv.run_tree(paths), cuda))
+        for name, vals in (("target_verify", ver), ("target_ar1", ar), ("target_ar2", ar2),
+                           ("target_linear_verify", lin), ("target_tree_forward", tree_fwd)):
+            out[f"{name}_ms"] = round(statistics.mean(v[0] for v in vals[warm:]), 3)
+        out["target_verify_host_ms"] = round(statistics.mean(v[1] for v in ver[warm:]), 3)
         te.ops.check()
     out["speedup_vs_reference_h800"] = {
         name: round(REFERENCE_H800_MS[name] / out[f"{name}_ms"], 2)

@@ -105,3 +105,19 @@ def test_full_verify_benchmark_aligns_on_cpu(capsys):
     assert out["logit_alignment"]["masked_tree"]["top1_match_rate"] == 1.0
     assert bench.prefix_tokens(bench.build_parser().parse_args(
         ["--model", "m", "--prefix-len", "5", "--prompt-token-ids", "1,2"])) == [1, 2, 1, 2, 1]
+
+
+def test_isolated_benchmark_reference_flags_on_cpu(capsys):
+    bench = _load("bench_isolated_components")
+    base = ["--drafter-model", "tiny-drafter", "--target-model", "tiny-target", "--device", "cpu", "--dtype",
+            "float32", "--prefix-len", "48", "--page-size", "4", "--k", "2", "--d", "2", "--iters", "2",
+            "--warmup", "0", "--mem-fraction-static", "0.7", "--legacy-token-attention-metadata"]
+    assert bench.main(base + ["--pair-order-seed", "1", "--skip-verify"]) == 0
+    out = json.loads(capsys.readouterr().out.strip().splitlines()[-1])
+    assert out["orders"] == ["BA", "AB"] and out["tree_over_batch_ar_blocks"]["blocks"] == 1
+    assert "target_verify_ms" not in out and "forest_ms" in out
+    assert bench.main(base + ["--skip-forest", "--skip-native-batch-ar", "--shared-path-tokens", "1",
+                              "--repeat-token-id", "9"]) == 0
+    out = json.loads(capsys.readouterr().out.strip().splitlines()[-1])
+    assert "tree_ms" in out and "forest_ms" not in out and "batch_ar_k_ms" not in out
+    assert "tree_over_batch_ar" not in out and out["target_verify_ms"] > 0
