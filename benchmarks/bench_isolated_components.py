@@ -63,6 +63,36 @@ class PerRouteTop1Selection:
         return [c for c in candidates if c.rank_in_parent == 0]
 
 
+class DrafterArms:
+    """The drafter workloads on one prefilled drafter (``dr`` bound to ``store``): the stage-1
+    tree, the matched batch AR of any width, and the forest grown after an untimed tree."""
+
+    def __init__(self, dr, store, k: int, d: int) -> None:
+        self.dr, self.store, self.k, self.d = dr, store, int(k), int(d)
+        self.builders, self.frontier = pkg("runtime.builders"), pkg("runtime.frontier")
+
+    def tree(self):
+        b = self.builders
+        routes = b.initialize_stage1_routes(self.dr.prefix_state(), k=self.k, route_store=self.store)
+        return routes, b.build_tree_depths(routes, depth=self.d, k=self.k, route_store=self.store,
+                                           model_backend=self.dr)
+
+    def batch_ar(self, width: int) -> None:
+        routes = self.builders.initialize_stage1_routes(self.dr.prefix_state(), k=width, route_store=self.store)
+        for _ in range(self.d):
+            routes = self.frontier.advance_frontier_one_token(
+                routes, k=1, route_store=self.store, model_backend=self.dr,
+                selection_policy=PerRouteTop1Selection()).next_routes
+
+    def forest_after_tree(self):
+        """Build the tree (untimed) and return the timed part: forest init + d forest depths."""
+        b = self.builders
+        _, res = self.tree()
+        return lambda: b.build_forest_depths(
+            b.initialize_forest_routes(res.completed_routes, res.last_logits, k=self.k, route_store=self.store),
+            depth=self.d, k=self.k, route_store=self.store, model_backend=self.dr)
+
+
 def abba_order(i: int) -> tuple[str, str]:
     """Arm order of iteration ``i``: A B, then B A, so each block of two iterations is A B B A."""
     return ("a", "b") if i % 2 == 0 else ("b", "a")
@@ -145,8 +175,7 @@ def main(argv=None) -> int:
     args = build_parser().parse_args(argv)
     check_pairs(args.pairs)
     llama, engine_mod = pkg("models.llama"), pkg("runtime.engine")
-    drafter_mod, store_mod, builders = pkg("runtime.drafter"), pkg("runtime.store"), pkg("runtime.builders")
-    frontier = pkg("runtime.frontier")
+    drafter_mod, store_mod = pkg("runtime.drafter"), pkg("runtime.store")
     dt = getattr(torch, args.dtype)
     dev = torch.device(args.device if args.gpu_id is None else f"cuda:{args.gpu_id}")
     if dev.type == "cuda":
@@ -177,23 +206,8 @@ def main(argv=None) -> int:
     dr.bind_store(store)
     dr.prefill(prompt)
 
-    def tree():
-        routes = builders.initialize_stage1_routes(dr.prefix_state(), k=k, route_store=store)
-        res = builders.build_tree_depths(routes, depth=d, k=k, route_store=store, model_backend=dr)
-        return routes, res
-
-    def batch_ar(width):
-        routes = builders.initialize_stage1_routes(dr.prefix_state(), k=width, route_store=store)
-        for _ in range(d):
-            routes = frontier.advance_frontier_one_token(routes, k=1, route_store=store, model_backend=dr,
-                                                         selection_policy=PerRouteTop1Selection()).next_routes
-
-    def forest_after_tree():
-        # The stage-1 tree is built untimed; the timed part is forest init + d forest depths.
-        _, res = tree()
-        return lambda: builders.build_forest_depths(
-            builders.initialize_forest_routes(res.completed_routes, res.last_logits, k=k, route_store=store),
-            depth=d, k=k, route_store=store, model_backend=dr)
+    arms_ = DrafterArms(dr, store, k, d)
+    tree, batch_ar, forest_after_tree = arms_.tree, arms_.batch_ar, arms_.forest_after_tree
 
     def run(name, fn):
         if name == "forest":

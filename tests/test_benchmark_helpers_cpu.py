@@ -121,3 +121,17 @@ def test_isolated_benchmark_reference_flags_on_cpu(capsys):
     out = json.loads(capsys.readouterr().out.strip().splitlines()[-1])
     assert "tree_ms" in out and "forest_ms" not in out and "batch_ar_k_ms" not in out
     assert "tree_over_batch_ar" not in out and out["target_verify_ms"] > 0
+
+
+def test_tree_forest_sweep_on_cpu(capsys):
+    bench = _load("bench_tree_forest_sweep")
+    assert bench.main(["--model", "tiny-drafter", "--target-model", "tiny-target", "--device", "cpu", "--dtype",
+                       "float32", "--prefix-len", "40", "--page-size", "4", "--pairs", "2", "2", "--pairs", "3", "1",
+                       "--warmup", "0", "--iters", "1", "--context-length", "64", "--nccl-port", "1",
+                       "--alignment-atol", "1e-4", "--alignment-rtol", "1e-4", "--fail-on-logit-mismatch"]) == 0
+    out = json.loads(capsys.readouterr().out.strip().splitlines()[-1])
+    assert [(p["k"], p["d"]) for p in out["pairs"]] == [(2, 2), (3, 1)]
+    p = out["pairs"][1]
+    assert {"batch1_ar_1_tokens", "batch3_ar_1_tokens", "atlas_tree_k3_d1", "batch9_ar_1_tokens",
+            "atlas_forest_k3_d1"} <= set(p)
+    assert p["target"]["logits_aligned"] and out["metadata"]["effective_context_length"] >= 40 + 2 + 64
