@@ -135,3 +135,40 @@ def test_tree_forest_sweep_on_cpu(capsys):
     assert {"batch1_ar_1_tokens", "batch3_ar_1_tokens", "atlas_tree_k3_d1", "batch9_ar_1_tokens",
             "atlas_forest_k3_d1"} <= set(p)
     assert p["target"]["logits_aligned"] and out["metadata"]["effective_context_length"] >= 40 + 2 + 64
+
+
+def test_hf_kv_baseline_arms_match_the_oracle(capsys, tmp_path):
+    """The transformers baseline runs the same model as this package's oracle, and its tree step
+    (global top-k, cache reordered to the parents) decodes the routes it selected."""
+    bench = _load("bench_hf_kv_baseline")
+    llama = mod("models.llama")
+    assert bench.main(["--drafter-model", "tiny-drafter", "--device", "cpu", "--dtype", "float32",
+                       "--prefix-len", "24", "--k", "2", "--d", "2", "--warmup", "0", "--iters", "1"]) == 0
+    out = json.loads(capsys.readouterr().out.strip().splitlines()[-1])
+    assert {"batch1_ar_2_tokens", "build_tree_stage1_k2_d2", "build_forest_stage2_k2_4_d2"} <= set(out["drafter"])
+    assert "target_verify_k2_paths_d2" in out["target"]
+
+    w = llama.random_weights(llama.get_config("tiny-drafter"), seed=0, dtype=torch.float32)
+    model = bench.load_hf("tiny-drafter", dtype=torch.float32, device=torch.device("cpu"), seed=0,
+                          scratch=str(tmp_path), trust=False)
+    prompt = [(7 * i + 3) % 1000 for i in range(24)]
+    arms = bench.HFArms(model, prompt, torch.device("cpu"))
+    k = 3
+    state = arms.tree_state(k)
+    ref = torch.log_softmax(llama.reference_forward(w, prompt)[-1], -1)
+    lp0, t0 = torch.topk(ref, k)
+    assert torch.equal(state[1], t0)
+    past, ids, scores = arms.tree(state, k, 1)
+    # Expected depth-1 selection from the oracle: the k best of the k x k children.
+    cands = []
+    for r in range(k):
+        lp = torch.log_softmax(llama.reference_forward(w, prompt + [int(t0[r])])[-1], -1)
+        v, t = torch.topk(lp, k)
+        cands += [(float(lp0[r] + v[j]), r, int(t[j])) for j in range(k)]
+    best = sorted(cands, key=lambda c: -c[0])[:k]
+    assert [c[2] for c in best] == ids.tolist()
+    assert torch.allclose(scores, torch.tensor([c[0] for c in best]), atol=1e-4)
+    got = arms.step(past, ids)
+    for i, (_, r, tok) in enumerate(best):
+        want = llama.reference_forward(w, prompt + [int(t0[r]), tok])[-1]
+        assert float((got[i] - want).abs().max()) < 1e-3
