@@ -126,10 +126,16 @@ def save_hf_checkpoint(w: LlamaWeights, path: str | os.PathLike) -> None:
     """Write Hugging Face Llama naming (config.json + model.safetensors)."""
     from safetensors.torch import save_file
 
-    cfg = w.config
     root = Path(path)
     root.mkdir(parents=True, exist_ok=True)
-    (root / "config.json").write_text(json.dumps(config_to_hf(cfg), indent=2))
+    (root / "config.json").write_text(json.dumps(config_to_hf(w.config), indent=2))
+    out = {name: t.detach().contiguous().cpu() for name, t in hf_state_dict(w).items()}
+    save_file(out, str(root / "model.safetensors"))
+
+
+def hf_state_dict(w: LlamaWeights) -> dict[str, torch.Tensor]:
+    """The weights under Hugging Face Llama names (views of ``w`` where the layout allows)."""
+    cfg = w.config
     out: dict[str, torch.Tensor] = {"model.embed_tokens.weight": w.embed, "model.norm.weight": w.final_norm}
     if not cfg.tie_word_embeddings:
         out["lm_head.weight"] = w.lm_head
@@ -148,7 +154,7 @@ def save_hf_checkpoint(w: LlamaWeights, path: str | os.PathLike) -> None:
             pre + "mlp.up_proj.weight": up,
             pre + "mlp.down_proj.weight": lw.wd,
         })
-    save_file({k: v.detach().contiguous().cpu() for k, v in out.items()}, str(root / "model.safetensors"))
+    return out
 
 
 def resolve_model(spec: str, *, dtype: str | torch.dtype = "float16", device: str | torch.device = "cpu",

@@ -5,8 +5,8 @@
         --prefix-len 8192 --k 3 --d 4 --warmup 3 --iters 10
 
 Nothing of this framework runs in the timed regions: the models are transformers'
-``LlamaForCausalLM`` (presets are written once as a Hugging Face checkpoint from this
-package's seeded random weights, checkpoint directories load as they are) and the cache is
+``LlamaForCausalLM`` (presets carry this package's seeded random weights under Hugging Face
+names, checkpoint directories load as they are) and the cache is
 transformers' ``DynamicCache``, one copy of the prefix per batch row, reordered along the
 batch after each selection.  It gives the numbers the paged, shared-prefix runtime is to be
 compared with:
@@ -32,7 +32,6 @@ import json
 import os
 import statistics
 import sys
-import tempfile
 import time
 
 import torch
@@ -84,18 +83,24 @@ def prompt_tokens(args, vocab: int) -> list[int]:
     return (base * ((n + len(base) - 1) // len(base)))[:n]
 
 
-def load_hf(spec: str, *, dtype: torch.dtype, device: torch.device, seed: int, scratch: str, trust: bool):
-    """transformers' Llama for a checkpoint directory, or for a preset written once as one."""
-    from transformers import AutoModelForCausalLM
+def load_hf(spec: str, *, dtype: torch.dtype, device: torch.device, seed: int, trust: bool):
+    """transformers' Llama: loaded from a checkpoint directory, or built for a preset and given
+    this package's seeded weights (drawn on ``device``, as the engines draw presets) in memory."""
+    from transformers import AutoModelForCausalLM, LlamaConfig, LlamaForCausalLM
 
-    path = spec
-    if not os.path.isdir(spec):
-        loader, llama = pkg("models.loader"), pkg("models.llama")
-        path = os.path.join(scratch, spec)
-        if not os.path.isdir(path):
-            loader.save_hf_checkpoint(llama.random_weights(llama.get_config(spec), seed=seed, dtype=dtype), path)
-    model = AutoModelForCausalLM.from_pretrained(path, dtype=dtype, trust_remote_code=trust)
-    return model.to(device).eval()
+    if os.path.isdir(spec):
+        return AutoModelForCausalLM.from_pretrained(spec, dtype=dtype, trust_remote_code=trust).to(device).eval()
+    loader, llama = pkg("models.loader"), pkg("models.llama")
+    w = llama.random_weights(llama.get_config(spec), seed=seed, dtype=dtype, device=device)
+    prev = torch.get_default_dtype()
+    torch.set_default_dtype(dtype)
+    try:
+        with torch.device(device):
+            model = LlamaForCausalLM(LlamaConfig(**loader.config_to_hf(w.config)))
+    finally:
+        torch.set_default_dtype(prev)
+    model.load_state_dict(loader.hf_state_dict(w), strict=not w.config.tie_word_embeddings)
+    return model.eval()
 
 
 class Stats:
@@ -223,50 +228,47 @@ def run(args) -> dict:
                  "drafter_model": args.drafter_model, "target_model": args.target_model or args.drafter_model,
                  "k": k, "d": d, "dtype": args.dtype, "device": str(dev), "warmup": W, "iters": I,
                  "stateful_cache": bool(S), "prefill_excluded_from_timing": True}
-    with tempfile.TemporaryDirectory(prefix="hf_kv_baseline_") as scratch:
-        m = load_hf(args.drafter_model, dtype=dt, device=dev, seed=args.seed, scratch=scratch,
-                    trust=args.trust_remote_code)
-        prompt = prompt_tokens(args, m.config.vocab_size)
-        out["prefix_len"] = len(prompt)
+    m = load_hf(args.drafter_model, dtype=dt, device=dev, seed=args.seed, trust=args.trust_remote_code)
+    prompt = prompt_tokens(args, m.config.vocab_size)
+    out["prefix_len"] = len(prompt)
+    a = HFArms(m, prompt, dev)
+
+    def ar_setup(b):
+        def setup():
+            past, logits = a.prefill(b)
+            return past, logits.argmax(-1)
+        return setup
+
+    dr = {}
+    dr[f"batch1_ar_{d}_tokens"] = st.measure(ar_setup(1), lambda s: a.ar(s, d), W, I, S)
+    dr[f"batch{k}_ar_{d}_tokens"] = st.measure(ar_setup(k), lambda s: a.ar(s, d), W, I, S)
+    dr[f"build_tree_stage1_k{k}_d{d}"] = st.measure(lambda: a.tree_state(k), lambda s: a.tree(s, k, d), W, I, S)
+    dr[f"batch{k * k}_ar_{d}_tokens"] = st.measure(ar_setup(k * k), lambda s: a.ar(s, d), W, I, S)
+    dr[f"build_forest_stage2_k2_{k * k}_d{d}"] = st.measure(lambda: a.forest_state(k, d),
+                                                             lambda s: a.forest(s, k, d), W, I, S)
+    med = {n: v["median_ms"] for n, v in dr.items()}
+    tree, forest = med[f"build_tree_stage1_k{k}_d{d}"], med[f"build_forest_stage2_k2_{k * k}_d{d}"]
+    dr["ratios_median"] = {"tree_over_batch1_ar": tree / med[f"batch1_ar_{d}_tokens"],
+                           "tree_over_batchk_ar": tree / med[f"batch{k}_ar_{d}_tokens"],
+                           "forest_over_batch1_ar": forest / med[f"batch1_ar_{d}_tokens"],
+                           "forest_over_batchk2_ar": forest / med[f"batch{k * k}_ar_{d}_tokens"]}
+    out["drafter"] = dr
+    if args.target_model and args.target_model != args.drafter_model:
+        del a, m
+        if dev.type == "cuda":
+            torch.cuda.empty_cache()
+        m = load_hf(args.target_model, dtype=dt, device=dev, seed=args.seed + 1, trust=args.trust_remote_code)
         a = HFArms(m, prompt, dev)
-
-        def ar_setup(b):
-            def setup():
-                past, logits = a.prefill(b)
-                return past, logits.argmax(-1)
-            return setup
-
-        dr = {}
-        dr[f"batch1_ar_{d}_tokens"] = st.measure(ar_setup(1), lambda s: a.ar(s, d), W, I, S)
-        dr[f"batch{k}_ar_{d}_tokens"] = st.measure(ar_setup(k), lambda s: a.ar(s, d), W, I, S)
-        dr[f"build_tree_stage1_k{k}_d{d}"] = st.measure(lambda: a.tree_state(k), lambda s: a.tree(s, k, d), W, I, S)
-        dr[f"batch{k * k}_ar_{d}_tokens"] = st.measure(ar_setup(k * k), lambda s: a.ar(s, d), W, I, S)
-        dr[f"build_forest_stage2_k2_{k * k}_d{d}"] = st.measure(lambda: a.forest_state(k, d),
-                                                                 lambda s: a.forest(s, k, d), W, I, S)
-        med = {n: v["median_ms"] for n, v in dr.items()}
-        tree, forest = med[f"build_tree_stage1_k{k}_d{d}"], med[f"build_forest_stage2_k2_{k * k}_d{d}"]
-        dr["ratios_median"] = {"tree_over_batch1_ar": tree / med[f"batch1_ar_{d}_tokens"],
-                               "tree_over_batchk_ar": tree / med[f"batch{k}_ar_{d}_tokens"],
-                               "forest_over_batch1_ar": forest / med[f"batch1_ar_{d}_tokens"],
-                               "forest_over_batchk2_ar": forest / med[f"batch{k * k}_ar_{d}_tokens"]}
-        out["drafter"] = dr
-        if args.target_model and args.target_model != args.drafter_model:
-            del a, m
-            if dev.type == "cuda":
-                torch.cuda.empty_cache()
-            m = load_hf(args.target_model, dtype=dt, device=dev, seed=args.seed + 1, scratch=scratch,
-                        trust=args.trust_remote_code)
-            a = HFArms(m, prompt, dev)
-        tg = {}
-        tg["target_batch1_decode_1_token"] = st.measure(ar_setup(1), lambda s: a.ar(s, 1), W, I, S)
-        tg[f"target_batch1_ar_{d}_tokens"] = st.measure(ar_setup(1), lambda s: a.ar(s, d), W, I, S)
-        tg[f"target_batch{k}_ar_{d}_tokens"] = st.measure(ar_setup(k), lambda s: a.ar(s, d), W, I, S)
-        tg[f"target_verify_k{k}_paths_d{d}"] = st.measure(lambda: a.verify_state(k, d), a.verify, W, I, S)
-        v = tg[f"target_verify_k{k}_paths_d{d}"]["median_ms"]
-        tg["ratios_median"] = {"verify_over_decode1": v / tg["target_batch1_decode_1_token"]["median_ms"],
-                               "verify_over_batch1_ar": v / tg[f"target_batch1_ar_{d}_tokens"]["median_ms"],
-                               "verify_over_batchk_ar": v / tg[f"target_batch{k}_ar_{d}_tokens"]["median_ms"]}
-        out["target"] = tg
+    tg = {}
+    tg["target_batch1_decode_1_token"] = st.measure(ar_setup(1), lambda s: a.ar(s, 1), W, I, S)
+    tg[f"target_batch1_ar_{d}_tokens"] = st.measure(ar_setup(1), lambda s: a.ar(s, d), W, I, S)
+    tg[f"target_batch{k}_ar_{d}_tokens"] = st.measure(ar_setup(k), lambda s: a.ar(s, d), W, I, S)
+    tg[f"target_verify_k{k}_paths_d{d}"] = st.measure(lambda: a.verify_state(k, d), a.verify, W, I, S)
+    v = tg[f"target_verify_k{k}_paths_d{d}"]["median_ms"]
+    tg["ratios_median"] = {"verify_over_decode1": v / tg["target_batch1_decode_1_token"]["median_ms"],
+                           "verify_over_batch1_ar": v / tg[f"target_batch1_ar_{d}_tokens"]["median_ms"],
+                           "verify_over_batchk_ar": v / tg[f"target_batch{k}_ar_{d}_tokens"]["median_ms"]}
+    out["target"] = tg
     return out
 
 

@@ -178,7 +178,7 @@ def main(argv=None) -> int:
     drafter_mod, store_mod = pkg("runtime.drafter"), pkg("runtime.store")
     dt = getattr(torch, args.dtype)
     dev = torch.device(args.device if args.gpu_id is None else f"cuda:{args.gpu_id}")
-    if dev.type == "cuda":
+    if dev.type == "cuda" and dev.index is not None:
         torch.cuda.set_device(dev)
     cuda = dev.type == "cuda"
     k, d, P, ps = args.k, args.d, args.prefix, int(args.page_size)

@@ -112,7 +112,7 @@ def main(argv=None) -> int:
     llama, loader = pkg("models.llama"), pkg("models.loader")
     engine_mod, drafter_mod, store_mod = pkg("runtime.engine"), pkg("runtime.drafter"), pkg("runtime.store")
     dev = torch.device(args.device if args.gpu_id is None else f"cuda:{args.gpu_id}")
-    if dev.type == "cuda":
+    if dev.type == "cuda" and dev.index is not None:
         torch.cuda.set_device(dev)
     cuda = dev.type == "cuda"
     dw = loader.resolve_model(args.model, dtype=args.dtype, device=dev, seed=args.seed)

@@ -137,7 +137,7 @@ def test_tree_forest_sweep_on_cpu(capsys):
     assert p["target"]["logits_aligned"] and out["metadata"]["effective_context_length"] >= 40 + 2 + 64
 
 
-def test_hf_kv_baseline_arms_match_the_oracle(capsys, tmp_path):
+def test_hf_kv_baseline_arms_match_the_oracle(capsys):
     """The transformers baseline runs the same model as this package's oracle, and its tree step
     (global top-k, cache reordered to the parents) decodes the routes it selected."""
     bench = _load("bench_hf_kv_baseline")
@@ -149,8 +149,7 @@ def test_hf_kv_baseline_arms_match_the_oracle(capsys, tmp_path):
     assert "target_verify_k2_paths_d2" in out["target"]
 
     w = llama.random_weights(llama.get_config("tiny-drafter"), seed=0, dtype=torch.float32)
-    model = bench.load_hf("tiny-drafter", dtype=torch.float32, device=torch.device("cpu"), seed=0,
-                          scratch=str(tmp_path), trust=False)
+    model = bench.load_hf("tiny-drafter", dtype=torch.float32, device=torch.device("cpu"), seed=0, trust=False)
     prompt = [(7 * i + 3) % 1000 for i in range(24)]
     arms = bench.HFArms(model, prompt, torch.device("cpu"))
     k = 3
