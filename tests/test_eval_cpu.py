@@ -178,3 +178,47 @@ def test_mtbench_reference_one_command_form(tmp_path, monkeypatch):
         assert sorted({x["source"] for x in js}) == ["answers", "ar:ar_1b"]
     finally:
         judge.close()
+
+
+def test_gsm8k_sweeps(tmp_path):
+    sw = mod("eval.sweep")
+    data = tmp_path / "test.jsonl"
+    data.write_text("\n".join(json.dumps({"question": f"What is {i}+1?", "answer": f"x\n#### {i + 1}"})
+                              for i in range(2)) + "\n")
+    gen = ["--data-file", str(data), "--dtype", "float32", "--page-size", "4", "--max-new-tokens", "4", "--k", "2",
+           "--d", "2", "--device", "cpu", "--context-length", "512", "--warmup-runs", "0"]
+    out = tmp_path / "fb"
+    assert sw.main(["fallback", "--drafter-model", "tiny-drafter", "--target-model", "tiny-target", "--output-dir",
+                    str(out), "--thresholds", "none", "1e9", *gen]) == 0
+    rows = json.loads((out / "results.json").read_text())
+    assert [r["fallback_threshold"] for r in rows] == [None, 1e9]
+    assert rows[0]["fallback_rounds"] == 0 and rows[1]["fallback_rate"] == 1.0 and rows[1]["samples"] == 2
+    exp = json.loads((out / "experiment.json").read_text())
+    assert exp["changed_variable"] == "fallback_threshold" and len(exp["fixed_path_score_weights"]) == 2
+    assert (out / "threshold_none" / "summary.json").exists() and (out / "results.csv").exists()
+    pw = tmp_path / "pw"
+    assert sw.main(["path-weights", "--drafter-model", "tiny-drafter", "--target-model", "tiny-target",
+                    "--output-dir", str(pw), "--alphas", "0", "0.5", "--dry-run", *gen]) == 0
+    exp = json.loads((pw / "experiment.json").read_text())
+    assert [r["output_dir"].rsplit("/", 1)[-1] for r in exp["runs"]] == ["alpha_0", "alpha_0p5"]
+    assert exp["weights_by_alpha"]["0"] == [0.5, 0.5] and not (pw / "results.json").exists()
+
+
+def test_gsm8k_launcher_script(tmp_path):
+    import os
+    import subprocess
+
+    from conftest import REPO
+
+    data = tmp_path / "test.jsonl"
+    data.write_text(json.dumps({"question": "What is 1+1?", "answer": "x\n#### 2"}) + "\n")
+    env = dict(os.environ, DRAFTER_MODEL="tiny-drafter", TARGET_MODEL="tiny-target", GSM8K_FILE=str(data),
+               OUTPUT_DIR=str(tmp_path / "out"), K="2", D="2", MAX_NEW_TOKENS="4", CONTEXT_LENGTH="512",
+               WARMUP_RUNS="0")
+    script = os.path.join(REPO, "0709_b200", "eval", "run_gsm8k.sh")
+    r = subprocess.run(["bash", script, "atlas-serial", "--device", "cpu", "--dtype", "float32", "--page-size", "4",
+                        "--path-score-weights", ""], env=env, capture_output=True, text=True, timeout=600)
+    assert r.returncode == 0, r.stderr[-2000:]
+    assert json.loads((tmp_path / "out" / "summary.json").read_text())["backend"] == "atlas_serial"
+    bad = subprocess.run(["bash", script, "nope"], env=env, capture_output=True, text=True, timeout=60)
+    assert bad.returncode == 2
