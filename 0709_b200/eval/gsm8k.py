@@ -21,6 +21,8 @@ from __future__ import annotations
 import argparse
 import json
 import re
+import statistics
+import sys
 from pathlib import Path
 
 from ..serving.prompts import decode, encode, load_tokenizer
@@ -68,6 +70,44 @@ def build_prompt(question: str, fewshot: list[dict], system_prompt: str = "") ->
     return "\n".join(parts)
 
 
+# Per-sample timing of the serial generator kept in each prediction row, summed by ``serial_speed``.
+SERIAL_KEYS = ("generated_tokens", "rounds", "fallback_rounds", "drafter_elapsed_s", "target_elapsed_s",
+               "total_elapsed_s", "fallback_appended_tokens", "fallback_append_elapsed_s")
+
+
+def serial_speed(preds: list[dict]) -> dict:
+    """Drafter / target / overall committed-token rates of the serial generator over all samples
+    (target prompt prefill excluded, as in its per-sample metadata)."""
+    tot = {key: sum(float((r.get("serial") or {}).get(key) or 0) for r in preds) for key in SERIAL_KEYS}
+    n = tot["generated_tokens"]
+
+    def rate(t: float) -> float | None:
+        return n / t if t else None
+
+    return {**tot, "fallback_rate": tot["fallback_rounds"] / tot["rounds"] if tot["rounds"] else None,
+            "drafter_tokens_per_second": rate(tot["drafter_elapsed_s"]),
+            "target_tokens_per_second": rate(tot["target_elapsed_s"]),
+            "overall_tokens_per_second": rate(tot["total_elapsed_s"]),
+            "fallback_append_tokens_per_second": (tot["fallback_appended_tokens"] / tot["fallback_append_elapsed_s"]
+                                                  if tot["fallback_append_elapsed_s"] else None),
+            "token_definition": "committed_generated_tokens", "excludes_target_prompt_prefill": True}
+
+
+def settings(args, num_fewshot: int) -> dict:
+    """The generation settings of the run, recorded beside its results."""
+    atlas = args.backend.startswith("atlas")
+    keep = ("protocol", "max_new_tokens", "strict_marker", "system_prompt", "context_length", "dtype", "page_size",
+            "generation_seed", "drafter_do_sample", "drafter_temperature")
+    out = {key: getattr(args, key) for key in keep}
+    out["num_fewshot"] = num_fewshot
+    out["target_model"] = (args.target_model or args.target_url) if atlas else None
+    for key in ("k", "d", "fixed_forest_depth", "path_score_weights", "path_weight_alpha", "fallback_threshold",
+                "first_token_threshold", "fallback_ar_tokens", "route_selection_policy",
+                "route_sampling_temperature"):
+        out[key] = getattr(args, key) if atlas else None
+    return out
+
+
 def build_parser() -> argparse.ArgumentParser:
     p = argparse.ArgumentParser(description="GSM8K exact match")
     add_generation_flags(p)
@@ -106,9 +146,15 @@ def main(argv=None) -> int:
     if pending:
         warm_up(generate, encode(tok, build_prompt(str(pending[0][1]["question"]), fewshot, args.system_prompt)),
                 args.warmup_runs)
+    failures_path = out / "failures.jsonl"
     for i, row in pending:
         ids = encode(tok, build_prompt(str(row["question"]), fewshot, args.system_prompt))
-        (gen_ids, meta, rounds), secs = timed(generate, ids)
+        try:
+            (gen_ids, meta, rounds), secs = timed(generate, ids)
+        except Exception as exc:  # noqa: BLE001 - recorded per sample; the run goes on (resume retries it)
+            print(f"sample {i} failed: {exc!r}", file=sys.stderr, flush=True)
+            append_jsonl(failures_path, {"index": i, "error": repr(exc)})
+            continue
         text = decode(tok, gen_ids) or ""
         pred, gold = extract(text, strict=args.strict_marker), gold_answer(row)
         rec = {"index": i, "question": row["question"], "gold": gold, "prediction": pred,
@@ -120,13 +166,22 @@ def main(argv=None) -> int:
                 [r.to_dict() if hasattr(r, "to_dict") else r for r in rounds]).items() if k != "rounds"}
             rec["rounds"] = len(rounds)
             rec["fallback_rounds"] = sum(getattr(r, "decision", "") == "fallback_ar" for r in rounds)
+        if args.backend == "atlas_serial":
+            rec["serial"] = {key: meta.get(key) for key in SERIAL_KEYS}
         append_jsonl(pred_path, rec)
-    preds = read_jsonl(pred_path)
+    preds = read_jsonl(pred_path) if pred_path.exists() else []
     acc = sum(bool(r["correct"]) for r in preds) / len(preds) if preds else None
-    summary = {"accuracy": acc, "correct": sum(bool(r["correct"]) for r in preds), **rows_summary(preds),
-               "extraction_failures": sum(r["prediction"] is None for r in preds), "backend": args.backend,
-               "model": args.model, "target": args.target_model or args.target_url,
-               "target_intervention": aggregate_prediction_interventions(preds)}
+    speeds = [r["generated_tokens"] / r["elapsed_s"] for r in preds if r.get("elapsed_s")]
+    base = rows_summary(preds)
+    summary = {"accuracy": acc, "correct": sum(bool(r["correct"]) for r in preds), **base, "count": len(preds),
+               "mean_tokens_per_second": statistics.fmean(speeds) if speeds else None,
+               "end_to_end_tokens_per_second": base["tokens_per_s"],
+               "extraction_failures": sum(r["prediction"] is None for r in preds),
+               "failures": len(read_jsonl(failures_path)) if failures_path.exists() else 0,
+               "backend": args.backend, "model": args.model, "target": args.target_model or args.target_url,
+               "target_intervention": aggregate_prediction_interventions(preds),
+               "serial_speed": serial_speed(preds) if args.backend == "atlas_serial" else None,
+               "settings": settings(args, len(fewshot))}
     (out / "summary.json").write_text(json.dumps(summary, indent=2, sort_keys=True) + "\n")
     print(json.dumps({k: summary[k] for k in ("accuracy", "samples", "tokens_per_s")}))
     return 0

@@ -219,6 +219,31 @@ def test_gsm8k_launcher_script(tmp_path):
     r = subprocess.run(["bash", script, "atlas-serial", "--device", "cpu", "--dtype", "float32", "--page-size", "4",
                         "--path-score-weights", ""], env=env, capture_output=True, text=True, timeout=600)
     assert r.returncode == 0, r.stderr[-2000:]
-    assert json.loads((tmp_path / "out" / "summary.json").read_text())["backend"] == "atlas_serial"
+    summary = json.loads((tmp_path / "out" / "summary.json").read_text())
+    assert summary["backend"] == "atlas_serial" and summary["count"] == 1 and summary["settings"]["k"] == 2
+    assert summary["serial_speed"]["rounds"] > 0 and summary["serial_speed"]["overall_tokens_per_second"] > 0
     bad = subprocess.run(["bash", script, "nope"], env=env, capture_output=True, text=True, timeout=60)
     assert bad.returncode == 2
+
+
+def test_gsm8k_records_failed_samples_and_goes_on(tmp_path, monkeypatch):
+    g = mod("eval.gsm8k")
+    data = tmp_path / "test.jsonl"
+    data.write_text("\n".join(json.dumps({"question": f"q{i}", "answer": f"#### {i}"}) for i in range(3)) + "\n")
+    calls = []
+
+    def fake_make_generate(args):
+        def run(ids):
+            calls.append(len(ids))
+            if len(calls) == 2:
+                raise RuntimeError("boom")
+            return [ord(c) for c in "The final answer is 2."], {}, []
+        return run
+
+    monkeypatch.setattr(g, "make_generate", fake_make_generate)
+    out = tmp_path / "out"
+    assert g.main(["--backend", "ar", "--model", "m", "--data-file", str(data), "--output-dir", str(out),
+                   "--warmup-runs", "0"]) == 0
+    summary = json.loads((out / "summary.json").read_text())
+    assert summary["count"] == 2 and summary["failures"] == 1 and summary["correct"] == 1
+    assert json.loads((out / "failures.jsonl").read_text())["index"] == 1
