@@ -45,10 +45,16 @@ class PagedGreedyARGenerator:
                                             model_backend=dr)
         try:
             while True:
-                yield int(route.pending_token_id)
+                tok = int(route.pending_token_id)
+                yield tok
                 step = build_tree_one_depth([route], k=1, route_store=store, model_backend=dr, sampling=sampling)
                 (route,), _ = dr.commit_stage1_and_promote(committed_route=step.decoded_routes[0],
                                                            retained_routes=step.next_routes)
+                if sampling.config.do_sample:
+                    # Keys hash the committed prefix plus the path after it: the token just
+                    # committed joins the prefix, as the route store's relative paths now start
+                    # after it.
+                    sampling = DrafterSamplingContext(sampling.config, (*sampling.committed_token_ids, tok))
         finally:
             dr.drop_speculative()
 

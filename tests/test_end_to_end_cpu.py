@@ -163,3 +163,22 @@ def test_every_handoff_depth_keeps_greedy_equivalence(models, forest_depth):
     modes = {r.handoff_mode for r in res.rounds[:-1]}
     want = "completed_forest_reused" if forest_depth == D else "partial_forest_pruned_then_build_tree"
     assert modes == {want}
+
+
+def test_equivalence_checker_cli(tmp_path):
+    """The user-facing k=1 first-route checker: greedy and keyed sampling both match AR."""
+    import json
+
+    chk = mod("serving.check_equivalence")
+    base = ["--drafter-model", "tiny-drafter", "--target-model", "tiny-target", "--device", "cpu", "--dtype",
+            "float32", "--page-size", "4", "--prompt-token-ids", "5,6,7,8,9,10", "--forest-depths", "live,0,3",
+            "--repeats", "1", "--max-new-tokens", "10", "--context-length", "256", "--d", "3"]
+    for extra in ([], ["--drafter-do-sample", "--drafter-temperature", "0.7", "--seed", "3"]):
+        out = tmp_path / f"eq{len(extra)}.json"
+        assert chk.main(base + extra + ["--json-out", str(out)]) == 0
+        rep = json.loads(out.read_text())
+        assert rep["passed"] and rep["checked"] == 3
+    with pytest.raises(SystemExit):
+        chk.check_target_policy({"route_selection_policy": "target_best"})
+    with pytest.raises(SystemExit):
+        chk.check_target_policy({"route_selection_policy": "first_route", "fallback_threshold": -0.5})
