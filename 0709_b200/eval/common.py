@@ -10,6 +10,7 @@ import hashlib
 import json
 import math
 import time
+from dataclasses import replace
 from pathlib import Path
 from typing import Any, Iterable, Mapping, Sequence
 
@@ -155,13 +156,17 @@ def make_generate(args):
                            page_size=args.page_size, max_positions=ctx + 64)
 
     drafter = DrafterRuntime(engine(args.model, args.seed), prefill_chunk_size=chunk)
+    do_sample = bool(getattr(args, "drafter_do_sample", False))
+    temperature = float(getattr(args, "drafter_temperature", 1.0))
     if args.backend == "ar":
         from ..serving.ar import PagedGreedyARGenerator
 
         gen = PagedGreedyARGenerator(drafter=drafter)
 
-        def run(ids):
-            r = gen.generate(ids, max_new_tokens=args.max_new_tokens, eos_token_id=args.eos_token_id)
+        def run(ids, seed=None):
+            r = gen.generate(ids, max_new_tokens=args.max_new_tokens, eos_token_id=args.eos_token_id,
+                             do_sample=do_sample, temperature=temperature,
+                             generation_seed=args.generation_seed if seed is None else int(seed))
             return r.generated_token_ids, dict(r.metadata), []
 
         return run
@@ -195,14 +200,16 @@ def make_generate(args):
     cfg = DistributedAtlasConfig(k=args.k, d=args.d, max_new_tokens=args.max_new_tokens,
                                  eos_token_id=args.eos_token_id, fallback_ar_tokens=args.fallback_ar_tokens,
                                  generation_seed=args.generation_seed,
-                                 drafter_do_sample=bool(getattr(args, "drafter_do_sample", False)),
-                                 drafter_temperature=float(getattr(args, "drafter_temperature", 1.0)),
+                                 drafter_do_sample=do_sample, drafter_temperature=temperature,
                                  fixed_forest_depth=(None if args.backend == "atlas_serial"
                                                      else getattr(args, "fixed_forest_depth", None)),
                                  validate_state_alignment=bool(getattr(args, "validate_state_alignment", False)))
     gen = cls(config=cfg, drafter=drafter, target_client=client)
 
-    def run(ids):
+    def run(ids, seed=None):
+        """One request; ``seed`` (default ``--generation-seed``) keys the drafter's sampling and
+        the target's route sampling for this request only."""
+        gen.config = replace(cfg, generation_seed=args.generation_seed if seed is None else int(seed))
         r = gen.generate(ids)
         return r.generated_token_ids, dict(r.metadata), list(r.rounds)
 

@@ -100,6 +100,7 @@ def settings(args, num_fewshot: int) -> dict:
             "generation_seed", "drafter_do_sample", "drafter_temperature")
     out = {key: getattr(args, key) for key in keep}
     out["num_fewshot"] = num_fewshot
+    out["request_seed_rule"] = "generation_seed_plus_gsm8k_index"
     out["target_model"] = (args.target_model or args.target_url) if atlas else None
     for key in ("k", "d", "fixed_forest_depth", "path_score_weights", "path_weight_alpha", "fallback_threshold",
                 "first_token_threshold", "fallback_ar_tokens", "route_selection_policy",
@@ -149,8 +150,9 @@ def main(argv=None) -> int:
     failures_path = out / "failures.jsonl"
     for i, row in pending:
         ids = encode(tok, build_prompt(str(row["question"]), fewshot, args.system_prompt))
+        seed = int(args.generation_seed) + int(i)  # one request seed per GSM8K index
         try:
-            (gen_ids, meta, rounds), secs = timed(generate, ids)
+            (gen_ids, meta, rounds), secs = timed(generate, ids, seed)
         except Exception as exc:  # noqa: BLE001 - recorded per sample; the run goes on (resume retries it)
             print(f"sample {i} failed: {exc!r}", file=sys.stderr, flush=True)
             append_jsonl(failures_path, {"index": i, "error": repr(exc)})
@@ -160,7 +162,7 @@ def main(argv=None) -> int:
         rec = {"index": i, "question": row["question"], "gold": gold, "prediction": pred,
                "correct": pred is not None and pred == gold, "response": text, "model": args.model,
                "backend": args.backend, "prompt_tokens": len(ids), "prompt_token_ids_sha256": token_ids_sha256(ids),
-               "generated_tokens": len(gen_ids), "elapsed_s": secs}
+               "generated_tokens": len(gen_ids), "elapsed_s": secs, "generation_seed": seed}
         if rounds:
             rec["target_intervention"] = {k: v for k, v in summarize_generation_interventions(
                 [r.to_dict() if hasattr(r, "to_dict") else r for r in rounds]).items() if k != "rounds"}

@@ -233,7 +233,7 @@ def test_gsm8k_records_failed_samples_and_goes_on(tmp_path, monkeypatch):
     calls = []
 
     def fake_make_generate(args):
-        def run(ids):
+        def run(ids, seed=None):
             calls.append(len(ids))
             if len(calls) == 2:
                 raise RuntimeError("boom")
@@ -247,3 +247,22 @@ def test_gsm8k_records_failed_samples_and_goes_on(tmp_path, monkeypatch):
     summary = json.loads((out / "summary.json").read_text())
     assert summary["count"] == 2 and summary["failures"] == 1 and summary["correct"] == 1
     assert json.loads((out / "failures.jsonl").read_text())["index"] == 1
+
+
+def test_gsm8k_request_seeds_and_sampled_ar(tmp_path):
+    """Each GSM8K request gets seed = generation seed + index; the AR backend samples with it."""
+    g = mod("eval.gsm8k")
+    data = tmp_path / "test.jsonl"
+    data.write_text("\n".join(json.dumps({"question": f"What is {i}+1?", "answer": f"#### {i + 1}"})
+                              for i in range(2)) + "\n")
+    rows = {}
+    for name, extra in (("greedy", []), ("sampled", ["--drafter-do-sample", "--drafter-temperature", "1.5"])):
+        out = tmp_path / name
+        assert g.main(["--backend", "ar", "--model", "tiny-drafter", "--dtype", "float32", "--page-size", "4",
+                       "--max-new-tokens", "8", "--device", "cpu", "--context-length", "256", "--warmup-runs", "0",
+                       "--generation-seed", "10", "--data-file", str(data), "--output-dir", str(out), *extra]) == 0
+        rows[name] = [json.loads(l) for l in (out / "predictions.jsonl").read_text().splitlines()]
+        assert json.loads((out / "summary.json").read_text())["settings"]["request_seed_rule"] == \
+            "generation_seed_plus_gsm8k_index"
+    assert [r["generation_seed"] for r in rows["sampled"]] == [10, 11]
+    assert [r["response"] for r in rows["greedy"]] != [r["response"] for r in rows["sampled"]]
