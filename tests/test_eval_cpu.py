@@ -266,3 +266,31 @@ def test_gsm8k_request_seeds_and_sampled_ar(tmp_path):
             "generation_seed_plus_gsm8k_index"
     assert [r["generation_seed"] for r in rows["sampled"]] == [10, 11]
     assert [r["response"] for r in rows["greedy"]] != [r["response"] for r in rows["sampled"]]
+
+
+def test_compare_interventions_pairs_runs(tmp_path):
+    import pytest
+
+    g, cmp_ = mod("eval.gsm8k"), mod("eval.compare_interventions")
+    data = tmp_path / "test.jsonl"
+    data.write_text("\n".join(json.dumps({"question": f"What is {i}+1?", "answer": f"x\n#### {i + 1}"})
+                              for i in range(2)) + "\n")
+    runs = {}
+    for policy in ("target_best", "first_route"):
+        out = tmp_path / policy
+        extra = ["--fallback-threshold", "none", "--first-token-threshold", "none"] if policy == "first_route" else []
+        assert g.main(_flags(tmp_path, "atlas_serial") + ["--data-file", str(data), "--output-dir", str(out),
+                                                        "--route-selection-policy", policy, "--warmup-runs", "0",
+                                                        *extra]) == 0
+        runs[policy] = out
+    rep = cmp_.compare(runs["target_best"], runs["first_route"])
+    assert rep["alignment"]["samples"] == 2 and rep["alignment"]["prompt_hash_checked"] == 2
+    assert rep["policies"] == {"target_best": "target_best", "first_route": "first_route",
+                               "policy_metadata_missing": False}
+    assert rep["paired_quality"]["pair_count"] == 2
+    with pytest.raises(ValueError):
+        cmp_.compare(runs["first_route"], runs["target_best"])  # the policies do not match their flags
+    out = tmp_path / "cmp.json"
+    assert cmp_.main(["--target-best", str(runs["target_best"] / "predictions.jsonl"), "--first-route",
+                      str(runs["first_route"]), "--json-out", str(out)]) == 0
+    assert json.loads(out.read_text())["comparison"] == "paired_target_best_vs_first_route"
