@@ -182,3 +182,34 @@ def test_equivalence_checker_cli(tmp_path):
         chk.check_target_policy({"route_selection_policy": "target_best"})
     with pytest.raises(SystemExit):
         chk.check_target_policy({"route_selection_policy": "first_route", "fallback_threshold": -0.5})
+
+
+def test_kv_reuse_diagnostics_cli(tmp_path):
+    import json
+
+    diag = mod("serving.diagnostics")
+    base = ["--device", "cpu", "--dtype", "float32", "--page-size", "4", "--prompt-token-ids", "5,6,7,8,9,10,11",
+            "--context-length", "256"]
+    out = tmp_path / "tc.json"
+    assert diag.main(["target-commit", "--model", "tiny-target", "--d", "3", "--rounds", "3", "--max-logit-diff",
+                      "1e-3", "--max-kv-diff", "1e-4", "--json-out", str(out), *base]) == 0
+    rep = json.loads(out.read_text())
+    assert rep["passed"] and rep["rounds"][-1]["prefix_len"] == 16 and "max_kv_diff" in rep["rounds"][-1]
+    out = tmp_path / "da.json"
+    assert diag.main(["drafter-alignment", "--model", "tiny-drafter", "--k", "2", "--d", "2", "--alignment-atol",
+                      "1e-4", "--alignment-rtol", "1e-4", "--json-out", str(out), *base]) == 0
+    stages = [s["stage"] for s in json.loads(out.read_text())["steps"]]
+    assert stages == ["tree", "tree", "forest", "post_commit_forest"]
+
+
+def test_prefix_kv_reads_positions_through_the_page_table():
+    diag, engine_mod, llama = mod("serving.diagnostics"), mod("runtime.engine"), mod("models.llama")
+    w = llama.random_weights(llama.get_config("tiny-drafter"), seed=1, dtype=torch.float32)
+    eng = engine_mod.LlamaEngine(w, num_pages=16, page_size=4, max_positions=64)
+    eng.kv.copy_(torch.randn_like(eng.kv))
+    pages = [7, 3, 11]
+    kv = diag.prefix_kv(eng, pages, 10)
+    L = eng.kv.shape[0]
+    assert tuple(kv.shape) == (L, 2, 10, eng.kv.shape[3], eng.kv.shape[5])
+    for pos in (0, 5, 9):
+        assert torch.equal(kv[1, 0, pos], eng.kv[1, pages[pos // 4], 0, :, pos % 4, :])
