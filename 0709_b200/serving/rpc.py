@@ -73,6 +73,11 @@ def selected_route_id_from_response(response: Mapping[str, object]) -> int:
     return int(response["selected_route_id"])
 
 
+# What this server understands beyond the reference's wire format (reported by /health, so a
+# client sends the compact forms only to a server that announced them).
+CAPABILITIES = ("prefix_tail_token_ids",)
+
+
 def _opt_int(v) -> int | None:
     return None if v is None else int(v)
 
@@ -102,7 +107,8 @@ class TargetServerApp:
         self.lock = threading.Lock()
 
     def health(self) -> dict[str, object]:
-        return {"ok": True, "service": "atlas_0709_target", "metadata": self.backend.runtime_metadata()}
+        return {"ok": True, "service": "atlas_0709_target", "capabilities": list(CAPABILITIES),
+                "metadata": self.backend.runtime_metadata()}
 
     def prefill(self, request: Mapping[str, Any]) -> dict[str, object]:
         toks = request.get("prompt_token_ids")
@@ -234,12 +240,22 @@ def serve_target(app: TargetServerApp, *, host: str, port: int) -> None:
 
 
 class RemoteTargetClient:
-    """HTTP client; ``session_id`` (optional) addresses one session of a multi-session server."""
+    """HTTP client; ``session_id`` (optional) addresses one session of a multi-session server.
 
-    def __init__(self, base_url: str, *, timeout: float = 600.0, session_id: str | None = None) -> None:
+    ``prefix_tail`` (default 8): when the server's ``/health`` announces ``prefix_tail_token_ids``,
+    a verify request carries the prefix length and its last ``prefix_tail`` tokens instead of the
+    whole committed prefix (the server checks both against the prefix whose KV it holds), so a
+    round's request no longer grows with the context.  ``None`` always sends the full prefix (the
+    reference's wire format, which every server accepts).
+    """
+
+    def __init__(self, base_url: str, *, timeout: float = 600.0, session_id: str | None = None,
+                 prefix_tail: int | None = 8) -> None:
         self.base_url = base_url.rstrip("/")
         self.timeout = float(timeout)
         self.session_id = session_id
+        self.prefix_tail = None if prefix_tail is None else max(1, int(prefix_tail))
+        self._compact: bool | None = None  # learned from /health on the first verify
 
     def health(self) -> dict[str, object]:
         with urllib.request.urlopen(f"{self.base_url}/health", timeout=self.timeout) as r:
@@ -250,10 +266,16 @@ class RemoteTargetClient:
 
     def verify(self, *, prefix_token_ids, routes, fallback_max_tokens=None, selected_path_max_tokens=None,
                eos_token_id=None, route_sampling_seed=None, route_sampling_round=None) -> dict[str, object]:
-        payload: dict[str, object] = {
-            "prefix_token_ids": [int(t) for t in prefix_token_ids],
-            "routes": [dict(r) for r in routes],
-        }
+        prefix = [int(t) for t in prefix_token_ids]
+        if self._compact is None:
+            self._compact = self.prefix_tail is not None and "prefix_tail_token_ids" in (
+                self.health().get("capabilities") or [])
+        if self._compact:
+            payload: dict[str, object] = {"prefix_len": len(prefix),
+                                          "prefix_tail_token_ids": prefix[-self.prefix_tail:]}
+        else:
+            payload = {"prefix_token_ids": prefix}
+        payload["routes"] = [dict(r) for r in routes]
         for key, val in (
             ("fallback_max_tokens", fallback_max_tokens),
             ("selected_path_max_tokens", selected_path_max_tokens),

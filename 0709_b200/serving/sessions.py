@@ -49,8 +49,10 @@ class MultiSessionTargetApp:
         return str((request or {}).get("session_id", "default"))
 
     def health(self, request: Mapping[str, Any] | None = None) -> dict[str, object]:
-        return {"ok": True, "service": "atlas_0709_target_multi_session", "sessions": sorted(self.sessions),
-                "served": dict(self.served)}
+        from .rpc import CAPABILITIES
+
+        return {"ok": True, "service": "atlas_0709_target_multi_session", "capabilities": list(CAPABILITIES),
+                "sessions": sorted(self.sessions), "served": dict(self.served)}
 
     def prefill(self, request: Mapping[str, Any]) -> dict[str, object]:
         with self.lock:

@@ -103,12 +103,25 @@ def test_http_target_round_trip(tiny):
     th.start()
     try:
         url = f"http://127.0.0.1:{server.server_address[1]}"
-        client = rpc.RemoteTargetClient(url, timeout=60)
-        assert client.health()["ok"] is True
         cfg = edge.DistributedAtlasConfig(k=2, d=2, max_new_tokens=10, validate_state_alignment=True)
-        dr = drafter.DrafterRuntime(engine.LlamaEngine(dw, num_pages=256, page_size=4, max_positions=256))
-        remote = edge.PagedDistributedAtlasGenerator(config=cfg, drafter=dr, target_client=client).generate(
-            list(range(40, 60)))
+        results = {}
+        # The compact prefix this server announces, then the reference's full prefix; the server keeps
+        # one session, so the second generation starts from its own /prefill.
+        for tail in (8, None):
+            client = rpc.RemoteTargetClient(url, timeout=60, prefix_tail=tail)
+            assert client.health()["ok"] is True
+            sent = []
+            post = client._post
+            client._post = lambda path, payload, post=post: (sent.append(dict(payload)), post(path, payload))[1]
+            dr = drafter.DrafterRuntime(engine.LlamaEngine(dw, num_pages=256, page_size=4, max_positions=256))
+            results[tail] = edge.PagedDistributedAtlasGenerator(config=cfg, drafter=dr,
+                                                                target_client=client).generate(list(range(40, 60)))
+            verifies = [p for p in sent if "routes" in p]
+            assert verifies
+            if tail:
+                assert all("prefix_token_ids" not in p and len(p["prefix_tail_token_ids"]) <= tail for p in verifies)
+            else:
+                assert all(len(p["prefix_token_ids"]) >= 20 for p in verifies)
     finally:
         server.shutdown()
         server.server_close()
@@ -117,8 +130,19 @@ def test_http_target_round_trip(tiny):
     local = edge.PagedDistributedAtlasGenerator(config=cfg, drafter=dr2,
                                                 target_client=rpc.InProcessTargetClient(tv2)).generate(
         list(range(40, 60)))
-    assert remote.generated_token_ids == local.generated_token_ids
-    assert [r.decision for r in remote.rounds] == [r.decision for r in local.rounds]
+    for remote in results.values():
+        assert remote.generated_token_ids == local.generated_token_ids
+        assert [r.decision for r in remote.rounds] == [r.decision for r in local.rounds]
+
+
+def test_client_sends_full_prefix_to_a_server_without_the_capability():
+    rpc = mod("serving.rpc")
+    client = rpc.RemoteTargetClient("http://127.0.0.1:9", prefix_tail=8)
+    sent = []
+    client.health = lambda: {"ok": True, "service": "atlas_0709_target"}  # e.g. the reference's server
+    client._post = lambda path, payload: sent.append(dict(payload)) or {}
+    client.verify(prefix_token_ids=list(range(30)), routes=[])
+    assert sent[0]["prefix_token_ids"] == list(range(30)) and "prefix_len" not in sent[0]
 
 
 def test_edge_cli_in_process_target(tmp_path, capsys):
