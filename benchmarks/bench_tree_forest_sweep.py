@@ -109,7 +109,7 @@ def required_context(prompt_len: int, pairs) -> int:
 def main(argv=None) -> int:
     args = build_parser().parse_args(argv)
     pairs = [tuple(x) for x in (args.pairs or [[3, 4]])]
-    llama, loader = pkg("models.llama"), pkg("models.loader")
+    loader = pkg("models.loader")
     engine_mod, drafter_mod, store_mod = pkg("runtime.engine"), pkg("runtime.drafter"), pkg("runtime.store")
     dev = torch.device(args.device if args.gpu_id is None else f"cuda:{args.gpu_id}")
     if dev.type == "cuda" and dev.index is not None:
