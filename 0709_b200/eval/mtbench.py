@@ -3,6 +3,7 @@
     python -m 0709_b200.eval.mtbench generate --backend atlas --questions q.jsonl --output-dir out ...
     python -m 0709_b200.eval.mtbench judge --answers out/answers.jsonl --judge-url https://.../v1/chat/completions
     python -m 0709_b200.eval.mtbench --drafter-model ... --target-url ... --questions-file q.jsonl --output-dir out
+    python -m 0709_b200.eval.mtbench --model-1b ... --model-8b ... --questions-file q.jsonl --output-dir ar_out
 
 ``generate`` reads local question records (``question_id``, ``category``,
 ``turns``: list of user turns), runs each conversation turn by turn (the
@@ -15,7 +16,9 @@ to an OpenAI-compatible chat-completions endpoint (API key from
 and writes judgments plus a per-category average.  This machine has no
 network, so ``judge`` only runs where the endpoint is reachable.
 
-The third form is the reference's one command (generate, then judge; ``--skip-*`` and
+The fourth form writes the AR baselines: greedy answers of a 1B and an 8B model into one
+``generations.jsonl`` under a run id that an ATLAS run names with ``--ar-generations`` /
+``--ar-run-id``, then grades them.  The third form is the reference's one command (generate, then judge; ``--skip-*`` and
 ``--resume-*`` per phase; ``--ar-generations`` grades AR answers in the same run).  The judge
 retries HTTP 429 / 5xx and connection errors, can grade each answer ``--judge-repeats`` times,
 and sends the DeepSeek ``thinking`` / ``reasoning_effort`` fields when they are given.
@@ -27,6 +30,7 @@ rounds_detail :164-207, judge client :545-662, flags :1299-1383).
 from __future__ import annotations
 
 import argparse
+import hashlib
 import json
 import os
 import re
@@ -40,7 +44,8 @@ from pathlib import Path
 
 from ..serving.prompts import decode, encode, load_tokenizer
 from ..utils.interventions import summarize_generation_interventions
-from .common import add_atlas_flags, add_generation_flags, append_jsonl, make_generate, read_jsonl, timed, warm_up
+from .common import add_atlas_flags, add_generation_flags, add_runtime_compat_flags, append_jsonl, make_generate, \
+    read_jsonl, timed, warm_up
 
 RATING_RE = re.compile(r"\[\[(\d+(?:\.\d+)?)\]\]")
 JUDGE_PROMPT = (
@@ -70,14 +75,23 @@ def select_questions(qs: list[dict], args) -> list[dict]:
     return qs[: int(n)] if n is not None else qs
 
 
-def cmd_generate(args) -> int:
+def cmd_generate(args, *, path: Path | None = None, extra: dict | None = None, keep_file: bool = False) -> int:
+    """Answer every selected question into ``path`` (default ``<output-dir>/answers.jsonl``).
+    ``extra`` fields go into every record (an AR run's label and run id); with ``--resume`` the
+    questions already answered under the same ``extra`` are skipped; ``keep_file`` keeps records
+    of other runs in a shared file."""
     tok = load_tokenizer(args.tokenizer)
     qs = select_questions(read_jsonl(args.questions), args)
     out = Path(args.output_dir)
     out.mkdir(parents=True, exist_ok=True)
-    path = out / "answers.jsonl"
-    done = {r["question_id"] for r in read_jsonl(path)} if (args.resume and path.exists()) else set()
-    if not args.resume and path.exists():
+    path = path or out / "answers.jsonl"
+    extra = dict(extra or {})
+
+    def mine(r) -> bool:
+        return all(r.get(key) == val for key, val in extra.items())
+
+    done = {r["question_id"] for r in read_jsonl(path) if mine(r)} if (args.resume and path.exists()) else set()
+    if not args.resume and path.exists() and not keep_file:
         path.unlink()
     generate = make_generate(args)
     system = f"System: {args.system_prompt}\n" if getattr(args, "system_prompt", "") else ""
@@ -100,7 +114,7 @@ def cmd_generate(args) -> int:
             turns.append(turn)
             history = ids + list(gen) + encode(tok, "\n")
         append_jsonl(path, {"question_id": q["question_id"], "category": q.get("category"), "model": args.model,
-                            "backend": args.backend, "turns": turns})
+                            "backend": args.backend, "turns": turns, **extra})
     print(json.dumps({"answers": str(path), "questions": len(qs)}))
     return 0
 
@@ -178,7 +192,7 @@ def _answer_sets(args) -> list[tuple[str, list[dict]]]:
     ``--ar-generations``, the AR answers (records of ``generate --backend ar``; ``--ar-run-id``
     keeps the records whose ``run_id`` matches).  Each answer is graded on its own, so the
     judge never sees which system wrote it."""
-    sets = [("answers", read_jsonl(args.answers))]
+    sets = [("answers", read_jsonl(args.answers))] if getattr(args, "answers", None) else []
     extra = getattr(args, "ar_generations", None)
     if extra:
         recs = read_jsonl(extra)
@@ -201,7 +215,7 @@ def cmd_judge(args) -> int:
         key=os.environ.get(args.api_key_env) if args.api_key_env else None, timeout=args.timeout,
         retries=args.judge_retries, retry_delay=args.judge_retry_delay, max_tokens=args.judge_max_tokens,
         thinking=args.judge_thinking, reasoning_effort=args.judge_reasoning_effort)
-    out = Path(args.output or (Path(args.answers).parent / "judgments.jsonl"))
+    out = Path(args.output or (Path(args.answers or args.ar_generations).parent / "judgments.jsonl"))
     done: set[tuple] = set()
     if out.exists():
         if getattr(args, "resume", False):
@@ -314,8 +328,78 @@ def run_flat(argv) -> int:
     return cmd_judge(j)
 
 
+def ar_parser() -> argparse.ArgumentParser:
+    """The reference's AR-baseline command (scripts/mtbench_ar_deepseek_eval.py): greedy AR answers
+    of a 1B and an 8B model under one run id, then (optionally) their judging."""
+    p = argparse.ArgumentParser(description="MT-Bench AR baselines (1B and 8B greedy), then judging",
+                                allow_abbrev=False)
+    p.add_argument("--model-1b", required=True, help="preset or checkpoint directory")
+    p.add_argument("--model-8b", required=True, help="preset or checkpoint directory")
+    p.add_argument("--questions-file", required=True)
+    p.add_argument("--questions-url", default=None, help="not fetched: there is no network here")
+    p.add_argument("--download-timeout", type=float, default=60.0, help="No-op (nothing is downloaded).")
+    p.add_argument("--output-dir", required=True)
+    add_question_flags(p)
+    p.add_argument("--max-new-tokens", type=int, default=1024)
+    p.add_argument("--eos-token-id", type=int, default=None)
+    p.add_argument("--dtype", choices=["float16", "bfloat16", "float32"], default="float16")
+    p.add_argument("--context-length", type=int, default=16384)
+    p.add_argument("--page-size", type=int, default=16)
+    p.add_argument("--tokenizer", default=None)
+    p.add_argument("--device", default=None)
+    p.add_argument("--seed", type=int, default=0, help="seed of random-init presets")
+    add_runtime_compat_flags(p)
+    p.add_argument("--skip-generate", action="store_true")
+    p.add_argument("--resume-generate", action="store_true")
+    p.add_argument("--skip-judge", action="store_true")
+    p.add_argument("--resume-judge", action="store_true")
+    p.add_argument("--deepseek-api-key-env", default="DEEPSEEK_API_KEY")
+    p.add_argument("--judge-timeout", type=float, default=180.0)
+    add_judge_flags(p, flat=True)
+    p.set_defaults(judge_max_tokens=4096, judge_retries=4)
+    return p
+
+
+def ar_run_id(a) -> str:
+    """A stable id of the generation settings, so a later ATLAS run can name this AR run."""
+    keys = ("model_1b", "model_8b", "questions_file", "question_start", "question_end", "max_questions",
+            "turn_mode", "system_prompt", "max_new_tokens", "eos_token_id", "dtype", "page_size", "seed")
+    blob = json.dumps({key: getattr(a, key) for key in keys}, sort_keys=True, default=str)
+    return hashlib.sha256(blob.encode()).hexdigest()[:12]
+
+
+def run_ar(argv) -> int:
+    a = ar_parser().parse_args(argv)
+    if not Path(a.questions_file).exists():
+        raise SystemExit(f"{a.questions_file}: not found (questions are not downloaded; there is no network here)")
+    out = Path(a.output_dir)
+    gens = out / "generations.jsonl"
+    rid = ar_run_id(a)
+    if not a.skip_generate:
+        if gens.exists() and not a.resume_generate:
+            gens.unlink()
+        for label, model in (("ar_1b", a.model_1b), ("ar_8b", a.model_8b)):
+            g = argparse.Namespace(**vars(a), backend="ar", model=model, questions=a.questions_file,
+                                   resume=a.resume_generate, k=1, d=1, generation_seed=0, drafter_do_sample=False,
+                                   drafter_temperature=1.0, fallback_ar_tokens=1)
+            rc = cmd_generate(g, path=gens, extra={"model": label, "checkpoint": str(model), "run_id": rid},
+                              keep_file=True)
+            if rc:
+                return rc
+    print(json.dumps({"generation_run_id": rid, "generations": str(gens)}))
+    if a.skip_judge:
+        return 0
+    j = argparse.Namespace(**vars(a))
+    j.answers, j.questions, j.output = None, a.questions_file, str(out / "judgments.jsonl")
+    j.ar_generations, j.ar_run_id = str(gens), rid
+    j.judge_url, j.api_key_env, j.timeout, j.resume = None, a.deepseek_api_key_env, a.judge_timeout, a.resume_judge
+    return cmd_judge(j)
+
+
 def main(argv=None) -> int:
     argv = list(sys.argv[1:] if argv is None else argv)
+    if "--model-1b" in argv or "--model-8b" in argv:
+        return run_ar(argv)
     if not argv or argv[0] not in ("generate", "judge", "-h", "--help"):
         return run_flat(argv)
     p = argparse.ArgumentParser(description="MT-Bench generation and judging (or the reference's one-command "

@@ -294,3 +294,34 @@ def test_compare_interventions_pairs_runs(tmp_path):
     assert cmp_.main(["--target-best", str(runs["target_best"] / "predictions.jsonl"), "--first-route",
                       str(runs["first_route"]), "--json-out", str(out)]) == 0
     assert json.loads(out.read_text())["comparison"] == "paired_target_best_vs_first_route"
+
+
+def test_mtbench_ar_baselines_feed_the_atlas_run(tmp_path, monkeypatch):
+    mt = mod("eval.mtbench")
+    q = tmp_path / "q.jsonl"
+    q.write_text("\n".join(json.dumps({"question_id": i, "category": "c", "turns": ["hi"]}) for i in range(2)) + "\n")
+    judge = _Judge()
+    monkeypatch.setenv("TEST_JUDGE_KEY", "k")
+    common = ["--dtype", "float32", "--page-size", "4", "--max-new-tokens", "3", "--device", "cpu",
+              "--context-length", "128", "--questions-file", str(q), "--warmup-runs", "0",
+              "--judge-base-url", judge.base, "--deepseek-api-key-env", "TEST_JUDGE_KEY", "--judge-retry-delay", "0"]
+    try:
+        ar_out = tmp_path / "ar"
+        assert mt.main(["--model-1b", "tiny-drafter", "--model-8b", "tiny-target", "--output-dir", str(ar_out),
+                        *common]) == 0
+        gens = [json.loads(l) for l in (ar_out / "generations.jsonl").read_text().splitlines()]
+        assert sorted((g["model"], g["question_id"]) for g in gens) == [("ar_1b", 0), ("ar_1b", 1), ("ar_8b", 0),
+                                                                      ("ar_8b", 1)]
+        rid = gens[0]["run_id"]
+        assert {g["run_id"] for g in gens} == {rid}
+        js = [json.loads(l) for l in (ar_out / "judgments.jsonl").read_text().splitlines()]
+        assert sorted({x["source"] for x in js}) == ["ar:ar_1b", "ar:ar_8b"] and len(js) == 4
+        # The ATLAS run grades its own answers and the AR run's, named by its run id.
+        out = tmp_path / "atlas"
+        assert mt.main(["--drafter-model", "tiny-drafter", "--target-model", "tiny-target", "--k", "2", "--d", "2",
+                        "--path-score-weights", "", "--output-dir", str(out), "--ar-generations",
+                        str(ar_out / "generations.jsonl"), "--ar-run-id", rid, *common]) == 0
+        js = [json.loads(l) for l in (out / "judgments.jsonl").read_text().splitlines()]
+        assert sorted({x["source"] for x in js}) == ["answers", "ar:ar_1b", "ar:ar_8b"]
+    finally:
+        judge.close()
