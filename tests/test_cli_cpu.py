@@ -191,3 +191,24 @@ def test_forest_gate_flags_and_validation(tmp_path):
         edge.DistributedAtlasConfig(forest_gate="sometimes").validate()
     with pytest.raises(ValueError):
         edge.DistributedAtlasConfig(forest_gate_threshold=0.0).validate()
+
+
+def test_console_scripts_resolve():
+    """Every console script of pyproject.toml names a function of the entry module whose command
+    module exists and has a ``main``."""
+    import importlib
+    import os
+    import tomllib
+
+    from conftest import REPO
+
+    with open(os.path.join(REPO, "pyproject.toml"), "rb") as f:
+        scripts = tomllib.load(f)["project"]["scripts"]
+    assert "atlas-0709-run" in scripts and "atlas-target-server" in scripts
+    entry = importlib.import_module("atlas_b200_entry")
+    for name, ref in scripts.items():
+        module, func = ref.split(":")
+        assert module == "atlas_b200_entry" and callable(getattr(entry, func)), name
+    for module in ("serving.cli", "serving.target_server", "serving.distributed_system", "serving.check_equivalence",
+                   "serving.diagnostics", "eval.gsm8k", "eval.mtbench", "eval.sweep", "eval.compare_interventions"):
+        assert callable(mod(module).main)
