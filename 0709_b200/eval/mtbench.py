@@ -333,8 +333,10 @@ def ar_parser() -> argparse.ArgumentParser:
     of a 1B and an 8B model under one run id, then (optionally) their judging."""
     p = argparse.ArgumentParser(description="MT-Bench AR baselines (1B and 8B greedy), then judging",
                                 allow_abbrev=False)
-    p.add_argument("--model-1b", required=True, help="preset or checkpoint directory")
-    p.add_argument("--model-8b", required=True, help="preset or checkpoint directory")
+    p.add_argument("--model-1b", default=None, help="preset or checkpoint directory")
+    p.add_argument("--model-8b", default=None, help="preset or checkpoint directory")
+    p.add_argument("--candidate", choices=["1b", "8b", "both"], default="both",
+                   help="generate one AR candidate or both, one after the other")
     p.add_argument("--questions-file", required=True)
     p.add_argument("--questions-url", default=None, help="not fetched: there is no network here")
     p.add_argument("--download-timeout", type=float, default=60.0, help="No-op (nothing is downloaded).")
@@ -362,7 +364,7 @@ def ar_parser() -> argparse.ArgumentParser:
 
 def ar_run_id(a) -> str:
     """A stable id of the generation settings, so a later ATLAS run can name this AR run."""
-    keys = ("model_1b", "model_8b", "questions_file", "question_start", "question_end", "max_questions",
+    keys = ("model_1b", "model_8b", "candidate", "questions_file", "question_start", "question_end", "max_questions",
             "turn_mode", "system_prompt", "max_new_tokens", "eos_token_id", "dtype", "page_size", "seed")
     blob = json.dumps({key: getattr(a, key) for key in keys}, sort_keys=True, default=str)
     return hashlib.sha256(blob.encode()).hexdigest()[:12]
@@ -376,9 +378,16 @@ def run_ar(argv) -> int:
     gens = out / "generations.jsonl"
     rid = ar_run_id(a)
     if not a.skip_generate:
+        chosen = [(label, model) for label, model, key in (("ar_1b", a.model_1b, "1b"), ("ar_8b", a.model_8b, "8b"))
+                  if a.candidate in (key, "both")]
         if gens.exists() and not a.resume_generate:
-            gens.unlink()
-        for label, model in (("ar_1b", a.model_1b), ("ar_8b", a.model_8b)):
+            # Start these candidates over; other runs' and other candidates' answers stay.
+            labels = {label for label, _ in chosen}
+            keep = [r for r in read_jsonl(gens) if not (r.get("run_id") == rid and r.get("model") in labels)]
+            gens.write_text("".join(json.dumps(r) + "\n" for r in keep))
+        for label, model in chosen:
+            if model is None:
+                raise SystemExit(f"--candidate {a.candidate} needs --model-{label[3:]}")
             g = argparse.Namespace(**vars(a), backend="ar", model=model, questions=a.questions_file,
                                    resume=a.resume_generate, k=1, d=1, generation_seed=0, drafter_do_sample=False,
                                    drafter_temperature=1.0, fallback_ar_tokens=1)

@@ -57,6 +57,7 @@ def build_parser() -> argparse.ArgumentParser:
     t = sub.add_parser("target-commit", allow_abbrev=False)
     _common(t)
     t.add_argument("--rounds", type=int, default=4)
+    t.add_argument("--route-selection-policy", choices=["target_best", "first_route"], default="first_route")
     t.add_argument("--max-logit-diff", type=float, default=1.0)
     t.add_argument("--max-kv-diff", type=float, default=1.0)
     a = sub.add_parser("drafter-alignment", allow_abbrev=False)
@@ -65,6 +66,12 @@ def build_parser() -> argparse.ArgumentParser:
     a.add_argument("--skip-forest", action="store_true")
     a.add_argument("--alignment-atol", type=float, default=1.0)
     a.add_argument("--alignment-rtol", type=float, default=0.05)
+    a.add_argument("--check-hf-logits", action="store_true",
+                   help="accepted for the reference's command line: the recompute check always runs")
+    a.add_argument("--logits-tensor-out", default=None,
+                   help="torch.save every checked row's logits and its recompute reference to this file")
+    for flag in ("--legacy-token-attention-metadata", "--skip-page-layout-validation"):
+        a.add_argument(flag, action="store_true", help="No-op (the reference's SGLang page-table switches).")
     return p
 
 
@@ -120,7 +127,7 @@ def target_commit(args) -> dict:
     prompt = _prompt(args, vocab)
     if len(prompt) + args.rounds * args.d + 64 > args.context_length:
         raise SystemExit("--context-length is too short for the prompt and the committed rounds")
-    tv = TargetVerifier(_engine(w, args), k=3, d=args.d, route_selection_policy="first_route")
+    tv = TargetVerifier(_engine(w, args), k=3, d=args.d, route_selection_policy=args.route_selection_policy)
     tv.prefill(prompt)
     g = torch.Generator().manual_seed(args.seed)
     rounds = []
@@ -170,13 +177,18 @@ def drafter_alignment(args) -> dict:
     dr.bind_store(store)
     dr.prefill(prompt)
     steps = []
+    trace: list[dict] = []
 
     def check(stage: str, depth: int, step, prefix) -> None:
         logits = step.decode_output.next_token_logits.float()
         rows = []
         for i, r in enumerate(step.decoded_routes):
-            ref = llama.reference_forward(w_ref, list(prefix) + list(store.materialized_token_path(r)))[-1]
+            toks = list(prefix) + list(store.materialized_token_path(r))
+            ref = llama.reference_forward(w_ref, toks)[-1]
             got = logits[i].to(ref.device)
+            if args.logits_tensor_out:
+                trace.append({"stage": stage, "depth": depth, "tokens": toks, "logits": got.cpu(),
+                              "reference": ref.cpu()})
             gap = (got - ref).abs()
             rows.append({"max_abs_diff": float(gap.max()),
                          "within": bool((gap <= args.alignment_atol + args.alignment_rtol * ref.abs()).all()),
@@ -202,6 +214,8 @@ def drafter_alignment(args) -> dict:
         check("post_commit_forest", half + 1,
               builders.build_tree_one_depth(promoted, k=k, route_store=store, model_backend=dr), committed)
     dr.engine.ops.check()
+    if args.logits_tensor_out:
+        torch.save(trace, args.logits_tensor_out)
     return {"check": "drafter_route_kv_alignment", "passed": all(s["passed"] for s in steps), "model": args.model,
             "k": k, "d": d, "prompt_len": len(prompt), "atol": args.alignment_atol, "rtol": args.alignment_rtol,
             "steps": steps}

@@ -200,6 +200,13 @@ def test_kv_reuse_diagnostics_cli(tmp_path):
                       "1e-4", "--alignment-rtol", "1e-4", "--json-out", str(out), *base]) == 0
     stages = [s["stage"] for s in json.loads(out.read_text())["steps"]]
     assert stages == ["tree", "tree", "forest", "post_commit_forest"]
+    trace = tmp_path / "trace.pt"
+    assert diag.main(["drafter-alignment", "--model", "tiny-drafter", "--k", "2", "--d", "2", "--skip-forest",
+                      "--check-hf-logits", "--logits-tensor-out", str(trace), *base]) == 0
+    rows = torch.load(trace)
+    assert len(rows) == 4 and torch.allclose(rows[0]["logits"], rows[0]["reference"], atol=1e-3)
+    assert diag.main(["target-commit", "--model", "tiny-target", "--d", "2", "--rounds", "2",
+                      "--route-selection-policy", "target_best", *base]) == 0
 
 
 def test_prefix_kv_reads_positions_through_the_page_table():
