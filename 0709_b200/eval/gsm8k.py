@@ -25,7 +25,7 @@ import statistics
 import sys
 from pathlib import Path
 
-from ..serving.prompts import decode, encode, load_tokenizer
+from ..serving.prompts import chat_ids, chat_stop_token, decode, encode, load_chat_tokenizer, load_tokenizer
 from ..utils.interventions import aggregate_prediction_interventions, summarize_generation_interventions
 from .common import add_generation_flags, append_jsonl, done_indices, make_generate, read_jsonl, rows_summary, \
     timed, token_ids_sha256, warm_up
@@ -96,8 +96,8 @@ def serial_speed(preds: list[dict]) -> dict:
 def settings(args, num_fewshot: int) -> dict:
     """The generation settings of the run, recorded beside its results."""
     atlas = args.backend.startswith("atlas")
-    keep = ("protocol", "max_new_tokens", "strict_marker", "system_prompt", "context_length", "dtype", "page_size",
-            "generation_seed", "drafter_do_sample", "drafter_temperature")
+    keep = ("protocol", "chat_template", "max_new_tokens", "strict_marker", "system_prompt", "context_length", "dtype",
+            "page_size", "eos_token_id", "generation_seed", "drafter_do_sample", "drafter_temperature")
     out = {key: getattr(args, key) for key in keep}
     out["num_fewshot"] = num_fewshot
     out["request_seed_rule"] = "generation_seed_plus_gsm8k_index"
@@ -107,6 +107,17 @@ def settings(args, num_fewshot: int) -> dict:
                 "route_sampling_temperature"):
         out[key] = getattr(args, key) if atlas else None
     return out
+
+
+def build_messages(question: str, fewshot: list[dict], system_prompt: str = "") -> list[dict]:
+    """The same prompt as chat turns: the system prompt, each exemplar as a user/assistant pair,
+    then the question."""
+    msgs = [{"role": "system", "content": system_prompt}] if system_prompt else []
+    for ex in fewshot:
+        msgs += [{"role": "user", "content": f"{INSTRUCTION}\n\nQuestion: {ex['question']}"},
+                 {"role": "assistant", "content": str(ex["answer"])}]
+    msgs.append({"role": "user", "content": f"{INSTRUCTION}\n\nQuestion: {question}"})
+    return msgs
 
 
 def build_parser() -> argparse.ArgumentParser:
@@ -123,6 +134,9 @@ def build_parser() -> argparse.ArgumentParser:
                    help="llama-8shot: the eight chain-of-thought exemplars of --fewshot-file; zero-shot: none; "
                         "auto: few-shot exactly when --fewshot-file is given")
     p.add_argument("--system-prompt", default="", help="text placed before the instruction")
+    p.add_argument("--chat-template", choices=["auto", "off"], default="auto",
+                   help="auto: prompts as chat turns rendered by the tokenizer's chat template (and its "
+                        "end-of-turn token as EOS) when --tokenizer is a directory that has one")
     return p
 
 
@@ -139,17 +153,28 @@ def main(argv=None) -> int:
         raise SystemExit("--protocol llama-8shot needs the eight exemplars as JSONL in --fewshot-file "
                          f"(got {len(fewshot)}); there is no network here to fetch them")
     tok = load_tokenizer(args.tokenizer)
+    chat = load_chat_tokenizer(args.tokenizer) if args.chat_template == "auto" else None
+    if chat is not None and args.eos_token_id is None:
+        args.eos_token_id = chat_stop_token(chat)
+
+    def prompt_ids(question: str) -> list[int]:
+        if chat is not None:
+            return chat_ids(chat, build_messages(question, fewshot, args.system_prompt))
+        return encode(tok, build_prompt(question, fewshot, args.system_prompt))
+
+    def text_of(ids) -> str:
+        return (chat.decode(ids, skip_special_tokens=True) if chat is not None else decode(tok, ids)) or ""
+
     done = done_indices(pred_path) if args.resume else set()
     if not args.resume and pred_path.exists():
         pred_path.unlink()
     generate = make_generate(args)
     pending = [(i, row) for i, row in enumerate(rows, start=args.start) if i not in done]
     if pending:
-        warm_up(generate, encode(tok, build_prompt(str(pending[0][1]["question"]), fewshot, args.system_prompt)),
-                args.warmup_runs)
+        warm_up(generate, prompt_ids(str(pending[0][1]["question"])), args.warmup_runs)
     failures_path = out / "failures.jsonl"
     for i, row in pending:
-        ids = encode(tok, build_prompt(str(row["question"]), fewshot, args.system_prompt))
+        ids = prompt_ids(str(row["question"]))
         seed = int(args.generation_seed) + int(i)  # one request seed per GSM8K index
         try:
             (gen_ids, meta, rounds), secs = timed(generate, ids, seed)
@@ -157,7 +182,7 @@ def main(argv=None) -> int:
             print(f"sample {i} failed: {exc!r}", file=sys.stderr, flush=True)
             append_jsonl(failures_path, {"index": i, "error": repr(exc)})
             continue
-        text = decode(tok, gen_ids) or ""
+        text = text_of(gen_ids)
         pred, gold = extract(text, strict=args.strict_marker), gold_answer(row)
         rec = {"index": i, "question": row["question"], "gold": gold, "prediction": pred,
                "correct": pred is not None and pred == gold, "response": text, "model": args.model,

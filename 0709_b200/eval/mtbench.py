@@ -42,7 +42,7 @@ import urllib.request
 from dataclasses import dataclass
 from pathlib import Path
 
-from ..serving.prompts import decode, encode, load_tokenizer
+from ..serving.prompts import chat_ids, chat_stop_token, decode, encode, load_chat_tokenizer, load_tokenizer
 from ..utils.interventions import summarize_generation_interventions
 from .common import add_atlas_flags, add_generation_flags, add_runtime_compat_flags, append_jsonl, make_generate, \
     read_jsonl, timed, warm_up
@@ -93,20 +93,35 @@ def cmd_generate(args, *, path: Path | None = None, extra: dict | None = None, k
     done = {r["question_id"] for r in read_jsonl(path) if mine(r)} if (args.resume and path.exists()) else set()
     if not args.resume and path.exists() and not keep_file:
         path.unlink()
+    chat = load_chat_tokenizer(args.tokenizer) if getattr(args, "chat_template", "auto") == "auto" else None
+    if chat is not None and args.eos_token_id is None:
+        args.eos_token_id = chat_stop_token(chat)
     generate = make_generate(args)
-    system = f"System: {args.system_prompt}\n" if getattr(args, "system_prompt", "") else ""
+    sys_prompt = getattr(args, "system_prompt", "") or ""
+    system = f"System: {sys_prompt}\n" if sys_prompt else ""
     pending = [q for q in qs if q["question_id"] not in done]
     if pending:
-        warm_up(generate, encode(tok, f"{system}User: {pending[0]['turns'][0]}\nAssistant:"), args.warmup_runs)
+        first = pending[0]["turns"][0]
+        warm_up(generate, chat_ids(chat, [{"role": "user", "content": first}]) if chat is not None
+                else encode(tok, f"{system}User: {first}\nAssistant:"), args.warmup_runs)
     for q in pending:
-        history: list[int] = encode(tok, system) if system else []
+        history: list[int] = encode(tok, system) if system and chat is None else []
+        messages = [{"role": "system", "content": sys_prompt}] if sys_prompt else []
         turns = []
         user_turns = q["turns"][:1] if getattr(args, "turn_mode", "conversation") == "first" else q["turns"]
         for t, user in enumerate(user_turns):
-            ids = history + encode(tok, f"User: {user}\nAssistant:")
+            if chat is not None:
+                # The conversation so far, rendered by the checkpoint's own chat template.
+                messages.append({"role": "user", "content": user})
+                ids = chat_ids(chat, messages)
+            else:
+                ids = history + encode(tok, f"User: {user}\nAssistant:")
             (gen, meta, rounds), secs = timed(generate, ids)
-            text = decode(tok, gen) or ""
-            turn = {"turn": t, "answer": text, "generated_tokens": len(gen), "elapsed_s": secs}
+            text = (chat.decode(gen, skip_special_tokens=True) if chat is not None else decode(tok, gen)) or ""
+            if chat is not None:
+                messages.append({"role": "assistant", "content": text})
+            turn = {"turn": t, "answer": text, "prompt_tokens": len(ids), "generated_tokens": len(gen),
+                    "elapsed_s": secs}
             if rounds:
                 turn["rounds_detail"] = compact_rounds(rounds)
                 turn["target_intervention"] = {k: v for k, v in summarize_generation_interventions(
@@ -306,6 +321,9 @@ def add_question_flags(p) -> None:
     p.add_argument("--max-questions", type=int, default=None)
     p.add_argument("--turn-mode", choices=["first", "conversation"], default="conversation")
     p.add_argument("--system-prompt", default="")
+    p.add_argument("--chat-template", choices=["auto", "off"], default="auto",
+                   help="auto: turns rendered by the tokenizer's chat template (its end-of-turn token as EOS) "
+                        "when --tokenizer is a directory that has one")
 
 
 def run_flat(argv) -> int:

@@ -36,6 +36,48 @@ def decode(tokenizer, ids: Sequence[int]) -> str | None:
     return tokenizer.decode([int(t) for t in ids], skip_special_tokens=False)
 
 
+def load_chat_tokenizer(path: str | None):
+    """transformers' tokenizer of a checkpoint or tokenizer directory that carries a chat template
+    (``chat_template.jinja``, or ``chat_template`` in ``tokenizer_config.json``); else None."""
+    import json
+    import os
+
+    if not path or not os.path.isdir(path):
+        return None
+    cfg = os.path.join(path, "tokenizer_config.json")
+    has = os.path.exists(os.path.join(path, "chat_template.jinja"))
+    if not has and os.path.exists(cfg):
+        with open(cfg, encoding="utf-8") as f:
+            has = bool(json.load(f).get("chat_template"))
+    if not has:
+        return None
+    from transformers import AutoTokenizer
+
+    return AutoTokenizer.from_pretrained(path)
+
+
+def chat_ids(tokenizer, messages: Sequence[dict]) -> list[int]:
+    """Token ids of ``messages`` rendered by the tokenizer's chat template, ending with the
+    assistant's generation prompt."""
+    enc = tokenizer.apply_chat_template(list(messages), tokenize=True, add_generation_prompt=True)
+    if isinstance(enc, dict) or hasattr(enc, "keys"):
+        enc = enc["input_ids"]
+    if hasattr(enc, "tolist"):
+        enc = enc.tolist()
+    if enc and isinstance(enc[0], list):
+        enc = enc[0]
+    return [int(t) for t in enc]
+
+
+def chat_stop_token(tokenizer) -> int | None:
+    """The end-of-turn token of a chat tokenizer (``<|eot_id|>`` where the vocabulary has it),
+    else its end-of-sequence token."""
+    tid = tokenizer.convert_tokens_to_ids("<|eot_id|>")
+    if isinstance(tid, int) and tid >= 0 and tid != getattr(tokenizer, "unk_token_id", None):
+        return tid
+    return getattr(tokenizer, "eos_token_id", None)
+
+
 def parse_token_ids(raw: str | None, *, tokenizer, prompt: str, prefix_len: int | None = None,
                     repeat_token_id: int | None = None) -> list[int]:
     if repeat_token_id is not None:

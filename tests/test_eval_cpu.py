@@ -325,3 +325,57 @@ def test_mtbench_ar_baselines_feed_the_atlas_run(tmp_path, monkeypatch):
         assert sorted({x["source"] for x in js}) == ["answers", "ar:ar_1b", "ar:ar_8b"]
     finally:
         judge.close()
+
+
+def _chat_tokenizer(path):
+    """A small word-level tokenizer with a chat template and an end-of-turn token."""
+    from tokenizers import Tokenizer, models, pre_tokenizers
+    from transformers import PreTrainedTokenizerFast
+
+    words = ["<unk>", "<|eot_id|>", "<s>", "user:", "assistant:", "system:"] + [str(i) for i in range(10)] + \
+        ["What", "is", "The", "final", "answer", "Question:", "Solve", "the", "problem", "step", "by"]
+    t = Tokenizer(models.WordLevel({w: i for i, w in enumerate(words)}, unk_token="<unk>"))
+    t.pre_tokenizer = pre_tokenizers.WhitespaceSplit()
+    tok = PreTrainedTokenizerFast(tokenizer_object=t, unk_token="<unk>", eos_token="<s>")
+    tok.chat_template = ("{% for m in messages %}{{ m['role'] }}: {{ m['content'] }} <|eot_id|> {% endfor %}"
+                         "{% if add_generation_prompt %}assistant: {% endif %}")
+    tok.save_pretrained(path)
+    return tok
+
+
+def test_gsm8k_chat_template_prompts(tmp_path):
+    g, prompts = mod("eval.gsm8k"), mod("serving.prompts")
+    tok_dir = tmp_path / "tok"
+    _chat_tokenizer(str(tok_dir))
+    chat = prompts.load_chat_tokenizer(str(tok_dir))
+    assert chat is not None and prompts.chat_stop_token(chat) == 1
+    assert prompts.load_chat_tokenizer(str(tmp_path)) is None  # no template there
+    data = tmp_path / "test.jsonl"
+    data.write_text(json.dumps({"question": "What is 1 1", "answer": "#### 2"}) + "\n")
+    out = tmp_path / "out"
+    assert g.main(_flags(tmp_path, "atlas") + ["--data-file", str(data), "--output-dir", str(out), "--tokenizer",
+                                                 str(tok_dir), "--warmup-runs", "0", "--system-prompt", "by"]) == 0
+    row = json.loads((out / "predictions.jsonl").read_text())
+    want = prompts.chat_ids(chat, g.build_messages("What is 1 1", [], "by"))
+    assert row["prompt_tokens"] == len(want) and want[-1] == chat.convert_tokens_to_ids("assistant:")
+    summary = json.loads((out / "summary.json").read_text())
+    assert summary["settings"]["eos_token_id"] == 1 and summary["settings"]["chat_template"] == "auto"
+
+
+def test_mtbench_chat_template_conversation(tmp_path):
+    mt, prompts = mod("eval.mtbench"), mod("serving.prompts")
+    tok_dir = tmp_path / "tok"
+    chat = _chat_tokenizer(str(tok_dir))
+    q = tmp_path / "q.jsonl"
+    q.write_text(json.dumps({"question_id": 1, "category": "math", "turns": ["What is 1", "The 2"]}) + "\n")
+    out = tmp_path / "mt"
+    assert mt.main(["generate", *_flags(tmp_path, "atlas"), "--questions", str(q), "--output-dir", str(out),
+                    "--tokenizer", str(tok_dir), "--warmup-runs", "0"]) == 0
+    ans = json.loads((out / "answers.jsonl").read_text())
+    assert len(ans["turns"]) == 2
+    # The second prompt is the whole conversation rendered by the template (no tokens lost between turns).
+    first = prompts.chat_ids(chat, [{"role": "user", "content": "What is 1"}])
+    second = prompts.chat_ids(chat, [{"role": "user", "content": "What is 1"},
+                                     {"role": "assistant", "content": ans["turns"][0]["answer"]},
+                                     {"role": "user", "content": "The 2"}])
+    assert [t["prompt_tokens"] for t in ans["turns"]] == [len(first), len(second)]
