@@ -209,10 +209,15 @@ def main(argv=None) -> int:
     arms_ = DrafterArms(dr, store, k, d)
     tree, batch_ar, forest_after_tree = arms_.tree, arms_.batch_ar, arms_.forest_after_tree
 
+    counters = pkg("utils.counters")
+    hot: dict[str, list[dict[str, int]]] = {}
+
     def run(name, fn):
         if name == "forest":
-            fn = fn()
+            fn = fn()  # the untimed tree: before the counter snapshot too
+        before = counters.snapshot()
         dev_ms, host_ms = timed(fn, cuda)
+        hot.setdefault(name, []).append(counters.delta(before))
         dr.drop_speculative()
         return dev_ms, host_ms
 
@@ -238,6 +243,10 @@ def main(argv=None) -> int:
                 if i >= 0:
                     results.setdefault(name, []).append(r)
     out["orders"] = orders
+    # Hot-path counters per timed iteration (kernel launches of this package, host<->device bytes),
+    # averaged over the arm's timed and warm-up runs; set-up work is outside the snapshots.
+    out["hot_path_counters"] = {name: {key: round(statistics.mean(d[key] for d in ds), 1) for key in ds[0]}
+                                for name, ds in hot.items()}
     for name, vals in results.items():
         out[f"{name}_ms"] = round(statistics.mean(v[0] for v in vals), 3)
         out[f"{name}_host_ms"] = round(statistics.mean(v[1] for v in vals), 3)

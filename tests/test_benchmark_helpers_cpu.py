@@ -115,6 +115,8 @@ def test_isolated_benchmark_reference_flags_on_cpu(capsys):
     assert bench.main(base + ["--pair-order-seed", "1", "--skip-verify"]) == 0
     out = json.loads(capsys.readouterr().out.strip().splitlines()[-1])
     assert out["orders"] == ["BA", "AB"] and out["tree_over_batch_ar_blocks"]["blocks"] == 1
+    assert set(out["hot_path_counters"]) == {"tree", "batch_ar_k", "forest", "batch_ar_k2"}
+    assert {"launches", "h2d_bytes", "d2h_bytes"} <= set(out["hot_path_counters"]["forest"])
     assert "target_verify_ms" not in out and "forest_ms" in out
     assert bench.main(base + ["--skip-forest", "--skip-native-batch-ar", "--shared-path-tokens", "1",
                               "--repeat-token-id", "9"]) == 0
