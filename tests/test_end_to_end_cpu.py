@@ -220,3 +220,29 @@ def test_prefix_kv_reads_positions_through_the_page_table():
     assert tuple(kv.shape) == (L, 2, 10, eng.kv.shape[3], eng.kv.shape[5])
     for pos in (0, 5, 9):
         assert torch.equal(kv[1, 0, pos], eng.kv[1, pages[pos // 4], 0, :, pos % 4, :])
+
+
+def test_equivalence_checker_against_a_target_server(tmp_path):
+    """The checker's usual set-up: a running target server (first route, fallback off) over HTTP."""
+    import json
+    import threading
+
+    chk, rpc = mod("serving.check_equivalence"), mod("serving.rpc")
+    engine, target, llama = mod("runtime.engine"), mod("runtime.target"), mod("models.llama")
+    tw = llama.random_weights(llama.get_config("tiny-target"), seed=1, dtype=torch.float32)
+    tv = target.TargetVerifier(engine.LlamaEngine(tw, num_pages=256, page_size=4, max_positions=512), k=1, d=3,
+                               route_selection_policy="first_route")
+    server = rpc.make_server(rpc.TargetServerApp(tv), host="127.0.0.1", port=0)
+    threading.Thread(target=server.serve_forever, daemon=True).start()
+    try:
+        out = tmp_path / "eq.json"
+        url = f"http://127.0.0.1:{server.server_address[1]}"
+        assert chk.main(["--drafter-model", "tiny-drafter", "--target-url", url, "--device", "cpu", "--dtype",
+                         "float32", "--page-size", "4", "--prompt-token-ids", "3,4,5,6,7", "--forest-depths",
+                         "live,1", "--repeats", "1", "--max-new-tokens", "8", "--context-length", "256", "--d", "3",
+                         "--json-out", str(out)]) == 0
+        rep = json.loads(out.read_text())
+        assert rep["passed"] and rep["checked"] == 2 and rep["target_transport"] == "http"
+    finally:
+        server.shutdown()
+        server.server_close()
