@@ -101,16 +101,28 @@ def plan(args, passthrough: list[str]) -> tuple[dict, list[tuple[float | None, P
 
 
 def result_row(variable: str, value, run_dir: Path) -> dict:
+    """One run's row: the swept value, accuracy, speed and fallback figures (the serial generator's
+    own drafter / target / overall rates where the run used it)."""
     summary = json.loads((run_dir / "summary.json").read_text())
     preds = read_jsonl(run_dir / "predictions.jsonl")
     rounds = sum(int(r.get("rounds", 0)) for r in preds)
     fallback = sum(int(r.get("fallback_rounds", 0)) for r in preds)
-    n = summary.get("samples") or 0
-    return {variable: value, "samples": n, "correct": summary.get("correct"), "accuracy": summary.get("accuracy"),
-            "generated_tokens": summary.get("generated_tokens"), "rounds": rounds, "fallback_rounds": fallback,
-            "fallback_rate": fallback / rounds if rounds else None, "tokens_per_s": summary.get("tokens_per_s"),
-            "elapsed_s": summary.get("elapsed_s"),
-            "mean_elapsed_s_per_example": summary["elapsed_s"] / n if n and summary.get("elapsed_s") else None}
+    speed = summary.get("serial_speed") or {}
+    n = summary.get("count") or 0
+    row = {variable: value}
+    if variable == "fallback_threshold":
+        row["fallback_enabled"] = value is not None
+    row.update({"count": n, "correct": summary.get("correct"), "accuracy": summary.get("accuracy"),
+                "generated_tokens": summary.get("generated_tokens"), "fallback_rounds": fallback, "rounds": rounds,
+                "fallback_rate": fallback / rounds if rounds else None,
+                "fallback_appended_tokens": speed.get("fallback_appended_tokens"),
+                "end_to_end_tokens_per_second": summary.get("end_to_end_tokens_per_second"),
+                "serial_overall_tokens_per_second": speed.get("overall_tokens_per_second"),
+                "serial_drafter_tokens_per_second": speed.get("drafter_tokens_per_second"),
+                "serial_target_tokens_per_second": speed.get("target_tokens_per_second"),
+                "elapsed_s": summary.get("elapsed_s"),
+                "mean_elapsed_s_per_example": summary["elapsed_s"] / n if n and summary.get("elapsed_s") else None})
+    return row
 
 
 def main(argv=None) -> int:

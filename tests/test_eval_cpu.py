@@ -192,7 +192,8 @@ def test_gsm8k_sweeps(tmp_path):
                     str(out), "--thresholds", "none", "1e9", *gen]) == 0
     rows = json.loads((out / "results.json").read_text())
     assert [r["fallback_threshold"] for r in rows] == [None, 1e9]
-    assert rows[0]["fallback_rounds"] == 0 and rows[1]["fallback_rate"] == 1.0 and rows[1]["samples"] == 2
+    assert rows[0]["fallback_rounds"] == 0 and rows[1]["fallback_rate"] == 1.0 and rows[1]["count"] == 2
+    assert rows[0]["fallback_enabled"] is False and rows[1]["serial_overall_tokens_per_second"] > 0
     exp = json.loads((out / "experiment.json").read_text())
     assert exp["changed_variable"] == "fallback_threshold" and len(exp["fixed_path_score_weights"]) == 2
     assert (out / "threshold_none" / "summary.json").exists() and (out / "results.csv").exists()
